@@ -1,0 +1,759 @@
+// Varlen paged GQA attention: chunked-prefill and decode sequences in one launch.
+//
+// Replaces the reference's per-layer cache concat + masked SDPA
+// (hayate/model/attention.py:52-64) and the additive mask / position logic it
+// depends on (hayate/model/qwen.py:66-106).  Semantics: the j-th query token of
+// sequence i sits at position prefix_i + j (prefix_i = seq_len_k_i - q_len_i) and
+// attends to keys [0, prefix_i + j] of its own sequence -- the reference's causal
+// mask with cache-padding and left-padding columns removed.  The softmax scale is
+// 1/sqrt(128) (the SDPA default the reference uses).
+//
+// Memory: q/out are [tokens][q_heads][128]; the cache of one layer is
+// [block][2 (K,V)][kv_heads][16][128], all layers back to back.  Block tables are
+// rows of physical block ids (row i = sequence i, or seq_bt_row[i]).
+//
+// Work is planned on the device (plan_kernel) once per step and reused by every
+// layer:
+//   * prefill items -- (seq, kv_head, 16-token tile): one CTA, the 4 query heads
+//     of the group on its 4 warps, K/V tiles of 64 keys staged by TMA;
+//   * decode items  -- (seq, kv_head, block range): one warp with its own TMA
+//     ring of K/V block tiles, mma.sync for QK^T and PV, an online softmax;
+//     sequences split over several items are merged by combine_kernel.
+// The main kernel is persistent (grid = SMs x resident CTAs) and walks the plan
+// with a static stride, so its launch shape does not depend on the batch and a
+// whole step can be captured in a CUDA graph.
+#include "common.cuh"
+#include "attention.cuh"
+
+#include <math.h>
+
+namespace {
+
+constexpr int ATT_WARPS = 4;
+constexpr int ATT_THREADS = ATT_WARPS * 32;
+constexpr int DEC_STAGES = 4;                                    // TMA ring per decode warp
+constexpr int DEC_TILE_BYTES = 2 * HY_BLOCK * HY_HEAD_DIM * 2;   // K+V of one block: 8 KB
+constexpr int DEC_WARP_BYTES = DEC_STAGES * DEC_TILE_BYTES;      // 32 KB
+constexpr int PRE_KEYS = 64;                                     // keys per prefill tile
+constexpr int PRE_BLOCKS = PRE_KEYS / HY_BLOCK;                  // 4
+constexpr int PRE_QROWS = 16;                                    // query tokens per item
+constexpr int PRE_KV_BYTES = PRE_KEYS * HY_HEAD_DIM * 2;         // 16 KB (K or V)
+constexpr int PRE_STAGE_BYTES = 2 * PRE_KV_BYTES;                // 32 KB
+constexpr int PRE_STAGES = 2;
+constexpr int SMEM_PAYLOAD = (ATT_WARPS * DEC_WARP_BYTES > PRE_STAGES * PRE_STAGE_BYTES)
+                                 ? ATT_WARPS * DEC_WARP_BYTES
+                                 : PRE_STAGES * PRE_STAGE_BYTES;
+constexpr int SMEM_BYTES = SMEM_PAYLOAD + 1024;                  // + alignment slack
+constexpr int MIN_SPLIT = 4;                                     // blocks per decode item
+constexpr float NEG_INF = -INFINITY;
+
+struct Shared {
+  uint64_t dec_bar[ATT_WARPS][DEC_STAGES];
+  uint64_t pre_bar[PRE_STAGES];
+};
+
+HY_DEVICE uint8_t* payload_base(uint8_t* dyn) {
+  const uint32_t a = smem_u32(dyn);
+  return dyn + (((a + 1023u) & ~1023u) - a);
+}
+
+// ------------------------------------------------------------------ plan kernel
+constexpr int PLAN_THREADS = 1024;
+
+__device__ int plan_scan(int v, int* ws, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) ws[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = ws[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    ws[lane] = w;
+  }
+  __syncthreads();
+  const int before = warp ? ws[warp - 1] : 0;
+  total = ws[31];
+  __syncthreads();
+  return before + x - v;
+}
+
+__global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
+    const int32_t* __restrict__ cu_q, const int32_t* __restrict__ seq_lens_k, int S,
+    int kv_heads, int warp_slots, PlanView v, int32_t* err) {
+  __shared__ int ws[32];
+  __shared__ int s_total, s_cpre, s_cdec, s_bad;
+  if (threadIdx.x == 0) { s_total = 0; s_cpre = 0; s_cdec = 0; s_bad = 0; }
+  __syncthreads();
+  // Pass 1: KV blocks over all decode sequences.
+  int part = 0;
+  for (int i = threadIdx.x; i < S; i += PLAN_THREADS) {
+    const int q = cu_q[i + 1] - cu_q[i];
+    if (q == 1) part += (seq_lens_k[i] + HY_BLOCK - 1) / HY_BLOCK;
+  }
+  atomicAdd(&s_total, part);
+  __syncthreads();
+  const long target = 2L * warp_slots;
+  const long want = ((long)kv_heads * s_total + target - 1) / target;
+  const int split = (int)max((long)MIN_SPLIT, want);
+
+  // Pass 2: item counts, offsets, items.
+  for (int base = 0; base < S; base += PLAN_THREADS) {
+    const int i = base + threadIdx.x;
+    int npre = 0, ndec = 0, ns = 0, ntile = 0, nblk = 0;
+    if (i < S) {
+      const int q = cu_q[i + 1] - cu_q[i];
+      const int kv = seq_lens_k[i];
+      if (q < 0 || kv < q) atomicOr(&s_bad, HY_ERR_BOUNDS);
+      else if (q == 1) {
+        nblk = (kv + HY_BLOCK - 1) / HY_BLOCK;
+        ns = (nblk + split - 1) / split;
+        ndec = kv_heads * ns;
+      } else if (q > 1) {
+        ntile = (q + PRE_QROWS - 1) / PRE_QROWS;
+        npre = kv_heads * ntile;
+      }
+    }
+    int tpre, tdec;
+    const int opre = plan_scan(npre, ws, tpre);
+    const int odec = plan_scan(ndec, ws, tdec);
+    const int cpre = s_cpre, cdec = s_cdec;
+    if (i < S) {
+      const int p0 = cpre + opre, d0 = cdec + odec;
+      if (p0 + npre > v.max_pre || d0 + ndec > v.max_dec || i >= v.max_seqs) {
+        atomicOr(&s_bad, HY_ERR_PLAN);
+      } else {
+        v.seqinfo[i] = make_int2(d0, ns);
+        for (int g = 0; g < kv_heads; ++g) {
+          for (int s = 0; s < ns; ++s)
+            v.dec[d0 + g * ns + s] = make_int4(i, g, s * split, min(nblk, (s + 1) * split));
+          for (int t = 0; t < ntile; ++t)
+            v.pre[p0 + g * ntile + t] = make_int4(i, g, t * PRE_QROWS, 0);
+        }
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) { s_cpre += tpre; s_cdec += tdec; }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const bool bad = s_bad != 0;
+    v.header[0] = bad ? 0 : min(s_cpre, v.max_pre);
+    v.header[1] = bad ? 0 : min(s_cdec, v.max_dec);
+    v.header[2] = split;
+    v.header[3] = s_bad;
+    if (bad) hy_flag(err, s_bad);
+  }
+}
+
+// ------------------------------------------------------------------ decode item
+struct MainArgs {
+  const __nv_bfloat16* q;
+  __nv_bfloat16* out;
+  int q_heads, kv_heads;
+  int layer_row_base;     // first tensor-map row of this layer
+  int oob_row;            // a row past the end of the map: loads there read zeros
+  int num_blocks;
+  const int32_t* block_tables;
+  int bt_pitch;
+  const int32_t* seq_bt_row;
+  const int32_t* cu_q;
+  const int32_t* seq_lens_k;
+  float scale_log2;
+  int32_t* err;
+};
+
+// Tensor-map row of (block, K or V, kv head).
+HY_DEVICE int kv_row(const MainArgs& a, int blk, int kv, int g) {
+  return a.layer_row_base + ((blk * 2 + kv) * a.kv_heads + g) * HY_BLOCK;
+}
+
+// Returns false if a wait ran out (the caller stops).
+__device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
+                            int item, uint8_t* ring, uint64_t* bars, uint32_t& phase) {
+  const int lane = threadIdx.x & 31;
+  const int4 it = v.dec[item];
+  const int seq = it.x, g = it.y, b0 = it.z, b1 = it.w;
+  const int kv_len = a.seq_lens_k[seq];
+  const int tok = a.cu_q[seq];
+  const int ns = v.seqinfo[seq].y;
+  const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
+  const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
+  const int n = b1 - b0;
+
+  // Issue the K and V tiles of logical block b into ring stage s (lane 0 only).
+  auto issue = [&](int s, int blk) {
+    int rk, rv;
+    if (blk < 0 || blk >= a.num_blocks) {
+      hy_flag(a.err, HY_ERR_BOUNDS);
+      rk = rv = a.oob_row;
+    } else {
+      rk = kv_row(a, blk, 0, g);
+      rv = kv_row(a, blk, 1, g);
+    }
+    uint8_t* st = ring + s * DEC_TILE_BYTES;
+    fence_proxy_async();
+    mbar_arrive_expect_tx(&bars[s], DEC_TILE_BYTES);
+    tma_load_2d(st, map, 0, rk, &bars[s]);
+    tma_load_2d(st + 2048, map, 64, rk, &bars[s]);
+    tma_load_2d(st + 4096, map, 0, rv, &bars[s]);
+    tma_load_2d(st + 6144, map, 64, rv, &bars[s]);
+  };
+
+  if (lane == 0) {
+    for (int s = 0; s < DEC_STAGES && s < n; ++s) issue(s, bt[b0 + s]);
+  }
+  int next_id = (lane == 0 && DEC_STAGES < n) ? bt[b0 + DEC_STAGES] : 0;
+
+  // Query fragments: rows 0..3 are the group's 4 heads; rows 4..15 are zero.
+  const int r = lane >> 2, c = 2 * (lane & 3);
+  uint32_t qa[8][2];
+  {
+    const __nv_bfloat16* qp = a.q + ((size_t)tok * a.q_heads + g * HY_GROUP) * HY_HEAD_DIM;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      if (r < HY_GROUP) {
+        qa[kk][0] = *reinterpret_cast<const uint32_t*>(qp + r * HY_HEAD_DIM + 16 * kk + c);
+        qa[kk][1] = *reinterpret_cast<const uint32_t*>(qp + r * HY_HEAD_DIM + 16 * kk + c + 8);
+      } else {
+        qa[kk][0] = qa[kk][1] = 0u;
+      }
+    }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m = NEG_INF, l = 0.f;
+
+  // Per-lane ldmatrix coordinates.
+  const int mi = lane >> 3, ri = lane & 7;
+  const int k_key = ri + 8 * (mi >> 1), k_dsub = 8 * (mi & 1);   // K: non-transposed
+  const int v_key = ri + 8 * (mi & 1), v_dsub = 8 * (mi >> 1);   // V: transposed
+
+  bool ok = true;
+  for (int i = 0; i < n; ++i) {
+    const int s = i % DEC_STAGES;
+    const bool w_ok = mbar_wait(&bars[s], (phase >> s) & 1u, a.err);
+    if (__any_sync(0xffffffffu, !w_ok)) { ok = false; break; }
+    phase ^= (1u << s);
+    const uint32_t kb = smem_u32(ring + s * DEC_TILE_BYTES);
+    const uint32_t vb = kb + 4096;
+
+    float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int d = 16 * kk + k_dsub;
+      uint32_t b[4];
+      ldmatrix_x4(b, kb + (d >> 6) * 2048 + swz128(k_key, d & 63));
+      const uint32_t af[4] = {qa[kk][0], 0u, qa[kk][1], 0u};
+      mma_bf16_16816(sacc[0], af, b[0], b[1]);
+      mma_bf16_16816(sacc[1], af, b[2], b[3]);
+    }
+    const int kbase = (b0 + i) * HY_BLOCK;
+    float p[2][2];
+    float mx = NEG_INF;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = kbase + nt * 8 + c + e;
+        const float x = key < kv_len ? sacc[nt][e] * a.scale_log2 : NEG_INF;
+        p[nt][e] = x;
+        mx = fmaxf(mx, x);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m, mx);
+    const float m_use = (m_new == NEG_INF) ? 0.f : m_new;
+    const float alpha = exp2f(m - m_use);
+    float psum = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        p[nt][e] = exp2f(p[nt][e] - m_use);
+        psum += p[nt][e];
+      }
+    l = l * alpha + psum;
+    m = m_new;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) { o[j][0] *= alpha; o[j][1] *= alpha; }
+    const uint32_t pa[4] = {pack_bf16(p[0][0], p[0][1]), 0u, pack_bf16(p[1][0], p[1][1]), 0u};
+#pragma unroll
+    for (int j2 = 0; j2 < 8; ++j2) {
+      const int d = 16 * j2 + v_dsub;
+      uint32_t b[4];
+      ldmatrix_x4_trans(b, vb + (d >> 6) * 2048 + swz128(v_key, d & 63));
+      mma_bf16_16816(o[2 * j2], pa, b[0], b[1]);
+      mma_bf16_16816(o[2 * j2 + 1], pa, b[2], b[3]);
+    }
+    __syncwarp();
+    if (i + DEC_STAGES < n && lane == 0) {
+      issue(s, next_id);
+      next_id = (i + DEC_STAGES + 1 < n) ? bt[b0 + i + DEC_STAGES + 1] : 0;
+    }
+  }
+  if (!ok) {
+    // Let the copies still in flight land before the CTA can exit.
+    for (int s = 0; s < DEC_STAGES; ++s) mbar_wait(&bars[s], (phase >> s) & 1u, nullptr);
+    return false;
+  }
+
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  if (r < HY_GROUP) {
+    if (ns <= 1) {
+      const float inv = 1.f / l;
+      __nv_bfloat16* op = a.out + ((size_t)tok * a.q_heads + g * HY_GROUP + r) * HY_HEAD_DIM;
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        *reinterpret_cast<uint32_t*>(op + 8 * j + c) = pack_bf16(o[j][0] * inv, o[j][1] * inv);
+    } else {
+      float* po = v.part_o + ((size_t)item * HY_GROUP + r) * HY_HEAD_DIM;
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        *reinterpret_cast<float2*>(po + 8 * j + c) = make_float2(o[j][0], o[j][1]);
+      if ((lane & 3) == 0) v.part_ml[(size_t)item * HY_GROUP + r] = make_float2(m, l);
+    }
+  }
+  return true;
+}
+
+// ------------------------------------------------------------------ prefill tile
+// CTA-wide: warp w computes query head 4g+w for tokens [t0, t0+16) of seq.
+__device__ bool prefill_tile(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
+                             int item, uint8_t* payload, uint64_t* bars, uint32_t& phase) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int4 it = v.pre[item];
+  const int seq = it.x, g = it.y, t0 = it.z;
+  const int row0 = a.cu_q[seq];
+  const int q_len = a.cu_q[seq + 1] - row0;
+  const int kv_len = a.seq_lens_k[seq];
+  const int prefix = kv_len - q_len;
+  const int nrows = min(PRE_QROWS, q_len - t0);
+  const int kv_end = prefix + t0 + nrows;                   // keys [0, kv_end)
+  const int ntiles = (kv_end + PRE_KEYS - 1) / PRE_KEYS;
+  const int nblk = (kv_end + HY_BLOCK - 1) / HY_BLOCK;
+  const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
+  const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
+  const int hq = g * HY_GROUP + warp;
+
+  auto issue = [&](int t, int s) {
+    uint8_t* st = payload + s * PRE_STAGE_BYTES;
+    fence_proxy_async();
+    mbar_arrive_expect_tx(&bars[s], PRE_STAGE_BYTES);
+#pragma unroll
+    for (int j = 0; j < PRE_BLOCKS; ++j) {
+      const int b = t * PRE_BLOCKS + j;
+      int rk = a.oob_row, rv = a.oob_row;
+      if (b < nblk) {
+        const int blk = bt[b];
+        if (blk >= 0 && blk < a.num_blocks) { rk = kv_row(a, blk, 0, g); rv = kv_row(a, blk, 1, g); }
+        else hy_flag(a.err, HY_ERR_BOUNDS);
+      }
+      tma_load_2d(st + j * 4096, map, 0, rk, &bars[s]);
+      tma_load_2d(st + j * 4096 + 2048, map, 64, rk, &bars[s]);
+      tma_load_2d(st + PRE_KV_BYTES + j * 4096, map, 0, rv, &bars[s]);
+      tma_load_2d(st + PRE_KV_BYTES + j * 4096 + 2048, map, 64, rv, &bars[s]);
+    }
+  };
+
+  __syncthreads();                 // previous users of the payload are done
+  if (tid == 0) {
+    for (int t = 0; t < PRE_STAGES && t < ntiles; ++t) issue(t, t);
+  }
+
+  const int r = lane >> 2, c = 2 * (lane & 3);
+  // Query fragments for rows r and r+8 (tokens t0+r, t0+r+8) of head hq.
+  uint32_t qa[8][4];
+  {
+    const bool v0 = r < nrows, v1 = r + 8 < nrows;
+    const __nv_bfloat16* q0 = a.q + ((size_t)(row0 + t0 + r) * a.q_heads + hq) * HY_HEAD_DIM;
+    const __nv_bfloat16* q1 = q0 + (size_t)8 * a.q_heads * HY_HEAD_DIM;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int d = 16 * kk + c;
+      qa[kk][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d) : 0u;
+      qa[kk][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d) : 0u;
+      qa[kk][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d + 8) : 0u;
+      qa[kk][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d + 8) : 0u;
+    }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m[2] = {NEG_INF, NEG_INF}, l[2] = {0.f, 0.f};
+  const int lim0 = prefix + t0 + r, lim1 = lim0 + 8;        // last visible key per row
+  const int mi = lane >> 3, ri = lane & 7;
+  const int k_key = ri + 8 * (mi >> 1), k_dsub = 8 * (mi & 1);
+  const int v_key = ri + 8 * (mi & 1), v_dsub = 8 * (mi >> 1);
+
+  bool ok = true;
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t % PRE_STAGES;
+    const bool w_ok = mbar_wait(&bars[s], (phase >> s) & 1u, a.err);
+    if (__syncthreads_or(!w_ok)) { ok = false; break; }
+    phase ^= (1u << s);
+    const uint32_t kb = smem_u32(payload + s * PRE_STAGE_BYTES);
+    const uint32_t vb = kb + PRE_KV_BYTES;
+
+    float sacc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+#pragma unroll
+    for (int pr = 0; pr < 4; ++pr) {
+      const int key = 16 * pr + k_key;                        // 16 keys = one block
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int d = 16 * kk + k_dsub;
+        uint32_t b[4];
+        ldmatrix_x4(b, kb + pr * 4096 + (d >> 6) * 2048 + swz128(key & 15, d & 63));
+        mma_bf16_16816(sacc[2 * pr], qa[kk], b[0], b[1]);
+        mma_bf16_16816(sacc[2 * pr + 1], qa[kk], b[2], b[3]);
+      }
+    }
+    const int kbase = t * PRE_KEYS;
+    const bool need_mask = kbase + PRE_KEYS - 1 > prefix + t0;   // diagonal or tail tile
+    float mx0 = NEG_INF, mx1 = NEG_INF;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = kbase + nt * 8 + c + e;
+        float x0 = sacc[nt][e] * a.scale_log2, x1 = sacc[nt][2 + e] * a.scale_log2;
+        if (need_mask) {
+          if (key > lim0 || key >= kv_len) x0 = NEG_INF;
+          if (key > lim1 || key >= kv_len) x1 = NEG_INF;
+        }
+        sacc[nt][e] = x0;
+        sacc[nt][2 + e] = x1;
+        mx0 = fmaxf(mx0, x0);
+        mx1 = fmaxf(mx1, x1);
+      }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
+    const float mu0 = (mn0 == NEG_INF) ? 0.f : mn0, mu1 = (mn1 == NEG_INF) ? 0.f : mn1;
+    const float al0 = exp2f(m[0] - mu0), al1 = exp2f(m[1] - mu1);
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      sacc[nt][0] = exp2f(sacc[nt][0] - mu0);
+      sacc[nt][1] = exp2f(sacc[nt][1] - mu0);
+      sacc[nt][2] = exp2f(sacc[nt][2] - mu1);
+      sacc[nt][3] = exp2f(sacc[nt][3] - mu1);
+      ps0 += sacc[nt][0] + sacc[nt][1];
+      ps1 += sacc[nt][2] + sacc[nt][3];
+    }
+    l[0] = l[0] * al0 + ps0;
+    l[1] = l[1] * al1 + ps1;
+    m[0] = mn0;
+    m[1] = mn1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= al0; o[j][1] *= al0;
+      o[j][2] *= al1; o[j][3] *= al1;
+    }
+#pragma unroll
+    for (int kt = 0; kt < 4; ++kt) {
+      const uint32_t pa[4] = {pack_bf16(sacc[2 * kt][0], sacc[2 * kt][1]),
+                              pack_bf16(sacc[2 * kt][2], sacc[2 * kt][3]),
+                              pack_bf16(sacc[2 * kt + 1][0], sacc[2 * kt + 1][1]),
+                              pack_bf16(sacc[2 * kt + 1][2], sacc[2 * kt + 1][3])};
+      const int key = 16 * kt + v_key;
+#pragma unroll
+      for (int j2 = 0; j2 < 8; ++j2) {
+        const int d = 16 * j2 + v_dsub;
+        uint32_t b[4];
+        ldmatrix_x4_trans(b, vb + kt * 4096 + (d >> 6) * 2048 + swz128(key & 15, d & 63));
+        mma_bf16_16816(o[2 * j2], pa, b[0], b[1]);
+        mma_bf16_16816(o[2 * j2 + 1], pa, b[2], b[3]);
+      }
+    }
+    __syncthreads();
+    if (tid == 0 && t + PRE_STAGES < ntiles) issue(t + PRE_STAGES, s);
+  }
+  if (!ok) {
+    if (tid == 0)
+      for (int s = 0; s < PRE_STAGES; ++s) mbar_wait(&bars[s], (phase >> s) & 1u, nullptr);
+    __syncthreads();
+    return false;
+  }
+  l[0] += __shfl_xor_sync(0xffffffffu, l[0], 1);
+  l[0] += __shfl_xor_sync(0xffffffffu, l[0], 2);
+  l[1] += __shfl_xor_sync(0xffffffffu, l[1], 1);
+  l[1] += __shfl_xor_sync(0xffffffffu, l[1], 2);
+  const float inv0 = 1.f / l[0], inv1 = 1.f / l[1];
+  if (r < nrows) {
+    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + r) * a.q_heads + hq) * HY_HEAD_DIM;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      *reinterpret_cast<uint32_t*>(op + 8 * j + c) = pack_bf16(o[j][0] * inv0, o[j][1] * inv0);
+  }
+  if (r + 8 < nrows) {
+    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + r + 8) * a.q_heads + hq) * HY_HEAD_DIM;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      *reinterpret_cast<uint32_t*>(op + 8 * j + c) = pack_bf16(o[j][2] * inv1, o[j][3] * inv1);
+  }
+  __syncthreads();
+  return true;
+}
+
+__global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
+    const __grid_constant__ CUtensorMap kv_map, MainArgs a, PlanView v) {
+  __shared__ Shared sh;
+  extern __shared__ uint8_t dyn_smem[];
+  uint8_t* payload = payload_base(dyn_smem);
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&kv_map);
+    for (int w = 0; w < ATT_WARPS; ++w)
+      for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&sh.dec_bar[w][s], 1);
+    for (int s = 0; s < PRE_STAGES; ++s) mbar_init(&sh.pre_bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int n_pre = v.header[0], n_dec = v.header[1];
+  const int total = n_pre + (n_dec + ATT_WARPS - 1) / ATT_WARPS;
+  uint32_t dec_phase = 0, pre_phase = 0;
+  for (int k = blockIdx.x; k < total; k += gridDim.x) {
+    if (k < n_pre) {
+      if (!prefill_tile(&kv_map, a, v, k, payload, sh.pre_bar, pre_phase)) return;
+    } else {
+      const int item = (k - n_pre) * ATT_WARPS + warp;
+      if (item < n_dec) {
+        if (!decode_item(&kv_map, a, v, item, payload + warp * DEC_WARP_BYTES,
+                         sh.dec_bar[warp], dec_phase))
+          return;
+      }
+    }
+  }
+}
+
+// Merge the split-K partials of decode sequences with more than one item.
+__global__ void __launch_bounds__(256) combine_kernel(MainArgs a, PlanView v, int S) {
+  const int lane = threadIdx.x & 31;
+  const long total = (long)S * a.kv_heads * HY_GROUP;
+  const long nwarps = (long)gridDim.x * (blockDim.x >> 5);
+  for (long w = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += nwarps) {
+    const int seq = (int)(w / (a.kv_heads * HY_GROUP));
+    const int gh = (int)(w % (a.kv_heads * HY_GROUP));
+    const int g = gh / HY_GROUP, r = gh % HY_GROUP;
+    const int q = a.cu_q[seq + 1] - a.cu_q[seq];
+    if (q != 1) continue;
+    const int2 si = v.seqinfo[seq];
+    const int ns = si.y;
+    if (ns <= 1) continue;
+    const int first = si.x + g * ns;
+    float M = NEG_INF;
+    for (int s = 0; s < ns; ++s) M = fmaxf(M, v.part_ml[(size_t)(first + s) * HY_GROUP + r].x);
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < ns; ++s) {
+      const float2 ml = v.part_ml[(size_t)(first + s) * HY_GROUP + r];
+      const float wgt = exp2f(ml.x - M);
+      L += wgt * ml.y;
+      const float4 po = *reinterpret_cast<const float4*>(
+          v.part_o + ((size_t)(first + s) * HY_GROUP + r) * HY_HEAD_DIM + 4 * lane);
+      acc.x += wgt * po.x; acc.y += wgt * po.y; acc.z += wgt * po.z; acc.w += wgt * po.w;
+    }
+    const float inv = 1.f / L;
+    const int tok = a.cu_q[seq];
+    __nv_bfloat16* op = a.out + ((size_t)tok * a.q_heads + g * HY_GROUP + r) * HY_HEAD_DIM + 4 * lane;
+    uint2 pk;
+    pk.x = pack_bf16(acc.x * inv, acc.y * inv);
+    pk.y = pack_bf16(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(op) = pk;
+  }
+}
+
+// ------------------------------------------------------------------ fp32 path
+// Scalar fp32 attention for the parity build of the model: one warp per
+// (query token, query head), every key visited in order.
+__global__ void __launch_bounds__(256) attn_fp32_kernel(
+    const float* __restrict__ q, float* __restrict__ out, int T, int q_heads, int kv_heads,
+    const float* __restrict__ cache_layer, int num_blocks, const int32_t* __restrict__ block_tables,
+    int bt_pitch, const int32_t* __restrict__ seq_bt_row, const int32_t* __restrict__ cu_q,
+    const int32_t* __restrict__ seq_lens_k, int S, float scale, int32_t* err) {
+  const int lane = threadIdx.x & 31;
+  const long total = (long)T * q_heads;
+  const long nwarps = (long)gridDim.x * (blockDim.x >> 5);
+  for (long w = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += nwarps) {
+    const int row = (int)(w / q_heads), hq = (int)(w % q_heads);
+    const int g = hq / HY_GROUP;
+    int lo = 0, hi = S;                     // seq = last i with cu_q[i] <= row
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (cu_q[mid] <= row) lo = mid; else hi = mid;
+    }
+    const int seq = lo;
+    const int q_len = cu_q[seq + 1] - cu_q[seq];
+    const int prefix = seq_lens_k[seq] - q_len;
+    const int key_end = prefix + (row - cu_q[seq]) + 1;
+    const int bt_row = seq_bt_row ? seq_bt_row[seq] : seq;
+    const int32_t* bt = block_tables + (size_t)bt_row * bt_pitch;
+    const float4 qv = *reinterpret_cast<const float4*>(q + ((size_t)row * q_heads + hq) * HY_HEAD_DIM + 4 * lane);
+    float m = NEG_INF, l = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int key = 0; key < key_end; ++key) {
+      const int blk = bt[key / HY_BLOCK];
+      if (blk < 0 || blk >= num_blocks) { hy_flag(err, HY_ERR_BOUNDS); break; }
+      const size_t kofs = ((((size_t)blk * 2 + 0) * kv_heads + g) * HY_BLOCK + key % HY_BLOCK) * HY_HEAD_DIM;
+      const size_t vofs = kofs + (size_t)kv_heads * HY_BLOCK * HY_HEAD_DIM;
+      const float4 kv4 = *reinterpret_cast<const float4*>(cache_layer + kofs + 4 * lane);
+      float s = qv.x * kv4.x + qv.y * kv4.y + qv.z * kv4.z + qv.w * kv4.w;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      s *= scale;
+      const float m_new = fmaxf(m, s);
+      const float alpha = expf(m - m_new);
+      const float p = expf(s - m_new);
+      l = l * alpha + p;
+      const float4 vv = *reinterpret_cast<const float4*>(cache_layer + vofs + 4 * lane);
+      acc.x = acc.x * alpha + p * vv.x;
+      acc.y = acc.y * alpha + p * vv.y;
+      acc.z = acc.z * alpha + p * vv.z;
+      acc.w = acc.w * alpha + p * vv.w;
+      m = m_new;
+    }
+    const float inv = 1.f / l;
+    *reinterpret_cast<float4*>(out + ((size_t)row * q_heads + hq) * HY_HEAD_DIM + 4 * lane) =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+  }
+}
+
+int g_num_sms[64] = {0};
+int g_ctas_per_sm[64] = {0};
+
+int device_sms(int dev) {
+  if (dev < 0 || dev >= 64) return 148;
+  if (g_num_sms[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_num_sms[dev] = n > 0 ? n : 148;
+  }
+  return g_num_sms[dev];
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ host side
+int hy_attn_warp_slots(int dev) { return device_sms(dev) * ATT_WARPS; }
+
+PlanDims hy_attn_plan_dims(int max_seqs, int max_tokens, int kv_heads, int dev) {
+  PlanDims d;
+  d.max_seqs = max_seqs;
+  d.max_pre = kv_heads * (max_tokens / PRE_QROWS + max_seqs);
+  d.max_dec = kv_heads * max_seqs + 2 * hy_attn_warp_slots(dev);
+  return d;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+size_t hy_attn_workspace_bytes(const PlanDims& d) {
+  size_t off = 256;                                         // header
+  off = align256(off + (size_t)d.max_pre * sizeof(int4));
+  off = align256(off + (size_t)d.max_dec * sizeof(int4));
+  off = align256(off + (size_t)d.max_seqs * sizeof(int2));
+  off = align256(off + (size_t)d.max_dec * HY_GROUP * HY_HEAD_DIM * sizeof(float));
+  off = align256(off + (size_t)d.max_dec * HY_GROUP * sizeof(float2));
+  return off;
+}
+
+static PlanView make_view(void* ws, const PlanDims& d) {
+  PlanView v;
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  size_t off = 0;
+  v.header = reinterpret_cast<int*>(p);
+  off = 256;
+  v.pre = reinterpret_cast<int4*>(p + off);
+  off = align256(off + (size_t)d.max_pre * sizeof(int4));
+  v.dec = reinterpret_cast<int4*>(p + off);
+  off = align256(off + (size_t)d.max_dec * sizeof(int4));
+  v.seqinfo = reinterpret_cast<int2*>(p + off);
+  off = align256(off + (size_t)d.max_seqs * sizeof(int2));
+  v.part_o = reinterpret_cast<float*>(p + off);
+  off = align256(off + (size_t)d.max_dec * HY_GROUP * HY_HEAD_DIM * sizeof(float));
+  v.part_ml = reinterpret_cast<float2*>(p + off);
+  v.max_pre = d.max_pre;
+  v.max_dec = d.max_dec;
+  v.max_seqs = d.max_seqs;
+  return v;
+}
+
+cudaError_t hy_launch_attn_plan(const int32_t* cu_q, const int32_t* seq_lens_k, int S,
+                                int kv_heads, const PlanDims& d, void* ws, int32_t* err,
+                                int dev, cudaStream_t st) {
+  plan_kernel<<<1, PLAN_THREADS, 0, st>>>(cu_q, seq_lens_k, S, kv_heads,
+                                          hy_attn_warp_slots(dev), make_view(ws, d), err);
+  return cudaGetLastError();
+}
+
+cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* q, void* out, int q_heads,
+                                int kv_heads, int layer_row_base, int oob_row, int num_blocks,
+                                const int32_t* block_tables, int bt_pitch,
+                                const int32_t* seq_bt_row, const int32_t* cu_q,
+                                const int32_t* seq_lens_k, int S, float scale,
+                                const PlanDims& d, void* ws, int32_t* err, int dev,
+                                cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_main_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    int occ = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, attn_main_kernel, ATT_THREADS, SMEM_BYTES);
+    g_ctas_per_sm[dev] = occ > 0 ? occ : 1;
+    attr_set[dev] = true;
+  }
+  MainArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.q_heads = q_heads;
+  a.kv_heads = kv_heads;
+  a.layer_row_base = layer_row_base;
+  a.oob_row = oob_row;
+  a.num_blocks = num_blocks;
+  a.block_tables = block_tables;
+  a.bt_pitch = bt_pitch;
+  a.seq_bt_row = seq_bt_row;
+  a.cu_q = cu_q;
+  a.seq_lens_k = seq_lens_k;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.err = err;
+  const PlanView v = make_view(ws, d);
+  const int grid = device_sms(dev) * g_ctas_per_sm[dev < 64 && dev >= 0 ? dev : 0];
+  attn_main_kernel<<<grid, ATT_THREADS, SMEM_BYTES, st>>>(map, a, v);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int cgrid = device_sms(dev) * 4;
+  combine_kernel<<<cgrid, 256, 0, st>>>(a, v, S);
+  return cudaGetLastError();
+}
+
+cudaError_t hy_launch_attn_fp32(const float* q, float* out, int T, int q_heads, int kv_heads,
+                                const float* cache_layer, int num_blocks,
+                                const int32_t* block_tables, int bt_pitch,
+                                const int32_t* seq_bt_row, const int32_t* cu_q,
+                                const int32_t* seq_lens_k, int S, float scale, int32_t* err,
+                                cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  long warps = (long)T * q_heads;
+  long blocks = (warps + 7) / 8;
+  if (blocks > 148L * 32) blocks = 148L * 32;
+  attn_fp32_kernel<<<(int)blocks, 256, 0, st>>>(q, out, T, q_heads, kv_heads, cache_layer,
+                                                num_blocks, block_tables, bt_pitch, seq_bt_row,
+                                                cu_q, seq_lens_k, S, scale, err);
+  return cudaGetLastError();
+}

@@ -1,0 +1,46 @@
+// Plan layout shared by the attention kernels and the C-ABI layer.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+// Capacities of one attention workspace.
+struct PlanDims {
+  int max_pre;     // prefill items (kv_head x 16-token tile)
+  int max_dec;     // decode items (kv_head x block range)
+  int max_seqs;
+};
+
+// Device view of a workspace (see attention.cu for the layout).
+struct PlanView {
+  int* header;        // n_pre, n_dec, split, status
+  int4* pre;
+  int4* dec;
+  int2* seqinfo;      // per sequence: first decode item, number of splits
+  float* part_o;      // [max_dec][4][128]
+  float2* part_ml;    // [max_dec][4]  (running max in log2 units, sum)
+  int max_pre, max_dec, max_seqs;
+};
+
+int hy_attn_warp_slots(int dev);
+PlanDims hy_attn_plan_dims(int max_seqs, int max_tokens, int kv_heads, int dev);
+size_t hy_attn_workspace_bytes(const PlanDims& d);
+
+cudaError_t hy_launch_attn_plan(const int32_t* cu_q, const int32_t* seq_lens_k, int S,
+                                int kv_heads, const PlanDims& d, void* ws, int32_t* err,
+                                int dev, cudaStream_t st);
+cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* q, void* out, int q_heads,
+                                int kv_heads, int layer_row_base, int oob_row, int num_blocks,
+                                const int32_t* block_tables, int bt_pitch,
+                                const int32_t* seq_bt_row, const int32_t* cu_q,
+                                const int32_t* seq_lens_k, int S, float scale,
+                                const PlanDims& d, void* ws, int32_t* err, int dev,
+                                cudaStream_t st);
+cudaError_t hy_launch_attn_fp32(const float* q, float* out, int T, int q_heads, int kv_heads,
+                                const float* cache_layer, int num_blocks,
+                                const int32_t* block_tables, int bt_pitch,
+                                const int32_t* seq_bt_row, const int32_t* cu_q,
+                                const int32_t* seq_lens_k, int S, float scale, int32_t* err,
+                                cudaStream_t st);

@@ -1,0 +1,288 @@
+// C-ABI layer: argument checks, tensor-map cache, error reporting.
+#include "hayate_b200.h"
+#include "common.cuh"
+#include "attention.cuh"
+
+#include <mutex>
+#include <stdio.h>
+#include <string.h>
+
+// Launchers defined in the kernel files.
+cudaError_t hy_launch_pool_init(int32_t*, int32_t*, int, cudaStream_t);
+cudaError_t hy_launch_pack(const int32_t*, int, int, const int32_t*, int, int, int32_t*, int,
+                           int32_t*, int32_t*, int32_t*, int, int32_t*, int32_t*, int32_t*,
+                           int32_t*, int32_t*, int32_t*, int32_t*, int32_t*, cudaStream_t);
+cudaError_t hy_launch_free(const int32_t*, int, int, int32_t*, int, int32_t*, int32_t*,
+                           int32_t*, int, int32_t*, cudaStream_t);
+cudaError_t hy_launch_commit(const int32_t*, int, const int32_t*, const int32_t*, int, int32_t*,
+                             int, int, int32_t*, cudaStream_t);
+cudaError_t hy_launch_qk_norm_rope(int, const void*, int, int, int, int, const int32_t*,
+                                   const void*, const void*, const float*, const float*, int,
+                                   float, void*, void*, void*, const int32_t*, int, int32_t*,
+                                   cudaStream_t);
+cudaError_t hy_launch_kv_append(int, const void*, const void*, int, int, const int32_t*, void*,
+                                int, int32_t*, cudaStream_t);
+cudaError_t hy_launch_argmax(int, const void*, long, int, int, int32_t*, cudaStream_t);
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, const char* detail = nullptr) {
+  if (detail) snprintf(g_last_error, sizeof(g_last_error), fmt, detail);
+  else snprintf(g_last_error, sizeof(g_last_error), "%s", fmt);
+  return code;
+}
+
+int cuda_result(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) { g_last_error[0] = 0; return HY_OK; }
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s", what, cudaGetErrorString(e));
+  return HY_E_CUDA;
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+bool dtype_ok(int32_t dtype) { return dtype == HY_DTYPE_BF16 || dtype == HY_DTYPE_FP32; }
+
+// ---- tensor maps over the bf16 KV cache (one per cache allocation)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct MapEntry {
+  int dev;
+  const void* base;
+  long rows;
+  CUtensorMap map;
+};
+
+std::mutex g_map_mu;
+MapEntry g_maps[32];
+int g_nmaps = 0;
+EncodeTiledFn g_encode = nullptr;
+
+int get_encoder() {
+  if (g_encode) return HY_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                                   cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+    return fail(HY_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  return HY_OK;
+}
+
+// 2-D view of the cache: rows of 128 bf16 (256 B); a box is 16 rows x 64
+// columns (one half of a block's head tile), swizzled 128 B in shared memory.
+int kv_map_for(int dev, const void* base, long rows, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  for (int i = 0; i < g_nmaps; ++i)
+    if (g_maps[i].dev == dev && g_maps[i].base == base && g_maps[i].rows == rows) {
+      *out = g_maps[i].map;
+      return HY_OK;
+    }
+  int rc = get_encoder();
+  if (rc) return rc;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return fail(HY_E_INVALID, "kv_cache must be 16-byte aligned");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {HY_HEAD_DIM, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {HY_HEAD_DIM * 2};
+  cuuint32_t box[2] = {64, HY_BLOCK};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[64];
+    snprintf(buf, sizeof(buf), "%d", (int)r);
+    return fail(HY_E_CUDA, "cuTensorMapEncodeTiled failed (CUresult %s)", buf);
+  }
+  const int slot = g_nmaps < 32 ? g_nmaps++ : (int)(reinterpret_cast<uintptr_t>(base) >> 8) % 32;
+  g_maps[slot] = MapEntry{dev, base, rows, m};
+  *out = m;
+  return HY_OK;
+}
+
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hy_version(void) { return 100; }
+
+const char* hy_get_last_error(void) { return g_last_error; }
+
+int hy_block_pool_init(int32_t* free_stack, int32_t* free_top, int32_t num_blocks, void* stream) {
+  if (!free_stack || !free_top || num_blocks <= 0)
+    return fail(HY_E_INVALID, "hy_block_pool_init: null pointer or num_blocks <= 0");
+  return cuda_result(hy_launch_pool_init(free_stack, free_top, num_blocks, as_stream(stream)),
+                     "hy_block_pool_init");
+}
+
+int hy_pack_batch(const int32_t* sched, int32_t num_seqs, int32_t num_tokens,
+                  const int32_t* req_tokens, int32_t tok_pitch, int32_t max_reqs,
+                  int32_t* block_tables, int32_t bt_pitch, int32_t* req_num_blocks,
+                  int32_t* free_stack, int32_t* free_top, int32_t num_blocks,
+                  int32_t* input_ids, int32_t* positions, int32_t* slot_mapping,
+                  int32_t* cu_seqlens_q, int32_t* seq_lens_k, int32_t* sample_rows,
+                  int32_t* sample_seq, int32_t* err, void* stream) {
+  if (!sched || !req_tokens || !block_tables || !req_num_blocks || !free_stack || !free_top ||
+      !input_ids || !positions || !slot_mapping || !cu_seqlens_q || !seq_lens_k ||
+      !sample_rows || !sample_seq)
+    return fail(HY_E_INVALID, "hy_pack_batch: null pointer");
+  if (num_seqs <= 0 || num_tokens < 0 || tok_pitch <= 0 || max_reqs <= 0 || bt_pitch <= 0 ||
+      num_blocks <= 0)
+    return fail(HY_E_INVALID, "hy_pack_batch: non-positive size");
+  return cuda_result(hy_launch_pack(sched, num_seqs, num_tokens, req_tokens, tok_pitch, max_reqs,
+                                    block_tables, bt_pitch, req_num_blocks, free_stack, free_top,
+                                    num_blocks, input_ids, positions, slot_mapping, cu_seqlens_q,
+                                    seq_lens_k, sample_rows, sample_seq, err, as_stream(stream)),
+                     "hy_pack_batch");
+}
+
+int hy_free_blocks(const int32_t* slots, int32_t n, int32_t max_reqs, int32_t* block_tables,
+                   int32_t bt_pitch, int32_t* req_num_blocks, int32_t* free_stack,
+                   int32_t* free_top, int32_t num_blocks, int32_t* err, void* stream) {
+  if (n == 0) return HY_OK;
+  if (!slots || !block_tables || !req_num_blocks || !free_stack || !free_top || n < 0 ||
+      max_reqs <= 0 || bt_pitch <= 0 || num_blocks <= 0)
+    return fail(HY_E_INVALID, "hy_free_blocks: bad argument");
+  return cuda_result(hy_launch_free(slots, n, max_reqs, block_tables, bt_pitch, req_num_blocks,
+                                    free_stack, free_top, num_blocks, err, as_stream(stream)),
+                     "hy_free_blocks");
+}
+
+int hy_commit_tokens(const int32_t* next_tokens, int32_t n_sample, const int32_t* sample_seq,
+                     const int32_t* sched, int32_t num_seqs, int32_t* req_tokens,
+                     int32_t tok_pitch, int32_t max_reqs, int32_t* err, void* stream) {
+  if (n_sample == 0) return HY_OK;
+  if (!next_tokens || !sample_seq || !sched || !req_tokens || n_sample < 0 || num_seqs <= 0 ||
+      tok_pitch <= 0 || max_reqs <= 0)
+    return fail(HY_E_INVALID, "hy_commit_tokens: bad argument");
+  return cuda_result(hy_launch_commit(next_tokens, n_sample, sample_seq, sched, num_seqs,
+                                      req_tokens, tok_pitch, max_reqs, err, as_stream(stream)),
+                     "hy_commit_tokens");
+}
+
+int hy_qk_norm_rope(int32_t dtype, const void* qkv, int64_t ld, int32_t num_tokens,
+                    int32_t q_heads, int32_t kv_heads, const int32_t* positions,
+                    const void* q_norm_w, const void* k_norm_w, const float* rope_cos,
+                    const float* rope_sin, int32_t max_pos, float eps, void* q_out,
+                    void* k_out, void* kv_cache_layer, const int32_t* slot_mapping,
+                    int32_t num_blocks, int32_t* err, void* stream) {
+  if (!dtype_ok(dtype)) return fail(HY_E_INVALID, "hy_qk_norm_rope: dtype must be 0 or 1");
+  if (num_tokens == 0) return HY_OK;
+  if (!qkv || !positions || !q_norm_w || !k_norm_w || !rope_cos || !rope_sin || num_tokens < 0)
+    return fail(HY_E_INVALID, "hy_qk_norm_rope: bad argument");
+  if (q_heads != HY_GROUP * kv_heads || kv_heads <= 0)
+    return fail(HY_E_UNSUPPORTED, "hy_qk_norm_rope: q_heads must be 4 x kv_heads");
+  if (ld < (int64_t)(q_heads + 2 * kv_heads) * HY_HEAD_DIM || ld > INT32_MAX)
+    return fail(HY_E_INVALID, "hy_qk_norm_rope: ld smaller than one qkv row");
+  if (kv_cache_layer && (!slot_mapping || num_blocks <= 0))
+    return fail(HY_E_INVALID, "hy_qk_norm_rope: cache given without slot_mapping/num_blocks");
+  return cuda_result(
+      hy_launch_qk_norm_rope(dtype, qkv, (int)ld, num_tokens, q_heads, kv_heads, positions,
+                             q_norm_w, k_norm_w, rope_cos, rope_sin, max_pos, eps, q_out, k_out,
+                             kv_cache_layer, slot_mapping, num_blocks, err, as_stream(stream)),
+      "hy_qk_norm_rope");
+}
+
+int hy_kv_append(int32_t dtype, const void* k, const void* v, int32_t num_tokens,
+                 int32_t kv_heads, const int32_t* slot_mapping, void* kv_cache_layer,
+                 int32_t num_blocks, int32_t* err, void* stream) {
+  if (!dtype_ok(dtype)) return fail(HY_E_INVALID, "hy_kv_append: dtype must be 0 or 1");
+  if (num_tokens == 0) return HY_OK;
+  if (!k || !v || !slot_mapping || !kv_cache_layer || num_tokens < 0 || kv_heads <= 0 ||
+      num_blocks <= 0)
+    return fail(HY_E_INVALID, "hy_kv_append: bad argument");
+  return cuda_result(hy_launch_kv_append(dtype, k, v, num_tokens, kv_heads, slot_mapping,
+                                         kv_cache_layer, num_blocks, err, as_stream(stream)),
+                     "hy_kv_append");
+}
+
+size_t hy_attention_workspace_size(int32_t max_seqs, int32_t max_tokens, int32_t kv_heads) {
+  if (max_seqs <= 0 || max_tokens <= 0 || kv_heads <= 0) return 0;
+  return hy_attn_workspace_bytes(hy_attn_plan_dims(max_seqs, max_tokens, kv_heads,
+                                                   current_device()));
+}
+
+int hy_attention_plan(const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, int32_t num_seqs,
+                      int32_t kv_heads, int32_t max_seqs, int32_t max_tokens, void* workspace,
+                      size_t workspace_bytes, int32_t* err, void* stream) {
+  if (!cu_seqlens_q || !seq_lens_k || !workspace || num_seqs <= 0 || kv_heads <= 0)
+    return fail(HY_E_INVALID, "hy_attention_plan: bad argument");
+  if (num_seqs > max_seqs) return fail(HY_E_INVALID, "hy_attention_plan: num_seqs > max_seqs");
+  const int dev = current_device();
+  const PlanDims d = hy_attn_plan_dims(max_seqs, max_tokens, kv_heads, dev);
+  if (workspace_bytes < hy_attn_workspace_bytes(d))
+    return fail(HY_E_INVALID, "hy_attention_plan: workspace smaller than hy_attention_workspace_size");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(HY_E_INVALID, "hy_attention_plan: workspace must be 256-byte aligned");
+  return cuda_result(hy_launch_attn_plan(cu_seqlens_q, seq_lens_k, num_seqs, kv_heads, d,
+                                         workspace, err, dev, as_stream(stream)),
+                     "hy_attention_plan");
+}
+
+int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tokens,
+                        int32_t q_heads, int32_t kv_heads, const void* kv_cache,
+                        int32_t num_layers, int32_t num_blocks, int32_t layer,
+                        const int32_t* block_tables, int32_t bt_pitch,
+                        const int32_t* seq_bt_row, const int32_t* cu_seqlens_q,
+                        const int32_t* seq_lens_k, int32_t num_seqs, float scale,
+                        int32_t max_seqs, int32_t max_tokens, void* workspace,
+                        size_t workspace_bytes, int32_t* err, void* stream) {
+  if (!dtype_ok(dtype)) return fail(HY_E_INVALID, "hy_varlen_attention: dtype must be 0 or 1");
+  if (!q || !out || !kv_cache || !block_tables || !cu_seqlens_q || !seq_lens_k ||
+      num_seqs <= 0 || num_tokens < 0 || num_layers <= 0 || num_blocks <= 0 || layer < 0 ||
+      layer >= num_layers || bt_pitch <= 0)
+    return fail(HY_E_INVALID, "hy_varlen_attention: bad argument");
+  if (q_heads != HY_GROUP * kv_heads || kv_heads <= 0)
+    return fail(HY_E_UNSUPPORTED, "hy_varlen_attention: q_heads must be 4 x kv_heads");
+  if (num_tokens == 0) return HY_OK;
+  const long layer_rows = (long)num_blocks * 2 * kv_heads * HY_BLOCK;
+  if (dtype == HY_DTYPE_FP32) {
+    const float* base = static_cast<const float*>(kv_cache) + (size_t)layer * layer_rows * HY_HEAD_DIM;
+    return cuda_result(hy_launch_attn_fp32(static_cast<const float*>(q), static_cast<float*>(out),
+                                           num_tokens, q_heads, kv_heads, base, num_blocks,
+                                           block_tables, bt_pitch, seq_bt_row, cu_seqlens_q,
+                                           seq_lens_k, num_seqs, scale, err, as_stream(stream)),
+                       "hy_varlen_attention(fp32)");
+  }
+  if (!workspace) return fail(HY_E_INVALID, "hy_varlen_attention: bf16 needs a planned workspace");
+  const long rows = layer_rows * num_layers;
+  if (rows + HY_BLOCK >= (1L << 31))
+    return fail(HY_E_UNSUPPORTED, "hy_varlen_attention: cache exceeds 2^31 rows of 128");
+  const int dev = current_device();
+  const PlanDims d = hy_attn_plan_dims(max_seqs, max_tokens, kv_heads, dev);
+  if (workspace_bytes < hy_attn_workspace_bytes(d))
+    return fail(HY_E_INVALID, "hy_varlen_attention: workspace too small for max_seqs/max_tokens");
+  CUtensorMap map;
+  int rc = kv_map_for(dev, kv_cache, rows, &map);
+  if (rc) return rc;
+  return cuda_result(
+      hy_launch_attn_bf16(map, q, out, q_heads, kv_heads, (int)(layer * layer_rows), (int)rows,
+                          num_blocks, block_tables, bt_pitch, seq_bt_row, cu_seqlens_q,
+                          seq_lens_k, num_seqs, scale, d, workspace, err, dev, as_stream(stream)),
+      "hy_varlen_attention(bf16)");
+}
+
+int hy_argmax(int32_t dtype, const void* logits, int64_t ld, int32_t rows, int32_t vocab,
+              int32_t* out, void* stream) {
+  if (!dtype_ok(dtype)) return fail(HY_E_INVALID, "hy_argmax: dtype must be 0 or 1");
+  if (rows == 0) return HY_OK;
+  if (!logits || !out || rows < 0 || vocab <= 0 || ld < vocab)
+    return fail(HY_E_INVALID, "hy_argmax: bad argument");
+  return cuda_result(hy_launch_argmax(dtype, logits, (long)ld, rows, vocab, out, as_stream(stream)),
+                     "hy_argmax");
+}
+
+}  // extern "C"

@@ -1,0 +1,146 @@
+// Shared device helpers for the hayate_b200 kernels (sm_100a only).
+//
+// * a device-side error word: kernels OR a bit into it instead of trapping;
+// * bounded mbarrier waits (a wait that runs out sets HY_ERR_TIMEOUT and
+//   returns false, so a kernel never spins forever);
+// * TMA tensor loads without multicast, and the warp-level mma.sync/ldmatrix
+//   wrappers used by the decode path.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda.h>
+#include <stdint.h>
+
+// Bits of the device error word.
+#define HY_ERR_BOUNDS   1   // an index (slot, block, position, token) was out of range
+#define HY_ERR_TIMEOUT  2   // an mbarrier wait ran out
+#define HY_ERR_POOL     4   // the block pool had too few free blocks
+#define HY_ERR_PLAN     8   // the attention plan did not fit its workspace
+
+// Fixed geometry the kernels are specialised for.
+#define HY_HEAD_DIM   128
+#define HY_GROUP      4     // query heads per KV head
+#define HY_BLOCK      16    // tokens per KV block
+
+#define HY_DEVICE __device__ __forceinline__
+
+HY_DEVICE void hy_flag(int32_t* err, int bit) {
+  if (err) atomicOr(err, bit);
+}
+
+HY_DEVICE uint64_t hy_globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+HY_DEVICE uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+HY_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+HY_DEVICE void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+               :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+HY_DEVICE void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+
+HY_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete.  Gives up after
+// ~timeout_ns of wall time: sets HY_ERR_TIMEOUT and returns false.
+constexpr uint64_t HY_WAIT_TIMEOUT_NS = 2000000000ull;   // 2 s
+
+HY_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = hy_globaltimer();
+  uint32_t n = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++n & 63) == 0 && hy_globaltimer() - t0 > HY_WAIT_TIMEOUT_NS) {
+      hy_flag(err, HY_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+HY_DEVICE void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+HY_DEVICE void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- TMA
+// 2-D tiled tensor load into shared memory, completion counted on `bar`.
+// No multicast: every CTA loads its own tiles.
+HY_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];"
+      :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
+         "r"(smem_u32(bar))
+      : "memory");
+}
+
+HY_DEVICE void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------- mma.sync
+HY_DEVICE void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+
+HY_DEVICE void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
+HY_DEVICE void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+HY_DEVICE uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Byte offset of element (row, d) inside a [rows][64] bf16 tile region laid
+// out by a TMA load with CU_TENSOR_MAP_SWIZZLE_128B (region base 1024-aligned).
+HY_DEVICE uint32_t swz128(uint32_t row, uint32_t col64) {
+  return row * 128u + ((((col64 >> 3) ^ (row & 7u)) << 4) | ((col64 & 7u) << 1));
+}
+
+template <typename T> struct ElemTraits;
+template <> struct ElemTraits<float> {
+  static HY_DEVICE float to_f(float v) { return v; }
+  static HY_DEVICE float from_f(float v) { return v; }
+};
+template <> struct ElemTraits<__nv_bfloat16> {
+  static HY_DEVICE float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static HY_DEVICE __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};

@@ -1,0 +1,166 @@
+"""Torch-facing wrappers over the C ABI (device tensors in, launches out).
+
+Every function launches on ``torch.cuda.current_stream()`` and returns without
+synchronising.  Shapes and dtypes are checked on the host before the call;
+the kernels check indices on the device and report through the int32 error
+word (bits ``DEV_*``).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import check
+
+DEV_BOUNDS, DEV_TIMEOUT, DEV_POOL, DEV_PLAN = 1, 2, 4, 8
+DTYPES = {torch.bfloat16: 0, torch.float32: 1}
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _i32(t: torch.Tensor, name: str):
+    if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous int32 CUDA tensor")
+
+
+def _dt(t: torch.Tensor) -> int:
+    try:
+        return DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}; use bf16 or fp32") from None
+
+
+def describe_error(word: int) -> str:
+    names = [(DEV_BOUNDS, "index out of range"), (DEV_TIMEOUT, "wait timed out"),
+             (DEV_POOL, "KV block pool exhausted"), (DEV_PLAN, "attention plan overflow")]
+    return ", ".join(n for b, n in names if word & b) or "none"
+
+
+def block_pool_init(free_stack: torch.Tensor, free_top: torch.Tensor) -> None:
+    _i32(free_stack, "free_stack")
+    _i32(free_top, "free_top")
+    check(_lib.load().hy_block_pool_init(_ptr(free_stack), _ptr(free_top), free_stack.numel(),
+                                         _stream()), "hy_block_pool_init")
+
+
+def pack_batch(sched: torch.Tensor, num_seqs: int, num_tokens: int, req_tokens: torch.Tensor,
+               block_tables: torch.Tensor, req_num_blocks: torch.Tensor,
+               free_stack: torch.Tensor, free_top: torch.Tensor, input_ids: torch.Tensor,
+               positions: torch.Tensor, slot_mapping: torch.Tensor, cu_seqlens_q: torch.Tensor,
+               seq_lens_k: torch.Tensor, sample_rows: torch.Tensor, sample_seq: torch.Tensor,
+               err: torch.Tensor) -> None:
+    for n, t in (("sched", sched), ("req_tokens", req_tokens), ("block_tables", block_tables),
+                 ("req_num_blocks", req_num_blocks), ("free_stack", free_stack),
+                 ("free_top", free_top), ("input_ids", input_ids), ("positions", positions),
+                 ("slot_mapping", slot_mapping), ("cu_seqlens_q", cu_seqlens_q),
+                 ("seq_lens_k", seq_lens_k), ("sample_rows", sample_rows),
+                 ("sample_seq", sample_seq), ("err", err)):
+        _i32(t, n)
+    if sched.numel() < 4 * num_seqs or cu_seqlens_q.numel() < num_seqs + 1:
+        raise ValueError("sched/cu_seqlens_q too small for num_seqs")
+    if input_ids.numel() < num_tokens:
+        raise ValueError("token buffers smaller than num_tokens")
+    check(_lib.load().hy_pack_batch(
+        _ptr(sched), num_seqs, num_tokens, _ptr(req_tokens), req_tokens.shape[1],
+        req_tokens.shape[0], _ptr(block_tables), block_tables.shape[1], _ptr(req_num_blocks),
+        _ptr(free_stack), _ptr(free_top), free_stack.numel(), _ptr(input_ids), _ptr(positions),
+        _ptr(slot_mapping), _ptr(cu_seqlens_q), _ptr(seq_lens_k), _ptr(sample_rows),
+        _ptr(sample_seq), _ptr(err), _stream()), "hy_pack_batch")
+
+
+def free_blocks(slots: torch.Tensor, block_tables: torch.Tensor, req_num_blocks: torch.Tensor,
+                free_stack: torch.Tensor, free_top: torch.Tensor, err: torch.Tensor) -> None:
+    _i32(slots, "slots")
+    check(_lib.load().hy_free_blocks(
+        _ptr(slots), slots.numel(), block_tables.shape[0], _ptr(block_tables),
+        block_tables.shape[1], _ptr(req_num_blocks), _ptr(free_stack), _ptr(free_top),
+        free_stack.numel(), _ptr(err), _stream()), "hy_free_blocks")
+
+
+def commit_tokens(next_tokens: torch.Tensor, n_sample: int, sample_seq: torch.Tensor,
+                  sched: torch.Tensor, num_seqs: int, req_tokens: torch.Tensor,
+                  err: torch.Tensor) -> None:
+    check(_lib.load().hy_commit_tokens(
+        _ptr(next_tokens), n_sample, _ptr(sample_seq), _ptr(sched), num_seqs, _ptr(req_tokens),
+        req_tokens.shape[1], req_tokens.shape[0], _ptr(err), _stream()), "hy_commit_tokens")
+
+
+def qk_norm_rope(qkv: torch.Tensor, q_heads: int, kv_heads: int, positions: torch.Tensor,
+                 q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, rope_cos: torch.Tensor,
+                 rope_sin: torch.Tensor, eps: float, q_out: Optional[torch.Tensor] = None,
+                 k_out: Optional[torch.Tensor] = None, kv_cache_layer: Optional[torch.Tensor] = None,
+                 slot_mapping: Optional[torch.Tensor] = None, num_blocks: int = 0,
+                 err: Optional[torch.Tensor] = None) -> None:
+    T = qkv.shape[0]
+    if qkv.stride(1) != 1:
+        raise ValueError("qkv rows must be contiguous")
+    for t in (q_out, k_out, kv_cache_layer):
+        if t is not None and (t.dtype != qkv.dtype or not t.is_contiguous()):
+            raise ValueError("outputs must be contiguous and share qkv's dtype")
+    if rope_cos.dtype != torch.float32 or rope_cos.shape[1] != 64:
+        raise ValueError("rope tables must be fp32 [max_pos][64]")
+    check(_lib.load().hy_qk_norm_rope(
+        _dt(qkv), _ptr(qkv), qkv.stride(0), T, q_heads, kv_heads, _ptr(positions),
+        _ptr(q_norm_w), _ptr(k_norm_w), _ptr(rope_cos), _ptr(rope_sin), rope_cos.shape[0],
+        float(eps), _ptr(q_out), _ptr(k_out), _ptr(kv_cache_layer), _ptr(slot_mapping),
+        num_blocks, _ptr(err), _stream()), "hy_qk_norm_rope")
+
+
+def kv_append(k: torch.Tensor, v: torch.Tensor, slot_mapping: torch.Tensor,
+              kv_cache_layer: torch.Tensor, num_blocks: int,
+              err: Optional[torch.Tensor] = None) -> None:
+    T, kv_heads = k.shape[0], k.shape[1]
+    check(_lib.load().hy_kv_append(_dt(k), _ptr(k), _ptr(v), T, kv_heads, _ptr(slot_mapping),
+                                   _ptr(kv_cache_layer), num_blocks, _ptr(err), _stream()),
+          "hy_kv_append")
+
+
+def attention_workspace_size(max_seqs: int, max_tokens: int, kv_heads: int) -> int:
+    return int(_lib.load().hy_attention_workspace_size(max_seqs, max_tokens, kv_heads))
+
+
+def attention_plan(cu_seqlens_q: torch.Tensor, seq_lens_k: torch.Tensor, num_seqs: int,
+                   kv_heads: int, max_seqs: int, max_tokens: int, workspace: torch.Tensor,
+                   err: Optional[torch.Tensor] = None) -> None:
+    check(_lib.load().hy_attention_plan(
+        _ptr(cu_seqlens_q), _ptr(seq_lens_k), num_seqs, kv_heads, max_seqs, max_tokens,
+        _ptr(workspace), workspace.numel() * workspace.element_size(), _ptr(err), _stream()),
+        "hy_attention_plan")
+
+
+def varlen_attention(q: torch.Tensor, out: torch.Tensor, kv_cache: torch.Tensor, layer: int,
+                     block_tables: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                     seq_lens_k: torch.Tensor, num_seqs: int, max_seqs: int, max_tokens: int,
+                     workspace: Optional[torch.Tensor], seq_bt_row: Optional[torch.Tensor] = None,
+                     scale: Optional[float] = None, err: Optional[torch.Tensor] = None) -> None:
+    """kv_cache: [layers][blocks][2][kv_heads][16][128]; q/out: [tokens][q_heads][128]."""
+    T, q_heads, D = q.shape
+    L, NB, two, kv_heads, bs, D2 = kv_cache.shape
+    if (two, bs, D, D2) != (2, 16, 128, 128):
+        raise ValueError("kv_cache must be [layers][blocks][2][kv_heads][16][128]")
+    if q.dtype != kv_cache.dtype or out.dtype != q.dtype:
+        raise ValueError("q, out and kv_cache must share a dtype")
+    scale = (1.0 / D ** 0.5) if scale is None else scale
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(_lib.load().hy_varlen_attention(
+        _dt(q), _ptr(q), _ptr(out), T, q_heads, kv_heads, _ptr(kv_cache), L, NB, layer,
+        _ptr(block_tables), block_tables.shape[1], _ptr(seq_bt_row), _ptr(cu_seqlens_q),
+        _ptr(seq_lens_k), num_seqs, float(scale), max_seqs, max_tokens, _ptr(workspace),
+        ws_bytes, _ptr(err), _stream()), "hy_varlen_attention")
+
+
+def argmax(logits: torch.Tensor, out: torch.Tensor) -> None:
+    rows, V = logits.shape
+    if logits.stride(1) != 1:
+        raise ValueError("logits rows must be contiguous")
+    _i32(out, "out")
+    check(_lib.load().hy_argmax(_dt(logits), _ptr(logits), logits.stride(0), rows, V, _ptr(out),
+                                _stream()), "hy_argmax")

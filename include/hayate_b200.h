@@ -1,0 +1,154 @@
+/*
+ * hayate_b200 -- C ABI of the B200 continuous-batching kernels.
+ *
+ * Plain C: device pointers, sizes and a CUDA stream passed as void*.  The
+ * library allocates nothing: every buffer (including the attention workspace,
+ * sized by hy_attention_workspace_size) belongs to the caller.  All calls are
+ * asynchronous on the given stream; none synchronises.
+ *
+ * Return value: HY_OK, or a negative HY_E_* code with a message available from
+ * hy_get_last_error() (thread-local).  Device-side problems (an index out of
+ * range, a block pool that ran dry, a wait that ran out) do not trap: the
+ * kernels OR an HY_DEV_* bit into the caller's device error word `err`
+ * (nullable), which the caller reads back when it synchronises.
+ *
+ * Layouts (all row-major):
+ *   qkv           [tokens][ld]: q heads, then k heads, then v heads, 128 each
+ *   q, out        [tokens][q_heads][128]
+ *   KV cache      [layer][block][2 (K,V)][kv_heads][16][128]
+ *   block tables  [rows][bt_pitch] int32 physical block ids in position order
+ *   schedule      int32[4][num_seqs]: slot, start, q_len, flags (bit 0: sample)
+ * dtype: 0 = bf16, 1 = fp32.  q_heads must be 4 x kv_heads; head_dim is 128; a
+ * KV block holds 16 tokens.
+ *
+ * Each entry point names the reference code (axrshz/hayate) it replaces.
+ */
+#ifndef HAYATE_B200_H
+#define HAYATE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HY_OK 0
+#define HY_E_INVALID (-1)     /* bad argument (null pointer, size, dtype) */
+#define HY_E_CUDA (-2)        /* a CUDA call or launch failed */
+#define HY_E_UNSUPPORTED (-3) /* geometry the kernels are not built for */
+
+#define HY_DEV_BOUNDS 1       /* device error word bits */
+#define HY_DEV_TIMEOUT 2
+#define HY_DEV_POOL 4
+#define HY_DEV_PLAN 8
+
+#define HY_DTYPE_BF16 0
+#define HY_DTYPE_FP32 1
+
+/* Library version (major*10000 + minor*100 + patch). */
+int hy_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* hy_get_last_error(void);
+
+/* ---------------------------------------------------------------- packing */
+
+/* Fill the free-block stack with every block id; pops then return 0, 1, 2, ...
+ * Replaces: per-request Cache() creation, hayate/engine/engine.py:63-67 and
+ * hayate/model/cache.py:6-26 (the paged pool supersedes per-request tensors). */
+int hy_block_pool_init(int32_t* free_stack, int32_t* free_top, int32_t num_blocks,
+                       void* stream);
+
+/* Build one step's flat batch from device-resident request state: allocate the
+ * KV blocks the step needs, then write input ids, positions, slot mapping,
+ * cu_seqlens_q (num_seqs+1), seq_lens_k and the rows to sample.
+ * Replaces: Engine.prefill_batch / decode_batch token tensors and left padding
+ * (hayate/engine/engine.py:165-194), position ids and the padding/causal mask
+ * (hayate/model/qwen.py:66-106), and the pad-and-stack cache gather
+ * (engine.py:80-116). */
+int hy_pack_batch(const int32_t* sched, int32_t num_seqs, int32_t num_tokens,
+                  const int32_t* req_tokens, int32_t tok_pitch, int32_t max_reqs,
+                  int32_t* block_tables, int32_t bt_pitch, int32_t* req_num_blocks,
+                  int32_t* free_stack, int32_t* free_top, int32_t num_blocks,
+                  int32_t* input_ids, int32_t* positions, int32_t* slot_mapping,
+                  int32_t* cu_seqlens_q, int32_t* seq_lens_k, int32_t* sample_rows,
+                  int32_t* sample_seq, int32_t* err, void* stream);
+
+/* Return all blocks of the listed slots to the pool.
+ * Replaces: dropping a finished request's Cache (engine.py:196-200, cache.py:25-26). */
+int hy_free_blocks(const int32_t* slots, int32_t n, int32_t max_reqs, int32_t* block_tables,
+                   int32_t bt_pitch, int32_t* req_num_blocks, int32_t* free_stack,
+                   int32_t* free_top, int32_t num_blocks, int32_t* err, void* stream);
+
+/* Append each sampled token to its request's token row.
+ * Replaces: the device->host .item() and list append of
+ * Engine._finalize_generated_token (engine.py:73-78, 178-194). */
+int hy_commit_tokens(const int32_t* next_tokens, int32_t n_sample, const int32_t* sample_seq,
+                     const int32_t* sched, int32_t num_seqs, int32_t* req_tokens,
+                     int32_t tok_pitch, int32_t max_reqs, int32_t* err, void* stream);
+
+/* ------------------------------------------------- QK-norm + RoPE + append */
+
+/* Per-head RMSNorm of q and k, RoPE at `positions`, optional KV append.
+ * rope_cos/rope_sin: fp32 [max_pos][64] (first half of the reference tables).
+ * q_out [tokens][q_heads][128] and k_out [tokens][kv_heads][128] are nullable;
+ * kv_cache_layer (nullable) receives rotated k and raw v at slot_mapping.
+ * Replaces: q_norm/k_norm + apply_rope_vectorized + cache torch.cat,
+ * hayate/model/attention.py:40-56 and hayate/model/rope.py:31-44. */
+int hy_qk_norm_rope(int32_t dtype, const void* qkv, int64_t ld, int32_t num_tokens,
+                    int32_t q_heads, int32_t kv_heads, const int32_t* positions,
+                    const void* q_norm_w, const void* k_norm_w, const float* rope_cos,
+                    const float* rope_sin, int32_t max_pos, float eps, void* q_out,
+                    void* k_out, void* kv_cache_layer, const int32_t* slot_mapping,
+                    int32_t num_blocks, int32_t* err, void* stream);
+
+/* Scatter k and v ([tokens][kv_heads][128]) into the paged cache at
+ * slot_mapping (slot < 0: skipped).
+ * Replaces: torch.cat of new K/V onto the cache (hayate/model/attention.py:52-54)
+ * and the per-request compaction (hayate/engine/engine.py:118-141). */
+int hy_kv_append(int32_t dtype, const void* k, const void* v, int32_t num_tokens,
+                 int32_t kv_heads, const int32_t* slot_mapping, void* kv_cache_layer,
+                 int32_t num_blocks, int32_t* err, void* stream);
+
+/* ------------------------------------------------------------- attention */
+
+/* Bytes of attention workspace for batches of at most max_seqs sequences and
+ * max_tokens query tokens on the current device. */
+size_t hy_attention_workspace_size(int32_t max_seqs, int32_t max_tokens, int32_t kv_heads);
+
+/* Split the step's sequences into prefill tiles and decode items; the plan is
+ * written into the workspace and reused by every layer's hy_varlen_attention.
+ * Replaces: the per-step mask construction, hayate/model/qwen.py:79-106. */
+int hy_attention_plan(const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, int32_t num_seqs,
+                      int32_t kv_heads, int32_t max_seqs, int32_t max_tokens, void* workspace,
+                      size_t workspace_bytes, int32_t* err, void* stream);
+
+/* Causal varlen GQA attention over the paged cache of one layer, chunked
+ * prefill and decode in one launch.  seq_bt_row (nullable) maps sequence i to
+ * its block-table row.  bf16 runs the TMA + tensor-core kernel; fp32 a scalar
+ * kernel for parity runs.  max_seqs/max_tokens must equal those given to
+ * hy_attention_plan for the same workspace.
+ * Replaces: cat + F.scaled_dot_product_attention(attn_mask, enable_gqa=True),
+ * hayate/model/attention.py:52-64. */
+int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tokens,
+                        int32_t q_heads, int32_t kv_heads, const void* kv_cache,
+                        int32_t num_layers, int32_t num_blocks, int32_t layer,
+                        const int32_t* block_tables, int32_t bt_pitch,
+                        const int32_t* seq_bt_row, const int32_t* cu_seqlens_q,
+                        const int32_t* seq_lens_k, int32_t num_seqs, float scale,
+                        int32_t max_seqs, int32_t max_tokens, void* workspace,
+                        size_t workspace_bytes, int32_t* err, void* stream);
+
+/* ---------------------------------------------------------------- sampling */
+
+/* out[r] = argmax(logits[r][0:vocab]) with first-index ties (torch.argmax).
+ * Replaces: Engine.sample, hayate/engine/engine.py:69-71. */
+int hy_argmax(int32_t dtype, const void* logits, int64_t ld, int32_t rows, int32_t vocab,
+              int32_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HAYATE_B200_H */

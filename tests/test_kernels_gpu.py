@@ -1,0 +1,268 @@
+"""CUDA kernels against the oracle, through the C ABI (run on a B200)."""
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from helpers import random_paged_batch, reference_attention
+from hayate_b200 import kernels as K
+from hayate_b200.config import QWEN3_4B
+from oracle import paged as PS
+from oracle import reference as R
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def i32(a):
+    return torch.as_tensor(np.asarray(a), dtype=torch.int32, device=dev).contiguous()
+
+
+# ------------------------------------------------------------------ packing
+class DeviceState:
+    def __init__(self, st: PS.PagedState):
+        self.req_tokens = i32(st.req_tokens)
+        self.block_tables = i32(st.block_tables)
+        self.req_nblk = i32(st.req_nblk)
+        self.free_stack = torch.zeros(st.num_blocks, dtype=torch.int32, device=dev)
+        self.free_top = torch.zeros(1, dtype=torch.int32, device=dev)
+        K.block_pool_init(self.free_stack, self.free_top)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+
+def _pack_step(ds, st, sched, T):
+    S = sched.shape[1]
+    outs = {n: torch.full((max(T, 1),), -7, dtype=torch.int32, device=dev)
+            for n in ("input_ids", "positions", "slot_mapping")}
+    cu = torch.full((S + 1,), -7, dtype=torch.int32, device=dev)
+    kv = torch.full((S,), -7, dtype=torch.int32, device=dev)
+    sr = torch.full((S,), -7, dtype=torch.int32, device=dev)
+    ss = torch.full((S,), -7, dtype=torch.int32, device=dev)
+    K.pack_batch(i32(sched.reshape(-1)), S, T, ds.req_tokens, ds.block_tables, ds.req_nblk,
+                 ds.free_stack, ds.free_top, outs["input_ids"], outs["positions"],
+                 outs["slot_mapping"], cu, kv, sr, ss, ds.err)
+    want = PS.pack(st, sched, T)
+    torch.cuda.synchronize()
+    assert int(ds.err.item()) == 0, K.describe_error(int(ds.err.item()))
+    for n in ("input_ids", "positions", "slot_mapping"):
+        assert np.array_equal(outs[n][:T].cpu().numpy(), want[n]), n
+    assert np.array_equal(cu.cpu().numpy(), want["cu_seqlens_q"])
+    assert np.array_equal(kv.cpu().numpy(), want["seq_lens_k"])
+    ns = len(want["sample_rows"])
+    assert np.array_equal(sr[:ns].cpu().numpy(), want["sample_rows"])
+    assert np.array_equal(ss[:ns].cpu().numpy(), want["sample_seq"])
+    assert np.array_equal(ds.block_tables.cpu().numpy(), st.block_tables)
+    assert np.array_equal(ds.req_nblk.cpu().numpy(), st.req_nblk)
+    assert int(ds.free_top.item()) == st.free_top
+    return want, ss[:ns]
+
+
+def test_pack_commit_free_bit_exact():
+    rng = np.random.default_rng(0)
+    max_reqs, pitch, btp, NB = 40, 700, 48, 600
+    st = PS.PagedState(max_reqs, pitch, btp, NB)
+    st.req_tokens[:] = rng.integers(0, 151936, size=st.req_tokens.shape)
+    ds = DeviceState(st)
+    assert np.array_equal(ds.free_stack.cpu().numpy(), st.free_stack)
+    lens = {s: int(rng.integers(1, 400)) for s in range(0, 36, 2)}   # prompt lengths
+    done = {s: 0 for s in lens}                                       # cached tokens
+    step = 0
+    while any(done[s] < lens[s] + 3 for s in lens) and step < 40:
+        rows = []
+        for s in lens:
+            total = lens[s] + 3
+            if done[s] >= total:
+                continue
+            q = min(int(rng.integers(1, 130)), total - done[s]) if done[s] < lens[s] else 1
+            q = min(q, lens[s] - done[s]) if done[s] < lens[s] else 1
+            rows.append((s, done[s], q, int(done[s] + q >= lens[s])))
+        order = rng.permutation(len(rows))
+        rows = [rows[i] for i in order]
+        sched = PS.make_sched(*zip(*rows))
+        T = int(sched[2].sum())
+        want, ss = _pack_step(ds, st, sched, T)
+        # commit: sampled tokens land after each sequence's last token
+        nxt = rng.integers(0, 151936, size=len(want["sample_seq"])).astype(np.int32)
+        K.commit_tokens(i32(nxt), len(nxt), ss, i32(sched.reshape(-1)), sched.shape[1],
+                        ds.req_tokens, ds.err)
+        PS.commit(st, nxt, want["sample_seq"], sched)
+        for s, start, q, _ in rows:
+            done[s] = start + q
+        # release finished requests
+        fin = [s for s in lens if done[s] >= lens[s] + 3]
+        if fin and step % 3 == 0:
+            K.free_blocks(i32(fin), ds.block_tables, ds.req_nblk, ds.free_stack, ds.free_top,
+                          ds.err)
+            PS.free(st, fin)
+            for s in fin:
+                lens.pop(s)
+                done.pop(s)
+        torch.cuda.synchronize()
+        assert np.array_equal(ds.req_tokens.cpu().numpy(), st.req_tokens)
+        assert np.array_equal(ds.free_stack.cpu().numpy()[:st.free_top],
+                              st.free_stack[:st.free_top])
+        step += 1
+    assert int(ds.err.item()) == 0
+
+
+def test_pack_reports_pool_exhaustion():
+    st = PS.PagedState(4, 200, 16, 3)
+    ds = DeviceState(st)
+    sched = PS.make_sched([0], [0], [100], [1])    # needs 7 blocks, only 3 exist
+    S, T = 1, 100
+    bufs = [torch.zeros(T, dtype=torch.int32, device=dev) for _ in range(3)]
+    small = [torch.zeros(2, dtype=torch.int32, device=dev) for _ in range(4)]
+    K.pack_batch(i32(sched.reshape(-1)), S, T, ds.req_tokens, ds.block_tables, ds.req_nblk,
+                 ds.free_stack, ds.free_top, *bufs, *small, ds.err)
+    torch.cuda.synchronize()
+    assert int(ds.err.item()) & K.DEV_POOL
+
+
+# ------------------------------------------------------- QK-norm + RoPE + append
+@pytest.mark.parametrize("tag,dt", [("bf16", torch.bfloat16), ("fp32", torch.float32)])
+def test_qk_norm_rope_vs_reference_fixture(tag, dt):
+    f = np.load(os.path.join(GOLDEN, "qk_norm_rope.npz"))
+
+    def t(name):
+        a = torch.from_numpy(f[f"{tag}_{name}"])
+        return (a.view(torch.bfloat16) if dt == torch.bfloat16 else a).to(dev)
+    q, k = t("q"), t("k")
+    T, Hq, Hkv = q.shape[0], q.shape[1], k.shape[1]
+    v = torch.randn(T, Hkv, 128, device=dev).to(dt)
+    qkv = torch.cat([q.reshape(T, -1), k.reshape(T, -1), v.reshape(T, -1)], 1).contiguous()
+    cos, sin = R.rope_tables(128, QWEN3_4B.rope_theta, QWEN3_4B.max_position_embeddings)
+    cos64, sin64 = cos[:, :64].contiguous().to(dev), sin[:, :64].contiguous().to(dev)
+    pos = torch.from_numpy(f["positions"]).to(dev).int()
+    q_out = torch.empty_like(q)
+    k_out = torch.empty_like(k)
+    NB = 8
+    cache = torch.zeros(NB, 2, Hkv, 16, 128, dtype=dt, device=dev)
+    slots = torch.randperm(NB * 16, device=dev)[:T].int()
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    K.qk_norm_rope(qkv, Hq, Hkv, pos, t("wq"), t("wk"), cos64, sin64, QWEN3_4B.rms_norm_eps,
+                   q_out=q_out, k_out=k_out, kv_cache_layer=cache, slot_mapping=slots,
+                   num_blocks=NB, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for got, want in ((q_out, t("q_out")), (k_out, t("k_out"))):
+        if dt == torch.bfloat16:
+            # at most one bf16 ulp: the mean-of-squares summation order differs
+            gi = got.view(torch.int16).int()
+            wi = want.view(torch.int16).int()
+            assert (gi - wi).abs().max().item() <= 1
+            assert (gi != wi).float().mean().item() < 0.02
+        else:
+            torch.testing.assert_close(got, want, rtol=2e-6, atol=2e-6)
+    # the cache holds the rotated keys and raw values at their slots
+    want_cache = np.zeros((NB, 2, Hkv, 16, 128), np.float32)
+    PS.kv_append(want_cache, k_out.float().cpu().numpy(), v.float().cpu().numpy(),
+                 slots.cpu().numpy())
+    assert np.array_equal(cache.float().cpu().numpy(), want_cache)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_kv_append_bit_exact(dt):
+    T, Hkv, NB = 57, 8, 9
+    k = torch.randn(T, Hkv, 128, device=dev).to(dt)
+    v = torch.randn(T, Hkv, 128, device=dev).to(dt)
+    slots = torch.randperm(NB * 16, device=dev)[:T].int()
+    slots[3] = -1                                    # padding rows are skipped
+    cache = torch.zeros(NB, 2, Hkv, 16, 128, dtype=dt, device=dev)
+    K.kv_append(k, v, slots, cache, NB)
+    want = np.zeros((NB, 2, Hkv, 16, 128), np.float32)
+    PS.kv_append(want, k.float().cpu().numpy(), v.float().cpu().numpy(), slots.cpu().numpy())
+    torch.cuda.synchronize()
+    assert np.array_equal(cache.float().cpu().numpy(), want)
+
+
+# ------------------------------------------------------------------ attention
+def _run_attention(b, dt, kv_heads, bt_row=None, max_seqs=None, max_tokens=None):
+    S, T = b["S"], b["T"]
+    max_seqs = max_seqs or S
+    max_tokens = max_tokens or T
+    out = torch.full_like(b["q"], float("nan"))
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = None
+    if dt == torch.bfloat16:
+        nbytes = K.attention_workspace_size(max_seqs, max_tokens, kv_heads)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        K.attention_plan(b["cu"], b["kv"], S, kv_heads, max_seqs, max_tokens, ws, err)
+    bt = b["bt"] if bt_row is None else bt_row[0]
+    K.varlen_attention(b["q"], out, b["cache"], b["layer"], bt, b["cu"], b["kv"], S,
+                       max_seqs, max_tokens, ws, seq_bt_row=None if bt_row is None else bt_row[1],
+                       err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, K.describe_error(int(err.item()))
+    return out
+
+
+CASES = {
+    "decode_edges": ([1] * 6, [1, 15, 16, 17, 300, 1000]),
+    "decode_long_split": ([1] * 3, [16384, 5000, 70]),
+    "prefill_only": ([37, 64, 16, 3], [37, 164, 16, 1027]),
+    "mixed": ([1, 512, 1, 5, 1, 129, 1], [1000, 4096, 33, 12, 2049, 129, 7]),
+}
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_attention_bf16_vs_fp32_reference(name):
+    q_lens, kv_lens = CASES[name]
+    b = random_paged_batch(q_lens, kv_lens, kv_heads=8, dtype=torch.bfloat16, seed=sum(map(ord, name)))
+    got = _run_attention(b, torch.bfloat16, 8)
+    want = reference_attention(b)
+    err = (got.float() - want).abs().max().item()
+    assert err <= 2e-2, f"max abs err {err}"
+
+
+def test_attention_bf16_block_table_indirection_and_headroom():
+    q_lens, kv_lens = [1, 40, 1, 1], [77, 300, 16, 5]
+    b = random_paged_batch(q_lens, kv_lens, kv_heads=2, seed=5)
+    # the rows of the real table live at rows 3, 0, 5, 1 of a larger table
+    rows = [3, 0, 5, 1]
+    big = torch.full((6, b["bt"].shape[1]), -1, dtype=torch.int32, device=dev)
+    for i, r in enumerate(rows):
+        big[r] = b["bt"][i]
+    got = _run_attention(b, torch.bfloat16, 2, bt_row=(big, i32(rows)), max_seqs=64,
+                         max_tokens=1024)
+    want = reference_attention(b)
+    assert (got.float() - want).abs().max().item() <= 2e-2
+
+
+def test_attention_micro_shape_reduced():
+    rng = np.random.default_rng(0)
+    dec = np.round(np.exp(rng.uniform(math.log(256), math.log(16384), size=48))).astype(int)
+    q_lens = [512, 512] + [1] * len(dec)
+    kv_lens = [512, 512 + 1536] + dec.tolist()
+    b = random_paged_batch(q_lens, kv_lens, kv_heads=8, seed=11)
+    got = _run_attention(b, torch.bfloat16, 8)
+    want = reference_attention(b)
+    assert (got.float() - want).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("name", ["decode_edges", "mixed"])
+def test_attention_fp32_vs_reference(name):
+    q_lens, kv_lens = CASES[name]
+    b = random_paged_batch(q_lens, kv_lens, kv_heads=8, dtype=torch.float32, seed=3)
+    got = _run_attention(b, torch.float32, 8)
+    want = reference_attention(b)
+    torch.testing.assert_close(got, want, rtol=1e-4, atol=1e-4)
+
+
+# ------------------------------------------------------------------- argmax
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_argmax_first_index_ties(dt):
+    rows, V = 7, 151936
+    x = torch.randn(rows, V, device=dev).to(dt)
+    x[1, 5] = x[1, 100000] = 50.0           # tie -> lowest index
+    x[2, :] = 1.0                            # all equal -> 0
+    x[3, V - 1] = 60.0                       # last column
+    x[4, 77] = float("inf")
+    out = torch.empty(rows, dtype=torch.int32, device=dev)
+    K.argmax(x, out)
+    want = torch.argmax(x, dim=-1).int()
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    assert out[1].item() == 5 and out[2].item() == 0
