@@ -1,0 +1,301 @@
+"""The engine API of the reference, driving the B200 step.
+
+Same surface as hayate/engine/engine.py: ``Request`` (engine.py:17-32),
+``Engine(model_name, compile=False)`` (:35-61), ``add_request`` (:63-67),
+``sample`` (:69-71), ``generate()`` -- one continuous-batching step returning
+False when there is nothing to run (:202-217) -- and ``generate_text(prompts,
+max_tokens=100)`` returning one Request or a list (:219-234).  The attributes
+``pool`` (a ``queue.Queue``), ``current_batch`` and ``request_id`` behave as the
+benchmark expects (benchmark.py:249-264).
+
+What changes underneath: requests live in device-side rows (token ids, block
+tables) and a paged KV cache; each step is one mixed batch of decodes and
+prefill chunks built on the GPU (see ``model.Runner``); decode-only steps
+replay CUDA graphs; the host reads back one small array per step (the sampled
+tokens and the device error word) instead of one ``.item()`` per request.
+
+Prompts are token-id lists or strings.  Strings need a tokenizer: pass one
+with ``encode``/``decode``/``eos_token_id``, or a local Hugging Face tokenizer
+directory as ``model_name``; with no tokenizer, strings are encoded as UTF-8
+bytes.  ``eos_token_id`` stops a request as in the reference (engine.py:76).
+"""
+from __future__ import annotations
+
+import os
+import time
+from dataclasses import dataclass, field
+from queue import Queue
+from typing import Dict, List, Optional, Union
+
+import numpy as np
+import torch
+
+from . import kernels as K
+from . import weights as Wt
+from .config import EngineConfig, ModelConfig, QWEN3_4B, TINY
+from .model import Runner
+from .scheduler import SAMPLE, Scheduler, StepPlan, graph_bucket
+
+MODEL_CONFIGS = {"Qwen/Qwen3-4B": QWEN3_4B, "qwen3-4b": QWEN3_4B, "tiny": TINY}
+
+
+@dataclass
+class Request:
+    id: int = 0
+    prompt: Union[str, List[int]] = ""
+    max_tokens: int = 100
+
+    prompt_tokens: List[int] = field(default_factory=list)
+    tokens: List[int] = field(default_factory=list)
+    kv_cache: object = None          # kept for API compatibility; KV lives in the paged pool
+
+    cache_pos: int = 0               # tokens whose KV is in the cache
+    is_completed: bool = False
+    is_prefill: bool = True
+    use_cache: bool = True
+
+    response: Optional[str] = None
+
+    # engine bookkeeping
+    slot: int = -1
+    _blocks: int = 0
+    _uploaded: bool = False
+    _pinned: Optional[torch.Tensor] = None
+
+
+class ByteTokenizer:
+    """UTF-8 byte tokenizer used for string prompts when no tokenizer is given."""
+    eos_token_id = None
+    pad_token_id = 0
+
+    def encode(self, text):
+        return list(text.encode("utf-8")) if isinstance(text, str) else list(text)
+
+    def decode(self, ids, skip_special_tokens=True):
+        return bytes(i for i in ids if 0 <= i < 256).decode("utf-8", errors="replace")
+
+
+class Engine:
+    def __init__(self, model_name: str = "Qwen/Qwen3-4B", compile: bool = False, *,
+                 model_config: Optional[ModelConfig] = None,
+                 engine_config: Optional[EngineConfig] = None,
+                 dtype: torch.dtype = torch.bfloat16, weights="device", seed: int = 0,
+                 std: float = 0.02, tokenizer=None, device=None):
+        """``weights``: "device" (N(0,std) drawn on the GPU, fast), "exact" (the
+        CPU recipe of ``weights.py``, bit-identical to the parity fixtures), or a
+        ``weights.HostWeights``.  ``compile`` turns on CUDA-graph capture of
+        decode steps (the native counterpart of torch.compile's
+        reduce-overhead mode, engine.py:43-57); it is also on whenever
+        ``engine_config.cuda_graphs`` is set."""
+        if not torch.cuda.is_available():
+            raise RuntimeError("hayate_b200 needs a CUDA device (B200, sm_100a)")
+        self.cfg = model_config or MODEL_CONFIGS.get(model_name, QWEN3_4B)
+        self.ecfg = engine_config or EngineConfig()
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        torch.cuda.set_device(self.device)
+        self.dtype = dtype
+        if dtype == torch.float32:
+            torch.backends.cuda.matmul.allow_tf32 = False
+        self.num_layers = self.cfg.num_layers
+        self.num_kv_groups = self.cfg.num_kv_heads
+        self.head_dim = self.cfg.head_dim
+        self.tokenizer = tokenizer if tokenizer is not None else self._load_tokenizer(model_name)
+        self.eos_token_id = None if self.ecfg.ignore_eos else getattr(
+            self.tokenizer, "eos_token_id", None)
+
+        if isinstance(weights, Wt.HostWeights):
+            hw = weights
+            embed, layers, norms = hw.embed, hw.layers, hw.norms
+        elif weights == "exact":
+            hw = Wt.exact_seeded(self.cfg, seed, std=std)
+            embed, layers, norms = hw.embed, hw.layers, hw.norms
+        elif weights == "device":
+            embed, layers = Wt.device_seeded(self.cfg, seed, self.device, dtype, std=std)
+            norms = None
+        else:
+            raise ValueError(f"unknown weights source {weights!r}")
+        self.runner = Runner(self.cfg, self.ecfg, dtype, self.device, embed, layers, norms)
+        del embed, layers
+        self.scheduler = Scheduler(self.ecfg, self.runner.num_blocks, self.runner.max_reqs)
+        self.use_graphs = bool(compile or self.ecfg.cuda_graphs)
+        self._graphs: Dict[int, torch.cuda.CUDAGraph] = {}
+        self._graph_pool = None
+        S = self.ecfg.max_num_seqs
+        self._sched_host = torch.zeros(4 * S, dtype=torch.int32).pin_memory()
+        self._out_host = torch.zeros(1 + S, dtype=torch.int32).pin_memory()
+        self._done_event = torch.cuda.Event()
+        self._pad_ready = False
+        self.pool: Queue = Queue()
+        self.current_batch: List[Request] = []
+        self.request_id = 0
+        # counters for throughput accounting
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.steps = 0
+        self.graph_steps = 0
+
+    @staticmethod
+    def _load_tokenizer(model_name):
+        if os.path.isdir(model_name):
+            try:
+                from transformers import AutoTokenizer
+                return AutoTokenizer.from_pretrained(model_name, use_fast=True)
+            except Exception:                              # noqa: BLE001
+                pass
+        return ByteTokenizer()
+
+    # ------------------------------------------------------------------ API
+    def add_request(self, request: Request):
+        """adds a request in the pool"""
+        self.pool.put(request)
+
+    def sample(self, logits: torch.Tensor) -> torch.Tensor:
+        """select the next token greedily via argmax (on-GPU kernel)"""
+        logits = logits.contiguous()
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+        K.argmax(logits, out)
+        return out.long().unsqueeze(-1)
+
+    def generate(self) -> bool:
+        """One continuous-batching step; False when there is nothing to run."""
+        self._drain_pool()
+        sch = self.scheduler
+        for r in sch.admit():
+            self._upload_prompt(r)
+        self.current_batch = list(sch.running)
+        if not sch.running:
+            return False
+        plan = sch.schedule()
+        if plan.num_seqs == 0:
+            return True
+        self._run(plan)
+        self._finish(plan)
+        self.current_batch = list(sch.running)
+        return True
+
+    def generate_text(self, prompts, max_tokens: int = 100):
+        """the public api for generation"""
+        if isinstance(prompts, str) or (prompts and isinstance(prompts[0], int)):
+            prompts = [prompts]
+        requests = []
+        for p in prompts:
+            req = Request(id=self.request_id, prompt=p, max_tokens=max_tokens)
+            self.request_id += 1
+            self.add_request(req)
+            requests.append(req)
+        while self.generate():
+            pass
+        return requests[0] if len(requests) == 1 else requests
+
+    # ------------------------------------------------------------------ internals
+    def _drain_pool(self):
+        while not self.pool.empty():
+            r = self.pool.get()
+            if not r.prompt_tokens:
+                r.prompt_tokens = self.tokenizer.encode(r.prompt) if isinstance(r.prompt, str) \
+                    else list(r.prompt)
+            self.scheduler.check_request(r)
+            self.scheduler.waiting.append(r)
+
+    def _upload_prompt(self, r: Request):
+        t = torch.tensor(r.prompt_tokens, dtype=torch.int32).pin_memory()
+        r._pinned = t                                  # keep alive until the copy lands
+        self.runner.req_tokens[r.slot, :t.numel()].copy_(t, non_blocking=True)
+        self.h2d_bytes += t.numel() * 4
+
+    def _ensure_pad_slot(self):
+        """The padding row of graph batches owns one block and one token."""
+        if self._pad_ready:
+            return
+        self._pad_ready = True
+        pad = self.scheduler.pad_slot
+        self._write_sched([(pad, 0, 1, SAMPLE)])
+        self.runner.launch_step(1, 1, 1)
+
+    def _write_sched(self, rows):
+        S = len(rows)
+        a = self._sched_host.numpy()
+        for i, (slot, start, q, fl) in enumerate(rows):
+            a[i], a[S + i], a[2 * S + i], a[3 * S + i] = slot, start, q, fl
+        self.runner.sched[:4 * S].copy_(self._sched_host[:4 * S], non_blocking=True)
+        self.h2d_bytes += 16 * S
+
+    def _run(self, plan: StepPlan):
+        rows = [(e.req.slot, e.start, e.q_len, e.flags) for e in plan.entries]
+        S, T, ns = plan.num_seqs, plan.num_tokens, plan.num_sample
+        if self.use_graphs and plan.decode_only:
+            Sp = graph_bucket(S, self.ecfg.max_num_seqs)
+            self._ensure_pad_slot()
+            pad = self.scheduler.pad_slot
+            rows += [(pad, 0, 1, SAMPLE)] * (Sp - S)
+            self._write_sched(rows)
+            g = self._graphs.get(Sp)
+            if g is None:
+                g = self._capture(Sp)
+            g.replay()
+            self.runner.kernel_launches += self.runner.launches_per_step(True)
+            self.graph_steps += 1
+            n_read = Sp
+        else:
+            self._write_sched(rows)
+            self.runner.launch_step(S, T, ns)
+            n_read = ns
+        self.steps += 1
+        self._out_host[:1 + n_read].copy_(self.runner.out_buf[:1 + n_read], non_blocking=True)
+        self.d2h_bytes += 4 * (1 + n_read)
+        self._done_event.record()
+        self._done_event.synchronize()
+        err = int(self._out_host[0])
+        if err:
+            raise K._lib.HayateError(f"device error word {err}: {K.describe_error(err)}")
+
+    def _capture(self, Sp: int) -> torch.cuda.CUDAGraph:
+        r = self.runner
+        # warm-up on a side stream (allocator + one-time kernel setup), then capture
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        saved = r.sched[:4 * Sp].clone()
+        with torch.cuda.stream(s):
+            r.launch_step(Sp, Sp, Sp)
+        torch.cuda.current_stream().wait_stream(s)
+        # the warm-up wrote real tokens/KV for this step; replaying it rewrites
+        # the same values, so capture simply re-runs from the same schedule
+        r.sched[:4 * Sp].copy_(saved)
+        g = torch.cuda.CUDAGraph()
+        if self._graph_pool is None:
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        with torch.cuda.graph(g, pool=self._graph_pool):
+            r.launch_step(Sp, Sp, Sp)
+        self._graphs[Sp] = g
+        return g
+
+    def _finish(self, plan: StepPlan):
+        toks = self._out_host.numpy()
+        k = 0
+        done = []
+        for e in plan.entries:
+            r = e.req
+            r.cache_pos = e.start + e.q_len
+            if e.flags & SAMPLE:
+                tok = int(toks[1 + k])
+                k += 1
+                r.is_prefill = False
+                r.tokens.append(tok)
+                if tok == self.eos_token_id or len(r.tokens) >= r.max_tokens:
+                    r.is_completed = True
+                    r.response = self.tokenizer.decode(r.tokens, skip_special_tokens=True)
+                    done.append(r)
+        if done:
+            for r in done:
+                self.scheduler.release(r)
+                r._pinned = None
+            slots = torch.tensor([r.slot for r in done], dtype=torch.int32).pin_memory()
+            dslots = slots.to(self.device, non_blocking=True)
+            self.runner.free_slots(dslots)
+            self.h2d_bytes += 4 * len(done)
+
+    # ------------------------------------------------------------------ info
+    def check_device_errors(self) -> int:
+        torch.cuda.synchronize(self.device)
+        return int(self.runner.error_word.item())

@@ -1,0 +1,200 @@
+"""Qwen3 forward over packed ragged batches, on the paged KV cache.
+
+One ``Runner.launch_step`` is the device half of a continuous-batching step:
+
+  pack (on-GPU batch build + block allocation) -> attention plan ->
+  embed -> 36 x [RMSNorm, QKV GEMM, QK-norm+RoPE+KV append, varlen attention,
+  O GEMM + residual, RMSNorm, gate/up GEMM, SiLU*up, down GEMM + residual] ->
+  final RMSNorm on the sampled rows only -> LM-head GEMM -> argmax -> commit.
+
+It replaces ``Qwen3Model.forward`` (hayate/model/qwen.py:46-124) with its block
+and attention modules (block.py:21-31, attention.py:26-66, linear.py:11-14) and
+the engine's gather/scatter around it (engine.py:80-163).  The projections, the
+MLP and the LM head stay on cuBLAS through torch; the RMSNorms, residual adds
+and SiLU are torch element-wise ops with the reference's rounding points.  The
+LM head runs on the last row of each sampled sequence only, where the
+reference computes logits for every position (qwen.py:122-123).
+
+Nothing here synchronises: the step is a fixed sequence of launches over
+static buffers, so a decode step can be captured in a CUDA graph.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import kernels as K
+from .config import EngineConfig, ModelConfig, BLOCK_SIZE
+
+
+@dataclass
+class LayerWeights:
+    w_qkv: torch.Tensor       # (q + 2kv, H)   rows: q_proj | k_proj | v_proj
+    w_o: torch.Tensor         # (H, q)
+    w_gate_up: torch.Tensor   # (2I, H)        rows: gate_proj | up_proj
+    w_down: torch.Tensor      # (H, I)
+    ln1: torch.Tensor         # input_layernorm
+    ln2: torch.Tensor         # post_attention_layernorm
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+
+
+def rope_half_tables(cfg: ModelConfig, device):
+    """fp32 cos/sin [max_pos][64]: the reference's tables (rope.py:3-13; the
+    second half of each row repeats the first) computed with the same ops."""
+    d = cfg.head_dim
+    exps = torch.arange(0, d, 2, dtype=torch.float32)[: d // 2].float() / d
+    inv_freq = 1.0 / (int(cfg.rope_theta) ** exps)
+    pos = torch.arange(cfg.max_position_embeddings, dtype=torch.float32)
+    ang = pos.unsqueeze(1) * inv_freq.unsqueeze(0)
+    return torch.cos(ang).contiguous().to(device), torch.sin(ang).contiguous().to(device)
+
+
+class Runner:
+    """Device state (weights, KV cache, request rows, step buffers) + the step."""
+
+    def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, dtype: torch.dtype,
+                 device: torch.device, embed: torch.Tensor, layers: List[Dict[str, torch.Tensor]],
+                 norms: Optional[Dict[str, torch.Tensor]] = None):
+        cfg.check_kernel_support()
+        if dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("dtype must be bf16 or fp32")
+        if ecfg.block_size != BLOCK_SIZE:
+            raise ValueError(f"block_size must be {BLOCK_SIZE}")
+        self.cfg, self.ecfg, self.dtype, self.device = cfg, ecfg, dtype, device
+        H, I = cfg.hidden_size, cfg.intermediate_size
+        dev = device
+
+        def dn(name, n):
+            if norms is None:
+                return torch.ones(n, dtype=dtype, device=dev)
+            return norms[name].to(device=dev, dtype=dtype)
+
+        self.embed = embed.to(device=dev, dtype=dtype).contiguous()
+        self.layers: List[LayerWeights] = []
+        for l, blk in enumerate(layers):
+            g = lambda k: blk[k].to(device=dev, dtype=dtype)  # noqa: E731
+            self.layers.append(LayerWeights(
+                w_qkv=torch.cat([g("q_proj"), g("k_proj"), g("v_proj")], 0).contiguous(),
+                w_o=g("o_proj").contiguous(),
+                w_gate_up=torch.cat([g("gate_proj"), g("up_proj")], 0).contiguous(),
+                w_down=g("down_proj").contiguous(),
+                ln1=dn(f"layers.{l}.input_layernorm.weight", H),
+                ln2=dn(f"layers.{l}.post_attention_layernorm.weight", H),
+                q_norm=dn(f"layers.{l}.self_attn.q_norm.weight", cfg.head_dim),
+                k_norm=dn(f"layers.{l}.self_attn.k_norm.weight", cfg.head_dim)))
+            for k in list(blk):
+                if blk[k].device == dev:          # drop the per-matrix device copies
+                    del blk[k]
+        self.final_norm = dn("norm.weight", H)
+        self.rope_cos, self.rope_sin = rope_half_tables(cfg, dev)
+
+        # ---- KV cache: [layer][block][K/V][kv_head][16][128]
+        self.num_blocks = ecfg.num_kv_blocks or self._blocks_from_memory()
+        self.kv_cache = torch.zeros(cfg.num_layers, self.num_blocks, 2, cfg.num_kv_heads,
+                                    BLOCK_SIZE, cfg.head_dim, dtype=dtype, device=dev)
+        # ---- request rows (slot max_reqs-1 is the graph padding row)
+        self.max_reqs = ecfg.max_num_seqs + 1
+        self.bt_pitch = -(-ecfg.max_model_len // BLOCK_SIZE)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.req_tokens = torch.zeros(self.max_reqs, ecfg.max_model_len + 1, **i32)
+        self.block_tables = torch.zeros(self.max_reqs, self.bt_pitch, **i32)
+        self.req_nblk = torch.zeros(self.max_reqs, **i32)
+        self.free_stack = torch.zeros(self.num_blocks, **i32)
+        self.free_top = torch.zeros(1, **i32)
+        K.block_pool_init(self.free_stack, self.free_top)
+        # ---- step buffers
+        S, T = ecfg.max_num_seqs, ecfg.max_batched_tokens
+        self.sched = torch.zeros(4 * S, **i32)
+        self.input_ids = torch.zeros(T, **i32)
+        self.positions = torch.zeros(T, **i32)
+        self.slot_mapping = torch.zeros(T, **i32)
+        self.cu_q = torch.zeros(S + 1, **i32)
+        self.seq_lens_k = torch.zeros(S, **i32)
+        self.sample_rows = torch.zeros(S, **i32)
+        self.sample_seq = torch.zeros(S, **i32)
+        self.out_buf = torch.zeros(1 + S, **i32)        # [error word | next tokens]
+        self.q_buf = torch.empty(T, cfg.num_heads, cfg.head_dim, dtype=dtype, device=dev)
+        self.attn_buf = torch.empty_like(self.q_buf)
+        self.ws = None
+        if dtype == torch.bfloat16:
+            nbytes = K.attention_workspace_size(S, T, cfg.num_kv_heads)
+            self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        self.kernel_launches = 0
+
+    # ------------------------------------------------------------------ memory
+    def _blocks_from_memory(self) -> int:
+        free, _ = torch.cuda.mem_get_info(self.device)
+        per_block = (2 * self.cfg.num_kv_heads * BLOCK_SIZE * self.cfg.head_dim *
+                     self.cfg.num_layers * torch.tensor([], dtype=self.dtype).element_size())
+        act = 4 << 30                                    # activations + workspace headroom
+        n = int((free - act) * self.ecfg.kv_cache_fraction) // per_block
+        if n < 16:
+            raise RuntimeError("not enough device memory for the KV cache")
+        return n
+
+    @property
+    def error_word(self) -> torch.Tensor:
+        return self.out_buf[:1]
+
+    @property
+    def next_tokens(self) -> torch.Tensor:
+        return self.out_buf[1:]
+
+    # ------------------------------------------------------------------ step
+    def launch_step(self, S: int, T: int, n_sample: int) -> None:
+        """Enqueue one step for the schedule already in ``self.sched[:4*S]``."""
+        cfg, ecfg = self.cfg, self.ecfg
+        err = self.error_word
+        Hq, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        sched = self.sched[:4 * S]
+        K.pack_batch(sched, S, T, self.req_tokens, self.block_tables, self.req_nblk,
+                     self.free_stack, self.free_top, self.input_ids, self.positions,
+                     self.slot_mapping, self.cu_q, self.seq_lens_k, self.sample_rows,
+                     self.sample_seq, err)
+        cu_q, kv_lens, slots = self.cu_q[:S + 1], self.seq_lens_k[:S], sched[:S]
+        launches = 1
+        if self.ws is not None:
+            K.attention_plan(cu_q, kv_lens, S, Hkv, ecfg.max_num_seqs, ecfg.max_batched_tokens,
+                             self.ws, err)
+            launches += 1
+        pos, smap = self.positions[:T], self.slot_mapping[:T]
+        q, attn = self.q_buf[:T], self.attn_buf[:T]
+        x = F.embedding(self.input_ids[:T], self.embed)
+        eps = cfg.rms_norm_eps
+        I = cfg.intermediate_size
+        for l, w in enumerate(self.layers):
+            h = F.rms_norm(x, (cfg.hidden_size,), w.ln1, eps)
+            qkv = F.linear(h, w.w_qkv)
+            K.qk_norm_rope(qkv, Hq, Hkv, pos, w.q_norm, w.k_norm, self.rope_cos, self.rope_sin,
+                           eps, q_out=q, kv_cache_layer=self.kv_cache[l], slot_mapping=smap,
+                           num_blocks=self.num_blocks, err=err)
+            K.varlen_attention(q, attn, self.kv_cache, l, self.block_tables, cu_q, kv_lens, S,
+                               ecfg.max_num_seqs, ecfg.max_batched_tokens, self.ws,
+                               seq_bt_row=slots, err=err)
+            x = F.linear(attn.view(T, Hq * D), w.w_o) + x
+            h = F.rms_norm(x, (cfg.hidden_size,), w.ln2, eps)
+            gu = F.linear(h, w.w_gate_up)
+            x = F.linear(F.silu(gu[:, :I]) * gu[:, I:], w.w_down) + x
+            launches += 2 if self.ws is None else 3      # + combine kernel
+        if n_sample > 0:
+            hs = x.index_select(0, self.sample_rows[:n_sample])
+            hs = F.rms_norm(hs, (cfg.hidden_size,), self.final_norm, eps)
+            logits = F.linear(hs, self.embed)
+            K.argmax(logits, self.next_tokens[:n_sample])
+            K.commit_tokens(self.next_tokens[:n_sample], n_sample, self.sample_seq, sched, S,
+                            self.req_tokens, err)
+            launches += 2
+        self.kernel_launches += launches
+
+    def free_slots(self, slots: torch.Tensor) -> None:
+        K.free_blocks(slots, self.block_tables, self.req_nblk, self.free_stack, self.free_top,
+                      self.error_word)
+        self.kernel_launches += 1
+
+    def launches_per_step(self, n_sample: bool = True) -> int:
+        per_layer = 2 if self.ws is None else 3
+        return 1 + (self.ws is not None) + per_layer * len(self.layers) + (2 if n_sample else 0)

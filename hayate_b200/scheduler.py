@@ -1,0 +1,144 @@
+"""Host-side continuous-batching scheduler (pure Python, no device calls).
+
+Replaces the reference's step policy (hayate/engine/engine.py:196-217): FIFO
+admission, then every step one *mixed* batch -- all running decodes (one token
+each) followed by prefill chunks of at most ``prefill_chunk`` tokens -- within a
+``max_batched_tokens`` budget.  The reference instead runs padded prefill
+groups of 8 and a separate decode forward.
+
+Admission reserves a request's worst-case KV blocks (prompt + max_tokens) so
+the device block pool can never run dry mid-flight; no preemption is needed.
+Slot ``max_reqs - 1`` is kept for the padding rows of CUDA-graph batches.
+"""
+from __future__ import annotations
+
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Deque, List, Tuple
+
+from .config import EngineConfig
+
+# sched flags
+SAMPLE = 1
+
+
+@dataclass
+class StepEntry:
+    req: object          # the engine's Request
+    start: int           # tokens already in the KV cache
+    q_len: int           # tokens computed this step
+    flags: int           # SAMPLE if the last row yields a token
+
+
+@dataclass
+class StepPlan:
+    entries: List[StepEntry] = field(default_factory=list)
+
+    @property
+    def num_seqs(self) -> int:
+        return len(self.entries)
+
+    @property
+    def num_tokens(self) -> int:
+        return sum(e.q_len for e in self.entries)
+
+    @property
+    def num_sample(self) -> int:
+        return sum(1 for e in self.entries if e.flags & SAMPLE)
+
+    @property
+    def decode_only(self) -> bool:
+        return all(e.q_len == 1 and e.start > 0 for e in self.entries)
+
+
+def blocks_for(tokens: int, block_size: int) -> int:
+    return -(-tokens // block_size)
+
+
+class Scheduler:
+    def __init__(self, cfg: EngineConfig, num_blocks: int, max_reqs: int):
+        if cfg.max_num_seqs > cfg.max_batched_tokens:
+            raise ValueError("max_num_seqs must not exceed max_batched_tokens")
+        self.cfg = cfg
+        self.pad_slot = max_reqs - 1
+        self.free_slots: Deque[int] = deque(range(max_reqs - 1))
+        self.free_blocks = num_blocks - 1          # one block for the padding slot
+        self.waiting: Deque = deque()
+        self.running: List = []
+
+    # ---------------------------------------------------------------- admission
+    def reserve_for(self, req) -> int:
+        total = min(len(req.prompt_tokens) + max(req.max_tokens, 1), self.cfg.max_model_len)
+        return blocks_for(total, self.cfg.block_size)
+
+    def check_request(self, req) -> None:
+        n = len(req.prompt_tokens)
+        if n == 0:
+            raise ValueError(f"request {req.id}: empty prompt")
+        if n + 1 > self.cfg.max_model_len:
+            raise ValueError(f"request {req.id}: prompt of {n} tokens exceeds max_model_len "
+                             f"{self.cfg.max_model_len}")
+        if self.reserve_for(req) > self.free_blocks + self._reserved():
+            raise ValueError(f"request {req.id}: needs more KV blocks than the cache holds")
+
+    def _reserved(self) -> int:
+        return sum(r._blocks for r in self.running)
+
+    def admit(self) -> List:
+        """Move waiting requests into the running set (FIFO, stop at the first misfit)."""
+        admitted = []
+        while self.waiting and len(self.running) < self.cfg.max_num_seqs and self.free_slots:
+            req = self.waiting[0]
+            need = self.reserve_for(req)
+            if need > self.free_blocks:
+                break
+            self.waiting.popleft()
+            req.slot = self.free_slots.popleft()
+            req._blocks = need
+            self.free_blocks -= need
+            self.running.append(req)
+            admitted.append(req)
+        return admitted
+
+    def release(self, req) -> None:
+        self.running.remove(req)
+        self.free_slots.append(req.slot)
+        self.free_blocks += req._blocks
+        req._blocks = 0
+
+    # ---------------------------------------------------------------- one step
+    def schedule(self) -> StepPlan:
+        budget = self.cfg.max_batched_tokens
+        plan = StepPlan()
+        for r in self.running:                      # decodes first, one token each
+            if not r.is_prefill and not r.is_completed:
+                plan.entries.append(StepEntry(r, r.cache_pos, 1, SAMPLE))
+                budget -= 1
+        for r in self.running:                      # then prefill chunks, FIFO
+            if not r.is_prefill or budget <= 0:
+                continue
+            rem = len(r.prompt_tokens) - r.cache_pos
+            q = min(rem, self.cfg.prefill_chunk, budget)
+            if q <= 0:
+                continue
+            done = r.cache_pos + q == len(r.prompt_tokens)
+            plan.entries.append(StepEntry(r, r.cache_pos, q, SAMPLE if done else 0))
+            budget -= q
+        return plan
+
+
+def graph_bucket(n: int, max_seqs: int) -> int:
+    """Smallest captured batch size holding n decode rows."""
+    b = 1
+    while b < n:
+        b = b * 2 if b < 16 else b + 16
+    return min(b, max_seqs)
+
+
+def graph_buckets(max_seqs: int) -> List[int]:
+    out, b = [], 1
+    while b < max_seqs:
+        out.append(b)
+        b = b * 2 if b < 16 else b + 16
+    out.append(max_seqs)
+    return out

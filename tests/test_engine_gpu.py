@@ -1,0 +1,114 @@
+"""The engine end to end on a B200 against the reference's greedy tokens."""
+import json
+import os
+
+import pytest
+import torch
+
+from conftest import GOLDEN
+from hayate_b200 import weights as W
+from hayate_b200.config import EngineConfig, QWEN3_4B, TINY
+from hayate_b200.engine import Engine, Request
+
+pytestmark = pytest.mark.gpu
+
+TINY_GOLD = json.load(open(os.path.join(GOLDEN, "tiny_engine.json")))
+
+
+def tiny_engine(dtype, graphs, chunk=64, max_seqs=32):
+    ecfg = EngineConfig(max_num_seqs=max_seqs, max_batched_tokens=256, prefill_chunk=chunk,
+                        num_kv_blocks=512, max_model_len=1024, cuda_graphs=graphs)
+    hw = W.exact_seeded(TINY, 0, std=TINY_GOLD["std"])
+    return Engine("tiny", model_config=TINY, engine_config=ecfg, dtype=dtype, weights=hw)
+
+
+def run_scenario(eng, sc):
+    if sc["kind"] == "upfront":
+        reqs = eng.generate_text([r["prompt"] for r in sc["requests"]],
+                                 max_tokens=sc["requests"][0]["max_tokens"])
+        return reqs if isinstance(reqs, list) else [reqs]
+    arrivals = sorted((r["arrival_step"], i) for i, r in enumerate(sc["requests"]))
+    out = [None] * len(sc["requests"])
+    step = 0
+    while arrivals or eng.current_batch or not eng.pool.empty():
+        while arrivals and arrivals[0][0] <= step:
+            _, i = arrivals.pop(0)
+            r = sc["requests"][i]
+            out[i] = Request(id=eng.request_id, prompt=r["prompt"], max_tokens=r["max_tokens"])
+            eng.request_id += 1
+            eng.add_request(out[i])
+        eng.generate()
+        step += 1
+    return out
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+@pytest.mark.parametrize("name", sorted(TINY_GOLD["scenarios"]))
+def test_tiny_fp32_tokens_equal_reference(name, graphs):
+    eng = tiny_engine(torch.float32, graphs)
+    sc = TINY_GOLD["scenarios"][name]
+    reqs = run_scenario(eng, sc)
+    for r, want in zip(reqs, sc["requests"]):
+        assert r.is_completed
+        assert r.tokens == want["tokens"], (r.id, len(r.prompt_tokens))
+    assert eng.check_device_errors() == 0
+    if graphs and name in ("batch5", "staggered25"):
+        assert eng.graph_steps > 0
+
+
+def test_tiny_bf16_first_tokens_where_margin_is_clear():
+    eng = tiny_engine(torch.bfloat16, True)
+    checked = 0
+    for sc in TINY_GOLD["scenarios"].values():
+        reqs = run_scenario(eng, sc)
+        for r, want in zip(reqs, sc["requests"]):
+            assert r.is_completed and len(r.tokens) == len(want["tokens"])
+            if want["margins"][0] > 0.15:
+                assert r.tokens[0] == want["tokens"][0]
+                checked += 1
+    assert checked >= 10
+    assert eng.check_device_errors() == 0
+
+
+def test_engine_api_shapes():
+    eng = tiny_engine(torch.bfloat16, False)
+    one = eng.generate_text([5, 6, 7], max_tokens=3)
+    assert isinstance(one, Request) and len(one.tokens) == 3 and one.is_completed
+    many = eng.generate_text([[1, 2], [3]], max_tokens=2)
+    assert isinstance(many, list) and all(len(r.tokens) == 2 for r in many)
+    assert eng.generate() is False
+    s = eng.generate_text("hi", max_tokens=1)
+    assert s.prompt_tokens == list(b"hi") and s.response is not None
+
+
+FULL = json.load(open(os.path.join(GOLDEN, "full_greedy.json")))
+
+
+@pytest.fixture(scope="module")
+def full_fp32_engine():
+    hw = W.exact_seeded(QWEN3_4B, 0)
+    fp = W.fingerprint(hw)
+    for k, v in FULL["fingerprint"].items():
+        assert fp[k] == v, f"weights differ from the fixture's at {k}"
+    ecfg = EngineConfig(max_num_seqs=16, max_batched_tokens=4096, prefill_chunk=512,
+                        num_kv_blocks=2048, max_model_len=2048, cuda_graphs=True)
+    eng = Engine("Qwen/Qwen3-4B", engine_config=ecfg, dtype=torch.float32, weights=hw)
+    del hw
+    yield eng
+    del eng
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("case,ntok", [("single", 32), ("upfront", 32)])
+def test_qwen3_4b_fp32_greedy_matches_reference(full_fp32_engine, case, ntok):
+    eng = full_fp32_engine
+    want = FULL["cases"][case]
+    reqs = eng.generate_text([r["prompt"] for r in want], max_tokens=ntok)
+    reqs = reqs if isinstance(reqs, list) else [reqs]
+    for r, w in zip(reqs, want):
+        got, exp = r.tokens[:ntok], w["tokens"][:ntok]
+        if got != exp:
+            i = next(j for j in range(ntok) if got[j] != exp[j])
+            pytest.fail(f"request {r.id}: first divergence at token {i} "
+                        f"(reference top-2 margin there {w['margins'][i]:.3g})")
+    assert eng.check_device_errors() == 0
