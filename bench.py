@@ -1,0 +1,358 @@
+"""Throughput benchmark of the B200 continuous-batching engine (one JSON line).
+
+``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hayate|reference]``
+
+A *step* is one complete run of the "submit all upfront" workload through the
+engine: 10 requests with prompt lengths U[64,512] (uniform random token ids),
+256 greedy tokens each, Qwen3-4B architecture in bf16 with random N(0,0.02)
+weights (seed 0), continuous batching until every request finishes.  Under
+torchrun every rank is an independent replica on its own GPU with its own
+requests (seed = rank): request-level data parallelism, no collective on the
+data path (weak scaling).  ``value`` is total output tokens of all ranks over
+the slowest rank's device time; ``e2e`` is the same metric through
+``Engine.generate_text`` with host token lists in and out.
+
+The line also carries the ragged-attention roofline (the operator case of 256
+decode sequences with contexts log-uniform in [256,16384] plus 4 prefill
+chunks of 512 tokens, one layer, paged KV in 16-token blocks) and, at N=1, a
+CPU baseline: the reference algorithm (``oracle.reference``) timed on this
+host's cores.  ``--impl reference`` times only that CPU path.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+WORKLOAD = ("upfront: 10 requests/GPU, prompt lengths U[64,512], uniform-random ids, 256 greedy "
+            "tokens each, all submitted at once; Qwen3-4B arch (36 layers, hidden 2560, 32/8 "
+            "heads, MLP 9728, vocab 151936) bf16 random-init N(0,0.02) seed 0")
+N_REQ, MAX_TOKENS = 10, 256
+PEAKS_FILE = os.path.join(REPO, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ---------------------------------------------------------------------- dist
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world, local):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[local])
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.p = None
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+            self.p = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", uuid], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except Exception:                                   # noqa: BLE001
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------- engine arm
+def make_engine(device):
+    from hayate_b200.config import EngineConfig
+    from hayate_b200.engine import Engine
+    ecfg = EngineConfig(max_num_seqs=16, max_batched_tokens=8192, prefill_chunk=512,
+                        num_kv_blocks=1024, max_model_len=1024, cuda_graphs=True,
+                        ignore_eos=True)
+    return Engine("Qwen/Qwen3-4B", engine_config=ecfg, dtype=torch.bfloat16, weights="device",
+                  seed=0, device=device)
+
+
+def run_workload(eng, prompts, max_tokens):
+    reqs = eng.generate_text(prompts, max_tokens=max_tokens)
+    reqs = reqs if isinstance(reqs, list) else [reqs]
+    return sum(len(r.tokens) for r in reqs)
+
+
+def timed(eng, fn, steps):
+    """CUDA-event time (ms) of `steps` calls of fn on the engine's stream."""
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    start.record()
+    toks = 0
+    for _ in range(steps):
+        toks += fn()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end), toks, (time.perf_counter() - w0) * 1e3
+
+
+def read_peaks():
+    try:
+        with open(PEAKS_FILE) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:                                        # noqa: BLE001
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the attention kernel from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", "varlen_attention_micro.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------- CPU arm
+def cpu_reference_decode(steps: int, warmup: int, seed: int = 0):
+    """The reference step loop (oracle.reference.RefEngine) on this host's CPU
+    cores: decode steps of the 10-request upfront batch at its prompt lengths,
+    bf16, caches pre-filled with random values (a decode step's cost does not
+    depend on them).  Returns (output tok/s, seconds per step, threads)."""
+    from hayate_b200.config import QWEN3_4B as cfg
+    from hayate_b200.workloads import upfront
+    from oracle import reference as R
+    from hayate_b200 import weights as Wt
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(seed)
+
+    def rnd(*shape):
+        return (torch.randn(*shape, generator=g, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+    # the seed-0 weights of the parity fixtures, filled block-parallel
+    Wr = R.RefWeights.from_host(Wt.exact_seeded(cfg, seed), torch.bfloat16)
+    eng = R.RefEngine(Wr)
+    for sr in upfront(seed=seed):
+        r = eng.add(sr.prompt, 10 ** 6)
+        L = len(sr.prompt)
+        r.k = rnd(cfg.num_layers, cfg.num_kv_heads, L, cfg.head_dim)
+        r.v = rnd(cfg.num_layers, cfg.num_kv_heads, L, cfg.head_dim)
+        r.cache_pos, r.is_prefill, r.tokens = L, False, [int(sr.prompt[-1])]
+    for _ in range(warmup):
+        eng.step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        eng.step()
+    dt = (time.perf_counter() - t0) / steps
+    return N_REQ / dt, dt, threads
+
+
+def reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    tok_s, dt, threads = cpu_reference_decode(args.steps, args.warmup)
+    line = {
+        "impl": "reference", "metric": "total output tok/s", "value": tok_s, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "requests_per_gpu": N_REQ, "max_tokens": MAX_TOKENS},
+        "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": "one step = one decode step of the 10-request upfront batch "
+                                   "through the reference step loop restated on CPU "
+                                   "(oracle/reference.py, engine.py:184-217), bf16, caches at "
+                                   "the prompt lengths pre-filled with random values; prefill "
+                                   "not timed"},
+        "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="hayate", choices=["hayate", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--attn-iters", type=int, default=20)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warmup raised to 3 (timing rule)")
+        args.warmup = 3
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        reference_arm(args, world, rank)
+        return
+    from hayate_b200.workloads import upfront
+
+    device = torch.device("cuda", local)
+    eng = make_engine(device)
+    reqs = upfront(seed=rank)
+    host_prompts = [r.prompt for r in reqs]
+    dev_prompts = [torch.tensor(p, dtype=torch.int32, device=device) for p in host_prompts]
+
+    def device_run():
+        return run_workload(eng, dev_prompts, MAX_TOKENS)
+
+    def e2e_run():
+        return run_workload(eng, host_prompts, MAX_TOKENS)
+
+    for _ in range(args.warmup):
+        device_run()
+    e2e_run()
+    barrier(world, local)
+    launches0 = eng.runner.kernel_launches
+    clk = ClockSampler(local)
+    ms, toks, wall_ms = timed(eng, device_run, args.steps)
+    clocks = clk.stop()
+    launches = eng.runner.kernel_launches - launches0
+    barrier(world, local)
+    ms_max = max_over_ranks(ms, world)
+    toks_all = sum_over_ranks(toks, world)
+
+    h0, d0 = eng.h2d_bytes, eng.d2h_bytes
+    barrier(world, local)
+    ems, etoks, ewall = timed(eng, e2e_run, args.steps)
+    barrier(world, local)
+    ems_max = max_over_ranks(ems, world)
+    etoks_all = sum_over_ranks(etoks, world)
+    h2d = (eng.h2d_bytes - h0) / args.steps
+    d2h = (eng.d2h_bytes - d0) / args.steps
+    err = eng.check_device_errors()
+    if err:
+        raise RuntimeError(f"device error word {err}")
+
+    # ragged-attention roofline (every rank runs it; rank 0 reports)
+    del eng
+    torch.cuda.empty_cache()
+    from hayate_b200.microbench import attention_micro
+    am = attention_micro(args.attn_iters)
+    peak, peak_kind = read_peaks()
+    achieved = am["bytes"] / (am["ms_mean"] * 1e-3) / 1e9
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        tok_s, dt, threads = cpu_reference_decode(steps=3, warmup=1)
+        cpu = {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": "3 decode steps (after 1 warm-up) of the 10-request upfront batch "
+                         "through the reference step loop restated on CPU (oracle/reference.py), "
+                         "bf16, caches at the prompt lengths pre-filled with random values; "
+                         "prefill not timed"}
+    if rank == 0:
+        emit_line(args, world, toks_all, ms_max, wall_ms, etoks_all, ems_max, h2d, d2h, launches,
+                  am, achieved, peak, peak_kind, cpu, clocks)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def emit_line(args, world, toks_all, ms_max, wall_ms, etoks_all, ems_max, h2d, d2h, launches,
+              am, achieved, peak, peak_kind, cpu, clocks):
+    line = {
+        "metric": "total output tok/s", "value": toks_all / (ms_max * 1e-3), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform-random token ids, random-init weights)",
+        "config": {"workload": WORKLOAD, "requests_per_gpu": N_REQ, "max_tokens": MAX_TOKENS,
+                   "parallelism": f"request-level replicas x{world}",
+                   "step": "one full run of the workload (prefill + 256 decode steps)",
+                   "l2": "no flush: every decode step streams 8 GB of weights (> 126 MB L2)",
+                   "wall_ms_per_step": wall_ms / args.steps},
+        "e2e": {"value": etoks_all / (ems_max * 1e-3), "unit": "tok/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "Engine.generate_text(host token lists) -> Request.tokens"},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind,
+                     "traffic": profile_traffic(),
+                     "kernel": "varlen paged attention (attn_main_kernel + combine_kernel)",
+                     "workload": "256 decode seqs ctx log-uniform[256,16384] + 4 prefill chunks "
+                                 "of 512 (priors 0/512/1536/3584), 32/8 heads, d128, bf16, "
+                                 "16-token blocks, permuted block table, one layer",
+                     "algorithmic_bytes": am["bytes"], "ms_per_launch": am["ms_mean"],
+                     "prefill_flops": am["prefill_flops"]},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

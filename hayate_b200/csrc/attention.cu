@@ -14,8 +14,9 @@
 //
 // Work is planned on the device (plan_kernel) once per step and reused by every
 // layer:
-//   * prefill items -- (seq, kv_head, 16-token tile): one CTA, the 4 query heads
-//     of the group on its 4 warps, K/V tiles of 64 keys staged by TMA;
+//   * prefill items -- (seq, kv_head, 32-token tile): one CTA of 8 warps, the 4
+//     query heads of the group x 2 groups of 16 tokens, sharing K/V tiles of 64
+//     keys staged by TMA;
 //   * decode items  -- (seq, kv_head, block range): one warp with its own TMA
 //     ring of K/V block tiles, mma.sync for QK^T and PV, an online softmax;
 //     sequences split over several items are merged by combine_kernel.
@@ -29,14 +30,21 @@
 
 namespace {
 
-constexpr int ATT_WARPS = 4;
+#ifndef HY_ATT_WARPS
+#define HY_ATT_WARPS 8
+#endif
+#ifndef HY_DEC_STAGES
+#define HY_DEC_STAGES 3
+#endif
+constexpr int ATT_WARPS = HY_ATT_WARPS;                          // 8: two query-row groups
 constexpr int ATT_THREADS = ATT_WARPS * 32;
-constexpr int DEC_STAGES = 4;                                    // TMA ring per decode warp
+constexpr int DEC_STAGES = HY_DEC_STAGES;                        // TMA ring per decode warp
 constexpr int DEC_TILE_BYTES = 2 * HY_BLOCK * HY_HEAD_DIM * 2;   // K+V of one block: 8 KB
 constexpr int DEC_WARP_BYTES = DEC_STAGES * DEC_TILE_BYTES;      // 32 KB
 constexpr int PRE_KEYS = 64;                                     // keys per prefill tile
 constexpr int PRE_BLOCKS = PRE_KEYS / HY_BLOCK;                  // 4
-constexpr int PRE_QROWS = 16;                                    // query tokens per item
+constexpr int PRE_GROUPS = ATT_WARPS / 4;                        // 4 warps (heads) per group
+constexpr int PRE_QROWS = 16 * PRE_GROUPS;                       // query tokens per item
 constexpr int PRE_KV_BYTES = PRE_KEYS * HY_HEAD_DIM * 2;         // 16 KB (K or V)
 constexpr int PRE_STAGE_BYTES = 2 * PRE_KV_BYTES;                // 32 KB
 constexpr int PRE_STAGES = 2;
@@ -46,6 +54,11 @@ constexpr int SMEM_PAYLOAD = (ATT_WARPS * DEC_WARP_BYTES > PRE_STAGES * PRE_STAG
 constexpr int SMEM_BYTES = SMEM_PAYLOAD + 1024;                  // + alignment slack
 constexpr int MIN_SPLIT = 4;                                     // blocks per decode item
 constexpr float NEG_INF = -INFINITY;
+// Lazy rescaling: the running max is only raised when a new score exceeds it
+// by more than 2^RESCALE_LOG2; until then probabilities may exceed 1 by up to
+// that factor, which fp32 accumulators and bf16 P carry without loss of
+// relative precision.  Output = O / l is unchanged (both use the same max).
+constexpr float RESCALE_LOG2 = 8.0f;
 
 struct Shared {
   uint64_t dec_bar[ATT_WARPS][DEC_STAGES];
@@ -258,34 +271,37 @@ __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const Pla
       mma_bf16_16816(sacc[1], af, b[2], b[3]);
     }
     const int kbase = (b0 + i) * HY_BLOCK;
+    const bool tail = kbase + HY_BLOCK > kv_len;            // only the last block is partial
     float p[2][2];
     float mx = NEG_INF;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int key = kbase + nt * 8 + c + e;
-        const float x = key < kv_len ? sacc[nt][e] * a.scale_log2 : NEG_INF;
+        float x = sacc[nt][e] * a.scale_log2;
+        if (tail && kbase + nt * 8 + c + e >= kv_len) x = NEG_INF;
         p[nt][e] = x;
         mx = fmaxf(mx, x);
       }
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float m_new = fmaxf(m, mx);
-    const float m_use = (m_new == NEG_INF) ? 0.f : m_new;
-    const float alpha = exp2f(m - m_use);
-    float psum = 0.f;
+    const bool grow = mx > m + RESCALE_LOG2;                // true on the first block
+    if (__any_sync(0xffffffffu, grow)) {
+      const float m_new = grow ? mx : m;
+      const float alpha = exp2f(m - m_new);                 // 0 when m was -inf
+      l *= alpha;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) { o[j][0] *= alpha; o[j][1] *= alpha; }
+      m = m_new;
+    }
+    const float m_use = (m == NEG_INF) ? 0.f : m;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         p[nt][e] = exp2f(p[nt][e] - m_use);
-        psum += p[nt][e];
+        l += p[nt][e];
       }
-    l = l * alpha + psum;
-    m = m_new;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) { o[j][0] *= alpha; o[j][1] *= alpha; }
     const uint32_t pa[4] = {pack_bf16(p[0][0], p[0][1]), 0u, pack_bf16(p[1][0], p[1][1]), 0u};
 #pragma unroll
     for (int j2 = 0; j2 < 8; ++j2) {
@@ -328,7 +344,8 @@ __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const Pla
 }
 
 // ------------------------------------------------------------------ prefill tile
-// CTA-wide: warp w computes query head 4g+w for tokens [t0, t0+16) of seq.
+// CTA-wide: warp w computes query head 4g + (w % 4) for the 16 tokens
+// [t0 + 16*(w/4), +16) of seq; all warps share the K/V tiles of the CTA.
 __device__ bool prefill_tile(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
                              int item, uint8_t* payload, uint64_t* bars, uint32_t& phase) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -344,7 +361,9 @@ __device__ bool prefill_tile(const CUtensorMap* map, const MainArgs& a, const Pl
   const int nblk = (kv_end + HY_BLOCK - 1) / HY_BLOCK;
   const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
   const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
-  const int hq = g * HY_GROUP + warp;
+  const int hq = g * HY_GROUP + (warp & 3);
+  const int tg = 16 * (warp >> 2);                          // this warp's first token in the tile
+  const int wrows = nrows - tg;                             // valid rows of this warp (may be <= 0)
 
   auto issue = [&](int t, int s) {
     uint8_t* st = payload + s * PRE_STAGE_BYTES;
@@ -372,11 +391,12 @@ __device__ bool prefill_tile(const CUtensorMap* map, const MainArgs& a, const Pl
   }
 
   const int r = lane >> 2, c = 2 * (lane & 3);
-  // Query fragments for rows r and r+8 (tokens t0+r, t0+r+8) of head hq.
+  // Query fragments for rows r and r+8 (tokens t0+tg+r, +8) of head hq.
   uint32_t qa[8][4];
   {
-    const bool v0 = r < nrows, v1 = r + 8 < nrows;
-    const __nv_bfloat16* q0 = a.q + ((size_t)(row0 + t0 + r) * a.q_heads + hq) * HY_HEAD_DIM;
+    const bool v0 = r < wrows, v1 = r + 8 < wrows;
+    const size_t rowq = (size_t)(row0 + t0 + tg + r);
+    const __nv_bfloat16* q0 = a.q + (rowq * a.q_heads + hq) * HY_HEAD_DIM;
     const __nv_bfloat16* q1 = q0 + (size_t)8 * a.q_heads * HY_HEAD_DIM;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
@@ -391,7 +411,7 @@ __device__ bool prefill_tile(const CUtensorMap* map, const MainArgs& a, const Pl
 #pragma unroll
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m[2] = {NEG_INF, NEG_INF}, l[2] = {0.f, 0.f};
-  const int lim0 = prefix + t0 + r, lim1 = lim0 + 8;        // last visible key per row
+  const int lim0 = prefix + t0 + tg + r, lim1 = lim0 + 8;   // last visible key per row
   const int mi = lane >> 3, ri = lane & 7;
   const int k_key = ri + 8 * (mi >> 1), k_dsub = 8 * (mi & 1);
   const int v_key = ri + 8 * (mi & 1), v_dsub = 8 * (mi >> 1);
@@ -404,80 +424,83 @@ __device__ bool prefill_tile(const CUtensorMap* map, const MainArgs& a, const Pl
     phase ^= (1u << s);
     const uint32_t kb = smem_u32(payload + s * PRE_STAGE_BYTES);
     const uint32_t vb = kb + PRE_KV_BYTES;
-
-    float sacc[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
-#pragma unroll
-    for (int pr = 0; pr < 4; ++pr) {
-      const int key = 16 * pr + k_key;                        // 16 keys = one block
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const int d = 16 * kk + k_dsub;
-        uint32_t b[4];
-        ldmatrix_x4(b, kb + pr * 4096 + (d >> 6) * 2048 + swz128(key & 15, d & 63));
-        mma_bf16_16816(sacc[2 * pr], qa[kk], b[0], b[1]);
-        mma_bf16_16816(sacc[2 * pr + 1], qa[kk], b[2], b[3]);
-      }
-    }
     const int kbase = t * PRE_KEYS;
-    const bool need_mask = kbase + PRE_KEYS - 1 > prefix + t0;   // diagonal or tail tile
-    float mx0 = NEG_INF, mx1 = NEG_INF;
+    // Tiles wholly above this warp's first row contribute nothing; skip the math
+    // (the barrier protocol is unchanged).
+    if (wrows > 0 && kbase <= prefix + t0 + tg + min(wrows, 16) - 1) {
+      float sacc[8][4];
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 8; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int key = kbase + nt * 8 + c + e;
-        float x0 = sacc[nt][e] * a.scale_log2, x1 = sacc[nt][2 + e] * a.scale_log2;
-        if (need_mask) {
-          if (key > lim0 || key >= kv_len) x0 = NEG_INF;
-          if (key > lim1 || key >= kv_len) x1 = NEG_INF;
+      for (int pr = 0; pr < 4; ++pr) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const int d = 16 * kk + k_dsub;
+          uint32_t b[4];
+          ldmatrix_x4(b, kb + pr * 4096 + (d >> 6) * 2048 + swz128(k_key, d & 63));
+          mma_bf16_16816(sacc[2 * pr], qa[kk], b[0], b[1]);
+          mma_bf16_16816(sacc[2 * pr + 1], qa[kk], b[2], b[3]);
         }
-        sacc[nt][e] = x0;
-        sacc[nt][2 + e] = x1;
-        mx0 = fmaxf(mx0, x0);
-        mx1 = fmaxf(mx1, x1);
       }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
-    const float mu0 = (mn0 == NEG_INF) ? 0.f : mn0, mu1 = (mn1 == NEG_INF) ? 0.f : mn1;
-    const float al0 = exp2f(m[0] - mu0), al1 = exp2f(m[1] - mu1);
-    float ps0 = 0.f, ps1 = 0.f;
+      const bool need_mask = kbase + PRE_KEYS - 1 > prefix + t0 + tg;   // diagonal or tail
+      float mx0 = NEG_INF, mx1 = NEG_INF;
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      sacc[nt][0] = exp2f(sacc[nt][0] - mu0);
-      sacc[nt][1] = exp2f(sacc[nt][1] - mu0);
-      sacc[nt][2] = exp2f(sacc[nt][2] - mu1);
-      sacc[nt][3] = exp2f(sacc[nt][3] - mu1);
-      ps0 += sacc[nt][0] + sacc[nt][1];
-      ps1 += sacc[nt][2] + sacc[nt][3];
-    }
-    l[0] = l[0] * al0 + ps0;
-    l[1] = l[1] * al1 + ps1;
-    m[0] = mn0;
-    m[1] = mn1;
+      for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      o[j][0] *= al0; o[j][1] *= al0;
-      o[j][2] *= al1; o[j][3] *= al1;
-    }
+        for (int e = 0; e < 2; ++e) {
+          const int key = kbase + nt * 8 + c + e;
+          float x0 = sacc[nt][e] * a.scale_log2, x1 = sacc[nt][2 + e] * a.scale_log2;
+          if (need_mask) {
+            if (key > lim0 || key >= kv_len) x0 = NEG_INF;
+            if (key > lim1 || key >= kv_len) x1 = NEG_INF;
+          }
+          sacc[nt][e] = x0;
+          sacc[nt][2 + e] = x1;
+          mx0 = fmaxf(mx0, x0);
+          mx1 = fmaxf(mx1, x1);
+        }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const bool g0 = mx0 > m[0] + RESCALE_LOG2, g1 = mx1 > m[1] + RESCALE_LOG2;
+      if (__any_sync(0xffffffffu, g0 || g1)) {
+        const float n0 = g0 ? mx0 : m[0], n1 = g1 ? mx1 : m[1];
+        const float al0 = exp2f(m[0] - n0), al1 = exp2f(m[1] - n1);
+        l[0] *= al0;
+        l[1] *= al1;
 #pragma unroll
-    for (int kt = 0; kt < 4; ++kt) {
-      const uint32_t pa[4] = {pack_bf16(sacc[2 * kt][0], sacc[2 * kt][1]),
-                              pack_bf16(sacc[2 * kt][2], sacc[2 * kt][3]),
-                              pack_bf16(sacc[2 * kt + 1][0], sacc[2 * kt + 1][1]),
-                              pack_bf16(sacc[2 * kt + 1][2], sacc[2 * kt + 1][3])};
-      const int key = 16 * kt + v_key;
+        for (int j = 0; j < 16; ++j) {
+          o[j][0] *= al0; o[j][1] *= al0;
+          o[j][2] *= al1; o[j][3] *= al1;
+        }
+        m[0] = n0;
+        m[1] = n1;
+      }
+      const float mu0 = (m[0] == NEG_INF) ? 0.f : m[0], mu1 = (m[1] == NEG_INF) ? 0.f : m[1];
 #pragma unroll
-      for (int j2 = 0; j2 < 8; ++j2) {
-        const int d = 16 * j2 + v_dsub;
-        uint32_t b[4];
-        ldmatrix_x4_trans(b, vb + kt * 4096 + (d >> 6) * 2048 + swz128(key & 15, d & 63));
-        mma_bf16_16816(o[2 * j2], pa, b[0], b[1]);
-        mma_bf16_16816(o[2 * j2 + 1], pa, b[2], b[3]);
+      for (int nt = 0; nt < 8; ++nt) {
+        sacc[nt][0] = exp2f(sacc[nt][0] - mu0);
+        sacc[nt][1] = exp2f(sacc[nt][1] - mu0);
+        sacc[nt][2] = exp2f(sacc[nt][2] - mu1);
+        sacc[nt][3] = exp2f(sacc[nt][3] - mu1);
+        l[0] += sacc[nt][0] + sacc[nt][1];
+        l[1] += sacc[nt][2] + sacc[nt][3];
+      }
+#pragma unroll
+      for (int kt = 0; kt < 4; ++kt) {
+        const uint32_t pa[4] = {pack_bf16(sacc[2 * kt][0], sacc[2 * kt][1]),
+                                pack_bf16(sacc[2 * kt][2], sacc[2 * kt][3]),
+                                pack_bf16(sacc[2 * kt + 1][0], sacc[2 * kt + 1][1]),
+                                pack_bf16(sacc[2 * kt + 1][2], sacc[2 * kt + 1][3])};
+#pragma unroll
+        for (int j2 = 0; j2 < 8; ++j2) {
+          const int d = 16 * j2 + v_dsub;
+          uint32_t b[4];
+          ldmatrix_x4_trans(b, vb + kt * 4096 + (d >> 6) * 2048 + swz128(v_key, d & 63));
+          mma_bf16_16816(o[2 * j2], pa, b[0], b[1]);
+          mma_bf16_16816(o[2 * j2 + 1], pa, b[2], b[3]);
+        }
       }
     }
     __syncthreads();
@@ -494,14 +517,14 @@ __device__ bool prefill_tile(const CUtensorMap* map, const MainArgs& a, const Pl
   l[1] += __shfl_xor_sync(0xffffffffu, l[1], 1);
   l[1] += __shfl_xor_sync(0xffffffffu, l[1], 2);
   const float inv0 = 1.f / l[0], inv1 = 1.f / l[1];
-  if (r < nrows) {
-    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + r) * a.q_heads + hq) * HY_HEAD_DIM;
+  if (r < wrows) {
+    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + tg + r) * a.q_heads + hq) * HY_HEAD_DIM;
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       *reinterpret_cast<uint32_t*>(op + 8 * j + c) = pack_bf16(o[j][0] * inv0, o[j][1] * inv0);
   }
-  if (r + 8 < nrows) {
-    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + r + 8) * a.q_heads + hq) * HY_HEAD_DIM;
+  if (r + 8 < wrows) {
+    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + tg + r + 8) * a.q_heads + hq) * HY_HEAD_DIM;
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       *reinterpret_cast<uint32_t*>(op + 8 * j + c) = pack_bf16(o[j][2] * inv1, o[j][3] * inv1);

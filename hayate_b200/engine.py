@@ -176,7 +176,8 @@ class Engine:
 
     def generate_text(self, prompts, max_tokens: int = 100):
         """the public api for generation"""
-        if isinstance(prompts, str) or (prompts and isinstance(prompts[0], int)):
+        if isinstance(prompts, str) or (isinstance(prompts, torch.Tensor) and prompts.dim() == 1) \
+                or (isinstance(prompts, list) and prompts and isinstance(prompts[0], int)):
             prompts = [prompts]
         requests = []
         for p in prompts:
@@ -192,13 +193,22 @@ class Engine:
     def _drain_pool(self):
         while not self.pool.empty():
             r = self.pool.get()
-            if not r.prompt_tokens:
-                r.prompt_tokens = self.tokenizer.encode(r.prompt) if isinstance(r.prompt, str) \
-                    else list(r.prompt)
+            if not len(r.prompt_tokens):
+                if isinstance(r.prompt, torch.Tensor):
+                    # device-resident prompt: stays on the GPU (copied device to device)
+                    r.prompt_tokens = r.prompt.to(torch.int32).reshape(-1)
+                elif isinstance(r.prompt, str):
+                    r.prompt_tokens = self.tokenizer.encode(r.prompt)
+                else:
+                    r.prompt_tokens = list(r.prompt)
             self.scheduler.check_request(r)
             self.scheduler.waiting.append(r)
 
     def _upload_prompt(self, r: Request):
+        if isinstance(r.prompt_tokens, torch.Tensor) and r.prompt_tokens.is_cuda:
+            n = r.prompt_tokens.numel()
+            self.runner.req_tokens[r.slot, :n].copy_(r.prompt_tokens, non_blocking=True)
+            return
         t = torch.tensor(r.prompt_tokens, dtype=torch.int32).pin_memory()
         r._pinned = t                                  # keep alive until the copy lands
         self.runner.req_tokens[r.slot, :t.numel()].copy_(t, non_blocking=True)
