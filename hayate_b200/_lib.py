@@ -39,6 +39,8 @@ SIGNATURES = {
     "hy_varlen_attention": (C.c_int, [I32, P, P, I32, I32, I32, P, I32, I32, I32, P, I32, P, P,
                                       P, I32, F32, I32, I32, P, SZ, P, P]),
     "hy_argmax": (C.c_int, [I32, P, I64, I32, I32, P, P]),
+    "hy_varlen_attention_noalloc": (C.c_int, [P, P, I32, I32, I32, P, I32, I32, I32, P, I32, P,
+                                              P, P, I32, F32, P, P]),
 }
 
 

@@ -115,6 +115,13 @@ int current_device() {
 
 }  // namespace
 
+// Shared with other translation units of the library (not part of the C ABI).
+int hy_attention_kv_map(int dev, const void* base, long rows, CUtensorMap* out) {
+  return kv_map_for(dev, base, rows, out);
+}
+
+void hy_set_error(const char* msg) { snprintf(g_last_error, sizeof(g_last_error), "%s", msg); }
+
 extern "C" {
 
 int hy_version(void) { return 100; }

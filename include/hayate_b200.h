@@ -140,6 +140,25 @@ int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tok
                         int32_t max_seqs, int32_t max_tokens, void* workspace,
                         size_t workspace_bytes, int32_t* err, void* stream);
 
+/* Plan + bf16 attention in one call, with no caller workspace: for callers
+ * that cannot allocate device memory where they call the kernel (a plugin or
+ * FFI host that passes only the operation's tensors, a runtime whose memory
+ * pool owns all device memory, a latency-critical path that must not call
+ * cudaMalloc because it can synchronise the device).  Its scratch is a fixed
+ * 12 MiB device array inside the library, held by every GPU that loads it
+ * until the process exits; batches above 256 sequences, 8192 query tokens or
+ * 8 KV heads are rejected (HY_E_INVALID).  The first call on a device looks up
+ * the array's address there; make that first call before any stream capture.
+ * All calls share the array, so calls that overlap on the GPU race.  No
+ * counterpart in the reference: it adds an allocation-free way into
+ * hy_varlen_attention's kernels. */
+int hy_varlen_attention_noalloc(const void* q, void* out, int32_t num_tokens, int32_t q_heads,
+                                int32_t kv_heads, const void* kv_cache, int32_t num_layers,
+                                int32_t num_blocks, int32_t layer, const int32_t* block_tables,
+                                int32_t bt_pitch, const int32_t* seq_bt_row,
+                                const int32_t* cu_seqlens_q, const int32_t* seq_lens_k,
+                                int32_t num_seqs, float scale, int32_t* err, void* stream);
+
 /* ---------------------------------------------------------------- sampling */
 
 /* out[r] = argmax(logits[r][0:vocab]) with first-index ties (torch.argmax).
