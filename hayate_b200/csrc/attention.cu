@@ -19,7 +19,8 @@
 //     keys staged by TMA;
 //   * decode items  -- (seq, kv_head, block range): one warp with its own TMA
 //     ring of K/V block tiles, mma.sync for QK^T and PV, an online softmax;
-//     sequences split over several items are merged by combine_kernel.
+//     for a sequence split over several items, the last item to finish (an
+//     atomic count per sequence and KV head) merges the partials.
 // The main kernel is persistent (grid = SMs x resident CTAs) and walks the plan
 // with a static stride, so its launch shape does not depend on the batch and a
 // whole step can be captured in a CUDA graph.
@@ -63,7 +64,28 @@ constexpr float RESCALE_LOG2 = 8.0f;
 struct Shared {
   uint64_t dec_bar[ATT_WARPS][DEC_STAGES];
   uint64_t pre_bar[PRE_STAGES];
+  uint64_t tc_kv[2];         // tcgen05 prefill: K/V tile landed (TMA transaction bytes)
+  uint64_t tc_s;             // S = Q K^T complete (tcgen05.commit)
+  uint64_t tc_o;             // O += P V complete (tcgen05.commit)
+  uint32_t tmem_base;        // TMEM columns from tcgen05.alloc
 };
+
+#ifndef HY_PREFILL_TC
+#define HY_PREFILL_TC 1
+#endif
+// tcgen05 prefill tile: M = 128 query rows (4 heads x 32 tokens, head-major so
+// warp w < 4 owns TMEM lanes 32w.. = head w), KV tiles of 128 keys (8 blocks).
+constexpr int TC_QTOK = 32;
+constexpr int TC_KEYS = 128;
+constexpr int TC_KV_BYTES = TC_KEYS * HY_HEAD_DIM * 2;          // K or V of one tile: 32 KB
+constexpr int TC_Q_OFF = 0;                                      // Q: 32 KB
+constexpr int TC_K_OFF = 32768;                                  // K: 2 stages
+constexpr int TC_V_OFF = 32768 * 3;                              // V: 2 stages
+constexpr int TC_P_OFF = 32768 * 5;                              // P: 32 KB
+constexpr int TC_SMEM = 32768 * 6;                               // 192 KB
+constexpr uint32_t TC_TMEM_COLS = 256;                           // S: [0,128), O: [128,256)
+static_assert(TC_SMEM <= SMEM_PAYLOAD, "tcgen05 prefill tile does not fit the payload");
+static_assert(!HY_PREFILL_TC || PRE_QROWS == TC_QTOK, "plan tiles must match the MMA tile");
 
 HY_DEVICE uint8_t* payload_base(uint8_t* dyn) {
   const uint32_t a = smem_u32(dyn);
@@ -139,6 +161,8 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
     const int opre = plan_scan(npre, ws, tpre);
     const int odec = plan_scan(ndec, ws, tdec);
     const int cpre = s_cpre, cdec = s_cdec;
+    if (i < S && i < v.max_seqs)
+      for (int g = 0; g < kv_heads; ++g) v.counters[i * kv_heads + g] = 0;
     if (i < S) {
       const int p0 = cpre + opre, d0 = cdec + odec;
       if (p0 + npre > v.max_pre || d0 + ndec > v.max_dec || i >= v.max_seqs) {
@@ -340,6 +364,72 @@ __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const Pla
       if ((lane & 3) == 0) v.part_ml[(size_t)item * HY_GROUP + r] = make_float2(m, l);
     }
   }
+  if (ns > 1) {
+    // The last of the sequence's split items to finish merges all partials.
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&v.counters[seq * a.kv_heads + g], 1) == ns - 1;
+    if (__shfl_sync(0xffffffffu, last, 0)) {
+      __threadfence();
+      const int first = v.seqinfo[seq].x + g * ns;
+      // lane owns d = 4*lane..4*lane+3 of all 4 heads; partials are read through
+      // L2 (__ldcg) since other SMs wrote them during this launch.
+      float M[HY_GROUP], L[HY_GROUP];
+      float4 acc[HY_GROUP];
+#pragma unroll
+      for (int rr = 0; rr < HY_GROUP; ++rr) {
+        M[rr] = NEG_INF;
+        L[rr] = 0.f;
+        acc[rr] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      for (int s0 = 0; s0 < ns; s0 += 8) {             // (m, l) of 8 splits x 4 heads per pass
+        const int sl = s0 + (lane >> 2);
+        float2 ml = make_float2(NEG_INF, 0.f);
+        if (sl < ns) ml = __ldcg(&v.part_ml[(size_t)(first + sl) * HY_GROUP + (lane & 3)]);
+        float mx = ml.x;                                // max over the 8 splits of head lane&3
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+#pragma unroll
+        for (int rr = 0; rr < HY_GROUP; ++rr) {
+          const float mnew = fmaxf(M[rr], __shfl_sync(0xffffffffu, mx, rr));
+          const float sc = exp2f(M[rr] - mnew);
+          L[rr] *= sc;
+          acc[rr].x *= sc; acc[rr].y *= sc; acc[rr].z *= sc; acc[rr].w *= sc;
+          M[rr] = mnew;
+        }
+        const int nsl = min(8, ns - s0);
+        for (int k = 0; k < nsl; ++k) {
+          float4 po[HY_GROUP];
+#pragma unroll
+          for (int rr = 0; rr < HY_GROUP; ++rr)
+            po[rr] = __ldcg(reinterpret_cast<const float4*>(
+                v.part_o + ((size_t)(first + s0 + k) * HY_GROUP + rr) * HY_HEAD_DIM + 4 * lane));
+#pragma unroll
+          for (int rr = 0; rr < HY_GROUP; ++rr) {
+            const float ms = __shfl_sync(0xffffffffu, ml.x, 4 * k + rr);
+            const float ls = __shfl_sync(0xffffffffu, ml.y, 4 * k + rr);
+            const float wgt = exp2f(ms - M[rr]);
+            L[rr] += wgt * ls;
+            acc[rr].x += wgt * po[rr].x; acc[rr].y += wgt * po[rr].y;
+            acc[rr].z += wgt * po[rr].z; acc[rr].w += wgt * po[rr].w;
+          }
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < HY_GROUP; ++rr) {
+        const float inv = 1.f / L[rr];
+        __nv_bfloat16* op =
+            a.out + ((size_t)tok * a.q_heads + g * HY_GROUP + rr) * HY_HEAD_DIM + 4 * lane;
+        uint2 pk;
+        pk.x = pack_bf16(acc[rr].x * inv, acc[rr].y * inv);
+        pk.y = pack_bf16(acc[rr].z * inv, acc[rr].w * inv);
+        *reinterpret_cast<uint2*>(op) = pk;
+      }
+      if (lane == 0) v.counters[seq * a.kv_heads + g] = 0;   // ready for the next layer
+    }
+  }
   return true;
 }
 
@@ -533,6 +623,220 @@ __device__ bool prefill_tile(const CUtensorMap* map, const MainArgs& a, const Pl
   return true;
 }
 
+
+// ------------------------------------------------------------------ prefill tile (tcgen05)
+// CTA-wide.  Rows r = 32*h + j of the 128-row tile are query head 4g+h, token
+// t0+j.  Per KV tile t (128 keys, TMA-staged, double-buffered):
+//   thread 0: S = Q K^T  (8 x tcgen05.mma, M=128 N=128 K=16, into TMEM cols 0..127)
+//   warps 0-3 (thread = row): S row from TMEM, causal mask, online softmax with
+//     lazy rescaling of O (in TMEM), P row (bf16) into smem in the 128B-swizzled
+//     K-major layout the MMA reads
+//   thread 0: O += P V  (8 x tcgen05.mma, V as an MN-major operand, cols 128..255)
+// Q, K, V and P use the canonical 128-byte-swizzled layout: 8-row x 128 B atoms,
+// 1024 B between 8-row groups, the two 64-column halves 16 KB apart.
+__device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
+                                int item, uint8_t* payload, Shared& sh, uint32_t tmem,
+                                uint32_t& ph) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int4 it = v.pre[item];
+  const int seq = it.x, g = it.y, t0 = it.z;
+  const int row0 = a.cu_q[seq];
+  const int q_len = a.cu_q[seq + 1] - row0;
+  const int kv_len = a.seq_lens_k[seq];
+  const int prefix = kv_len - q_len;
+  const int nrows = min(TC_QTOK, q_len - t0);
+  const int kv_end = prefix + t0 + nrows;
+  const int ntiles = (kv_end + TC_KEYS - 1) / TC_KEYS;
+  const int nblk = (kv_end + HY_BLOCK - 1) / HY_BLOCK;
+  const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
+  const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
+  const uint32_t sbase = smem_u32(payload);
+
+  auto issue = [&](int t, int s) {
+    uint8_t* kst = payload + TC_K_OFF + s * TC_KV_BYTES;
+    uint8_t* vst = payload + TC_V_OFF + s * TC_KV_BYTES;
+    fence_proxy_async();
+    mbar_arrive_expect_tx(&sh.tc_kv[s], 2 * TC_KV_BYTES);
+#pragma unroll 1
+    for (int j = 0; j < TC_KEYS / HY_BLOCK; ++j) {
+      const int b = t * (TC_KEYS / HY_BLOCK) + j;
+      int rk = a.oob_row, rv = a.oob_row;
+      if (b < nblk) {
+        const int blk = bt[b];
+        if (blk >= 0 && blk < a.num_blocks) { rk = kv_row(a, blk, 0, g); rv = kv_row(a, blk, 1, g); }
+        else hy_flag(a.err, HY_ERR_BOUNDS);
+      }
+      tma_load_2d(kst + j * 2048, map, 0, rk, &sh.tc_kv[s]);
+      tma_load_2d(kst + 16384 + j * 2048, map, 64, rk, &sh.tc_kv[s]);
+      tma_load_2d(vst + j * 2048, map, 0, rv, &sh.tc_kv[s]);
+      tma_load_2d(vst + 16384 + j * 2048, map, 64, rv, &sh.tc_kv[s]);
+    }
+  };
+
+  __syncthreads();                              // previous users of smem / TMEM are done
+  if (tid == 0)
+    for (int t = 0; t < 2 && t < ntiles; ++t) issue(t, t);
+
+  const int row = tid & 127, h = row >> 5, j = row & 31;
+  if (warp < 4) {                               // Q tile -> smem (swizzled, K-major)
+    const bool valid = j < nrows;
+    const uint4* qp = reinterpret_cast<const uint4*>(
+        a.q + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const uint4 val = valid ? qp[c] : make_uint4(0u, 0u, 0u, 0u);
+      const int cc = c & 7;
+      *reinterpret_cast<uint4*>(payload + TC_Q_OFF + (c >> 3) * 16384 + (row >> 3) * 1024 +
+                                (row & 7) * 128 + ((cc ^ (row & 7)) << 4)) = val;
+    }
+  }
+  fence_proxy_async();                          // generic smem writes -> async proxy
+  __syncthreads();
+
+  constexpr uint32_t ID_S = tc_idesc_bf16(128, TC_KEYS, false);
+  constexpr uint32_t ID_O = tc_idesc_bf16(128, HY_HEAD_DIM, true);
+  const uint32_t tS = tmem, tO = tmem + TC_KEYS;
+  const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+  const int lim = prefix + t0 + j;              // last key row j may see
+  float m = NEG_INF, l = 0.f;
+  bool ok = true;
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t & 1;
+    bool w_ok = mbar_wait(&sh.tc_kv[s], (ph >> s) & 1u, a.err);
+    if (__syncthreads_or(!w_ok)) { ok = false; break; }
+    ph ^= 1u << s;
+    if (tid == 0) {                             // S = Q K^T
+      tc_fence_after();
+      const uint32_t kb = sbase + TC_K_OFF + s * TC_KV_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < HY_HEAD_DIM / 16; ++kk) {
+        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+        tc_mma_bf16(tS, tc_desc_sw128(sbase + TC_Q_OFF + off, 16, 1024),
+                    tc_desc_sw128(kb + off, 16, 1024), ID_S, kk > 0);
+      }
+      tc_commit(&sh.tc_s);
+    }
+    w_ok = true;
+    if (warp < 4) {
+      w_ok = mbar_wait(&sh.tc_s, (ph >> 2) & 1u, a.err);
+      if (w_ok) {
+        tc_fence_after();
+        float sc[TC_KEYS];
+#pragma unroll
+        for (int c = 0; c < TC_KEYS / 32; ++c) {
+          float chunk[32];
+          tmem_ld32(tS + lane_base + 32 * c, chunk);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sc[32 * c + i] = chunk[i];
+        }
+        const int kbase = t * TC_KEYS;
+        const bool need_mask = kbase + TC_KEYS - 1 > prefix + t0;
+        float mx = NEG_INF;
+#pragma unroll
+        for (int i = 0; i < TC_KEYS; ++i) {
+          float x = sc[i] * a.scale_log2;
+          if (need_mask && (kbase + i > lim || kbase + i >= kv_len)) x = NEG_INF;
+          sc[i] = x;
+          mx = fmaxf(mx, x);
+        }
+        const bool grow = mx > m + RESCALE_LOG2;
+        if (__any_sync(0xffffffffu, grow)) {
+          const float mnew = grow ? mx : m;
+          const float alpha = exp2f(m - mnew);
+          l *= alpha;
+          m = mnew;
+          if (t > 0) {                          // rescale this warp's O rows in TMEM
+#pragma unroll 1
+            for (int c = 0; c < HY_HEAD_DIM / 32; ++c) {
+              float o[32];
+              tmem_ld32(tO + lane_base + 32 * c, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] *= alpha;
+              tmem_st32(tO + lane_base + 32 * c, o);
+            }
+            tmem_wait_st();
+          }
+        }
+        const float mu = (m == NEG_INF) ? 0.f : m;
+        uint8_t* prow = payload + TC_P_OFF + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+        for (int cc = 0; cc < TC_KEYS / 8; ++cc) {
+          float p[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            p[e] = exp2f(sc[8 * cc + e] - mu);
+            l += p[e];
+          }
+          uint4 pk;
+          pk.x = pack_bf16(p[0], p[1]);
+          pk.y = pack_bf16(p[2], p[3]);
+          pk.z = pack_bf16(p[4], p[5]);
+          pk.w = pack_bf16(p[6], p[7]);
+          const int c8 = cc & 7;
+          *reinterpret_cast<uint4*>(prow + (cc >> 3) * 16384 + ((c8 ^ (row & 7)) << 4)) = pk;
+        }
+        fence_proxy_async();
+        tc_fence_before();
+      }
+    }
+    if (__syncthreads_or(!w_ok)) { ok = false; break; }
+    ph ^= 1u << 2;
+    if (tid == 0) {                             // O += P V
+      tc_fence_after();
+      const uint32_t vb = sbase + TC_V_OFF + s * TC_KV_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < TC_KEYS / 16; ++kk) {
+        tc_mma_bf16(tO, tc_desc_sw128(sbase + TC_P_OFF + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                    tc_desc_sw128(vb + kk * 2048, 16384, 1024), ID_O, (t > 0 || kk > 0));
+      }
+      tc_commit(&sh.tc_o);
+    }
+    w_ok = mbar_wait(&sh.tc_o, (ph >> 3) & 1u, a.err);
+    if (__syncthreads_or(!w_ok)) { ok = false; break; }
+    ph ^= 1u << 3;
+    tc_fence_after();
+    if (tid == 0 && t + 2 < ntiles) issue(t + 2, s);
+  }
+  if (!ok) {
+    // let outstanding copies and MMAs land before the caller frees TMEM
+    if (tid == 0) {
+      for (int s2 = 0; s2 < 2; ++s2) mbar_wait(&sh.tc_kv[s2], (ph >> s2) & 1u, nullptr);
+      mbar_wait(&sh.tc_s, (ph >> 2) & 1u, nullptr);
+      mbar_wait(&sh.tc_o, (ph >> 3) & 1u, nullptr);
+    }
+    __syncthreads();
+    return false;
+  }
+  if (warp < 4) {                               // epilogue: O / l -> out
+    // tcgen05.ld is warp-collective: every lane loads, only real rows store
+    const bool store = j < nrows;
+    const float inv = 1.f / l;
+    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM;
+#pragma unroll 1
+    for (int c = 0; c < HY_HEAD_DIM / 32; ++c) {
+      float o[32];
+      tmem_ld32(tO + lane_base + 32 * c, o);
+      tmem_wait_ld();
+      if (store) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint4 pk;
+          pk.x = pack_bf16(o[8 * q4 + 0] * inv, o[8 * q4 + 1] * inv);
+          pk.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
+          pk.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
+          pk.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
+          *reinterpret_cast<uint4*>(op + 32 * c + 8 * q4) = pk;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  return true;
+}
+
 __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     const __grid_constant__ CUtensorMap kv_map, MainArgs a, PlanView v) {
   __shared__ Shared sh;
@@ -544,60 +848,46 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     for (int w = 0; w < ATT_WARPS; ++w)
       for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&sh.dec_bar[w][s], 1);
     for (int s = 0; s < PRE_STAGES; ++s) mbar_init(&sh.pre_bar[s], 1);
+    for (int s = 0; s < 2; ++s) mbar_init(&sh.tc_kv[s], 1);
+    mbar_init(&sh.tc_s, 1);
+    mbar_init(&sh.tc_o, 1);
     fence_mbar_init();
   }
-  __syncthreads();
   const int n_pre = v.header[0], n_dec = v.header[1];
+  // TMEM for the tcgen05 prefill tiles (only CTAs that will run one allocate)
+  const bool use_tmem = HY_PREFILL_TC && (int)blockIdx.x < n_pre;
+  if (use_tmem && warp == 0) {
+    tmem_alloc(&sh.tmem_base, TC_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = use_tmem ? sh.tmem_base : 0u;
   const int total = n_pre + (n_dec + ATT_WARPS - 1) / ATT_WARPS;
   uint32_t dec_phase = 0, pre_phase = 0;
-  for (int k = blockIdx.x; k < total; k += gridDim.x) {
+  bool ok = true;
+  for (int k = blockIdx.x; k < total && ok; k += gridDim.x) {
     if (k < n_pre) {
-      if (!prefill_tile(&kv_map, a, v, k, payload, sh.pre_bar, pre_phase)) return;
+#if HY_PREFILL_TC
+      ok = prefill_tile_tc(&kv_map, a, v, k, payload, sh, tmem, pre_phase);
+#else
+      ok = prefill_tile(&kv_map, a, v, k, payload, sh.pre_bar, pre_phase);
+#endif
     } else {
       const int item = (k - n_pre) * ATT_WARPS + warp;
-      if (item < n_dec) {
-        if (!decode_item(&kv_map, a, v, item, payload + warp * DEC_WARP_BYTES,
-                         sh.dec_bar[warp], dec_phase))
-          return;
-      }
+      if (item < n_dec)
+        ok = decode_item(&kv_map, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
+                         dec_phase);
     }
   }
-}
-
-// Merge the split-K partials of decode sequences with more than one item.
-__global__ void __launch_bounds__(256) combine_kernel(MainArgs a, PlanView v, int S) {
-  const int lane = threadIdx.x & 31;
-  const long total = (long)S * a.kv_heads * HY_GROUP;
-  const long nwarps = (long)gridDim.x * (blockDim.x >> 5);
-  for (long w = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += nwarps) {
-    const int seq = (int)(w / (a.kv_heads * HY_GROUP));
-    const int gh = (int)(w % (a.kv_heads * HY_GROUP));
-    const int g = gh / HY_GROUP, r = gh % HY_GROUP;
-    const int q = a.cu_q[seq + 1] - a.cu_q[seq];
-    if (q != 1) continue;
-    const int2 si = v.seqinfo[seq];
-    const int ns = si.y;
-    if (ns <= 1) continue;
-    const int first = si.x + g * ns;
-    float M = NEG_INF;
-    for (int s = 0; s < ns; ++s) M = fmaxf(M, v.part_ml[(size_t)(first + s) * HY_GROUP + r].x);
-    float L = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < ns; ++s) {
-      const float2 ml = v.part_ml[(size_t)(first + s) * HY_GROUP + r];
-      const float wgt = exp2f(ml.x - M);
-      L += wgt * ml.y;
-      const float4 po = *reinterpret_cast<const float4*>(
-          v.part_o + ((size_t)(first + s) * HY_GROUP + r) * HY_HEAD_DIM + 4 * lane);
-      acc.x += wgt * po.x; acc.y += wgt * po.y; acc.z += wgt * po.z; acc.w += wgt * po.w;
+  if (use_tmem) {
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+      tc_fence_after();
+      tmem_dealloc(tmem, TC_TMEM_COLS);
     }
-    const float inv = 1.f / L;
-    const int tok = a.cu_q[seq];
-    __nv_bfloat16* op = a.out + ((size_t)tok * a.q_heads + g * HY_GROUP + r) * HY_HEAD_DIM + 4 * lane;
-    uint2 pk;
-    pk.x = pack_bf16(acc.x * inv, acc.y * inv);
-    pk.y = pack_bf16(acc.z * inv, acc.w * inv);
-    *reinterpret_cast<uint2*>(op) = pk;
   }
 }
 
@@ -679,6 +969,7 @@ PlanDims hy_attn_plan_dims(int max_seqs, int max_tokens, int kv_heads, int dev) 
   d.max_seqs = max_seqs;
   d.max_pre = kv_heads * (max_tokens / PRE_QROWS + max_seqs);
   d.max_dec = kv_heads * max_seqs + 2 * hy_attn_warp_slots(dev);
+  d.kv_heads = kv_heads;
   return d;
 }
 
@@ -691,6 +982,7 @@ size_t hy_attn_workspace_bytes(const PlanDims& d) {
   off = align256(off + (size_t)d.max_seqs * sizeof(int2));
   off = align256(off + (size_t)d.max_dec * HY_GROUP * HY_HEAD_DIM * sizeof(float));
   off = align256(off + (size_t)d.max_dec * HY_GROUP * sizeof(float2));
+  off = align256(off + (size_t)d.max_seqs * d.kv_heads * sizeof(int));
   return off;
 }
 
@@ -709,6 +1001,8 @@ static PlanView make_view(void* ws, const PlanDims& d) {
   v.part_o = reinterpret_cast<float*>(p + off);
   off = align256(off + (size_t)d.max_dec * HY_GROUP * HY_HEAD_DIM * sizeof(float));
   v.part_ml = reinterpret_cast<float2*>(p + off);
+  off = align256(off + (size_t)d.max_dec * HY_GROUP * sizeof(float2));
+  v.counters = reinterpret_cast<int*>(p + off);
   v.max_pre = d.max_pre;
   v.max_dec = d.max_dec;
   v.max_seqs = d.max_seqs;
@@ -758,10 +1052,6 @@ cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* q, void* out
   const PlanView v = make_view(ws, d);
   const int grid = device_sms(dev) * g_ctas_per_sm[dev < 64 && dev >= 0 ? dev : 0];
   attn_main_kernel<<<grid, ATT_THREADS, SMEM_BYTES, st>>>(map, a, v);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  const int cgrid = device_sms(dev) * 4;
-  combine_kernel<<<cgrid, 256, 0, st>>>(a, v, S);
   return cudaGetLastError();
 }
 

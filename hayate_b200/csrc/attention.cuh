@@ -11,6 +11,7 @@ struct PlanDims {
   int max_pre;     // prefill items (kv_head x 16-token tile)
   int max_dec;     // decode items (kv_head x block range)
   int max_seqs;
+  int kv_heads;
 };
 
 // Device view of a workspace (see attention.cu for the layout).
@@ -21,6 +22,7 @@ struct PlanView {
   int2* seqinfo;      // per sequence: first decode item, number of splits
   float* part_o;      // [max_dec][4][128]
   float2* part_ml;    // [max_dec][4]  (running max in log2 units, sum)
+  int* counters;      // [max_seqs][kv_heads] finished split items (zeroed by the plan)
   int max_pre, max_dec, max_seqs;
 };
 

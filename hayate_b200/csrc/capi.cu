@@ -23,6 +23,9 @@ cudaError_t hy_launch_qk_norm_rope(int, const void*, int, int, int, int, const i
 cudaError_t hy_launch_kv_append(int, const void*, const void*, int, int, const int32_t*, void*,
                                 int, int32_t*, cudaStream_t);
 cudaError_t hy_launch_argmax(int, const void*, long, int, int, int32_t*, cudaStream_t);
+cudaError_t hy_launch_add_rms_norm(int, void*, long, const void*, long, int, int, const void*,
+                                   float, void*, long, cudaStream_t);
+cudaError_t hy_launch_silu_mul(int, const void*, long, int, int, void*, long, cudaStream_t);
 
 namespace {
 
@@ -280,6 +283,40 @@ int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tok
                           num_blocks, block_tables, bt_pitch, seq_bt_row, cu_seqlens_q,
                           seq_lens_k, num_seqs, scale, d, workspace, err, dev, as_stream(stream)),
       "hy_varlen_attention(bf16)");
+}
+
+static bool vec_aligned(const void* p, int64_t ld, int32_t dtype, int32_t n) {
+  const int v = dtype == HY_DTYPE_BF16 ? 8 : 4;
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && ld % v == 0 && n % v == 0;
+}
+
+int hy_add_rms_norm(int32_t dtype, void* x, int64_t ldx, const void* delta, int64_t ldd,
+                    int32_t rows, int32_t cols, const void* w, float eps, void* y, int64_t ldy,
+                    void* stream) {
+  if (!dtype_ok(dtype)) return fail(HY_E_INVALID, "hy_add_rms_norm: dtype must be 0 or 1");
+  if (rows == 0) return HY_OK;
+  const int maxc = 4096;
+  if (!x || !w || !y || rows < 0 || cols <= 0 || cols > maxc || ldx < cols || ldy < cols ||
+      (delta && ldd < cols))
+    return fail(HY_E_INVALID, "hy_add_rms_norm: bad argument (cols must be in 1..4096)");
+  if (!vec_aligned(x, ldx, dtype, cols) || !vec_aligned(y, ldy, dtype, cols) ||
+      !vec_aligned(w, cols, dtype, cols) || (delta && !vec_aligned(delta, ldd, dtype, cols)))
+    return fail(HY_E_INVALID, "hy_add_rms_norm: rows must be 16-byte aligned vectors");
+  return cuda_result(hy_launch_add_rms_norm(dtype, x, (long)ldx, delta, (long)ldd, rows, cols, w,
+                                            eps, y, (long)ldy, as_stream(stream)),
+                     "hy_add_rms_norm");
+}
+
+int hy_silu_mul(int32_t dtype, const void* gu, int64_t ld, int32_t rows, int32_t inter, void* y,
+                int64_t ldy, void* stream) {
+  if (!dtype_ok(dtype)) return fail(HY_E_INVALID, "hy_silu_mul: dtype must be 0 or 1");
+  if (rows == 0) return HY_OK;
+  if (!gu || !y || rows < 0 || inter <= 0 || ld < 2 * (int64_t)inter || ldy < inter)
+    return fail(HY_E_INVALID, "hy_silu_mul: bad argument");
+  if (!vec_aligned(gu, ld, dtype, inter) || !vec_aligned(y, ldy, dtype, inter))
+    return fail(HY_E_INVALID, "hy_silu_mul: rows must be 16-byte aligned vectors");
+  return cuda_result(hy_launch_silu_mul(dtype, gu, (long)ld, rows, inter, y, (long)ldy,
+                                        as_stream(stream)), "hy_silu_mul");
 }
 
 int hy_argmax(int32_t dtype, const void* logits, int64_t ld, int32_t rows, int32_t vocab,

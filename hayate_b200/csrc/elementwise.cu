@@ -1,0 +1,166 @@
+// Row-wise residual-add + RMSNorm and SiLU(gate)*up around the cuBLAS GEMMs.
+//
+// Add+RMSNorm replaces the residual adds and nn.RMSNorm of a block
+// (hayate/model/block.py:18-31, qwen.py:35,122):
+//   x = round(delta + x);  y = round( (f32(x) * rstd) * f32(w) ),
+//   rstd = 1 / sqrt(mean(f32(x)^2) + eps)
+// SiLU*up replaces FeedForward's activation (hayate/model/linear.py:11-13):
+//   y = round( f32(round(silu(f32(g)))) * f32(u) ),  silu(g) = g / (1 + exp(-g))
+// with round() the model dtype, i.e. the rounding points of the reference's
+// separate torch ops.  16-byte vector loads.
+#include "common.cuh"
+
+namespace {
+
+template <typename T> struct Vec;   // 16 bytes of T
+template <> struct Vec<__nv_bfloat16> {
+  static constexpr int N = 8;
+  static HY_DEVICE void load(const __nv_bfloat16* p, float (&f)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __bfloat1622float2(h[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+  static HY_DEVICE void store(__nv_bfloat16* p, const float (&f)[8]) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+  }
+  static HY_DEVICE float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+};
+template <> struct Vec<float> {
+  static constexpr int N = 4;
+  static HY_DEVICE void load(const float* p, float (&f)[4]) {
+    const float4 u = *reinterpret_cast<const float4*>(p);
+    f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
+  }
+  static HY_DEVICE void store(float* p, const float (&f)[4]) {
+    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+  }
+  static HY_DEVICE float round(float v) { return v; }
+};
+
+// One CTA per row, RN_THREADS threads, up to 32 elements per thread in 16-byte
+// vectors: rows of at most 128 x 32 = 4096 elements.  The weight
+// vectors are loaded together with the row, so a row costs one memory round
+// trip plus a CTA reduction.
+constexpr int RN_THREADS = 128;
+
+// x <- round(x + delta) (when delta is given: the residual add of block.py:24,30),
+// y <- RMSNorm(x) * w.
+template <typename T>
+__global__ void __launch_bounds__(RN_THREADS) add_rms_norm_kernel(
+    T* __restrict__ x, long ldx, const T* __restrict__ delta, long ldd, int cols,
+    const T* __restrict__ w, float eps, T* __restrict__ y, long ldy) {
+  using V = Vec<T>;
+  constexpr int N = V::N;
+  constexpr int RN_VEC = 32 / N;
+  __shared__ float red[RN_THREADS / 32];
+  const long r = blockIdx.x;
+  const int nvec = cols / N;
+  T* xr = x + r * ldx;
+  float v[RN_VEC][N], wv[RN_VEC][N];
+#pragma unroll
+  for (int k = 0; k < RN_VEC; ++k) {
+    const int vi = threadIdx.x + RN_THREADS * k;
+    if (vi < nvec) {
+      V::load(xr + vi * N, v[k]);
+      V::load(w + vi * N, wv[k]);
+      if (delta != nullptr) {
+        float dv[N];
+        V::load(delta + r * ldd + vi * N, dv);
+#pragma unroll
+        for (int e = 0; e < N; ++e) v[k][e] = V::round(__fadd_rn(dv[e], v[k][e]));
+        V::store(xr + vi * N, v[k]);
+      }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < RN_VEC; ++k) {
+    const int vi = threadIdx.x + RN_THREADS * k;
+    if (vi < nvec) {
+#pragma unroll
+      for (int e = 0; e < N; ++e) ss = __fadd_rn(ss, __fmul_rn(v[k][e], v[k][e]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < RN_THREADS / 32; ++i) tot = __fadd_rn(tot, red[i]);
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)cols), eps)));
+  T* yr = y + r * ldy;
+#pragma unroll
+  for (int k = 0; k < RN_VEC; ++k) {
+    const int vi = threadIdx.x + RN_THREADS * k;
+    if (vi < nvec) {
+      float o[N];
+#pragma unroll
+      for (int e = 0; e < N; ++e) o[e] = __fmul_rn(__fmul_rn(v[k][e], rstd), wv[k][e]);
+      V::store(yr + vi * N, o);
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) silu_mul_kernel(
+    const T* __restrict__ gu, long ld, int rows, int inter, T* __restrict__ y, long ldy) {
+  using V = Vec<T>;
+  constexpr int N = V::N;
+  const int nvec = inter / N;
+  const long total = (long)rows * nvec;
+  const long stride = (long)gridDim.x * blockDim.x;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const long r = i / nvec;
+    const int c = (int)(i % nvec) * N;
+    float g[N], u[N], o[N];
+    V::load(gu + r * ld + c, g);
+    V::load(gu + r * ld + inter + c, u);
+#pragma unroll
+    for (int e = 0; e < N; ++e) {
+      const float s = V::round(__fdiv_rn(g[e], __fadd_rn(1.0f, expf(-g[e]))));
+      o[e] = __fmul_rn(s, u[e]);
+    }
+    V::store(y + r * ldy + c, o);
+  }
+}
+
+}  // namespace
+
+cudaError_t hy_launch_add_rms_norm(int dtype, void* x, long ldx, const void* delta, long ldd,
+                                   int rows, int cols, const void* w, float eps, void* y,
+                                   long ldy, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  if (dtype == 0)
+    add_rms_norm_kernel<__nv_bfloat16><<<rows, RN_THREADS, 0, st>>>(
+        (__nv_bfloat16*)x, ldx, (const __nv_bfloat16*)delta, ldd, cols,
+        (const __nv_bfloat16*)w, eps, (__nv_bfloat16*)y, ldy);
+  else
+    add_rms_norm_kernel<float><<<rows, RN_THREADS, 0, st>>>(
+        (float*)x, ldx, (const float*)delta, ldd, cols, (const float*)w, eps, (float*)y, ldy);
+  return cudaGetLastError();
+}
+
+cudaError_t hy_launch_silu_mul(int dtype, const void* gu, long ld, int rows, int inter, void* y,
+                               long ldy, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  const long vecs = (long)rows * inter / (dtype == 0 ? 8 : 4);
+  long blocks = (vecs + 255) / 256;
+  if (blocks > 148L * 32) blocks = 148L * 32;
+  if (dtype == 0)
+    silu_mul_kernel<__nv_bfloat16><<<(int)blocks, 256, 0, st>>>(
+        (const __nv_bfloat16*)gu, ld, rows, inter, (__nv_bfloat16*)y, ldy);
+  else
+    silu_mul_kernel<float><<<(int)blocks, 256, 0, st>>>((const float*)gu, ld, rows, inter,
+                                                        (float*)y, ldy);
+  return cudaGetLastError();
+}

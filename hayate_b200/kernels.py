@@ -157,6 +157,36 @@ def varlen_attention(q: torch.Tensor, out: torch.Tensor, kv_cache: torch.Tensor,
         ws_bytes, _ptr(err), _stream()), "hy_varlen_attention")
 
 
+def add_rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float,
+                 delta: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x += delta in place (if given), then return RMSNorm(x) * w."""
+    rows, cols = x.shape
+    if x.stride(1) != 1 or (delta is not None and delta.stride(1) != 1):
+        raise ValueError("rows must be contiguous")
+    out = torch.empty_like(x) if out is None else out
+    check(_lib.load().hy_add_rms_norm(
+        _dt(x), _ptr(x), x.stride(0), _ptr(delta), 0 if delta is None else delta.stride(0), rows,
+        cols, _ptr(w), float(eps), _ptr(out), out.stride(0), _stream()), "hy_add_rms_norm")
+    return out
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float,
+             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    return add_rms_norm(x, w, eps, None, out)
+
+
+def silu_mul(gu: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    rows, two_i = gu.shape
+    inter = two_i // 2
+    if gu.stride(1) != 1:
+        raise ValueError("gu rows must be contiguous")
+    out = torch.empty(rows, inter, dtype=gu.dtype, device=gu.device) if out is None else out
+    check(_lib.load().hy_silu_mul(_dt(gu), _ptr(gu), gu.stride(0), rows, inter, _ptr(out),
+                                  out.stride(0), _stream()), "hy_silu_mul")
+    return out
+
+
 def argmax(logits: torch.Tensor, out: torch.Tensor) -> None:
     rows, V = logits.shape
     if logits.stride(1) != 1:

@@ -3,15 +3,16 @@
 One ``Runner.launch_step`` is the device half of a continuous-batching step:
 
   pack (on-GPU batch build + block allocation) -> attention plan ->
-  embed -> 36 x [RMSNorm, QKV GEMM, QK-norm+RoPE+KV append, varlen attention,
-  O GEMM + residual, RMSNorm, gate/up GEMM, SiLU*up, down GEMM + residual] ->
-  final RMSNorm on the sampled rows only -> LM-head GEMM -> argmax -> commit.
+  embed -> RMSNorm -> 36 x [QKV GEMM, QK-norm+RoPE+KV append, varlen attention,
+  O GEMM, residual add + RMSNorm, gate/up GEMM, SiLU*up, down GEMM, residual add +
+  next RMSNorm] -> LM-head GEMM on the sampled rows only -> argmax -> commit.
 
 It replaces ``Qwen3Model.forward`` (hayate/model/qwen.py:46-124) with its block
 and attention modules (block.py:21-31, attention.py:26-66, linear.py:11-14) and
 the engine's gather/scatter around it (engine.py:80-163).  The projections, the
-MLP and the LM head stay on cuBLAS through torch; the RMSNorms, residual adds
-and SiLU are torch element-wise ops with the reference's rounding points.  The
+MLP and the LM head stay on cuBLAS through torch; the residual adds fused with
+the RMSNorms, and SiLU*up, are this library's row kernels with the reference's
+rounding points.  The
 LM head runs on the last row of each sampled sequence only, where the
 reference computes logits for every position (qwen.py:122-123).
 
@@ -166,8 +167,10 @@ class Runner:
         x = F.embedding(self.input_ids[:T], self.embed)
         eps = cfg.rms_norm_eps
         I = cfg.intermediate_size
+        h = K.add_rms_norm(x, self.layers[0].ln1, eps)
+        launches += 1
+        nl = len(self.layers)
         for l, w in enumerate(self.layers):
-            h = F.rms_norm(x, (cfg.hidden_size,), w.ln1, eps)
             qkv = F.linear(h, w.w_qkv)
             K.qk_norm_rope(qkv, Hq, Hkv, pos, w.q_norm, w.k_norm, self.rope_cos, self.rope_sin,
                            eps, q_out=q, kv_cache_layer=self.kv_cache[l], slot_mapping=smap,
@@ -175,15 +178,15 @@ class Runner:
             K.varlen_attention(q, attn, self.kv_cache, l, self.block_tables, cu_q, kv_lens, S,
                                ecfg.max_num_seqs, ecfg.max_batched_tokens, self.ws,
                                seq_bt_row=slots, err=err)
-            x = F.linear(attn.view(T, Hq * D), w.w_o) + x
-            h = F.rms_norm(x, (cfg.hidden_size,), w.ln2, eps)
-            gu = F.linear(h, w.w_gate_up)
-            x = F.linear(F.silu(gu[:, :I]) * gu[:, I:], w.w_down) + x
-            launches += 2 if self.ws is None else 3      # + combine kernel
+            # x += o_proj(attn); h = post_attention_layernorm(x)
+            h = K.add_rms_norm(x, w.ln2, eps, delta=F.linear(attn.view(T, Hq * D), w.w_o))
+            mlp = F.linear(K.silu_mul(F.linear(h, w.w_gate_up)), w.w_down)
+            # x += mlp(h); h = next block's input_layernorm(x), or the final norm
+            nxt = self.layers[l + 1].ln1 if l + 1 < nl else self.final_norm
+            h = K.add_rms_norm(x, nxt, eps, delta=mlp)
+            launches += self.LAYER_LAUNCHES + (self.ws is not None)   # + combine kernel
         if n_sample > 0:
-            hs = x.index_select(0, self.sample_rows[:n_sample])
-            hs = F.rms_norm(hs, (cfg.hidden_size,), self.final_norm, eps)
-            logits = F.linear(hs, self.embed)
+            logits = F.linear(h.index_select(0, self.sample_rows[:n_sample]), self.embed)
             K.argmax(logits, self.next_tokens[:n_sample])
             K.commit_tokens(self.next_tokens[:n_sample], n_sample, self.sample_seq, sched, S,
                             self.req_tokens, err)
@@ -195,6 +198,9 @@ class Runner:
                       self.error_word)
         self.kernel_launches += 1
 
+    # our kernels per layer: 2 add+RMSNorm, QK-norm+RoPE, attention, SiLU*up
+    LAYER_LAUNCHES = 5
+
     def launches_per_step(self, n_sample: bool = True) -> int:
-        per_layer = 2 if self.ws is None else 3
-        return 1 + (self.ws is not None) + per_layer * len(self.layers) + (2 if n_sample else 0)
+        per_layer = self.LAYER_LAUNCHES + (self.ws is not None)
+        return 2 + (self.ws is not None) + per_layer * len(self.layers) + (2 if n_sample else 0)

@@ -159,6 +159,23 @@ int hy_varlen_attention_noalloc(const void* q, void* out, int32_t num_tokens, in
                                 const int32_t* cu_seqlens_q, const int32_t* seq_lens_k,
                                 int32_t num_seqs, float scale, int32_t* err, void* stream);
 
+/* ------------------------------------------------------- layer elementwise */
+
+/* Residual add + RMSNorm, row-wise over `cols` (<= 4096, a multiple of 8 for
+ * bf16 / 4 for fp32): if delta is non-null, x[r] <- round(x[r] + delta[r]) in
+ * place; then y[r] = round(RMSNorm(x[r]) * w), fp32 math, as nn.RMSNorm.
+ * Replaces: the residual adds and input_layernorm / post_attention_layernorm /
+ * final norm, hayate/model/block.py:18-31 and hayate/model/qwen.py:35,122. */
+int hy_add_rms_norm(int32_t dtype, void* x, int64_t ldx, const void* delta, int64_t ldd,
+                    int32_t rows, int32_t cols, const void* w, float eps, void* y, int64_t ldy,
+                    void* stream);
+
+/* y[r][i] = silu(gu[r][i]) * gu[r][inter + i] with the reference's two rounding
+ * points (silu result, product).  `inter` a multiple of 8 (bf16) / 4 (fp32).
+ * Replaces: FeedForward's silu(gate) * up, hayate/model/linear.py:11-13. */
+int hy_silu_mul(int32_t dtype, const void* gu, int64_t ld, int32_t rows, int32_t inter, void* y,
+                int64_t ldy, void* stream);
+
 /* ---------------------------------------------------------------- sampling */
 
 /* out[r] = argmax(logits[r][0:vocab]) with first-index ties (torch.argmax).

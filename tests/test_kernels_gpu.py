@@ -266,3 +266,41 @@ def test_argmax_first_index_ties(dt):
     torch.cuda.synchronize()
     assert torch.equal(out, want)
     assert out[1].item() == 5 and out[2].item() == 0
+
+
+# --------------------------------------------------------- RMSNorm, SiLU*up
+def _ulp_diff_bf16(a, b):
+    return (a.view(torch.int16).int() - b.view(torch.int16).int()).abs()
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("cols", [2560, 256])
+@pytest.mark.parametrize("residual", [False, True])
+def test_add_rms_norm_vs_reference(dt, cols, residual):
+    x = (torch.randn(37, cols, device=dev) * 3).to(dt)
+    delta = (torch.randn(37, cols, device=dev) * 3).to(dt) if residual else None
+    w = (1 + 0.1 * torch.randn(cols, device=dev)).to(dt)
+    want_x = x + delta if residual else x.clone()      # block.py:24,30 residual add
+    want = R.rms_norm(want_x, w, 1e-6)                  # nn.RMSNorm semantics (F.rms_norm)
+    got = K.add_rms_norm(x, w, 1e-6, delta=delta)
+    torch.cuda.synchronize()
+    assert torch.equal(x, want_x)                       # residual updated in place, exactly
+    if dt == torch.bfloat16:
+        d = _ulp_diff_bf16(got, want)
+        assert d.max().item() <= 1 and (d > 0).float().mean().item() < 0.02
+    else:
+        torch.testing.assert_close(got, want, rtol=2e-6, atol=2e-6)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_silu_mul_vs_reference(dt):
+    gu = (torch.randn(19, 2 * 9728, device=dev) * 2).to(dt)
+    got = K.silu_mul(gu)
+    I = 9728
+    want = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]   # linear.py:13
+    torch.cuda.synchronize()
+    if dt == torch.bfloat16:
+        d = _ulp_diff_bf16(got, want)
+        assert d.max().item() <= 1 and (d > 0).float().mean().item() < 0.01
+    else:
+        torch.testing.assert_close(got, want, rtol=1e-6, atol=1e-6)
