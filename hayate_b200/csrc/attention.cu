@@ -68,6 +68,7 @@ struct Shared {
   uint64_t tc_s;             // S = Q K^T complete (tcgen05.commit)
   uint64_t tc_o;             // O += P V complete (tcgen05.commit)
   uint32_t tmem_base;        // TMEM columns from tcgen05.alloc
+  float tc_red[2][128];      // per-row partials of the two column halves
 };
 
 #ifndef HY_PREFILL_TC
@@ -628,9 +629,9 @@ __device__ bool prefill_tile(const CUtensorMap* map, const MainArgs& a, const Pl
 // CTA-wide.  Rows r = 32*h + j of the 128-row tile are query head 4g+h, token
 // t0+j.  Per KV tile t (128 keys, TMA-staged, double-buffered):
 //   thread 0: S = Q K^T  (8 x tcgen05.mma, M=128 N=128 K=16, into TMEM cols 0..127)
-//   warps 0-3 (thread = row): S row from TMEM, causal mask, online softmax with
-//     lazy rescaling of O (in TMEM), P row (bf16) into smem in the 128B-swizzled
-//     K-major layout the MMA reads
+//   all 8 warps (two threads per row, 64 columns each): S from TMEM, causal
+//     mask, online softmax with lazy rescaling of O (in TMEM), P (bf16) into smem
+//     in the 128B-swizzled K-major layout the MMA reads
 //   thread 0: O += P V  (8 x tcgen05.mma, V as an MN-major operand, cols 128..255)
 // Q, K, V and P use the canonical 128-byte-swizzled layout: 8-row x 128 B atoms,
 // 1024 B between 8-row groups, the two 64-column halves 16 KB apart.
@@ -652,42 +653,52 @@ __device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const
   const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
   const uint32_t sbase = smem_u32(payload);
 
-  auto issue = [&](int t, int s) {
+  constexpr int TB = TC_KEYS / HY_BLOCK;         // blocks per KV tile
+  // Block ids of tile t, loaded together (thread 0) ahead of their issue.
+  auto fetch_ids = [&](int t, int (&ids)[TB]) {
+#pragma unroll
+    for (int jb = 0; jb < TB; ++jb) {
+      const int b = t * TB + jb;
+      ids[jb] = b < nblk ? bt[b] : -1;
+    }
+  };
+  auto issue = [&](int s, const int (&ids)[TB]) {
     uint8_t* kst = payload + TC_K_OFF + s * TC_KV_BYTES;
     uint8_t* vst = payload + TC_V_OFF + s * TC_KV_BYTES;
     fence_proxy_async();
     mbar_arrive_expect_tx(&sh.tc_kv[s], 2 * TC_KV_BYTES);
-#pragma unroll 1
-    for (int j = 0; j < TC_KEYS / HY_BLOCK; ++j) {
-      const int b = t * (TC_KEYS / HY_BLOCK) + j;
-      int rk = a.oob_row, rv = a.oob_row;
-      if (b < nblk) {
-        const int blk = bt[b];
-        if (blk >= 0 && blk < a.num_blocks) { rk = kv_row(a, blk, 0, g); rv = kv_row(a, blk, 1, g); }
-        else hy_flag(a.err, HY_ERR_BOUNDS);
-      }
-      tma_load_2d(kst + j * 2048, map, 0, rk, &sh.tc_kv[s]);
-      tma_load_2d(kst + 16384 + j * 2048, map, 64, rk, &sh.tc_kv[s]);
-      tma_load_2d(vst + j * 2048, map, 0, rv, &sh.tc_kv[s]);
-      tma_load_2d(vst + 16384 + j * 2048, map, 64, rv, &sh.tc_kv[s]);
+#pragma unroll
+    for (int jb = 0; jb < TB; ++jb) {
+      int rk = a.oob_row, rv = a.oob_row;       // ids < 0: past the end, zero fill
+      if (ids[jb] >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
+      else if (ids[jb] >= 0) { rk = kv_row(a, ids[jb], 0, g); rv = kv_row(a, ids[jb], 1, g); }
+      tma_load_2d(kst + jb * 2048, map, 0, rk, &sh.tc_kv[s]);
+      tma_load_2d(kst + 16384 + jb * 2048, map, 64, rk, &sh.tc_kv[s]);
+      tma_load_2d(vst + jb * 2048, map, 0, rv, &sh.tc_kv[s]);
+      tma_load_2d(vst + 16384 + jb * 2048, map, 64, rv, &sh.tc_kv[s]);
     }
   };
 
   __syncthreads();                              // previous users of smem / TMEM are done
+  int ids[TB];
   if (tid == 0)
-    for (int t = 0; t < 2 && t < ntiles; ++t) issue(t, t);
+    for (int t = 0; t < 2 && t < ntiles; ++t) {
+      fetch_ids(t, ids);
+      issue(t, ids);
+    }
 
-  const int row = tid & 127, h = row >> 5, j = row & 31;
-  if (warp < 4) {                               // Q tile -> smem (swizzled, K-major)
+  // Thread (row, half): row = 32*h + j of the tile, half = which 64 columns of
+  // the row's S / P / O it owns.  Warps w and w+4 share TMEM lane quarter w.
+  const int row = tid & 127, half = tid >> 7, h = row >> 5, j = row & 31;
+  {                                             // Q tile -> smem (swizzled, K-major)
     const bool valid = j < nrows;
     const uint4* qp = reinterpret_cast<const uint4*>(
-        a.q + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM);
+        a.q + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM) + 8 * half;
+    uint8_t* qrow = payload + TC_Q_OFF + half * 16384 + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
+    for (int c = 0; c < 8; ++c) {
       const uint4 val = valid ? qp[c] : make_uint4(0u, 0u, 0u, 0u);
-      const int cc = c & 7;
-      *reinterpret_cast<uint4*>(payload + TC_Q_OFF + (c >> 3) * 16384 + (row >> 3) * 1024 +
-                                (row & 7) * 128 + ((cc ^ (row & 7)) << 4)) = val;
+      *reinterpret_cast<uint4*>(qrow + ((c ^ (row & 7)) << 4)) = val;
     }
   }
   fence_proxy_async();                          // generic smem writes -> async proxy
@@ -697,14 +708,18 @@ __device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const
   constexpr uint32_t ID_O = tc_idesc_bf16(128, HY_HEAD_DIM, true);
   const uint32_t tS = tmem, tO = tmem + TC_KEYS;
   const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+  const uint32_t col0 = 64 * half;
   const int lim = prefix + t0 + j;              // last key row j may see
-  float m = NEG_INF, l = 0.f;
+  const float sl2 = a.scale_log2;
+  float m = NEG_INF, l = 0.f;                   // m in scaled log2 units
+  uint8_t* prow = payload + TC_P_OFF + half * 16384 + (row >> 3) * 1024 + (row & 7) * 128;
   bool ok = true;
   for (int t = 0; t < ntiles; ++t) {
     const int s = t & 1;
     bool w_ok = mbar_wait(&sh.tc_kv[s], (ph >> s) & 1u, a.err);
     if (__syncthreads_or(!w_ok)) { ok = false; break; }
     ph ^= 1u << s;
+    if (tid == 0 && t + 2 < ntiles) fetch_ids(t + 2, ids);   // lands while this tile runs
     if (tid == 0) {                             // S = Q K^T
       tc_fence_after();
       const uint32_t kb = sbase + TC_K_OFF + s * TC_KV_BYTES;
@@ -716,73 +731,65 @@ __device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const
       }
       tc_commit(&sh.tc_s);
     }
-    w_ok = true;
-    if (warp < 4) {
-      w_ok = mbar_wait(&sh.tc_s, (ph >> 2) & 1u, a.err);
-      if (w_ok) {
-        tc_fence_after();
-        float sc[TC_KEYS];
+    w_ok = mbar_wait(&sh.tc_s, (ph >> 2) & 1u, a.err);
+    float sc[64];
+    float mx = NEG_INF;
+    const int kbase = t * TC_KEYS + col0;
+    if (w_ok) {
+      tc_fence_after();
+      tmem_ld32(tS + lane_base + col0, *reinterpret_cast<float(*)[32]>(&sc[0]));
+      tmem_ld32(tS + lane_base + col0 + 32, *reinterpret_cast<float(*)[32]>(&sc[32]));
+      tmem_wait_ld();
+      if (t * TC_KEYS + TC_KEYS - 1 > prefix + t0) {   // diagonal or tail tile: mask
 #pragma unroll
-        for (int c = 0; c < TC_KEYS / 32; ++c) {
-          float chunk[32];
-          tmem_ld32(tS + lane_base + 32 * c, chunk);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) sc[32 * c + i] = chunk[i];
-        }
-        const int kbase = t * TC_KEYS;
-        const bool need_mask = kbase + TC_KEYS - 1 > prefix + t0;
-        float mx = NEG_INF;
-#pragma unroll
-        for (int i = 0; i < TC_KEYS; ++i) {
-          float x = sc[i] * a.scale_log2;
-          if (need_mask && (kbase + i > lim || kbase + i >= kv_len)) x = NEG_INF;
-          sc[i] = x;
-          mx = fmaxf(mx, x);
-        }
-        const bool grow = mx > m + RESCALE_LOG2;
-        if (__any_sync(0xffffffffu, grow)) {
-          const float mnew = grow ? mx : m;
-          const float alpha = exp2f(m - mnew);
-          l *= alpha;
-          m = mnew;
-          if (t > 0) {                          // rescale this warp's O rows in TMEM
-#pragma unroll 1
-            for (int c = 0; c < HY_HEAD_DIM / 32; ++c) {
-              float o[32];
-              tmem_ld32(tO + lane_base + 32 * c, o);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] *= alpha;
-              tmem_st32(tO + lane_base + 32 * c, o);
-            }
-            tmem_wait_st();
-          }
-        }
-        const float mu = (m == NEG_INF) ? 0.f : m;
-        uint8_t* prow = payload + TC_P_OFF + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-        for (int cc = 0; cc < TC_KEYS / 8; ++cc) {
-          float p[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            p[e] = exp2f(sc[8 * cc + e] - mu);
-            l += p[e];
-          }
-          uint4 pk;
-          pk.x = pack_bf16(p[0], p[1]);
-          pk.y = pack_bf16(p[2], p[3]);
-          pk.z = pack_bf16(p[4], p[5]);
-          pk.w = pack_bf16(p[6], p[7]);
-          const int c8 = cc & 7;
-          *reinterpret_cast<uint4*>(prow + (cc >> 3) * 16384 + ((c8 ^ (row & 7)) << 4)) = pk;
-        }
-        fence_proxy_async();
-        tc_fence_before();
+        for (int i = 0; i < 64; ++i)
+          if (kbase + i > lim || kbase + i >= kv_len) sc[i] = NEG_INF;
       }
+#pragma unroll
+      for (int i = 0; i < 64; ++i) mx = fmaxf(mx, sc[i]);
+      sh.tc_red[half][row] = mx;
     }
     if (__syncthreads_or(!w_ok)) { ok = false; break; }
     ph ^= 1u << 2;
+    mx = fmaxf(sh.tc_red[0][row], sh.tc_red[1][row]) * sl2;   // row max, scaled
+    const bool grow = mx > m + RESCALE_LOG2;
+    if (__any_sync(0xffffffffu, grow)) {
+      const float mnew = grow ? mx : m;
+      const float alpha = exp2f(m - mnew);      // 0 when m was -inf
+      l *= alpha;
+      m = mnew;
+      if (t > 0) {                              // rescale this thread's half of its O row
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float o[32];
+          tmem_ld32(tO + lane_base + col0 + 32 * c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tO + lane_base + col0 + 32 * c, o);
+        }
+        tmem_wait_st();
+      }
+    }
+    const float mneg = (m == NEG_INF) ? 0.f : -m;
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {
+      float p[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        p[e] = exp2f(fmaf(sc[8 * cc + e], sl2, mneg));
+        l += p[e];
+      }
+      uint4 pk;
+      pk.x = pack_bf16(p[0], p[1]);
+      pk.y = pack_bf16(p[2], p[3]);
+      pk.z = pack_bf16(p[4], p[5]);
+      pk.w = pack_bf16(p[6], p[7]);
+      *reinterpret_cast<uint4*>(prow + ((cc ^ (row & 7)) << 4)) = pk;
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
     if (tid == 0) {                             // O += P V
       tc_fence_after();
       const uint32_t vb = sbase + TC_V_OFF + s * TC_KV_BYTES;
@@ -797,7 +804,7 @@ __device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const
     if (__syncthreads_or(!w_ok)) { ok = false; break; }
     ph ^= 1u << 3;
     tc_fence_after();
-    if (tid == 0 && t + 2 < ntiles) issue(t + 2, s);
+    if (tid == 0 && t + 2 < ntiles) issue(s, ids);
   }
   if (!ok) {
     // let outstanding copies and MMAs land before the caller frees TMEM
@@ -809,15 +816,17 @@ __device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const
     __syncthreads();
     return false;
   }
-  if (warp < 4) {                               // epilogue: O / l -> out
+  sh.tc_red[half][row] = l;                     // epilogue: O / l -> out
+  __syncthreads();
+  {
     // tcgen05.ld is warp-collective: every lane loads, only real rows store
     const bool store = j < nrows;
-    const float inv = 1.f / l;
-    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM;
+    const float inv = 1.f / (sh.tc_red[0][row] + sh.tc_red[1][row]);
+    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM + col0;
 #pragma unroll 1
-    for (int c = 0; c < HY_HEAD_DIM / 32; ++c) {
+    for (int c = 0; c < 2; ++c) {
       float o[32];
-      tmem_ld32(tO + lane_base + 32 * c, o);
+      tmem_ld32(tO + lane_base + col0 + 32 * c, o);
       tmem_wait_ld();
       if (store) {
 #pragma unroll
