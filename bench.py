@@ -66,25 +66,29 @@ def dist_setup():
 def barrier(world, local):
     if world > 1:
         import torch.distributed as dist
-        dist.barrier(device_ids=[local])
+        if dist.get_backend() == "nccl":
+            dist.barrier(device_ids=[local])
+        else:
+            dist.barrier()
+
+
+def _reduce(x: float, world: int, op: str) -> float:
+    """All-reduce one number over the ranks (NCCL on GPUs, gloo on CPU)."""
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=getattr(dist.ReduceOp, op))
+    return float(t.item())
 
 
 def max_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return _reduce(x, world, "MAX")
 
 
 def sum_over_ranks(x: float, world: int) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    return _reduce(x, world, "SUM")
 
 
 # ---------------------------------------------------------------------- clocks
@@ -342,7 +346,7 @@ def emit_line(args, world, toks_all, ms_max, wall_ms, etoks_all, ems_max, h2d, d
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind,
                      "traffic": profile_traffic(),
-                     "kernel": "varlen paged attention (attn_main_kernel + combine_kernel)",
+                     "kernel": "varlen paged attention (attn_main_kernel)",
                      "workload": "256 decode seqs ctx log-uniform[256,16384] + 4 prefill chunks "
                                  "of 512 (priors 0/512/1536/3584), 32/8 heads, d128, bf16, "
                                  "16-token blocks, permuted block table, one layer",

@@ -1,0 +1,20 @@
+"""The reference's benchmark modes run end to end on the engine (small sizes)."""
+import pytest
+
+from hayate_b200 import benchmark
+
+pytestmark = pytest.mark.gpu
+
+
+def test_benchmark_modes_small():
+    rows = benchmark.main(["3", "--repetitions", "1", "--max-tokens", "8",
+                           "--min-prompt-tokens", "16", "--max-prompt-tokens", "40",
+                           "--arrival-gap-ms", "5", "--modes", "single,upfront,staggered"])
+    names = [t for t, _ in rows]
+    assert names == ["single request", "submit all upfront", "staggered arrivals"]
+    for _, r in rows:
+        assert r["generated_tokens"] > 0 and r["elapsed"] > 0
+        assert len(r["latencies"]) >= 1
+    # single mode: 3 requests x 8 tokens; upfront: one run of 3 x 8
+    assert rows[0][1]["generated_tokens"] == 24
+    assert rows[1][1]["generated_tokens"] == 24
