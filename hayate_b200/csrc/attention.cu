@@ -14,9 +14,9 @@
 //
 // Work is planned on the device (plan_kernel) once per step and reused by every
 // layer:
-//   * prefill items -- (seq, kv_head, 32-token tile): one CTA of 8 warps, the 4
-//     query heads of the group x 2 groups of 16 tokens, sharing K/V tiles of 64
-//     keys staged by TMA;
+//   * prefill items -- (seq, kv_head, 32-token tile): one CTA; the 4 query heads
+//     of the group x 32 tokens form one M=128 tcgen05 tile (accumulators in
+//     TMEM), K/V tiles of 64 keys staged by TMA in 4-slot rings;
 //   * decode items  -- (seq, kv_head, block range): one warp with its own TMA
 //     ring of K/V block tiles, mma.sync for QK^T and PV, an online softmax;
 //     for a sequence split over several items, the last item to finish (an
@@ -37,21 +37,30 @@ namespace {
 #ifndef HY_DEC_STAGES
 #define HY_DEC_STAGES 3
 #endif
-constexpr int ATT_WARPS = HY_ATT_WARPS;                          // 8: two query-row groups
+constexpr int ATT_WARPS = HY_ATT_WARPS;                          // 8
 constexpr int ATT_THREADS = ATT_WARPS * 32;
 constexpr int DEC_STAGES = HY_DEC_STAGES;                        // TMA ring per decode warp
 constexpr int DEC_TILE_BYTES = 2 * HY_BLOCK * HY_HEAD_DIM * 2;   // K+V of one block: 8 KB
 constexpr int DEC_WARP_BYTES = DEC_STAGES * DEC_TILE_BYTES;      // 32 KB
-constexpr int PRE_KEYS = 64;                                     // keys per prefill tile
-constexpr int PRE_BLOCKS = PRE_KEYS / HY_BLOCK;                  // 4
-constexpr int PRE_GROUPS = ATT_WARPS / 4;                        // 4 warps (heads) per group
-constexpr int PRE_QROWS = 16 * PRE_GROUPS;                       // query tokens per item
-constexpr int PRE_KV_BYTES = PRE_KEYS * HY_HEAD_DIM * 2;         // 16 KB (K or V)
-constexpr int PRE_STAGE_BYTES = 2 * PRE_KV_BYTES;                // 32 KB
-constexpr int PRE_STAGES = 2;
-constexpr int SMEM_PAYLOAD = (ATT_WARPS * DEC_WARP_BYTES > PRE_STAGES * PRE_STAGE_BYTES)
-                                 ? ATT_WARPS * DEC_WARP_BYTES
-                                 : PRE_STAGES * PRE_STAGE_BYTES;
+constexpr int PRE_QROWS = 32;                                    // query tokens per prefill item
+// tcgen05 prefill tile: M = 128 query rows (4 heads x 32 tokens, head-major so
+// warp w owns TMEM lane quarter w % 4), KV tiles of 64 keys (4 blocks) in rings
+// of TC_NS slots, so each K/V load has TC_NS - 1 tiles of lead.
+constexpr int TC_KEYS = 64;
+constexpr int TC_NS = 4;                                         // K and V ring slots
+constexpr int TC_KV_BYTES = TC_KEYS * HY_HEAD_DIM * 2;          // K or V of one tile: 16 KB
+constexpr int TC_HALF = TC_KEYS * 128;                           // one 64-column half: 8 KB
+constexpr int TC_P_BYTES = 128 * TC_KEYS * 2;                    // P of one tile: 16 KB
+constexpr int TC_Q_OFF = 0;                                      // Q: 32 KB
+constexpr int TC_K_OFF = 32768;                                  // K ring
+constexpr int TC_V_OFF = TC_K_OFF + TC_NS * TC_KV_BYTES;         // V ring
+constexpr int TC_P_OFF = TC_V_OFF + TC_NS * TC_KV_BYTES;         // P: 2 slots
+constexpr int TC_IDS_OFF = TC_P_OFF + 2 * TC_P_BYTES;            // block ids of the item
+constexpr int TC_MAX_IDS = 40960 / HY_BLOCK;                     // positions / block
+constexpr int TC_SMEM = TC_IDS_OFF + TC_MAX_IDS * 4;             // 202 KB
+constexpr uint32_t TC_TMEM_COLS = 256;                           // S: 2 x 64, O: 128
+constexpr int SMEM_PAYLOAD = ATT_WARPS * DEC_WARP_BYTES > TC_SMEM ? ATT_WARPS * DEC_WARP_BYTES
+                                                                   : TC_SMEM;
 constexpr int SMEM_BYTES = SMEM_PAYLOAD + 1024;                  // + alignment slack
 constexpr int MIN_SPLIT = 4;                                     // blocks per decode item
 constexpr float NEG_INF = -INFINITY;
@@ -63,30 +72,14 @@ constexpr float RESCALE_LOG2 = 8.0f;
 
 struct Shared {
   uint64_t dec_bar[ATT_WARPS][DEC_STAGES];
-  uint64_t pre_bar[PRE_STAGES];
-  uint64_t tc_kv[2];         // tcgen05 prefill: K/V tile landed (TMA transaction bytes)
-  uint64_t tc_s;             // S = Q K^T complete (tcgen05.commit)
-  uint64_t tc_o;             // O += P V complete (tcgen05.commit)
+  // tcgen05 prefill; K/V by ring slot, S/O by (tile counter & 1):
+  uint64_t tc_k[TC_NS];      // K tile landed (TMA transaction bytes)
+  uint64_t tc_v[TC_NS];      // V tile landed
+  uint64_t tc_s[2];          // S = Q K^T complete (tcgen05.commit)
+  uint64_t tc_o[2];          // O += P V complete (tcgen05.commit)
   uint32_t tmem_base;        // TMEM columns from tcgen05.alloc
   float tc_red[2][128];      // per-row partials of the two column halves
 };
-
-#ifndef HY_PREFILL_TC
-#define HY_PREFILL_TC 1
-#endif
-// tcgen05 prefill tile: M = 128 query rows (4 heads x 32 tokens, head-major so
-// warp w < 4 owns TMEM lanes 32w.. = head w), KV tiles of 128 keys (8 blocks).
-constexpr int TC_QTOK = 32;
-constexpr int TC_KEYS = 128;
-constexpr int TC_KV_BYTES = TC_KEYS * HY_HEAD_DIM * 2;          // K or V of one tile: 32 KB
-constexpr int TC_Q_OFF = 0;                                      // Q: 32 KB
-constexpr int TC_K_OFF = 32768;                                  // K: 2 stages
-constexpr int TC_V_OFF = 32768 * 3;                              // V: 2 stages
-constexpr int TC_P_OFF = 32768 * 5;                              // P: 32 KB
-constexpr int TC_SMEM = 32768 * 6;                               // 192 KB
-constexpr uint32_t TC_TMEM_COLS = 256;                           // S: [0,128), O: [128,256)
-static_assert(TC_SMEM <= SMEM_PAYLOAD, "tcgen05 prefill tile does not fit the payload");
-static_assert(!HY_PREFILL_TC || PRE_QROWS == TC_QTOK, "plan tiles must match the MMA tile");
 
 HY_DEVICE uint8_t* payload_base(uint8_t* dyn) {
   const uint32_t a = smem_u32(dyn);
@@ -435,11 +428,22 @@ __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const Pla
 }
 
 // ------------------------------------------------------------------ prefill tile
-// CTA-wide: warp w computes query head 4g + (w % 4) for the 16 tokens
-// [t0 + 16*(w/4), +16) of seq; all warps share the K/V tiles of the CTA.
-__device__ bool prefill_tile(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
-                             int item, uint8_t* payload, uint64_t* bars, uint32_t& phase) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+// tcgen05, CTA-wide.  Rows r = 32*h + j of the 128-row tile are query head 4g+h,
+// token t0+j; two threads own each row (half = which 32 of a tile's 64 keys, and
+// which 64 columns of the output).  KV tile t = 64 keys (4 paged blocks), global
+// tile counter c = c0 + t: K/V ring slot c % TC_NS, S/P slot c & 1.
+//   start of t : thread 0 issues S_{t+1} = Q K_{t+1}^T (tcgen05.mma, runs during
+//                softmax(t)); once S_t is complete the warps refill its K slot
+//                with K_{t+TC_NS} (each warp issues one of the 8 TMA boxes);
+//   softmax(t) : S_t from TMEM, causal mask, online softmax with lazy rescaling
+//                of O in TMEM, P_t (bf16) into smem (128B-swizzled, K-major);
+//   end of t   : thread 0 issues O += P_t V_t (runs during softmax(t+1)); the warps
+//                refill the V slot PV_{t-1} freed with V_{t-1+TC_NS}.
+// Each K/V load has TC_NS - 1 tiles of lead; O stays in TMEM (columns 128..255).
+__device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
+                                int item, uint8_t* payload, Shared& sh, uint32_t tmem,
+                                uint32_t& ctr) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int4 it = v.pre[item];
   const int seq = it.x, g = it.y, t0 = it.z;
   const int row0 = a.cu_q[seq];
@@ -447,248 +451,22 @@ __device__ bool prefill_tile(const CUtensorMap* map, const MainArgs& a, const Pl
   const int kv_len = a.seq_lens_k[seq];
   const int prefix = kv_len - q_len;
   const int nrows = min(PRE_QROWS, q_len - t0);
-  const int kv_end = prefix + t0 + nrows;                   // keys [0, kv_end)
-  const int ntiles = (kv_end + PRE_KEYS - 1) / PRE_KEYS;
-  const int nblk = (kv_end + HY_BLOCK - 1) / HY_BLOCK;
-  const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
-  const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
-  const int hq = g * HY_GROUP + (warp & 3);
-  const int tg = 16 * (warp >> 2);                          // this warp's first token in the tile
-  const int wrows = nrows - tg;                             // valid rows of this warp (may be <= 0)
-
-  auto issue = [&](int t, int s) {
-    uint8_t* st = payload + s * PRE_STAGE_BYTES;
-    fence_proxy_async();
-    mbar_arrive_expect_tx(&bars[s], PRE_STAGE_BYTES);
-#pragma unroll
-    for (int j = 0; j < PRE_BLOCKS; ++j) {
-      const int b = t * PRE_BLOCKS + j;
-      int rk = a.oob_row, rv = a.oob_row;
-      if (b < nblk) {
-        const int blk = bt[b];
-        if (blk >= 0 && blk < a.num_blocks) { rk = kv_row(a, blk, 0, g); rv = kv_row(a, blk, 1, g); }
-        else hy_flag(a.err, HY_ERR_BOUNDS);
-      }
-      tma_load_2d(st + j * 4096, map, 0, rk, &bars[s]);
-      tma_load_2d(st + j * 4096 + 2048, map, 64, rk, &bars[s]);
-      tma_load_2d(st + PRE_KV_BYTES + j * 4096, map, 0, rv, &bars[s]);
-      tma_load_2d(st + PRE_KV_BYTES + j * 4096 + 2048, map, 64, rv, &bars[s]);
-    }
-  };
-
-  __syncthreads();                 // previous users of the payload are done
-  if (tid == 0) {
-    for (int t = 0; t < PRE_STAGES && t < ntiles; ++t) issue(t, t);
-  }
-
-  const int r = lane >> 2, c = 2 * (lane & 3);
-  // Query fragments for rows r and r+8 (tokens t0+tg+r, +8) of head hq.
-  uint32_t qa[8][4];
-  {
-    const bool v0 = r < wrows, v1 = r + 8 < wrows;
-    const size_t rowq = (size_t)(row0 + t0 + tg + r);
-    const __nv_bfloat16* q0 = a.q + (rowq * a.q_heads + hq) * HY_HEAD_DIM;
-    const __nv_bfloat16* q1 = q0 + (size_t)8 * a.q_heads * HY_HEAD_DIM;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int d = 16 * kk + c;
-      qa[kk][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d) : 0u;
-      qa[kk][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d) : 0u;
-      qa[kk][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + d + 8) : 0u;
-      qa[kk][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + d + 8) : 0u;
-    }
-  }
-  float o[16][4];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float m[2] = {NEG_INF, NEG_INF}, l[2] = {0.f, 0.f};
-  const int lim0 = prefix + t0 + tg + r, lim1 = lim0 + 8;   // last visible key per row
-  const int mi = lane >> 3, ri = lane & 7;
-  const int k_key = ri + 8 * (mi >> 1), k_dsub = 8 * (mi & 1);
-  const int v_key = ri + 8 * (mi & 1), v_dsub = 8 * (mi >> 1);
-
-  bool ok = true;
-  for (int t = 0; t < ntiles; ++t) {
-    const int s = t % PRE_STAGES;
-    const bool w_ok = mbar_wait(&bars[s], (phase >> s) & 1u, a.err);
-    if (__syncthreads_or(!w_ok)) { ok = false; break; }
-    phase ^= (1u << s);
-    const uint32_t kb = smem_u32(payload + s * PRE_STAGE_BYTES);
-    const uint32_t vb = kb + PRE_KV_BYTES;
-    const int kbase = t * PRE_KEYS;
-    // Tiles wholly above this warp's first row contribute nothing; skip the math
-    // (the barrier protocol is unchanged).
-    if (wrows > 0 && kbase <= prefix + t0 + tg + min(wrows, 16) - 1) {
-      float sacc[8][4];
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
-#pragma unroll
-      for (int pr = 0; pr < 4; ++pr) {
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const int d = 16 * kk + k_dsub;
-          uint32_t b[4];
-          ldmatrix_x4(b, kb + pr * 4096 + (d >> 6) * 2048 + swz128(k_key, d & 63));
-          mma_bf16_16816(sacc[2 * pr], qa[kk], b[0], b[1]);
-          mma_bf16_16816(sacc[2 * pr + 1], qa[kk], b[2], b[3]);
-        }
-      }
-      const bool need_mask = kbase + PRE_KEYS - 1 > prefix + t0 + tg;   // diagonal or tail
-      float mx0 = NEG_INF, mx1 = NEG_INF;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = kbase + nt * 8 + c + e;
-          float x0 = sacc[nt][e] * a.scale_log2, x1 = sacc[nt][2 + e] * a.scale_log2;
-          if (need_mask) {
-            if (key > lim0 || key >= kv_len) x0 = NEG_INF;
-            if (key > lim1 || key >= kv_len) x1 = NEG_INF;
-          }
-          sacc[nt][e] = x0;
-          sacc[nt][2 + e] = x1;
-          mx0 = fmaxf(mx0, x0);
-          mx1 = fmaxf(mx1, x1);
-        }
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const bool g0 = mx0 > m[0] + RESCALE_LOG2, g1 = mx1 > m[1] + RESCALE_LOG2;
-      if (__any_sync(0xffffffffu, g0 || g1)) {
-        const float n0 = g0 ? mx0 : m[0], n1 = g1 ? mx1 : m[1];
-        const float al0 = exp2f(m[0] - n0), al1 = exp2f(m[1] - n1);
-        l[0] *= al0;
-        l[1] *= al1;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          o[j][0] *= al0; o[j][1] *= al0;
-          o[j][2] *= al1; o[j][3] *= al1;
-        }
-        m[0] = n0;
-        m[1] = n1;
-      }
-      const float mu0 = (m[0] == NEG_INF) ? 0.f : m[0], mu1 = (m[1] == NEG_INF) ? 0.f : m[1];
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        sacc[nt][0] = exp2f(sacc[nt][0] - mu0);
-        sacc[nt][1] = exp2f(sacc[nt][1] - mu0);
-        sacc[nt][2] = exp2f(sacc[nt][2] - mu1);
-        sacc[nt][3] = exp2f(sacc[nt][3] - mu1);
-        l[0] += sacc[nt][0] + sacc[nt][1];
-        l[1] += sacc[nt][2] + sacc[nt][3];
-      }
-#pragma unroll
-      for (int kt = 0; kt < 4; ++kt) {
-        const uint32_t pa[4] = {pack_bf16(sacc[2 * kt][0], sacc[2 * kt][1]),
-                                pack_bf16(sacc[2 * kt][2], sacc[2 * kt][3]),
-                                pack_bf16(sacc[2 * kt + 1][0], sacc[2 * kt + 1][1]),
-                                pack_bf16(sacc[2 * kt + 1][2], sacc[2 * kt + 1][3])};
-#pragma unroll
-        for (int j2 = 0; j2 < 8; ++j2) {
-          const int d = 16 * j2 + v_dsub;
-          uint32_t b[4];
-          ldmatrix_x4_trans(b, vb + kt * 4096 + (d >> 6) * 2048 + swz128(v_key, d & 63));
-          mma_bf16_16816(o[2 * j2], pa, b[0], b[1]);
-          mma_bf16_16816(o[2 * j2 + 1], pa, b[2], b[3]);
-        }
-      }
-    }
-    __syncthreads();
-    if (tid == 0 && t + PRE_STAGES < ntiles) issue(t + PRE_STAGES, s);
-  }
-  if (!ok) {
-    if (tid == 0)
-      for (int s = 0; s < PRE_STAGES; ++s) mbar_wait(&bars[s], (phase >> s) & 1u, nullptr);
-    __syncthreads();
-    return false;
-  }
-  l[0] += __shfl_xor_sync(0xffffffffu, l[0], 1);
-  l[0] += __shfl_xor_sync(0xffffffffu, l[0], 2);
-  l[1] += __shfl_xor_sync(0xffffffffu, l[1], 1);
-  l[1] += __shfl_xor_sync(0xffffffffu, l[1], 2);
-  const float inv0 = 1.f / l[0], inv1 = 1.f / l[1];
-  if (r < wrows) {
-    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + tg + r) * a.q_heads + hq) * HY_HEAD_DIM;
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      *reinterpret_cast<uint32_t*>(op + 8 * j + c) = pack_bf16(o[j][0] * inv0, o[j][1] * inv0);
-  }
-  if (r + 8 < wrows) {
-    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + tg + r + 8) * a.q_heads + hq) * HY_HEAD_DIM;
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      *reinterpret_cast<uint32_t*>(op + 8 * j + c) = pack_bf16(o[j][2] * inv1, o[j][3] * inv1);
-  }
-  __syncthreads();
-  return true;
-}
-
-
-// ------------------------------------------------------------------ prefill tile (tcgen05)
-// CTA-wide.  Rows r = 32*h + j of the 128-row tile are query head 4g+h, token
-// t0+j.  Per KV tile t (128 keys, TMA-staged, double-buffered):
-//   thread 0: S = Q K^T  (8 x tcgen05.mma, M=128 N=128 K=16, into TMEM cols 0..127)
-//   all 8 warps (two threads per row, 64 columns each): S from TMEM, causal
-//     mask, online softmax with lazy rescaling of O (in TMEM), P (bf16) into smem
-//     in the 128B-swizzled K-major layout the MMA reads
-//   thread 0: O += P V  (8 x tcgen05.mma, V as an MN-major operand, cols 128..255)
-// Q, K, V and P use the canonical 128-byte-swizzled layout: 8-row x 128 B atoms,
-// 1024 B between 8-row groups, the two 64-column halves 16 KB apart.
-__device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
-                                int item, uint8_t* payload, Shared& sh, uint32_t tmem,
-                                uint32_t& ph) {
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int4 it = v.pre[item];
-  const int seq = it.x, g = it.y, t0 = it.z;
-  const int row0 = a.cu_q[seq];
-  const int q_len = a.cu_q[seq + 1] - row0;
-  const int kv_len = a.seq_lens_k[seq];
-  const int prefix = kv_len - q_len;
-  const int nrows = min(TC_QTOK, q_len - t0);
   const int kv_end = prefix + t0 + nrows;
   const int ntiles = (kv_end + TC_KEYS - 1) / TC_KEYS;
-  const int nblk = (kv_end + HY_BLOCK - 1) / HY_BLOCK;
+  const int nblk = min((kv_end + HY_BLOCK - 1) / HY_BLOCK, TC_MAX_IDS);
   const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
   const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
   const uint32_t sbase = smem_u32(payload);
-
-  constexpr int TB = TC_KEYS / HY_BLOCK;         // blocks per KV tile
-  // Block ids of tile t, loaded together (thread 0) ahead of their issue.
-  auto fetch_ids = [&](int t, int (&ids)[TB]) {
-#pragma unroll
-    for (int jb = 0; jb < TB; ++jb) {
-      const int b = t * TB + jb;
-      ids[jb] = b < nblk ? bt[b] : -1;
-    }
-  };
-  auto issue = [&](int s, const int (&ids)[TB]) {
-    uint8_t* kst = payload + TC_K_OFF + s * TC_KV_BYTES;
-    uint8_t* vst = payload + TC_V_OFF + s * TC_KV_BYTES;
-    fence_proxy_async();
-    mbar_arrive_expect_tx(&sh.tc_kv[s], 2 * TC_KV_BYTES);
-#pragma unroll
-    for (int jb = 0; jb < TB; ++jb) {
-      int rk = a.oob_row, rv = a.oob_row;       // ids < 0: past the end, zero fill
-      if (ids[jb] >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
-      else if (ids[jb] >= 0) { rk = kv_row(a, ids[jb], 0, g); rv = kv_row(a, ids[jb], 1, g); }
-      tma_load_2d(kst + jb * 2048, map, 0, rk, &sh.tc_kv[s]);
-      tma_load_2d(kst + 16384 + jb * 2048, map, 64, rk, &sh.tc_kv[s]);
-      tma_load_2d(vst + jb * 2048, map, 0, rv, &sh.tc_kv[s]);
-      tma_load_2d(vst + 16384 + jb * 2048, map, 64, rv, &sh.tc_kv[s]);
-    }
-  };
+  int32_t* sids = reinterpret_cast<int32_t*>(payload + TC_IDS_OFF);
+  const uint32_t c0 = ctr;
+  ctr += ntiles;
+  auto kslot = [&](int t) { return (c0 + (uint32_t)t) % TC_NS; };
+  auto kpar = [&](int t) { return ((c0 + (uint32_t)t) / TC_NS) & 1u; };
+  auto s2 = [&](int t) { return (c0 + (uint32_t)t) & 1u; };
+  auto par2 = [&](int t) { return ((c0 + (uint32_t)t) >> 1) & 1u; };
 
   __syncthreads();                              // previous users of smem / TMEM are done
-  int ids[TB];
-  if (tid == 0)
-    for (int t = 0; t < 2 && t < ntiles; ++t) {
-      fetch_ids(t, ids);
-      issue(t, ids);
-    }
-
-  // Thread (row, half): row = 32*h + j of the tile, half = which 64 columns of
-  // the row's S / P / O it owns.  Warps w and w+4 share TMEM lane quarter w.
+  for (int i = tid; i < nblk; i += ATT_THREADS) sids[i] = bt[i];
   const int row = tid & 127, half = tid >> 7, h = row >> 5, j = row & 31;
   {                                             // Q tile -> smem (swizzled, K-major)
     const bool valid = j < nrows;
@@ -704,53 +482,91 @@ __device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const
   fence_proxy_async();                          // generic smem writes -> async proxy
   __syncthreads();
 
+  // Load K (kv = 0) or V (kv = 1) of tile t into its ring slot.  Called by
+  // every warp: lane 0 of warp w issues box w (block w / 2, column half w % 2),
+  // so no warp carries the whole issue cost; thread 0 posts the byte count.
+  constexpr int TB = TC_KEYS / HY_BLOCK;
+  static_assert(2 * TB == ATT_WARPS, "one TMA box per warp");
+  auto load = [&](int t, int kv) {
+    const uint32_t b = kslot(t);
+    uint64_t* bar = kv ? &sh.tc_v[b] : &sh.tc_k[b];
+    if (tid == 0) mbar_arrive_expect_tx(bar, TC_KV_BYTES);
+    if (lane == 0) {
+      const int jb = warp >> 1, hf = warp & 1;
+      const int blk = t * TB + jb;
+      const int id = blk < nblk ? sids[blk] : -1;
+      int r = a.oob_row;                        // past the end: zero fill
+      if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
+      else if (id >= 0) r = kv_row(a, id, kv, g);
+      tma_load_2d(payload + (kv ? TC_V_OFF : TC_K_OFF) + b * TC_KV_BYTES + hf * TC_HALF + jb * 2048,
+                  map, 64 * hf, r, bar);
+    }
+  };
+
   constexpr uint32_t ID_S = tc_idesc_bf16(128, TC_KEYS, false);
   constexpr uint32_t ID_O = tc_idesc_bf16(128, HY_HEAD_DIM, true);
-  const uint32_t tS = tmem, tO = tmem + TC_KEYS;
+  const uint32_t tO = tmem + 2 * TC_KEYS;
+  const uint64_t dQ = tc_desc_sw128(sbase + TC_Q_OFF, 16, 1024);
+  auto issue_s = [&](int t) {                   // S_t = Q K_t^T into TMEM slot
+    const uint64_t dK = tc_desc_sw128(sbase + TC_K_OFF + kslot(t) * TC_KV_BYTES, 16, 1024);
+    const uint32_t d = tmem + s2(t) * TC_KEYS;
+    tc_fence_after();
+#pragma unroll
+    for (int kk = 0; kk < HY_HEAD_DIM / 16; ++kk)
+      tc_mma_bf16(d, dQ + (uint64_t)((((kk >> 2) * 16384) + (kk & 3) * 32) >> 4),
+                  dK + (uint64_t)((((kk >> 2) * TC_HALF) + (kk & 3) * 32) >> 4), ID_S, kk > 0);
+    tc_commit(&sh.tc_s[s2(t)]);
+  };
+  auto issue_o = [&](int t) {                   // O += P_t V_t
+    const uint64_t dP = tc_desc_sw128(sbase + TC_P_OFF + s2(t) * TC_P_BYTES, 16, 1024);
+    const uint64_t dV = tc_desc_sw128(sbase + TC_V_OFF + kslot(t) * TC_KV_BYTES, TC_HALF, 1024);
+    tc_fence_after();
+#pragma unroll
+    for (int kk = 0; kk < TC_KEYS / 16; ++kk)
+      tc_mma_bf16(tO, dP + (uint64_t)((kk * 32) >> 4), dV + (uint64_t)((kk * 2048) >> 4), ID_O,
+                  (t > 0 || kk > 0));
+    tc_commit(&sh.tc_o[s2(t)]);
+  };
+
+  bool ok = true;
+  for (int t = 0; t < TC_NS && t < ntiles; ++t) { load(t, 0); load(t, 1); }
+  if (tid == 0) {
+    ok = mbar_wait(&sh.tc_k[kslot(0)], kpar(0), a.err);
+    if (ok) issue_s(0);
+  }
+  if (__syncthreads_or(!ok)) ok = false;
+
   const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-  const uint32_t col0 = 64 * half;
+  const int key0 = 32 * half;                   // this thread's keys within a tile
+  const uint32_t ocol = 64 * half;              // this thread's output columns
   const int lim = prefix + t0 + j;              // last key row j may see
   const float sl2 = a.scale_log2;
   float m = NEG_INF, l = 0.f;                   // m in scaled log2 units
-  uint8_t* prow = payload + TC_P_OFF + half * 16384 + (row >> 3) * 1024 + (row & 7) * 128;
-  bool ok = true;
-  for (int t = 0; t < ntiles; ++t) {
-    const int s = t & 1;
-    bool w_ok = mbar_wait(&sh.tc_kv[s], (ph >> s) & 1u, a.err);
-    if (__syncthreads_or(!w_ok)) { ok = false; break; }
-    ph ^= 1u << s;
-    if (tid == 0 && t + 2 < ntiles) fetch_ids(t + 2, ids);   // lands while this tile runs
-    if (tid == 0) {                             // S = Q K^T
-      tc_fence_after();
-      const uint32_t kb = sbase + TC_K_OFF + s * TC_KV_BYTES;
-#pragma unroll
-      for (int kk = 0; kk < HY_HEAD_DIM / 16; ++kk) {
-        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-        tc_mma_bf16(tS, tc_desc_sw128(sbase + TC_Q_OFF + off, 16, 1024),
-                    tc_desc_sw128(kb + off, 16, 1024), ID_S, kk > 0);
-      }
-      tc_commit(&sh.tc_s);
+  for (int t = 0; t < ntiles && ok; ++t) {
+    bool w_ok = true;
+    if (tid == 0 && t + 1 < ntiles) {           // S_{t+1} runs during softmax(t)
+      w_ok = mbar_wait(&sh.tc_k[kslot(t + 1)], kpar(t + 1), a.err);
+      if (w_ok) issue_s(t + 1);
     }
-    w_ok = mbar_wait(&sh.tc_s, (ph >> 2) & 1u, a.err);
-    float sc[64];
+    if (w_ok) w_ok = mbar_wait(&sh.tc_s[s2(t)], par2(t), a.err);   // S_t done
+    if (w_ok && t + TC_NS < ntiles) load(t + TC_NS, 0);  // K slot of S_t is free
+    float sc[32];
     float mx = NEG_INF;
-    const int kbase = t * TC_KEYS + col0;
+    const int kbase = t * TC_KEYS + key0;
     if (w_ok) {
       tc_fence_after();
-      tmem_ld32(tS + lane_base + col0, *reinterpret_cast<float(*)[32]>(&sc[0]));
-      tmem_ld32(tS + lane_base + col0 + 32, *reinterpret_cast<float(*)[32]>(&sc[32]));
+      tmem_ld32(tmem + s2(t) * TC_KEYS + lane_base + key0, sc);
       tmem_wait_ld();
-      if (t * TC_KEYS + TC_KEYS - 1 > prefix + t0) {   // diagonal or tail tile: mask
+      if (t * TC_KEYS + TC_KEYS - 1 > prefix + t0) {      // diagonal or tail tile: mask
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
+        for (int i = 0; i < 32; ++i)
           if (kbase + i > lim || kbase + i >= kv_len) sc[i] = NEG_INF;
       }
 #pragma unroll
-      for (int i = 0; i < 64; ++i) mx = fmaxf(mx, sc[i]);
+      for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sc[i]);
       sh.tc_red[half][row] = mx;
     }
     if (__syncthreads_or(!w_ok)) { ok = false; break; }
-    ph ^= 1u << 2;
     mx = fmaxf(sh.tc_red[0][row], sh.tc_red[1][row]) * sl2;   // row max, scaled
     const bool grow = mx > m + RESCALE_LOG2;
     if (__any_sync(0xffffffffu, grow)) {
@@ -758,22 +574,27 @@ __device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const
       const float alpha = exp2f(m - mnew);      // 0 when m was -inf
       l *= alpha;
       m = mnew;
-      if (t > 0) {                              // rescale this thread's half of its O row
+      if (t > 0) {                              // O holds tiles < t: wait for PV_{t-1}
+        w_ok = mbar_wait(&sh.tc_o[s2(t - 1)], par2(t - 1), a.err);
+        tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
           float o[32];
-          tmem_ld32(tO + lane_base + col0 + 32 * c, o);
+          tmem_ld32(tO + lane_base + ocol + 32 * c, o);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tO + lane_base + col0 + 32 * c, o);
+          tmem_st32(tO + lane_base + ocol + 32 * c, o);
         }
         tmem_wait_st();
       }
     }
+    // P slot s2(t) was last read by PV_{t-2}
+    if (t >= 2 && w_ok) w_ok = mbar_wait(&sh.tc_o[s2(t)], par2(t - 2), a.err);
     const float mneg = (m == NEG_INF) ? 0.f : -m;
+    uint8_t* prow = payload + TC_P_OFF + s2(t) * TC_P_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
-    for (int cc = 0; cc < 8; ++cc) {
+    for (int cc = 0; cc < 4; ++cc) {
       float p[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -785,48 +606,55 @@ __device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const
       pk.y = pack_bf16(p[2], p[3]);
       pk.z = pack_bf16(p[4], p[5]);
       pk.w = pack_bf16(p[6], p[7]);
-      *reinterpret_cast<uint4*>(prow + ((cc ^ (row & 7)) << 4)) = pk;
+      const int chunk = 4 * half + cc;          // 16-byte chunk of the row's 128 bytes
+      *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = pk;
     }
     fence_proxy_async();
     tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {                             // O += P V
-      tc_fence_after();
-      const uint32_t vb = sbase + TC_V_OFF + s * TC_KV_BYTES;
-#pragma unroll
-      for (int kk = 0; kk < TC_KEYS / 16; ++kk) {
-        tc_mma_bf16(tO, tc_desc_sw128(sbase + TC_P_OFF + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                    tc_desc_sw128(vb + kk * 2048, 16384, 1024), ID_O, (t > 0 || kk > 0));
-      }
-      tc_commit(&sh.tc_o);
-    }
-    w_ok = mbar_wait(&sh.tc_o, (ph >> 3) & 1u, a.err);
     if (__syncthreads_or(!w_ok)) { ok = false; break; }
-    ph ^= 1u << 3;
-    tc_fence_after();
-    if (tid == 0 && t + 2 < ntiles) issue(s, ids);
+    if (tid == 0) {
+      ok = mbar_wait(&sh.tc_v[kslot(t)], kpar(t), a.err);   // V_t landed
+      if (ok) issue_o(t);
+    }
+    if (t >= 1 && t - 1 + TC_NS < ntiles && lane == 0) {    // V slot of PV_{t-1}
+      if (mbar_wait(&sh.tc_o[s2(t - 1)], par2(t - 1), a.err)) load(t - 1 + TC_NS, 1);
+      else ok = false;
+    }
+    // a failure here reaches the others at the next __syncthreads_or
+  }
+  if (__syncthreads_or(!ok)) ok = false;
+  if (ok) {
+    ok = mbar_wait(&sh.tc_o[s2(ntiles - 1)], par2(ntiles - 1), a.err);   // last PV
+    if (__syncthreads_or(!ok)) ok = false;
   }
   if (!ok) {
-    // let outstanding copies and MMAs land before the caller frees TMEM
+    // let outstanding MMAs land before the caller frees TMEM
     if (tid == 0) {
-      for (int s2 = 0; s2 < 2; ++s2) mbar_wait(&sh.tc_kv[s2], (ph >> s2) & 1u, nullptr);
-      mbar_wait(&sh.tc_s, (ph >> 2) & 1u, nullptr);
-      mbar_wait(&sh.tc_o, (ph >> 3) & 1u, nullptr);
+      for (int t = max(0, ntiles - TC_NS); t < ntiles; ++t) {
+        mbar_wait(&sh.tc_k[kslot(t)], kpar(t), nullptr);
+        mbar_wait(&sh.tc_v[kslot(t)], kpar(t), nullptr);
+      }
+      for (int t = max(0, ntiles - 2); t < ntiles; ++t) {
+        mbar_wait(&sh.tc_s[s2(t)], par2(t), nullptr);
+        mbar_wait(&sh.tc_o[s2(t)], par2(t), nullptr);
+      }
     }
     __syncthreads();
     return false;
   }
+  tc_fence_after();
   sh.tc_red[half][row] = l;                     // epilogue: O / l -> out
   __syncthreads();
   {
     // tcgen05.ld is warp-collective: every lane loads, only real rows store
     const bool store = j < nrows;
     const float inv = 1.f / (sh.tc_red[0][row] + sh.tc_red[1][row]);
-    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM + col0;
+    __nv_bfloat16* op =
+        a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM + ocol;
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
       float o[32];
-      tmem_ld32(tO + lane_base + col0 + 32 * c, o);
+      tmem_ld32(tO + lane_base + ocol + 32 * c, o);
       tmem_wait_ld();
       if (store) {
 #pragma unroll
@@ -856,15 +684,19 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     prefetch_tmap(&kv_map);
     for (int w = 0; w < ATT_WARPS; ++w)
       for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&sh.dec_bar[w][s], 1);
-    for (int s = 0; s < PRE_STAGES; ++s) mbar_init(&sh.pre_bar[s], 1);
-    for (int s = 0; s < 2; ++s) mbar_init(&sh.tc_kv[s], 1);
-    mbar_init(&sh.tc_s, 1);
-    mbar_init(&sh.tc_o, 1);
+    for (int s = 0; s < TC_NS; ++s) {
+      mbar_init(&sh.tc_k[s], 1);
+      mbar_init(&sh.tc_v[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sh.tc_s[s], 1);
+      mbar_init(&sh.tc_o[s], 1);
+    }
     fence_mbar_init();
   }
   const int n_pre = v.header[0], n_dec = v.header[1];
   // TMEM for the tcgen05 prefill tiles (only CTAs that will run one allocate)
-  const bool use_tmem = HY_PREFILL_TC && (int)blockIdx.x < n_pre;
+  const bool use_tmem = (int)blockIdx.x < n_pre;
   if (use_tmem && warp == 0) {
     tmem_alloc(&sh.tmem_base, TC_TMEM_COLS);
     tmem_relinquish();
@@ -874,15 +706,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   tc_fence_after();
   const uint32_t tmem = use_tmem ? sh.tmem_base : 0u;
   const int total = n_pre + (n_dec + ATT_WARPS - 1) / ATT_WARPS;
-  uint32_t dec_phase = 0, pre_phase = 0;
+  uint32_t dec_phase = 0, tile_ctr = 0;
   bool ok = true;
   for (int k = blockIdx.x; k < total && ok; k += gridDim.x) {
     if (k < n_pre) {
-#if HY_PREFILL_TC
-      ok = prefill_tile_tc(&kv_map, a, v, k, payload, sh, tmem, pre_phase);
-#else
-      ok = prefill_tile(&kv_map, a, v, k, payload, sh.pre_bar, pre_phase);
-#endif
+      ok = prefill_tile_tc(&kv_map, a, v, k, payload, sh, tmem, tile_ctr);
     } else {
       const int item = (k - n_pre) * ATT_WARPS + warp;
       if (item < n_dec)

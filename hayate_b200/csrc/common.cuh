@@ -80,6 +80,22 @@ HY_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
   }
 }
 
+// Named barrier over the first `n` threads (ids 1..15; id 0 is __syncthreads).
+HY_DEVICE void named_sync(uint32_t id, uint32_t n) {
+  asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(n) : "memory");
+}
+// Named barrier that also ORs a predicate over its `n` threads.
+HY_DEVICE bool named_sync_or(uint32_t id, uint32_t n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(n) : "memory");
+  return r != 0;
+}
+
 HY_DEVICE void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
