@@ -59,8 +59,10 @@ class Request:
     # engine bookkeeping
     slot: int = -1
     _blocks: int = 0
-    _uploaded: bool = False
     _pinned: Optional[torch.Tensor] = None
+    _pending: int = 0             # sampled tokens launched, not yet read back
+    _inflight: int = 0            # launched steps containing this request, not yet read back
+    _last_launched: bool = False  # the step that samples its last token is launched
 
 
 class ByteTokenizer:
@@ -122,9 +124,12 @@ class Engine:
         self._graphs: Dict[int, torch.cuda.CUDAGraph] = {}
         self._graph_pool = None
         S = self.ecfg.max_num_seqs
-        self._sched_host = torch.zeros(4 * S, dtype=torch.int32).pin_memory()
-        self._out_host = torch.zeros(1 + S, dtype=torch.int32).pin_memory()
-        self._done_event = torch.cuda.Event()
+        # two of each: step n+1 is prepared while step n may still be running
+        self._sched_host = [torch.zeros(4 * S, dtype=torch.int32).pin_memory() for _ in range(2)]
+        self._out_host = [torch.zeros(1 + S, dtype=torch.int32).pin_memory() for _ in range(2)]
+        self._events = [torch.cuda.Event() for _ in range(2)]
+        self._inflight = None          # (plan, buffer index) of the step not yet read back
+        self._step_idx = 0
         self._pad_ready = False
         self.pool: Queue = Queue()
         self.current_batch: List[Request] = []
@@ -158,20 +163,33 @@ class Engine:
         return out.long().unsqueeze(-1)
 
     def generate(self) -> bool:
-        """One continuous-batching step; False when there is nothing to run."""
+        """One continuous-batching step; False when there is nothing to run.
+
+        The engine runs one step ahead of the host: a call launches the next
+        step (its inputs -- tokens sampled by the previous step -- are committed
+        on the device) and then reads back the previous step's tokens, so the
+        host's bookkeeping overlaps the GPU's work.  Requests therefore report
+        completion one call after their last token is sampled."""
         self._drain_pool()
         sch = self.scheduler
         for r in sch.admit():
             self._upload_prompt(r)
-        self.current_batch = list(sch.running)
-        if not sch.running:
-            return False
-        plan = sch.schedule()
-        if plan.num_seqs == 0:
-            return True
-        self._run(plan)
-        self._finish(plan)
-        self.current_batch = list(sch.running)
+        launched = False
+        if sch.running:
+            plan = sch.schedule()
+            if plan.num_seqs:
+                prev = self._inflight
+                self._inflight = self._launch(plan)
+                launched = True
+                if prev is not None:
+                    self._collect(*prev)
+        if not launched:
+            if self._inflight is None:
+                self.current_batch = [r for r in sch.running if not r.is_completed]
+                return bool(sch.running)
+            prev, self._inflight = self._inflight, None
+            self._collect(*prev)
+        self.current_batch = [r for r in sch.running if not r.is_completed]
         return True
 
     def generate_text(self, prompts, max_tokens: int = 100):
@@ -220,18 +238,23 @@ class Engine:
             return
         self._pad_ready = True
         pad = self.scheduler.pad_slot
-        self._write_sched([(pad, 0, 1, SAMPLE)])
+        self._write_sched([(pad, 0, 1, SAMPLE)], self._step_idx & 1)
         self.runner.launch_step(1, 1, 1)
+        torch.cuda.current_stream().synchronize()     # once, before any graph capture
 
-    def _write_sched(self, rows):
+    def _write_sched(self, rows, buf: int = 0):
         S = len(rows)
-        a = self._sched_host.numpy()
+        host = self._sched_host[buf]
+        a = host.numpy()
         for i, (slot, start, q, fl) in enumerate(rows):
             a[i], a[S + i], a[2 * S + i], a[3 * S + i] = slot, start, q, fl
-        self.runner.sched[:4 * S].copy_(self._sched_host[:4 * S], non_blocking=True)
+        self.runner.sched[:4 * S].copy_(host[:4 * S], non_blocking=True)
         self.h2d_bytes += 16 * S
 
-    def _run(self, plan: StepPlan):
+    def _launch(self, plan: StepPlan):
+        """Enqueue one step and the read-back of its tokens; no synchronisation."""
+        buf = self._step_idx & 1
+        self._step_idx += 1
         rows = [(e.req.slot, e.start, e.q_len, e.flags) for e in plan.entries]
         S, T, ns = plan.num_seqs, plan.num_tokens, plan.num_sample
         if self.use_graphs and plan.decode_only:
@@ -239,7 +262,7 @@ class Engine:
             self._ensure_pad_slot()
             pad = self.scheduler.pad_slot
             rows += [(pad, 0, 1, SAMPLE)] * (Sp - S)
-            self._write_sched(rows)
+            self._write_sched(rows, buf)
             g = self._graphs.get(Sp)
             if g is None:
                 g = self._capture(Sp)
@@ -248,17 +271,57 @@ class Engine:
             self.graph_steps += 1
             n_read = Sp
         else:
-            self._write_sched(rows)
+            self._write_sched(rows, buf)
             self.runner.launch_step(S, T, ns)
             n_read = ns
         self.steps += 1
-        self._out_host[:1 + n_read].copy_(self.runner.out_buf[:1 + n_read], non_blocking=True)
+        self._out_host[buf][:1 + n_read].copy_(self.runner.out_buf[:1 + n_read],
+                                                non_blocking=True)
         self.d2h_bytes += 4 * (1 + n_read)
-        self._done_event.record()
-        self._done_event.synchronize()
-        err = int(self._out_host[0])
+        self._events[buf].record()
+        # host state advances at launch: the next schedule builds on this step
+        for e in plan.entries:
+            r = e.req
+            r.cache_pos = e.start + e.q_len
+            r._inflight += 1
+            if e.flags & SAMPLE:
+                r.is_prefill = False
+                r._pending += 1
+                if len(r.tokens) + r._pending >= max(r.max_tokens, 1):
+                    r._last_launched = True
+        return plan, buf
+
+    def _collect(self, plan: StepPlan, buf: int):
+        """Wait for a launched step, then apply its tokens and stop conditions."""
+        self._events[buf].synchronize()
+        toks = self._out_host[buf].numpy()
+        err = int(toks[0])
         if err:
             raise K._lib.HayateError(f"device error word {err}: {K.describe_error(err)}")
+        k = 0
+        for e in plan.entries:
+            r = e.req
+            r._inflight -= 1
+            if e.flags & SAMPLE:
+                tok = int(toks[1 + k])
+                k += 1
+                r._pending -= 1
+                if r.is_completed:
+                    continue                    # stopped at an earlier token (eos)
+                r.tokens.append(tok)
+                if tok == self.eos_token_id or len(r.tokens) >= r.max_tokens:
+                    r.is_completed = True
+                    r._last_launched = True
+                    r.response = self.tokenizer.decode(r.tokens, skip_special_tokens=True)
+        done = [r for r in self.scheduler.running if r.is_completed and r._inflight == 0]
+        if done:
+            for r in done:
+                self.scheduler.release(r)
+                r._pinned = None
+            slots = torch.tensor([r.slot for r in done], dtype=torch.int32).pin_memory()
+            dslots = slots.to(self.device, non_blocking=True)
+            self.runner.free_slots(dslots)
+            self.h2d_bytes += 4 * len(done)
 
     def _capture(self, Sp: int) -> torch.cuda.CUDAGraph:
         r = self.runner
@@ -279,31 +342,6 @@ class Engine:
             r.launch_step(Sp, Sp, Sp)
         self._graphs[Sp] = g
         return g
-
-    def _finish(self, plan: StepPlan):
-        toks = self._out_host.numpy()
-        k = 0
-        done = []
-        for e in plan.entries:
-            r = e.req
-            r.cache_pos = e.start + e.q_len
-            if e.flags & SAMPLE:
-                tok = int(toks[1 + k])
-                k += 1
-                r.is_prefill = False
-                r.tokens.append(tok)
-                if tok == self.eos_token_id or len(r.tokens) >= r.max_tokens:
-                    r.is_completed = True
-                    r.response = self.tokenizer.decode(r.tokens, skip_special_tokens=True)
-                    done.append(r)
-        if done:
-            for r in done:
-                self.scheduler.release(r)
-                r._pinned = None
-            slots = torch.tensor([r.slot for r in done], dtype=torch.int32).pin_memory()
-            dslots = slots.to(self.device, non_blocking=True)
-            self.runner.free_slots(dslots)
-            self.h2d_bytes += 4 * len(done)
 
     # ------------------------------------------------------------------ info
     def check_device_errors(self) -> int:

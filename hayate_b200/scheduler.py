@@ -111,7 +111,7 @@ class Scheduler:
         budget = self.cfg.max_batched_tokens
         plan = StepPlan()
         for r in self.running:                      # decodes first, one token each
-            if not r.is_prefill and not r.is_completed:
+            if not r.is_prefill and not r.is_completed and not r._last_launched:
                 plan.entries.append(StepEntry(r, r.cache_pos, 1, SAMPLE))
                 budget -= 1
         for r in self.running:                      # then prefill chunks, FIFO

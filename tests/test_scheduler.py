@@ -9,7 +9,8 @@ from hayate_b200.scheduler import SAMPLE, Scheduler, graph_bucket, graph_buckets
 
 def req(i, n, max_tokens=4):
     return SimpleNamespace(id=i, prompt_tokens=list(range(n)), max_tokens=max_tokens, slot=-1,
-                           _blocks=0, cache_pos=0, is_prefill=True, is_completed=False)
+                           _blocks=0, cache_pos=0, is_prefill=True, is_completed=False,
+                           _last_launched=False)
 
 
 def test_admission_is_fifo_and_bounded_by_slots_and_blocks():
