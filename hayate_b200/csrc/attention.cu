@@ -21,9 +21,10 @@
 //     ring of K/V block tiles, mma.sync for QK^T and PV, an online softmax;
 //     for a sequence split over several items, the last item to finish (an
 //     atomic count per sequence and KV head) merges the partials.
-// The main kernel is persistent (grid = SMs x resident CTAs) and walks the plan
-// with a static stride, so its launch shape does not depend on the batch and a
-// whole step can be captured in a CUDA graph.
+// The main kernel is persistent (grid = SMs x resident CTAs): prefill tiles are
+// strided over the CTAs, decode items are pulled by warps from a per-layer
+// atomic counter, so its launch shape does not depend on the batch and a whole
+// step can be captured in a CUDA graph.
 #include "common.cuh"
 #include "attention.cuh"
 
@@ -63,6 +64,7 @@ constexpr int SMEM_PAYLOAD = ATT_WARPS * DEC_WARP_BYTES > TC_SMEM ? ATT_WARPS * 
                                                                    : TC_SMEM;
 constexpr int SMEM_BYTES = SMEM_PAYLOAD + 1024;                  // + alignment slack
 constexpr int MIN_SPLIT = 4;                                     // blocks per decode item
+constexpr int ITEMS_PER_WARP = 3;                                // decode items aimed at per warp
 constexpr float NEG_INF = -INFINITY;
 // Lazy rescaling: the running max is only raised when a new score exceeds it
 // by more than 2^RESCALE_LOG2; until then probabilities may exceed 1 by up to
@@ -130,7 +132,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
   }
   atomicAdd(&s_total, part);
   __syncthreads();
-  const long target = 2L * warp_slots;
+  const long target = (long)ITEMS_PER_WARP * warp_slots;
   const long want = ((long)kv_heads * s_total + target - 1) / target;
   const int split = (int)max((long)MIN_SPLIT, want);
 
@@ -164,8 +166,9 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
       } else {
         v.seqinfo[i] = make_int2(d0, ns);
         for (int g = 0; g < kv_heads; ++g) {
-          for (int s = 0; s < ns; ++s)
-            v.dec[d0 + g * ns + s] = make_int4(i, g, s * split, min(nblk, (s + 1) * split));
+          for (int s = 0; s < ns; ++s)             // splits differ by at most one block
+            v.dec[d0 + g * ns + s] = make_int4(i, g, (int)((long)s * nblk / ns),
+                                               (int)((long)(s + 1) * nblk / ns));
           for (int t = 0; t < ntile; ++t)
             v.pre[p0 + g * ntile + t] = make_int4(i, g, t * PRE_QROWS, 0);
         }
@@ -175,6 +178,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
     if (threadIdx.x == 0) { s_cpre += tpre; s_cdec += tdec; }
     __syncthreads();
   }
+  if (threadIdx.x < 128) v.grab[threadIdx.x] = 0;
   if (threadIdx.x == 0) {
     const bool bad = s_bad != 0;
     v.header[0] = bad ? 0 : min(s_cpre, v.max_pre);
@@ -190,6 +194,7 @@ struct MainArgs {
   const __nv_bfloat16* q;
   __nv_bfloat16* out;
   int q_heads, kv_heads;
+  int layer;              // layer index (selects the work counters)
   int layer_row_base;     // first tensor-map row of this layer
   int oob_row;            // a row past the end of the map: loads there read zeros
   int num_blocks;
@@ -705,17 +710,40 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = use_tmem ? sh.tmem_base : 0u;
-  const int total = n_pre + (n_dec + ATT_WARPS - 1) / ATT_WARPS;
   uint32_t dec_phase = 0, tile_ctr = 0;
   bool ok = true;
-  for (int k = blockIdx.x; k < total && ok; k += gridDim.x) {
-    if (k < n_pre) {
-      ok = prefill_tile_tc(&kv_map, a, v, k, payload, sh, tmem, tile_ctr);
-    } else {
-      const int item = (k - n_pre) * ATT_WARPS + warp;
-      if (item < n_dec)
-        ok = decode_item(&kv_map, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
-                         dec_phase);
+  // prefill tiles: CTA-wide, statically strided over the grid (they come first
+  // so that long tiles start early)
+  for (int k = blockIdx.x; k < n_pre && ok; k += gridDim.x)
+    ok = prefill_tile_tc(&kv_map, a, v, k, payload, sh, tmem, tile_ctr);
+  // decode items: each warp takes the next one from this layer's counter, so
+  // warps that finish early keep pulling work.  A launch whose decode items fit
+  // one round of warps (and has no prefill tiles) assigns them statically and
+  // skips the counter's round trips.
+  const int lane = threadIdx.x & 31;
+  const int nw = (int)gridDim.x * ATT_WARPS;
+  if (n_pre == 0 && n_dec <= nw) {
+    const int item = (int)blockIdx.x * ATT_WARPS + warp;
+    if (item < n_dec && ok)
+      ok = decode_item(&kv_map, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
+                       dec_phase);
+  } else {
+    int* grab = v.grab + 2 * (a.layer & 63);
+    while (ok) {
+      int item = 0;
+      if (lane == 0) item = atomicAdd(&grab[0], 1);
+      item = __shfl_sync(0xffffffffu, item, 0);
+      if (item >= n_dec) break;
+      ok = decode_item(&kv_map, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
+                       dec_phase);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {                     // the last CTA out resets the counter pair
+      __threadfence();
+      if (atomicAdd(&grab[1], 1) == (int)gridDim.x - 1) {
+        atomicExch(&grab[0], 0);
+        atomicExch(&grab[1], 0);
+      }
     }
   }
   if (use_tmem) {
@@ -805,7 +833,7 @@ PlanDims hy_attn_plan_dims(int max_seqs, int max_tokens, int kv_heads, int dev) 
   PlanDims d;
   d.max_seqs = max_seqs;
   d.max_pre = kv_heads * (max_tokens / PRE_QROWS + max_seqs);
-  d.max_dec = kv_heads * max_seqs + 2 * hy_attn_warp_slots(dev);
+  d.max_dec = kv_heads * max_seqs + ITEMS_PER_WARP * hy_attn_warp_slots(dev);
   d.kv_heads = kv_heads;
   return d;
 }
@@ -820,6 +848,7 @@ size_t hy_attn_workspace_bytes(const PlanDims& d) {
   off = align256(off + (size_t)d.max_dec * HY_GROUP * HY_HEAD_DIM * sizeof(float));
   off = align256(off + (size_t)d.max_dec * HY_GROUP * sizeof(float2));
   off = align256(off + (size_t)d.max_seqs * d.kv_heads * sizeof(int));
+  off = align256(off + 128 * sizeof(int));
   return off;
 }
 
@@ -840,6 +869,8 @@ static PlanView make_view(void* ws, const PlanDims& d) {
   v.part_ml = reinterpret_cast<float2*>(p + off);
   off = align256(off + (size_t)d.max_dec * HY_GROUP * sizeof(float2));
   v.counters = reinterpret_cast<int*>(p + off);
+  off = align256(off + (size_t)d.max_seqs * d.kv_heads * sizeof(int));
+  v.grab = reinterpret_cast<int*>(p + off);
   v.max_pre = d.max_pre;
   v.max_dec = d.max_dec;
   v.max_seqs = d.max_seqs;
@@ -877,6 +908,7 @@ cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* q, void* out
   a.q_heads = q_heads;
   a.kv_heads = kv_heads;
   a.layer_row_base = layer_row_base;
+  a.layer = layer_row_base / (num_blocks * 2 * kv_heads * HY_BLOCK);
   a.oob_row = oob_row;
   a.num_blocks = num_blocks;
   a.block_tables = block_tables;

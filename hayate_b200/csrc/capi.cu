@@ -118,6 +118,17 @@ int current_device() {
 
 }  // namespace
 
+// Waits on an mbarrier that nothing arrives on: the bounded wait must give up,
+// set HY_ERR_TIMEOUT in the error word and let the kernel return.
+__global__ void wait_timeout_probe_kernel(int32_t* err, uint64_t timeout_ns, int32_t* done) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) mbar_init(&bar, 1);
+  fence_mbar_init();
+  __syncthreads();
+  const bool ok = mbar_wait(&bar, 0u, err, timeout_ns);
+  if (threadIdx.x == 0) *done = ok ? 2 : 1;
+}
+
 // Shared with other translation units of the library (not part of the C ABI).
 int hy_attention_kv_map(int dev, const void* base, long rows, CUtensorMap* out) {
   return kv_map_for(dev, base, rows, out);
@@ -317,6 +328,14 @@ int hy_silu_mul(int32_t dtype, const void* gu, int64_t ld, int32_t rows, int32_t
     return fail(HY_E_INVALID, "hy_silu_mul: rows must be 16-byte aligned vectors");
   return cuda_result(hy_launch_silu_mul(dtype, gu, (long)ld, rows, inter, y, (long)ldy,
                                         as_stream(stream)), "hy_silu_mul");
+}
+
+int hy_selftest_wait_timeout(int32_t* err, int32_t timeout_ms, int32_t* done, void* stream) {
+  if (!err || !done || timeout_ms <= 0 || timeout_ms > 10000)
+    return fail(HY_E_INVALID, "hy_selftest_wait_timeout: bad argument (timeout 1..10000 ms)");
+  wait_timeout_probe_kernel<<<1, 32, 0, as_stream(stream)>>>(err, (uint64_t)timeout_ms * 1000000ull,
+                                                             done);
+  return cuda_result(cudaGetLastError(), "hy_selftest_wait_timeout");
 }
 
 int hy_argmax(int32_t dtype, const void* logits, int64_t ld, int32_t rows, int32_t vocab,

@@ -67,13 +67,14 @@ HY_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // ~timeout_ns of wall time: sets HY_ERR_TIMEOUT and returns false.
 constexpr uint64_t HY_WAIT_TIMEOUT_NS = 2000000000ull;   // 2 s
 
-HY_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
+HY_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err,
+                         uint64_t timeout_ns = HY_WAIT_TIMEOUT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = hy_globaltimer();
   uint32_t n = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++n & 63) == 0 && hy_globaltimer() - t0 > HY_WAIT_TIMEOUT_NS) {
+    if ((++n & 63) == 0 && hy_globaltimer() - t0 > timeout_ns) {
       hy_flag(err, HY_ERR_TIMEOUT);
       return false;
     }

@@ -183,6 +183,15 @@ int hy_silu_mul(int32_t dtype, const void* gu, int64_t ld, int32_t rows, int32_t
 int hy_argmax(int32_t dtype, const void* logits, int64_t ld, int32_t rows, int32_t vocab,
               int32_t* out, void* stream);
 
+/* ------------------------------------------------------------- diagnostics */
+
+/* Failure-detection self-test (no reference counterpart: the reference has no
+ * device waits).  Launches one CTA that waits on an mbarrier nothing arrives
+ * on, with a limit of timeout_ms; the wait gives up, ORs HY_DEV_TIMEOUT into
+ * *err and the kernel returns, writing *done = 1 (2 if the wait had succeeded).
+ * The kernels' own waits use the same bounded wait (limit 2 s). */
+int hy_selftest_wait_timeout(int32_t* err, int32_t timeout_ms, int32_t* done, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -304,3 +304,22 @@ def test_silu_mul_vs_reference(dt):
         assert d.max().item() <= 1 and (d > 0).float().mean().item() < 0.01
     else:
         torch.testing.assert_close(got, want, rtol=1e-6, atol=1e-6)
+
+
+# ------------------------------------------------------- bounded device waits
+def test_bounded_wait_gives_up_and_reports():
+    """A wait nothing completes ends after its limit with HY_DEV_TIMEOUT set; the
+    context stays usable (a kernel runs correctly right after)."""
+    from hayate_b200 import _lib
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    done = torch.zeros(1, dtype=torch.int32, device=dev)
+    rc = _lib.load().hy_selftest_wait_timeout(err.data_ptr(), 50, done.data_ptr(),
+                                              torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(done.item()) == 1
+    assert int(err.item()) & K.DEV_TIMEOUT
+    x = torch.randn(3, 1000, device=dev)
+    out = torch.empty(3, dtype=torch.int32, device=dev)
+    K.argmax(x, out)
+    assert torch.equal(out, torch.argmax(x, -1).int())
