@@ -14,17 +14,19 @@
 //
 // Work is planned on the device (plan_kernel) once per step and reused by every
 // layer:
-//   * prefill items -- (seq, kv_head, 32-token tile): one CTA; the 4 query heads
-//     of the group x 32 tokens form one M=128 tcgen05 tile (accumulators in
-//     TMEM), K/V tiles of 64 keys staged by TMA in 4-slot rings;
+//   * prefill items -- (seq, kv_head, 64-token tile): one CTA, warp-specialised:
+//     two M=128 tcgen05 tiles (two query heads x 64 tokens each) share every
+//     64-key K/V tile a load warp stages by TMA in 4-slot rings; an MMA warp
+//     issues S = Q K^T and O += P V with S, P and O in TMEM; two softmax
+//     warpgroups run one thread per query row;
 //   * decode items  -- (seq, kv_head, block range): one warp with its own TMA
 //     ring of K/V block tiles, mma.sync for QK^T and PV, an online softmax;
 //     for a sequence split over several items, the last item to finish (an
 //     atomic count per sequence and KV head) merges the partials.
-// The main kernel is persistent (grid = SMs x resident CTAs): prefill tiles are
-// strided over the CTAs, decode items are pulled by warps from a per-layer
-// atomic counter, so its launch shape does not depend on the batch and a whole
-// step can be captured in a CUDA graph.
+// The main kernel is persistent (grid = SMs x resident CTAs): CTAs pull prefill
+// items (heaviest first) and then decode items (per warp) from per-layer atomic
+// counters, so its launch shape does not depend on the batch and a whole step
+// can be captured in a CUDA graph.
 #include "common.cuh"
 #include "attention.cuh"
 
@@ -38,33 +40,34 @@ namespace {
 #ifndef HY_DEC_STAGES
 #define HY_DEC_STAGES 3
 #endif
-constexpr int ATT_WARPS = HY_ATT_WARPS;                          // 8
-constexpr int ATT_THREADS = ATT_WARPS * 32;
+constexpr int ATT_WARPS = HY_ATT_WARPS;                          // 8 decode / softmax warps
+constexpr int TC_MMA_WARP = ATT_WARPS;                           // prefill: tcgen05 issue
+constexpr int TC_LOAD_WARP = ATT_WARPS + 1;                      // prefill: TMA issue
+constexpr int ATT_THREADS = (ATT_WARPS + 2) * 32;                // 320
 constexpr int DEC_STAGES = HY_DEC_STAGES;                        // TMA ring per decode warp
 constexpr int DEC_TILE_BYTES = 2 * HY_BLOCK * HY_HEAD_DIM * 2;   // K+V of one block: 8 KB
-constexpr int DEC_WARP_BYTES = DEC_STAGES * DEC_TILE_BYTES;      // 32 KB
-constexpr int PRE_QROWS = 32;                                    // query tokens per prefill item
-// tcgen05 prefill tile: M = 128 query rows (4 heads x 32 tokens, head-major so
-// warp w owns TMEM lane quarter w % 4), KV tiles of 64 keys (4 blocks) in rings
-// of TC_NS slots, so each K/V load has TC_NS - 1 tiles of lead.
+constexpr int DEC_WARP_BYTES = DEC_STAGES * DEC_TILE_BYTES;      // 24 KB
+constexpr int PRE_QROWS = 64;                                    // query tokens per prefill item
+// tcgen05 prefill: sub-tile X (0, 1) = 128 rows r: query head 4g + 2X + r / 64,
+// token t0 + r % 64; KV tiles of 64 keys (4 blocks) in rings of TC_NS slots.
 constexpr int TC_KEYS = 64;
 constexpr int TC_NS = 4;                                         // K and V ring slots
 constexpr int TC_KV_BYTES = TC_KEYS * HY_HEAD_DIM * 2;          // K or V of one tile: 16 KB
 constexpr int TC_HALF = TC_KEYS * 128;                           // one 64-column half: 8 KB
-constexpr int TC_P_BYTES = 128 * TC_KEYS * 2;                    // P of one tile: 16 KB
-constexpr int TC_Q_OFF = 0;                                      // Q: 32 KB
-constexpr int TC_K_OFF = 32768;                                  // K ring
+constexpr int TC_Q_BYTES = 128 * HY_HEAD_DIM * 2;                // Q of one sub-tile: 32 KB
+constexpr int TC_K_OFF = 2 * TC_Q_BYTES;                         // K ring
 constexpr int TC_V_OFF = TC_K_OFF + TC_NS * TC_KV_BYTES;         // V ring
-constexpr int TC_P_OFF = TC_V_OFF + TC_NS * TC_KV_BYTES;         // P: 2 slots
-constexpr int TC_IDS_OFF = TC_P_OFF + 2 * TC_P_BYTES;            // block ids of the item
-constexpr int TC_MAX_IDS = 40960 / HY_BLOCK;                     // positions / block
-constexpr int TC_SMEM = TC_IDS_OFF + TC_MAX_IDS * 4;             // 202 KB
-constexpr uint32_t TC_TMEM_COLS = 256;                           // S: 2 x 64, O: 128
+constexpr int TC_SMEM = TC_V_OFF + TC_NS * TC_KV_BYTES;          // 192 KB
+// TMEM columns: S_X at 64 X, O_X at 128 + 128 X, P_X (bf16 pairs) at 384 + 32 X
+constexpr uint32_t TC_TMEM_COLS = 512;
+constexpr uint32_t TM_S = 0, TM_O = 128, TM_P = 384;
 constexpr int SMEM_PAYLOAD = ATT_WARPS * DEC_WARP_BYTES > TC_SMEM ? ATT_WARPS * DEC_WARP_BYTES
                                                                    : TC_SMEM;
 constexpr int SMEM_BYTES = SMEM_PAYLOAD + 1024;                  // + alignment slack
 constexpr int MIN_SPLIT = 4;                                     // blocks per decode item
 constexpr int ITEMS_PER_WARP = 3;                                // decode items aimed at per warp
+constexpr int GRAB_INTS = 4;                                     // per layer: decode item, CTAs
+                                                                 // done, prefill item, spare
 constexpr float NEG_INF = -INFINITY;
 // Lazy rescaling: the running max is only raised when a new score exceeds it
 // by more than 2^RESCALE_LOG2; until then probabilities may exceed 1 by up to
@@ -74,13 +77,19 @@ constexpr float RESCALE_LOG2 = 8.0f;
 
 struct Shared {
   uint64_t dec_bar[ATT_WARPS][DEC_STAGES];
-  // tcgen05 prefill; K/V by ring slot, S/O by (tile counter & 1):
-  uint64_t tc_k[TC_NS];      // K tile landed (TMA transaction bytes)
-  uint64_t tc_v[TC_NS];      // V tile landed
-  uint64_t tc_s[2];          // S = Q K^T complete (tcgen05.commit)
-  uint64_t tc_o[2];          // O += P V complete (tcgen05.commit)
+  // tcgen05 prefill.  Ring barriers complete once per use of their slot, the
+  // per-sub-tile ones once per key tile.
+  uint64_t tc_kfull[TC_NS];  // K tile landed (TMA transaction bytes)
+  uint64_t tc_vfull[TC_NS];  // V tile landed
+  uint64_t tc_kfree[TC_NS];  // both S MMAs that read the K slot are done
+  uint64_t tc_vfree[TC_NS];  // both PV MMAs that read the V slot are done
+  uint64_t tc_sfull[2];      // S_X = Q_X K^T complete
+  uint64_t tc_sfree[2];      // S_X read out by the 4 softmax warps of X
+  uint64_t tc_pfull[2];      // P_X written to TMEM by the 4 softmax warps of X
+  uint64_t tc_odone[2];      // O_X += P_X V complete
+  uint64_t tc_drain;         // error path: all issued MMAs complete
   uint32_t tmem_base;        // TMEM columns from tcgen05.alloc
-  float tc_red[2][128];      // per-row partials of the two column halves
+  int pre_item;              // prefill item handed to this CTA
 };
 
 HY_DEVICE uint8_t* payload_base(uint8_t* dyn) {
@@ -117,6 +126,12 @@ __device__ int plan_scan(int v, int* ws, int& total) {
   return before + x - v;
 }
 
+// a * b / c for non-negative ints, in 32-bit arithmetic when the product fits
+HY_DEVICE int mul_div(int a, int b, int c) {
+  const long long p = (long long)a * b;
+  return p <= 0x7fffffffLL ? (int)((unsigned)p / (unsigned)c) : (int)(p / c);
+}
+
 __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
     const int32_t* __restrict__ cu_q, const int32_t* __restrict__ seq_lens_k, int S,
     int kv_heads, int warp_slots, PlanView v, int32_t* err) {
@@ -130,7 +145,9 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
     const int q = cu_q[i + 1] - cu_q[i];
     if (q == 1) part += (seq_lens_k[i] + HY_BLOCK - 1) / HY_BLOCK;
   }
-  atomicAdd(&s_total, part);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if ((threadIdx.x & 31) == 0) atomicAdd(&s_total, part);   // 32 shared atomics, not 1024
   __syncthreads();
   const long target = (long)ITEMS_PER_WARP * warp_slots;
   const long want = ((long)kv_heads * s_total + target - 1) / target;
@@ -159,26 +176,44 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
     const int cpre = s_cpre, cdec = s_cdec;
     if (i < S && i < v.max_seqs)
       for (int g = 0; g < kv_heads; ++g) v.counters[i * kv_heads + g] = 0;
+    bool wr = false;
+    int p0 = 0, d0 = 0;
     if (i < S) {
-      const int p0 = cpre + opre, d0 = cdec + odec;
+      p0 = cpre + opre;
+      d0 = cdec + odec;
       if (p0 + npre > v.max_pre || d0 + ndec > v.max_dec || i >= v.max_seqs) {
         atomicOr(&s_bad, HY_ERR_PLAN);
       } else {
         v.seqinfo[i] = make_int2(d0, ns);
-        for (int g = 0; g < kv_heads; ++g) {
-          for (int s = 0; s < ns; ++s)             // splits differ by at most one block
-            v.dec[d0 + g * ns + s] = make_int4(i, g, (int)((long)s * nblk / ns),
-                                               (int)((long)(s + 1) * nblk / ns));
-          for (int t = 0; t < ntile; ++t)
-            v.pre[p0 + g * ntile + t] = make_int4(i, g, t * PRE_QROWS, 0);
-        }
+        wr = true;
+      }
+    }
+    // The warp writes the items of its sequences together, one sequence at a
+    // time (item k of a sequence: head k / n, split or tile k % n).
+    const int lane = threadIdx.x & 31;
+    unsigned todo = __ballot_sync(0xffffffffu, wr);
+    while (todo) {
+      const int j = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const int ji = __shfl_sync(0xffffffffu, i, j);
+      const int jp0 = __shfl_sync(0xffffffffu, p0, j), jd0 = __shfl_sync(0xffffffffu, d0, j);
+      const int jns = __shfl_sync(0xffffffffu, ns, j), jnb = __shfl_sync(0xffffffffu, nblk, j);
+      const int jnt = __shfl_sync(0xffffffffu, ntile, j);
+      for (int k = lane; k < kv_heads * jns; k += 32) {   // splits differ by at most one block
+        const int g = k / jns, sp = k - g * jns;
+        const int lo = mul_div(sp, jnb, jns), hi = mul_div(sp + 1, jnb, jns);
+        v.dec[jd0 + k] = make_int4(ji, g, lo, hi);
+      }
+      for (int k = lane; k < kv_heads * jnt; k += 32) {
+        const int g = k / jnt, t = k - g * jnt;
+        v.pre[jp0 + k] = make_int4(ji, g, t * PRE_QROWS, 0);
       }
     }
     __syncthreads();
     if (threadIdx.x == 0) { s_cpre += tpre; s_cdec += tdec; }
     __syncthreads();
   }
-  if (threadIdx.x < 128) v.grab[threadIdx.x] = 0;
+  if (threadIdx.x < 64 * GRAB_INTS) v.grab[threadIdx.x] = 0;
   if (threadIdx.x == 0) {
     const bool bad = s_bad != 0;
     v.header[0] = bad ? 0 : min(s_cpre, v.max_pre);
@@ -432,20 +467,26 @@ __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const Pla
   return true;
 }
 
-// ------------------------------------------------------------------ prefill tile
-// tcgen05, CTA-wide.  Rows r = 32*h + j of the 128-row tile are query head 4g+h,
-// token t0+j; two threads own each row (half = which 32 of a tile's 64 keys, and
-// which 64 columns of the output).  KV tile t = 64 keys (4 paged blocks), global
-// tile counter c = c0 + t: K/V ring slot c % TC_NS, S/P slot c & 1.
-//   start of t : thread 0 issues S_{t+1} = Q K_{t+1}^T (tcgen05.mma, runs during
-//                softmax(t)); once S_t is complete the warps refill its K slot
-//                with K_{t+TC_NS} (each warp issues one of the 8 TMA boxes);
-//   softmax(t) : S_t from TMEM, causal mask, online softmax with lazy rescaling
-//                of O in TMEM, P_t (bf16) into smem (128B-swizzled, K-major);
-//   end of t   : thread 0 issues O += P_t V_t (runs during softmax(t+1)); the warps
-//                refill the V slot PV_{t-1} freed with V_{t-1+TC_NS}.
-// Each K/V load has TC_NS - 1 tiles of lead; O stays in TMEM (columns 128..255).
-__device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
+// ------------------------------------------------------------------ prefill item
+// tcgen05, warp-specialised.  Item = (seq, kv head g, 64-token tile t0): two
+// M=128 sub-tiles X of the same tokens (query heads 4g+2X, 4g+2X+1), which see
+// the same keys and masks, so each 64-key K/V tile is loaded once for both.
+//   warps 0-3 / 4-7  softmax of sub-tile 0 / 1: thread = row = TMEM lane, so a
+//                    row's max and sum stay in one thread.  Per key tile: S_X
+//                    from TMEM, causal mask, online softmax with lazy rescaling
+//                    of O_X, P_X (bf16 pairs) back into TMEM;
+//   warp 8, lane 0   issues S_X(t) = Q_X K_t^T for both X, then
+//                    O_X += P_X(t-1) V_{t-1} (A operand read from TMEM), each
+//                    followed by tcgen05.commit to the barrier its consumer waits on;
+//   warp 9, lane 0   loads K_t and V_t (8 TMA boxes each: 4 paged blocks x two
+//                    64-column halves) into ring slot c % TC_NS once the MMAs of
+//                    the slot's previous use are done.
+// c = c0 + t counts key tiles over all items of the launch; every barrier
+// completes exactly once per tile (sub-tile barriers) or per use of its slot
+// (ring barriers), so a wait is always on the current or the previous phase.
+// Returns false if a wait ran out; the roles then drain their own asynchronous
+// work before the item ends.
+__device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
                                 int item, uint8_t* payload, Shared& sh, uint32_t tmem,
                                 uint32_t& ctr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -458,225 +499,229 @@ __device__ bool prefill_tile_tc(const CUtensorMap* map, const MainArgs& a, const
   const int nrows = min(PRE_QROWS, q_len - t0);
   const int kv_end = prefix + t0 + nrows;
   const int ntiles = (kv_end + TC_KEYS - 1) / TC_KEYS;
-  const int nblk = min((kv_end + HY_BLOCK - 1) / HY_BLOCK, TC_MAX_IDS);
-  const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
-  const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
+  const int nblk = (kv_end + HY_BLOCK - 1) / HY_BLOCK;
   const uint32_t sbase = smem_u32(payload);
-  int32_t* sids = reinterpret_cast<int32_t*>(payload + TC_IDS_OFF);
   const uint32_t c0 = ctr;
   ctr += ntiles;
-  auto kslot = [&](int t) { return (c0 + (uint32_t)t) % TC_NS; };
-  auto kpar = [&](int t) { return ((c0 + (uint32_t)t) / TC_NS) & 1u; };
-  auto s2 = [&](int t) { return (c0 + (uint32_t)t) & 1u; };
-  auto par2 = [&](int t) { return ((c0 + (uint32_t)t) >> 1) & 1u; };
+  bool ok = true;
 
-  __syncthreads();                              // previous users of smem / TMEM are done
-  for (int i = tid; i < nblk; i += ATT_THREADS) sids[i] = bt[i];
-  const int row = tid & 127, half = tid >> 7, h = row >> 5, j = row & 31;
-  {                                             // Q tile -> smem (swizzled, K-major)
+  if (warp < ATT_WARPS) {                       // Q rows -> smem (128B-swizzled, K-major)
+    const int X = warp >> 2, r = (warp & 3) * 32 + lane;
+    const int h = 2 * X + (r >> 6), j = r & 63;
     const bool valid = j < nrows;
     const uint4* qp = reinterpret_cast<const uint4*>(
-        a.q + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM) + 8 * half;
-    uint8_t* qrow = payload + TC_Q_OFF + half * 16384 + (row >> 3) * 1024 + (row & 7) * 128;
+        a.q + ((size_t)(row0 + t0 + (valid ? j : 0)) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM);
+    uint8_t* qrow = payload + X * TC_Q_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < 16; ++c) {
       const uint4 val = valid ? qp[c] : make_uint4(0u, 0u, 0u, 0u);
-      *reinterpret_cast<uint4*>(qrow + ((c ^ (row & 7)) << 4)) = val;
+      *reinterpret_cast<uint4*>(qrow + (c >> 3) * (TC_Q_BYTES / 2) + (((c & 7) ^ (r & 7)) << 4)) = val;
     }
+    fence_proxy_async();                        // generic smem writes -> async proxy
   }
-  fence_proxy_async();                          // generic smem writes -> async proxy
   __syncthreads();
 
-  // Load K (kv = 0) or V (kv = 1) of tile t into its ring slot.  Called by
-  // every warp: lane 0 of warp w issues box w (block w / 2, column half w % 2),
-  // so no warp carries the whole issue cost; thread 0 posts the byte count.
-  constexpr int TB = TC_KEYS / HY_BLOCK;
-  static_assert(2 * TB == ATT_WARPS, "one TMA box per warp");
-  auto load = [&](int t, int kv) {
-    const uint32_t b = kslot(t);
-    uint64_t* bar = kv ? &sh.tc_v[b] : &sh.tc_k[b];
-    if (tid == 0) mbar_arrive_expect_tx(bar, TC_KV_BYTES);
-    if (lane == 0) {
-      const int jb = warp >> 1, hf = warp & 1;
-      const int blk = t * TB + jb;
-      const int id = blk < nblk ? sids[blk] : -1;
-      int r = a.oob_row;                        // past the end: zero fill
-      if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
-      else if (id >= 0) r = kv_row(a, id, kv, g);
-      tma_load_2d(payload + (kv ? TC_V_OFF : TC_K_OFF) + b * TC_KV_BYTES + hf * TC_HALF + jb * 2048,
-                  map, 64 * hf, r, bar);
-    }
-  };
-
-  constexpr uint32_t ID_S = tc_idesc_bf16(128, TC_KEYS, false);
-  constexpr uint32_t ID_O = tc_idesc_bf16(128, HY_HEAD_DIM, true);
-  const uint32_t tO = tmem + 2 * TC_KEYS;
-  const uint64_t dQ = tc_desc_sw128(sbase + TC_Q_OFF, 16, 1024);
-  auto issue_s = [&](int t) {                   // S_t = Q K_t^T into TMEM slot
-    const uint64_t dK = tc_desc_sw128(sbase + TC_K_OFF + kslot(t) * TC_KV_BYTES, 16, 1024);
-    const uint32_t d = tmem + s2(t) * TC_KEYS;
-    tc_fence_after();
-#pragma unroll
-    for (int kk = 0; kk < HY_HEAD_DIM / 16; ++kk)
-      tc_mma_bf16(d, dQ + (uint64_t)((((kk >> 2) * 16384) + (kk & 3) * 32) >> 4),
-                  dK + (uint64_t)((((kk >> 2) * TC_HALF) + (kk & 3) * 32) >> 4), ID_S, kk > 0);
-    tc_commit(&sh.tc_s[s2(t)]);
-  };
-  auto issue_o = [&](int t) {                   // O += P_t V_t
-    const uint64_t dP = tc_desc_sw128(sbase + TC_P_OFF + s2(t) * TC_P_BYTES, 16, 1024);
-    const uint64_t dV = tc_desc_sw128(sbase + TC_V_OFF + kslot(t) * TC_KV_BYTES, TC_HALF, 1024);
-    tc_fence_after();
-#pragma unroll
-    for (int kk = 0; kk < TC_KEYS / 16; ++kk)
-      tc_mma_bf16(tO, dP + (uint64_t)((kk * 32) >> 4), dV + (uint64_t)((kk * 2048) >> 4), ID_O,
-                  (t > 0 || kk > 0));
-    tc_commit(&sh.tc_o[s2(t)]);
-  };
-
-  bool ok = true;
-  for (int t = 0; t < TC_NS && t < ntiles; ++t) { load(t, 0); load(t, 1); }
-  if (tid == 0) {
-    ok = mbar_wait(&sh.tc_k[kslot(0)], kpar(0), a.err);
-    if (ok) issue_s(0);
-  }
-  if (__syncthreads_or(!ok)) ok = false;
-
-  const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-  const int key0 = 32 * half;                   // this thread's keys within a tile
-  const uint32_t ocol = 64 * half;              // this thread's output columns
-  const int lim = prefix + t0 + j;              // last key row j may see
-  const float sl2 = a.scale_log2;
-  float m = NEG_INF, l = 0.f;                   // m in scaled log2 units
-  for (int t = 0; t < ntiles && ok; ++t) {
-    bool w_ok = true;
-    if (tid == 0 && t + 1 < ntiles) {           // S_{t+1} runs during softmax(t)
-      w_ok = mbar_wait(&sh.tc_k[kslot(t + 1)], kpar(t + 1), a.err);
-      if (w_ok) issue_s(t + 1);
-    }
-    if (w_ok) w_ok = mbar_wait(&sh.tc_s[s2(t)], par2(t), a.err);   // S_t done
-    if (w_ok && t + TC_NS < ntiles) load(t + TC_NS, 0);  // K slot of S_t is free
-    float sc[32];
-    float mx = NEG_INF;
-    const int kbase = t * TC_KEYS + key0;
-    if (w_ok) {
-      tc_fence_after();
-      tmem_ld32(tmem + s2(t) * TC_KEYS + lane_base + key0, sc);
-      tmem_wait_ld();
-      if (t * TC_KEYS + TC_KEYS - 1 > prefix + t0) {      // diagonal or tail tile: mask
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (kbase + i > lim || kbase + i >= kv_len) sc[i] = NEG_INF;
+  if (warp == TC_LOAD_WARP) {
+    const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
+    const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
+    int ids = -1;                               // lane i: block 32 (t / 8) + i of the sequence
+    int issued = 0;
+    for (int t = 0; t < ntiles && ok; ++t) {
+      if ((t & 7) == 0) {
+        const int b = 4 * t + lane;
+        ids = (b < nblk && b < a.bt_pitch) ? bt[b] : -1;
       }
+      int id[4];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sc[i]);
-      sh.tc_red[half][row] = mx;
-    }
-    if (__syncthreads_or(!w_ok)) { ok = false; break; }
-    mx = fmaxf(sh.tc_red[0][row], sh.tc_red[1][row]) * sl2;   // row max, scaled
-    const bool grow = mx > m + RESCALE_LOG2;
-    if (__any_sync(0xffffffffu, grow)) {
-      const float mnew = grow ? mx : m;
-      const float alpha = exp2f(m - mnew);      // 0 when m was -inf
-      l *= alpha;
-      m = mnew;
-      if (t > 0) {                              // O holds tiles < t: wait for PV_{t-1}
-        w_ok = mbar_wait(&sh.tc_o[s2(t - 1)], par2(t - 1), a.err);
-        tc_fence_after();
+      for (int jb = 0; jb < 4; ++jb) id[jb] = __shfl_sync(0xffffffffu, ids, (4 * t + jb) & 31);
+      if (lane == 0) {
+        const uint32_t c = c0 + t, slot = c % TC_NS, use = c / TC_NS;
 #pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float o[32];
-          tmem_ld32(tO + lane_base + ocol + 32 * c, o);
-          tmem_wait_ld();
+        for (int kv = 0; kv < 2 && ok; ++kv) {
+          if (!mbar_wait(kv ? &sh.tc_vfree[slot] : &sh.tc_kfree[slot], (use & 1) ^ 1, a.err)) {
+            ok = false;
+            break;
+          }
+          uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
+          mbar_arrive_expect_tx(full, TC_KV_BYTES);
+          uint8_t* dst = payload + (kv ? TC_V_OFF : TC_K_OFF) + slot * TC_KV_BYTES;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tO + lane_base + ocol + 32 * c, o);
+          for (int jb = 0; jb < 4; ++jb) {
+            int r = a.oob_row;                  // past the end: zero fill
+            if (id[jb] >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
+            else if (id[jb] >= 0) r = kv_row(a, id[jb], kv, g);
+            tma_load_2d(dst + jb * 2048, map, 0, r, full);
+            tma_load_2d(dst + TC_HALF + jb * 2048, map, 64, r, full);
+          }
         }
-        tmem_wait_st();
+        if (ok) issued = t + 1;
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    }
+    if (!ok && lane == 0) {                     // loads still in flight must land first
+      for (int t = max(0, issued - TC_NS); t < issued; ++t) {
+        const uint32_t c = c0 + t;
+        mbar_wait(&sh.tc_kfull[c % TC_NS], (c / TC_NS) & 1, nullptr);
+        mbar_wait(&sh.tc_vfull[c % TC_NS], (c / TC_NS) & 1, nullptr);
       }
     }
-    // P slot s2(t) was last read by PV_{t-2}
-    if (t >= 2 && w_ok) w_ok = mbar_wait(&sh.tc_o[s2(t)], par2(t - 2), a.err);
-    const float mneg = (m == NEG_INF) ? 0.f : -m;
-    uint8_t* prow = payload + TC_P_OFF + s2(t) * TC_P_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-    for (int cc = 0; cc < 4; ++cc) {
-      float p[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        p[e] = exp2f(fmaf(sc[8 * cc + e], sl2, mneg));
-        l += p[e];
-      }
-      uint4 pk;
-      pk.x = pack_bf16(p[0], p[1]);
-      pk.y = pack_bf16(p[2], p[3]);
-      pk.z = pack_bf16(p[4], p[5]);
-      pk.w = pack_bf16(p[6], p[7]);
-      const int chunk = 4 * half + cc;          // 16-byte chunk of the row's 128 bytes
-      *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = pk;
-    }
-    fence_proxy_async();
-    tc_fence_before();
-    if (__syncthreads_or(!w_ok)) { ok = false; break; }
-    if (tid == 0) {
-      ok = mbar_wait(&sh.tc_v[kslot(t)], kpar(t), a.err);   // V_t landed
-      if (ok) issue_o(t);
-    }
-    if (t >= 1 && t - 1 + TC_NS < ntiles && lane == 0) {    // V slot of PV_{t-1}
-      if (mbar_wait(&sh.tc_o[s2(t - 1)], par2(t - 1), a.err)) load(t - 1 + TC_NS, 1);
-      else ok = false;
-    }
-    // a failure here reaches the others at the next __syncthreads_or
-  }
-  if (__syncthreads_or(!ok)) ok = false;
-  if (ok) {
-    ok = mbar_wait(&sh.tc_o[s2(ntiles - 1)], par2(ntiles - 1), a.err);   // last PV
-    if (__syncthreads_or(!ok)) ok = false;
-  }
-  if (!ok) {
-    // let outstanding MMAs land before the caller frees TMEM
-    if (tid == 0) {
-      for (int t = max(0, ntiles - TC_NS); t < ntiles; ++t) {
-        mbar_wait(&sh.tc_k[kslot(t)], kpar(t), nullptr);
-        mbar_wait(&sh.tc_v[kslot(t)], kpar(t), nullptr);
-      }
-      for (int t = max(0, ntiles - 2); t < ntiles; ++t) {
-        mbar_wait(&sh.tc_s[s2(t)], par2(t), nullptr);
-        mbar_wait(&sh.tc_o[s2(t)], par2(t), nullptr);
-      }
-    }
-    __syncthreads();
-    return false;
-  }
-  tc_fence_after();
-  sh.tc_red[half][row] = l;                     // epilogue: O / l -> out
-  __syncthreads();
-  {
-    // tcgen05.ld is warp-collective: every lane loads, only real rows store
-    const bool store = j < nrows;
-    const float inv = 1.f / (sh.tc_red[0][row] + sh.tc_red[1][row]);
-    __nv_bfloat16* op =
-        a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM + ocol;
+  } else if (warp == TC_MMA_WARP) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = tc_idesc_bf16(128, TC_KEYS, false);
+      constexpr uint32_t ID_O = tc_idesc_bf16(128, HY_HEAD_DIM, true);
+      for (int t = 0; t <= ntiles && ok; ++t) {
+        if (t < ntiles) {                       // S_X(t) = Q_X K_t^T
+          const uint32_t c = c0 + t, slot = c % TC_NS;
+          ok = mbar_wait(&sh.tc_kfull[slot], (c / TC_NS) & 1, a.err);
+          const uint64_t dK = tc_desc_sw128(sbase + TC_K_OFF + slot * TC_KV_BYTES, 16, 1024);
 #pragma unroll 1
-    for (int c = 0; c < 2; ++c) {
-      float o[32];
-      tmem_ld32(tO + lane_base + ocol + 32 * c, o);
-      tmem_wait_ld();
-      if (store) {
+          for (int X = 0; X < 2 && ok; ++X) {
+            ok = mbar_wait(&sh.tc_sfree[X], (c & 1) ^ 1, a.err);   // S_X(t-1) read out
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t dQ = tc_desc_sw128(sbase + X * TC_Q_BYTES, 16, 1024);
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint4 pk;
-          pk.x = pack_bf16(o[8 * q4 + 0] * inv, o[8 * q4 + 1] * inv);
-          pk.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
-          pk.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
-          pk.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
-          *reinterpret_cast<uint4*>(op + 32 * c + 8 * q4) = pk;
+            for (int kk = 0; kk < HY_HEAD_DIM / 16; ++kk)
+              tc_mma_bf16(tmem + TM_S + 64 * X,
+                          dQ + (uint64_t)((((kk >> 2) * (TC_Q_BYTES / 2)) + (kk & 3) * 32) >> 4),
+                          dK + (uint64_t)((((kk >> 2) * TC_HALF) + (kk & 3) * 32) >> 4), ID_S,
+                          kk > 0);
+            tc_commit(&sh.tc_sfull[X]);
+          }
+          if (!ok) break;
+          tc_commit(&sh.tc_kfree[slot]);
+        }
+        if (t > 0) {                            // O_X += P_X(t-1) V_{t-1}
+          const uint32_t c = c0 + t - 1, slot = c % TC_NS;
+          ok = mbar_wait(&sh.tc_vfull[slot], (c / TC_NS) & 1, a.err);
+          const uint64_t dV = tc_desc_sw128(sbase + TC_V_OFF + slot * TC_KV_BYTES, TC_HALF, 1024);
+#pragma unroll 1
+          for (int X = 0; X < 2 && ok; ++X) {
+            ok = mbar_wait(&sh.tc_pfull[X], c & 1, a.err);
+            if (!ok) break;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < TC_KEYS / 16; ++kk)
+              tc_mma_bf16_ta(tmem + TM_O + 128 * X, tmem + TM_P + 32 * X + 8 * kk,
+                             dV + (uint64_t)((kk * 2048) >> 4), ID_O, (t > 1 || kk > 0));
+            tc_commit(&sh.tc_odone[X]);
+          }
+          if (!ok) break;
+          tc_commit(&sh.tc_vfree[slot]);
+        }
+      }
+      if (!ok) {                                // let every issued MMA finish
+        tc_commit(&sh.tc_drain);
+        mbar_wait(&sh.tc_drain, 0, nullptr);
+      }
+    }
+    __syncwarp();
+  } else {                                      // softmax warpgroups
+    const int X = warp >> 2, r = (warp & 3) * 32 + lane, j = r & 63;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_base + TM_S + 64 * X;
+    const uint32_t tO = tmem + lane_base + TM_O + 128 * X;
+    const uint32_t tP = tmem + lane_base + TM_P + 32 * X;
+    const int lim = prefix + t0 + j;            // last key row r may see
+    const float sl2 = a.scale_log2;
+    float m = NEG_INF, l = 0.f;                 // m in scaled log2 units
+    for (int t = 0; t < ntiles && ok; ++t) {
+      const uint32_t c = c0 + t;
+      // waits are made warp-uniform: tcgen05.ld/st below are warp-collective
+      ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_sfull[X], c & 1, a.err));
+      if (!ok) break;
+      tc_fence_after();
+      float s[64];
+      tmem_ld32(tS, *reinterpret_cast<float(*)[32]>(&s[0]));
+      tmem_ld32(tS + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.tc_sfree[X]);
+      const int kb = t * TC_KEYS;
+      if (kb + TC_KEYS - 1 > prefix + t0) {     // the tile reaches the diagonal or the end
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (kb + i > lim || kb + i >= kv_len) s[i] = NEG_INF;
+      }
+      float mx = NEG_INF;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) mx = fmaxf(mx, s[i]);
+      mx *= sl2;
+      const bool grow = mx > m + RESCALE_LOG2;
+      bool odone = false;                       // O_X += P_X V of tile t-1 is complete
+      if (__any_sync(0xffffffffu, grow)) {
+        const float mnew = grow ? mx : m;
+        const float alpha = exp2f(m - mnew);    // 0 when m was -inf
+        l *= alpha;
+        m = mnew;
+        if (t > 0) {                            // O holds tiles < t
+          ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_odone[X], (c & 1) ^ 1, a.err));
+          odone = true;
+          tc_fence_after();
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {
+            float o[32];
+            tmem_ld32(tO + 32 * cc, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(tO + 32 * cc, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      const float mneg = (m == NEG_INF) ? 0.f : -m;
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float p0 = exp2f(fmaf(s[2 * i], sl2, mneg));
+        const float p1 = exp2f(fmaf(s[2 * i + 1], sl2, mneg));
+        l += p0;
+        l += p1;
+        pk[i] = pack_bf16(p0, p1);
+      }
+      if (!odone) {                             // P_X is free once PV of tile t-1 is done
+        ok = __all_sync(0xffffffffu, ok && mbar_wait(&sh.tc_odone[X], (c & 1) ^ 1, a.err));
+        tc_fence_after();
+      }
+      tmem_st32u(tP, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.tc_pfull[X]);
+    }
+    if (ok) {                                   // epilogue: O_X / l -> out
+      const uint32_t c = c0 + ntiles - 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_odone[X], c & 1, a.err));
+      tc_fence_after();
+      // tcgen05.ld is warp-collective: every lane loads, only real rows store
+      const bool store = ok && j < nrows;
+      const float inv = 1.f / l;
+      __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + 2 * X +
+                                   (r >> 6)) * HY_HEAD_DIM;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        float o[32];
+        tmem_ld32(tO + 32 * cc, o);
+        tmem_wait_ld();
+        if (store) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint4 pk4;
+            pk4.x = pack_bf16(o[8 * q4 + 0] * inv, o[8 * q4 + 1] * inv);
+            pk4.y = pack_bf16(o[8 * q4 + 2] * inv, o[8 * q4 + 3] * inv);
+            pk4.z = pack_bf16(o[8 * q4 + 4] * inv, o[8 * q4 + 5] * inv);
+            pk4.w = pack_bf16(o[8 * q4 + 6] * inv, o[8 * q4 + 7] * inv);
+            *reinterpret_cast<uint4*>(op + 32 * cc + 8 * q4) = pk4;
+          }
         }
       }
     }
   }
   tc_fence_before();
-  __syncthreads();
-  return true;
+  if (__syncthreads_or(!ok)) ok = false;
+  return ok;
 }
 
 __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
@@ -690,17 +735,23 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     for (int w = 0; w < ATT_WARPS; ++w)
       for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&sh.dec_bar[w][s], 1);
     for (int s = 0; s < TC_NS; ++s) {
-      mbar_init(&sh.tc_k[s], 1);
-      mbar_init(&sh.tc_v[s], 1);
+      mbar_init(&sh.tc_kfull[s], 1);
+      mbar_init(&sh.tc_vfull[s], 1);
+      mbar_init(&sh.tc_kfree[s], 1);
+      mbar_init(&sh.tc_vfree[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&sh.tc_s[s], 1);
-      mbar_init(&sh.tc_o[s], 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&sh.tc_sfull[x], 1);
+      mbar_init(&sh.tc_sfree[x], 4);            // one arrival per softmax warp
+      mbar_init(&sh.tc_pfull[x], 4);
+      mbar_init(&sh.tc_odone[x], 1);
     }
+    mbar_init(&sh.tc_drain, 1);
     fence_mbar_init();
   }
   const int n_pre = v.header[0], n_dec = v.header[1];
-  // TMEM for the tcgen05 prefill tiles (only CTAs that will run one allocate)
+  // TMEM for the tcgen05 prefill items: only the first n_pre CTAs take prefill
+  // items, and only they allocate
   const bool use_tmem = (int)blockIdx.x < n_pre;
   if (use_tmem && warp == 0) {
     tmem_alloc(&sh.tmem_base, TC_TMEM_COLS);
@@ -712,24 +763,32 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   const uint32_t tmem = use_tmem ? sh.tmem_base : 0u;
   uint32_t dec_phase = 0, tile_ctr = 0;
   bool ok = true;
-  // prefill tiles: CTA-wide, statically strided over the grid (they come first
-  // so that long tiles start early)
-  for (int k = blockIdx.x; k < n_pre && ok; k += gridDim.x)
-    ok = prefill_tile_tc(&kv_map, a, v, k, payload, sh, tmem, tile_ctr);
-  // decode items: each warp takes the next one from this layer's counter, so
-  // warps that finish early keep pulling work.  A launch whose decode items fit
-  // one round of warps (and has no prefill tiles) assigns them statically and
-  // skips the counter's round trips.
+  int* grab = v.grab + GRAB_INTS * (a.layer & 63);
+  // prefill items: CTA-wide, heaviest first (within a sequence later tiles see
+  // more keys; sequences with longer prefixes come later in a batch)
+  if (use_tmem) {
+    while (ok) {
+      if (threadIdx.x == 0) sh.pre_item = atomicAdd(&grab[2], 1);
+      __syncthreads();
+      const int k = sh.pre_item;
+      __syncthreads();                          // read before thread 0 writes the next one
+      if (k >= n_pre) break;
+      ok = prefill_item_tc(&kv_map, a, v, n_pre - 1 - k, payload, sh, tmem, tile_ctr);
+    }
+  }
+  // decode items (warps 0..ATT_WARPS-1): each warp takes the next one from this
+  // layer's counter, so warps that finish early keep pulling work.  A launch
+  // whose decode items fit one round of warps (and has no prefill items)
+  // assigns them statically and skips the counters' round trips.
   const int lane = threadIdx.x & 31;
   const int nw = (int)gridDim.x * ATT_WARPS;
   if (n_pre == 0 && n_dec <= nw) {
     const int item = (int)blockIdx.x * ATT_WARPS + warp;
-    if (item < n_dec && ok)
+    if (warp < ATT_WARPS && item < n_dec && ok)
       ok = decode_item(&kv_map, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
                        dec_phase);
   } else {
-    int* grab = v.grab + 2 * (a.layer & 63);
-    while (ok) {
+    while (ok && warp < ATT_WARPS) {
       int item = 0;
       if (lane == 0) item = atomicAdd(&grab[0], 1);
       item = __shfl_sync(0xffffffffu, item, 0);
@@ -738,10 +797,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
                        dec_phase);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {                     // the last CTA out resets the counter pair
+    if (threadIdx.x == 0) {                     // the last CTA out resets the counters
       __threadfence();
       if (atomicAdd(&grab[1], 1) == (int)gridDim.x - 1) {
         atomicExch(&grab[0], 0);
+        atomicExch(&grab[2], 0);
         atomicExch(&grab[1], 0);
       }
     }
@@ -848,7 +908,7 @@ size_t hy_attn_workspace_bytes(const PlanDims& d) {
   off = align256(off + (size_t)d.max_dec * HY_GROUP * HY_HEAD_DIM * sizeof(float));
   off = align256(off + (size_t)d.max_dec * HY_GROUP * sizeof(float2));
   off = align256(off + (size_t)d.max_seqs * d.kv_heads * sizeof(int));
-  off = align256(off + 128 * sizeof(int));
+  off = align256(off + 64 * GRAB_INTS * sizeof(int));
   return off;
 }
 

@@ -23,7 +23,7 @@ struct PlanView {
   float* part_o;      // [max_dec][4][128]
   float2* part_ml;    // [max_dec][4]  (running max in log2 units, sum)
   int* counters;      // [max_seqs][kv_heads] finished split items (zeroed by the plan)
-  int* grab;          // [64] per layer: next decode item to hand out, then CTAs done
+  int* grab;          // [64][4] per layer: next decode item, CTAs done, next prefill item
   int max_pre, max_dec, max_seqs;
 };
 

@@ -194,6 +194,8 @@ int hy_commit_tokens(const int32_t* next_tokens, int32_t n_sample, const int32_t
                      "hy_commit_tokens");
 }
 
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 int hy_qk_norm_rope(int32_t dtype, const void* qkv, int64_t ld, int32_t num_tokens,
                     int32_t q_heads, int32_t kv_heads, const int32_t* positions,
                     const void* q_norm_w, const void* k_norm_w, const float* rope_cos,
@@ -210,6 +212,10 @@ int hy_qk_norm_rope(int32_t dtype, const void* qkv, int64_t ld, int32_t num_toke
     return fail(HY_E_INVALID, "hy_qk_norm_rope: ld smaller than one qkv row");
   if (kv_cache_layer && (!slot_mapping || num_blocks <= 0))
     return fail(HY_E_INVALID, "hy_qk_norm_rope: cache given without slot_mapping/num_blocks");
+  if (!aligned16(qkv) || ld % (dtype == 0 ? 8 : 4) != 0 || !aligned16(q_norm_w) ||
+      !aligned16(k_norm_w) || !aligned16(rope_cos) || !aligned16(rope_sin) || !aligned16(q_out) ||
+      !aligned16(k_out) || !aligned16(kv_cache_layer))
+    return fail(HY_E_INVALID, "hy_qk_norm_rope: rows and tables must be 16-byte aligned");
   return cuda_result(
       hy_launch_qk_norm_rope(dtype, qkv, (int)ld, num_tokens, q_heads, kv_heads, positions,
                              q_norm_w, k_norm_w, rope_cos, rope_sin, max_pos, eps, q_out, k_out,
@@ -225,6 +231,8 @@ int hy_kv_append(int32_t dtype, const void* k, const void* v, int32_t num_tokens
   if (!k || !v || !slot_mapping || !kv_cache_layer || num_tokens < 0 || kv_heads <= 0 ||
       num_blocks <= 0)
     return fail(HY_E_INVALID, "hy_kv_append: bad argument");
+  if (!aligned16(k) || !aligned16(v) || !aligned16(kv_cache_layer))
+    return fail(HY_E_INVALID, "hy_kv_append: k, v and the cache must be 16-byte aligned");
   return cuda_result(hy_launch_kv_append(dtype, k, v, num_tokens, kv_heads, slot_mapping,
                                          kv_cache_layer, num_blocks, err, as_stream(stream)),
                      "hy_kv_append");

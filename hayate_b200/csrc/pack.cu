@@ -20,6 +20,7 @@
 namespace {
 
 constexpr int PACK_THREADS = 1024;
+constexpr int PACK_SMEM_SEQS = 4096;          // sequences whose offsets fit in shared memory
 
 // Exclusive scan over one CTA of PACK_THREADS threads; returns the prefix for
 // this thread and writes the CTA total to `total`.
@@ -60,6 +61,7 @@ __global__ void __launch_bounds__(PACK_THREADS) pack_kernel(
     int32_t* __restrict__ sample_seq, int32_t* err) {
   __shared__ int warp_sums[32];
   __shared__ int s_top0, s_carry_q, s_carry_n, s_carry_s, s_bad;
+  __shared__ int s_cu[PACK_SMEM_SEQS + 1];      // cu_seqlens_q, for token -> sequence
   const int32_t* s_slot = sched;
   const int32_t* s_start = sched + S;
   const int32_t* s_qlen = sched + 2 * S;
@@ -101,6 +103,7 @@ __global__ void __launch_bounds__(PACK_THREADS) pack_kernel(
     const int cq = s_carry_q, cn = s_carry_n, cs = s_carry_s;
     if (live) {
       cu_q[i] = cq + oq;
+      if (S <= PACK_SMEM_SEQS) s_cu[i] = cq + oq;
       seq_lens_k[i] = start + q;
       for (int j = 0; j < need; ++j) {
         const int k = cn + on + j;          // k-th pop of this step
@@ -121,28 +124,50 @@ __global__ void __launch_bounds__(PACK_THREADS) pack_kernel(
   }
   if (threadIdx.x == 0) {
     cu_q[S] = s_carry_q;
+    if (S <= PACK_SMEM_SEQS) s_cu[S] = s_carry_q;
     if (s_carry_q != T) s_bad |= 1;
     if (s_carry_n > top0) s_bad |= 4;
     *free_top = max(0, top0 - s_carry_n);
   }
   __syncthreads();
 
-  // Phase B: per-token rows, one warp per sequence.
+  // Phase B: per-token rows.  With the sequences' row offsets staged in shared
+  // memory a thread takes a token and finds its sequence by binary search, so
+  // all of the step's token loads are independent; batches of more than
+  // PACK_SMEM_SEQS sequences take one warp per sequence instead.
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int i = warp; i < S; i += PACK_THREADS / 32) {
-    const int slot = s_slot[i], start = s_start[i];
-    const int q = cu_q[i + 1] - cu_q[i];
-    const int row0 = cu_q[i];
-    if (slot < 0 || slot >= max_reqs) continue;
-    const int32_t* toks = req_tokens + (size_t)slot * tok_pitch;
-    const int32_t* bt = block_tables + (size_t)slot * bt_pitch;
-    for (int j = lane; j < q; j += 32) {
-      const int pos = start + j;
-      const int r = row0 + j;
-      if (r >= T) { atomicOr(&s_bad, 1); continue; }
-      input_ids[r] = toks[pos];
+  if (S <= PACK_SMEM_SEQS) {
+    for (int r = threadIdx.x; r < T; r += PACK_THREADS) {
+      if (r >= s_cu[S]) { atomicOr(&s_bad, 1); continue; }
+      int lo = 0, hi = S;                       // last i with s_cu[i] <= r
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_cu[mid] <= r) lo = mid; else hi = mid;
+      }
+      const int slot = s_slot[lo];
+      if (slot < 0 || slot >= max_reqs) continue;
+      const int pos = s_start[lo] + (r - s_cu[lo]);
+      input_ids[r] = req_tokens[(size_t)slot * tok_pitch + pos];
       positions[r] = pos;
-      slot_mapping[r] = bt[pos / HY_BLOCK] * HY_BLOCK + (pos % HY_BLOCK);
+      slot_mapping[r] = block_tables[(size_t)slot * bt_pitch + pos / HY_BLOCK] * HY_BLOCK +
+                        (pos % HY_BLOCK);
+    }
+  } else {
+    for (int i = warp; i < S; i += PACK_THREADS / 32) {
+      const int slot = s_slot[i], start = s_start[i];
+      const int q = cu_q[i + 1] - cu_q[i];
+      const int row0 = cu_q[i];
+      if (slot < 0 || slot >= max_reqs) continue;
+      const int32_t* toks = req_tokens + (size_t)slot * tok_pitch;
+      const int32_t* bt = block_tables + (size_t)slot * bt_pitch;
+      for (int j = lane; j < q; j += 32) {
+        const int pos = start + j;
+        const int r = row0 + j;
+        if (r >= T) { atomicOr(&s_bad, 1); continue; }
+        input_ids[r] = toks[pos];
+        positions[r] = pos;
+        slot_mapping[r] = bt[pos / HY_BLOCK] * HY_BLOCK + (pos % HY_BLOCK);
+      }
     }
   }
   __syncthreads();

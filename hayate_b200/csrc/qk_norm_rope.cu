@@ -119,30 +119,172 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   }
 }
 
-// Plain KV append: k, v are [T][kv_heads][128]; one warp moves one head row.
+// bf16 path of the same operation, laid out for bandwidth: a head row (128
+// elements, 256 bytes) is one 16-byte vector per lane of a half-warp, so every
+// load and store is a full 16-byte access and a warp moves two rows at once.
+// Work unit = (token, pass of 16 head rows): a CTA's 16 half-warps take one
+// pass each, so a batch of T tokens spreads over T x ceil(heads / 16) CTAs (a
+// decode step of a few tokens still fills many SMs); with more units than CTAs
+// each CTA walks units QNR_UNROLL at a time, their loads issued together.  The
+// RoPE partner of element d (d +- 64) sits 8 lanes away and comes over a
+// shuffle.  Rounding points and the order of the products are those of the
+// kernel above; only the order of the sum of squares differs (8 in-lane terms,
+// then a 16-lane butterfly).
+constexpr int QNR_THREADS = 256;
+constexpr int QNR_GROUPS = QNR_THREADS / 16;        // head rows per unit
+constexpr int QNR_UNROLL = 2;                       // units in flight per CTA
+
+HY_DEVICE void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+HY_DEVICE uint4 f32_to_bf16x8(const float (&f)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return u;
+}
+
+__global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int ld, int T_tokens, int q_heads, int kv_heads,
+    const int32_t* __restrict__ positions, const __nv_bfloat16* __restrict__ q_w,
+    const __nv_bfloat16* __restrict__ k_w, const float* __restrict__ rope_cos,
+    const float* __restrict__ rope_sin, int max_pos, float eps, __nv_bfloat16* __restrict__ q_out,
+    __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ cache,
+    const int32_t* __restrict__ slot_mapping, int num_blocks, int32_t* err) {
+  using B = __nv_bfloat16;
+  const int grp = threadIdx.x >> 4, l = threadIdx.x & 15;
+  const int heads = q_heads + 2 * kv_heads;
+  const int npass = (heads + QNR_GROUPS - 1) / QNR_GROUPS;
+  const long units = (long)T_tokens * npass;
+  const int d0 = l * 8;                    // this lane's 8 elements of a row
+  const int c0 = (l & 7) * 8;              // ... and their RoPE table columns
+  const bool upper = l >= 8;               // elements 64..127: partner is d - 64
+  for (long u0 = blockIdx.x; u0 < units; u0 += (long)gridDim.x * QNR_UNROLL) {
+    int tok[QNR_UNROLL], hh[QNR_UNROLL];
+    uint4 raw[QNR_UNROLL];
+#pragma unroll
+    for (int u = 0; u < QNR_UNROLL; ++u) {           // the rows' loads first
+      const long unit = u0 + (long)u * gridDim.x;
+      const bool uv = unit < units;
+      tok[u] = uv ? (int)(unit / npass) : -1;
+      hh[u] = uv ? (int)(unit % npass) * QNR_GROUPS + grp : heads;
+      raw[u] = hh[u] < heads ? *reinterpret_cast<const uint4*>(
+                                   qkv + (size_t)tok[u] * ld + (size_t)hh[u] * HY_HEAD_DIM + d0)
+                             : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < QNR_UNROLL; ++u) {
+      const int t = tok[u], h = hh[u];
+      const bool valid = h < heads;                  // uniform over the warp's half-warps
+      if (t < 0) continue;                           // uniform over the CTA
+      int pos = positions[t];
+      if (pos < 0 || pos >= max_pos) { hy_flag(err, HY_ERR_BOUNDS); pos = 0; }
+      int slot = -1;
+      if (cache != nullptr && valid && h >= q_heads) {
+        slot = slot_mapping[t];
+        if (slot >= (long)num_blocks * HY_BLOCK) { hy_flag(err, HY_ERR_BOUNDS); slot = -1; }
+      }
+      if (valid && h >= q_heads + kv_heads) {        // value head: cache copy only
+        if (slot >= 0)
+          *reinterpret_cast<uint4*>(cache_ptr(cache, slot, 1, h - q_heads - kv_heads, kv_heads) + d0) = raw[u];
+      }
+      float cs[8], sn[8];
+      {
+        const float4* cp = reinterpret_cast<const float4*>(rope_cos + (size_t)pos * 64 + c0);
+        const float4* sp = reinterpret_cast<const float4*>(rope_sin + (size_t)pos * 64 + c0);
+        const float4 a = cp[0], b = cp[1], e = sp[0], f = sp[1];
+        cs[0] = a.x; cs[1] = a.y; cs[2] = a.z; cs[3] = a.w; cs[4] = b.x; cs[5] = b.y; cs[6] = b.z; cs[7] = b.w;
+        sn[0] = e.x; sn[1] = e.y; sn[2] = e.z; sn[3] = e.w; sn[4] = f.x; sn[5] = f.y; sn[6] = f.z; sn[7] = f.w;
+      }
+      // every lane of the warp takes part in the shuffles below
+      float x[8];
+      bf16x8_to_f32(raw[u], x);
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      // mean = ss / 128 exactly (a power of two)
+      const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / HY_HEAD_DIM), eps)));
+      float w[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(((h < q_heads) ? q_w : k_w) + d0), w);
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        y[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], rstd), w[e])));
+      const uint4 yb = f32_to_bf16x8(y);          // exact: y is already bf16-valued
+      uint4 pb;
+      pb.x = __shfl_xor_sync(0xffffffffu, yb.x, 8);
+      pb.y = __shfl_xor_sync(0xffffffffu, yb.y, 8);
+      pb.z = __shfl_xor_sync(0xffffffffu, yb.z, 8);
+      pb.w = __shfl_xor_sync(0xffffffffu, yb.w, 8);
+      float p[8];
+      bf16x8_to_f32(pb, p);
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {               // lower: y*cos + (-y[d+64])*sin; upper: y*cos + y[d-64]*sin
+        const float pe = upper ? p[e] : -p[e];
+        o[e] = __fadd_rn(__fmul_rn(y[e], cs[e]), __fmul_rn(pe, sn[e]));
+      }
+      if (!valid || h >= q_heads + kv_heads) continue;
+      const uint4 ob = f32_to_bf16x8(o);
+      if (h < q_heads) {
+        if (q_out) *reinterpret_cast<uint4*>(q_out + ((size_t)t * q_heads + h) * HY_HEAD_DIM + d0) = ob;
+      } else {
+        const int kh = h - q_heads;
+        if (k_out) *reinterpret_cast<uint4*>(k_out + ((size_t)t * kv_heads + kh) * HY_HEAD_DIM + d0) = ob;
+        if (slot >= 0) *reinterpret_cast<uint4*>(cache_ptr(cache, slot, 0, kh, kv_heads) + d0) = ob;
+      }
+    }
+  }
+}
+
+// Plain KV append: k, v are [T][kv_heads][128].  A head row is one 16-byte
+// vector per lane of a lane group (16 lanes for bf16, 32 for fp32); item
+// i = token * 2 * kv_heads + row (K rows, then V rows); KVA_UNROLL items'
+// loads are in flight per lane before the stores.
+constexpr int KVA_THREADS = 256;
+constexpr int KVA_UNROLL = 4;
+
 template <typename T>
-__global__ void __launch_bounds__(256) kv_append_kernel(
+__global__ void __launch_bounds__(KVA_THREADS) kv_append_kernel(
     const T* __restrict__ k, const T* __restrict__ v, int T_tokens, int kv_heads,
     const int32_t* __restrict__ slot_mapping, T* __restrict__ cache, int num_blocks,
     int32_t* err) {
-  const int lane = threadIdx.x & 31;
-  const long total = (long)T_tokens * kv_heads * 2;
-  const long nwarps = (long)gridDim.x * (blockDim.x >> 5);
-  constexpr int PER_LANE = HY_HEAD_DIM / 32;       // 4 elements
-  for (long w = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += nwarps) {
-    const int kv = (int)(w & 1);
-    const long th = w >> 1;
-    const int t = (int)(th / kv_heads), h = (int)(th % kv_heads);
-    const int slot = slot_mapping[t];
-    if (slot < 0) continue;
-    if (slot >= (long)num_blocks * HY_BLOCK) { hy_flag(err, HY_ERR_BOUNDS); continue; }
-    const T* src = (kv ? v : k) + ((size_t)t * kv_heads + h) * HY_HEAD_DIM + lane * PER_LANE;
-    T* dst = cache_ptr(cache, slot, kv, h, kv_heads) + lane * PER_LANE;
-    if constexpr (sizeof(T) == 2) {
-      *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(src);
-    } else {
-      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+  constexpr int E = 16 / (int)sizeof(T);           // elements per lane
+  constexpr int LPR = HY_HEAD_DIM / E;             // lanes per row
+  constexpr int G = KVA_THREADS / LPR;             // rows per CTA pass
+  const int grp = threadIdx.x / LPR, l = threadIdx.x % LPR;
+  const int R = 2 * kv_heads;
+  const long total = (long)T_tokens * R;
+  const long stride = (long)gridDim.x * G;
+  for (long base = (long)blockIdx.x * G + grp; base < total; base += stride * KVA_UNROLL) {
+    uint4 val[KVA_UNROLL];
+    T* dst[KVA_UNROLL];
+#pragma unroll
+    for (int u = 0; u < KVA_UNROLL; ++u) {
+      const long i = base + u * stride;
+      dst[u] = nullptr;
+      if (i < total) {                            // the row's load does not wait for its slot
+        const int t = (int)(i / R), r = (int)(i % R);
+        const int kv = r >= kv_heads, h = kv ? r - kv_heads : r;
+        val[u] = *reinterpret_cast<const uint4*>((kv ? v : k) + ((size_t)t * kv_heads + h) * HY_HEAD_DIM + l * E);
+        const int slot = slot_mapping[t];
+        if (slot >= (long)num_blocks * HY_BLOCK) hy_flag(err, HY_ERR_BOUNDS);
+        else if (slot >= 0) dst[u] = cache_ptr(cache, slot, kv, h, kv_heads) + l * E;
+      }
     }
+#pragma unroll
+    for (int u = 0; u < KVA_UNROLL; ++u)
+      if (dst[u] != nullptr) *reinterpret_cast<uint4*>(dst[u]) = val[u];
   }
 }
 
@@ -161,14 +303,16 @@ cudaError_t hy_launch_qk_norm_rope(int dtype, const void* qkv, int ld, int T, in
                                    const int32_t* slot_mapping, int num_blocks, int32_t* err,
                                    cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
-  const int grid = grid_for((long)T * (q_heads + 2 * kv_heads));
   if (dtype == 0) {
     using B = __nv_bfloat16;
-    qk_norm_rope_kernel<B><<<grid, 256, 0, st>>>(
+    const long units = (long)T * ((q_heads + 2 * kv_heads + QNR_GROUPS - 1) / QNR_GROUPS);
+    const int grid = (int)(units < 148L * 8 ? units : 148L * 8);   // up to 8 CTAs per SM
+    qk_norm_rope_bf16_kernel<<<grid, QNR_THREADS, 0, st>>>(
         (const B*)qkv, ld, T, q_heads, kv_heads, positions, (const B*)q_w, (const B*)k_w,
         rope_cos, rope_sin, max_pos, eps, (B*)q_out, (B*)k_out, (B*)cache, slot_mapping,
         num_blocks, err);
   } else {
+    const int grid = grid_for((long)T * (q_heads + 2 * kv_heads));
     qk_norm_rope_kernel<float><<<grid, 256, 0, st>>>(
         (const float*)qkv, ld, T, q_heads, kv_heads, positions, (const float*)q_w,
         (const float*)k_w, rope_cos, rope_sin, max_pos, eps, (float*)q_out, (float*)k_out,
@@ -181,13 +325,16 @@ cudaError_t hy_launch_kv_append(int dtype, const void* k, const void* v, int T, 
                                 const int32_t* slot_mapping, void* cache, int num_blocks,
                                 int32_t* err, cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
-  const int grid = grid_for((long)T * kv_heads * 2);
+  const long rows = (long)T * kv_heads * 2;
+  const int per_cta = KVA_THREADS / (HY_HEAD_DIM / (dtype == 0 ? 8 : 4));
+  long blocks = (rows + (long)per_cta * KVA_UNROLL - 1) / ((long)per_cta * KVA_UNROLL);
+  const int grid = (int)(blocks < 148L * 8 ? (blocks > 0 ? blocks : 1) : 148L * 8);
   if (dtype == 0) {
     using B = __nv_bfloat16;
-    kv_append_kernel<B><<<grid, 256, 0, st>>>((const B*)k, (const B*)v, T, kv_heads,
+    kv_append_kernel<B><<<grid, KVA_THREADS, 0, st>>>((const B*)k, (const B*)v, T, kv_heads,
                                               slot_mapping, (B*)cache, num_blocks, err);
   } else {
-    kv_append_kernel<float><<<grid, 256, 0, st>>>((const float*)k, (const float*)v, T, kv_heads,
+    kv_append_kernel<float><<<grid, KVA_THREADS, 0, st>>>((const float*)k, (const float*)v, T, kv_heads,
                                                   slot_mapping, (float*)cache, num_blocks, err);
   }
   return cudaGetLastError();

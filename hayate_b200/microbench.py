@@ -1,12 +1,22 @@
-"""Operator microbenchmark of the varlen paged attention kernel.
+"""Operator microbenchmarks of the hot-path kernels.
 
-The ragged attention case: 256 decode sequences with contexts log-uniform in
-[256,16384] plus 4 prefill chunks of 512 query tokens (prior contexts 0, 512,
-1536, 3584), 32 query / 8 KV heads, head_dim 128, bf16 Q/K/V ~ N(0,1), paged KV
-in 16-token blocks behind a randomly permuted block table, one layer.  The KV
-of this case (~4 GB) is far larger than L2, so launches need no L2 flush.
+attention: the ragged attention case -- 256 decode sequences with contexts
+log-uniform in [256,16384] plus 4 prefill chunks of 512 query tokens (prior
+contexts 0, 512, 1536, 3584), 32 query / 8 KV heads, head_dim 128, bf16 Q/K/V
+~ N(0,1), paged KV in 16-token blocks behind a randomly permuted block table,
+one layer.  Its KV (~4 GB) is far larger than L2, so launches need no flush.
 
-``python -m hayate_b200.microbench [--iters N]`` prints one JSON line.
+qk_norm_rope / kv_append / pack / argmax: the same batch (2304 query tokens:
+256 decode rows + 4 x 512 prefill rows) through the fused QK-norm+RoPE+append
+kernel, the standalone KV append, the packing kernel and the greedy argmax over
+the 256+4 sampled rows (vocab 151936).  These inputs fit in L2, so each timed
+launch is preceded by an L2 flush (a 256 MiB write outside the timed window).
+``--tokens`` raises the token count of the append kernels (prefill-sized
+batches).  Every op reports its algorithmic bytes; packing is latency-bound,
+so its microseconds are the figure of merit.
+
+``python -m hayate_b200.microbench [--op attention|qk_norm_rope|kv_append|pack|argmax|all]
+[--iters N]`` prints one JSON line per op.
 """
 from __future__ import annotations
 
@@ -77,17 +87,211 @@ def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True):
             "decode_seqs": len(w.decode_ctx), "prefill_chunks": len(w.prefill_prior)}
 
 
+L2_FLUSH_BYTES = 256 << 20
+
+
+def _time(launch, iters: int, flush: bool):
+    """CUDA-event time of each launch (ms), after 3 warm-up launches; an L2
+    flush precedes every timed launch when ``flush``."""
+    buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda") if flush else None
+    for _ in range(3):
+        launch()
+    torch.cuda.synchronize()
+    ms = []
+    for _ in range(iters):
+        if buf is not None:
+            buf.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        launch()
+        b.record()
+        b.synchronize()
+        ms.append(a.elapsed_time(b))
+    return ms
+
+
+def _summary(op, ms, nbytes, **extra):
+    mean = statistics.mean(ms)
+    out = {"op": op, "ms_mean": mean, "ms_min": min(ms), "us_mean": mean * 1e3,
+           "bytes": nbytes, "gbs": nbytes / (mean * 1e-3) / 1e9, "iters": len(ms)}
+    out.update(extra)
+    return out
+
+
+def _batch_rows(n_decode: int, tokens: int):
+    """(prior contexts, q_lens) of the operator batch: decode rows of the
+    attention case, then prefill chunks of 512 up to ``tokens`` query tokens."""
+    from hayate_b200.workloads import attn_micro
+    w = attn_micro(seed=0, n_decode=n_decode)
+    prior = list(w.decode_ctx)
+    q = [1] * len(prior)
+    pre = [0, 512, 1536, 3584]
+    k = 0
+    while sum(q) + 512 <= tokens:
+        prior.append(pre[k % 4] + 4096 * (k // 4))
+        q.append(512)
+        k += 1
+    return prior, q
+
+
+def append_micro(iters: int = 20, n_decode: int = 256, tokens: int = 2304, fused: bool = True):
+    """Fused QK-RMSNorm + RoPE + paged KV append (``fused``) or the standalone
+    KV append, over the tokens of the operator batch."""
+    from hayate_b200 import kernels as K
+    prior, q_lens = _batch_rows(n_decode, tokens)
+    T = sum(q_lens)
+    Hq, Hkv, D = 32, 8, 128
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    # only the blocks the step writes exist; they sit at random places in the cache
+    spans = [(p // 16, (p + q - 1) // 16) for p, q in zip(prior, q_lens)]
+    NB = sum(b - a + 1 for a, b in spans) + 64
+    cache = torch.zeros(NB, 2, Hkv, 16, D, device=dev, dtype=torch.bfloat16)
+    perm = torch.randperm(NB, device=dev, generator=g).tolist()
+    slots, pos, off = [], [], 0
+    for (p, q), (a, b) in zip(zip(prior, q_lens), spans):
+        pos += list(range(p, p + q))
+        slots += [perm[off + t // 16 - a] * 16 + t % 16 for t in range(p, p + q)]
+        off += b - a + 1
+    smap = torch.tensor(slots, dtype=torch.int32, device=dev)
+    positions = torch.tensor(pos, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    if fused:
+        max_pos = 40960
+        qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=dev, dtype=torch.bfloat16, generator=g)
+        qn = torch.ones(D, device=dev, dtype=torch.bfloat16)
+        ang = torch.rand(max_pos, 64, device=dev, generator=g) * 6.28
+        cos, sin = torch.cos(ang), torch.sin(ang)
+        q_out = torch.empty(T, Hq, D, device=dev, dtype=torch.bfloat16)
+
+        def launch():
+            K.qk_norm_rope(qkv, Hq, Hkv, positions, qn, qn, cos, sin, 1e-6, q_out=q_out,
+                           kv_cache_layer=cache, slot_mapping=smap, num_blocks=NB, err=err)
+        # qkv row in, q out, K and V into the cache, position + slot, cos + sin rows
+        nbytes = T * ((Hq + 2 * Hkv) * D * 2 + Hq * D * 2 + 2 * Hkv * D * 2 + 8 + 2 * 64 * 4)
+        op = "qk_norm_rope"
+    else:
+        k = torch.randn(T, Hkv, D, device=dev, dtype=torch.bfloat16, generator=g)
+        v = torch.randn(T, Hkv, D, device=dev, dtype=torch.bfloat16, generator=g)
+
+        def launch():
+            K.kv_append(k, v, smap, cache, NB, err=err)
+        nbytes = T * (2 * 2 * Hkv * D * 2 + 4)        # K and V read and written, slot
+        op = "kv_append"
+    ms = _time(launch, iters, flush=True)
+    if int(err.item()) != 0:
+        raise RuntimeError(f"{op} micro: device error {int(err.item())}")
+    return _summary(op, ms, nbytes, tokens=T)
+
+
+def pack_micro(iters: int = 20, n_decode: int = 256, tokens: int = 2304):
+    """Packing of the operator batch: every sequence has its prior context
+    cached (its blocks owned), the step adds q_len tokens and allocates the
+    blocks they start."""
+    from hayate_b200 import kernels as K
+    prior, q_lens = _batch_rows(n_decode, tokens)
+    S, T = len(prior), sum(q_lens)
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    max_reqs = S + 1
+    tok_pitch = max(p + q for p, q in zip(prior, q_lens))
+    bt_pitch = -(-tok_pitch // 16)
+    have = [-(-p // 16) for p in prior]
+    need = [-(-(p + q) // 16) - h for p, q, h in zip(prior, q_lens, have)]
+    NB = sum(have) + sum(need) + 64
+    req_tokens = torch.randint(0, 151936, (max_reqs, tok_pitch), device=dev,
+                               dtype=torch.int32, generator=g)
+    bt0 = torch.full((max_reqs, bt_pitch), -1, dtype=torch.int32, device=dev)
+    perm = torch.randperm(NB, device=dev, generator=g).to(torch.int32)
+    off = 0
+    for i, h in enumerate(have):
+        bt0[i, :h] = perm[off:off + h]
+        off += h
+    free0 = torch.full((NB,), -1, dtype=torch.int32, device=dev)
+    free0[:NB - off] = perm[off:]
+    nblk0 = torch.tensor(have + [0], dtype=torch.int32, device=dev)
+    top0 = torch.tensor([NB - off], dtype=torch.int32, device=dev)
+    sched = torch.tensor([list(range(S)), prior, q_lens, [1] * S], dtype=torch.int32,
+                         device=dev).flatten().contiguous()
+    bt, nblk, free, top = bt0.clone(), nblk0.clone(), free0.clone(), top0.clone()
+    ids, positions, smap = (torch.empty(T, dtype=torch.int32, device=dev) for _ in range(3))
+    cu_q, kv_lens = (torch.empty(S + 1, dtype=torch.int32, device=dev) for _ in range(2))
+    rows, seqs = (torch.empty(S, dtype=torch.int32, device=dev) for _ in range(2))
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def launch():
+        K.pack_batch(sched, S, T, req_tokens, bt, nblk, free, top, ids, positions, smap,
+                     cu_q, kv_lens, rows, seqs, err)
+
+    def reset():
+        bt.copy_(bt0); nblk.copy_(nblk0); free.copy_(free0); top.copy_(top0)
+
+    ms = []
+    buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for i in range(iters + 3):
+        reset()
+        buf.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        launch()
+        b.record()
+        b.synchronize()
+        if i >= 3:
+            ms.append(a.elapsed_time(b))
+    if int(err.item()) != 0:
+        raise RuntimeError(f"pack micro: device error {int(err.item())}")
+    # reads: schedule, owned-block counts, token ids, block-table entries, popped
+    # stack entries; writes: ids, positions, slots, cu_q, seq_lens_k, sample rows,
+    # new block-table entries, counts
+    nbytes = 4 * (4 * S + S + T + T + sum(need)) + 4 * (3 * T + (S + 1) + S + 2 * S + sum(need) + S)
+    return _summary("pack", ms, nbytes, seqs=S, tokens=T, new_blocks=sum(need))
+
+
+def argmax_micro(iters: int = 20, rows: int = 260, vocab: int = 151936):
+    """Greedy argmax over ``rows`` bf16 logit rows (the sampled rows of the
+    operator batch)."""
+    from hayate_b200 import kernels as K
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    logits = torch.randn(rows, vocab, device=dev, dtype=torch.bfloat16, generator=g)
+    out = torch.empty(rows, dtype=torch.int32, device=dev)
+    ms = _time(lambda: K.argmax(logits, out), iters, flush=True)
+    if not torch.equal(out.long(), logits.argmax(dim=1)):
+        raise RuntimeError("argmax micro: result differs from torch.argmax")
+    return _summary("argmax", ms, rows * vocab * 2 + rows * 4, rows=rows)
+
+
+OPS = ("attention", "qk_norm_rope", "kv_append", "pack", "argmax")
+
+
+def run_op(op: str, iters: int, n_decode: int = 256, prefill: bool = True, tokens: int = 2304):
+    if op == "attention":
+        r = attention_micro(iters, n_decode, prefill)
+        r["op"] = op
+        r["gbs"] = r["bytes"] / (r["ms_mean"] * 1e-3) / 1e9
+        return r
+    if op in ("qk_norm_rope", "kv_append"):
+        return append_micro(iters, n_decode, tokens, fused=op == "qk_norm_rope")
+    if op == "pack":
+        return pack_micro(iters, n_decode, tokens)
+    if op == "argmax":
+        return argmax_micro(iters, rows=max(1, n_decode + max(0, tokens - n_decode) // 512))
+    raise ValueError(f"unknown op {op!r}; one of {OPS} or 'all'")
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--op", default="attention", help="one of " + ", ".join(OPS) + ", or all")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--decode", type=int, default=256,
                     help="decode sequences (fewer: a smaller case for profiling)")
-    ap.add_argument("--no-prefill", action="store_true", help="decode sequences only")
+    ap.add_argument("--no-prefill", action="store_true", help="attention: decode sequences only")
+    ap.add_argument("--tokens", type=int, default=2304,
+                    help="query tokens of the batch for the append, pack and argmax ops")
     a = ap.parse_args()
     torch.cuda.set_device(0)
-    r = attention_micro(a.iters, a.decode, not a.no_prefill)
-    r["gbs"] = r["bytes"] / (r["ms_mean"] * 1e-3) / 1e9
-    print(json.dumps(r))
+    for op in (OPS if a.op == "all" else (a.op,)):
+        print(json.dumps(run_op(op, a.iters, a.decode, not a.no_prefill, a.tokens)), flush=True)
 
 
 if __name__ == "__main__":

@@ -94,6 +94,7 @@ int hy_commit_tokens(const int32_t* next_tokens, int32_t n_sample, const int32_t
  * rope_cos/rope_sin: fp32 [max_pos][64] (first half of the reference tables).
  * q_out [tokens][q_heads][128] and k_out [tokens][kv_heads][128] are nullable;
  * kv_cache_layer (nullable) receives rotated k and raw v at slot_mapping.
+ * Every pointer given, and each qkv row (ld), is 16-byte aligned.
  * Replaces: q_norm/k_norm + apply_rope_vectorized + cache torch.cat,
  * hayate/model/attention.py:40-56 and hayate/model/rope.py:31-44. */
 int hy_qk_norm_rope(int32_t dtype, const void* qkv, int64_t ld, int32_t num_tokens,
@@ -104,7 +105,7 @@ int hy_qk_norm_rope(int32_t dtype, const void* qkv, int64_t ld, int32_t num_toke
                     int32_t num_blocks, int32_t* err, void* stream);
 
 /* Scatter k and v ([tokens][kv_heads][128]) into the paged cache at
- * slot_mapping (slot < 0: skipped).
+ * slot_mapping (slot < 0: skipped).  k, v and the cache are 16-byte aligned.
  * Replaces: torch.cat of new K/V onto the cache (hayate/model/attention.py:52-54)
  * and the per-request compaction (hayate/engine/engine.py:118-141). */
 int hy_kv_append(int32_t dtype, const void* k, const void* v, int32_t num_tokens,

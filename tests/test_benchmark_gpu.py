@@ -18,3 +18,10 @@ def test_benchmark_modes_small():
     # single mode: 3 requests x 8 tokens; upfront: one run of 3 x 8
     assert rows[0][1]["generated_tokens"] == 24
     assert rows[1][1]["generated_tokens"] == 24
+
+
+@pytest.mark.parametrize("op", ["qk_norm_rope", "kv_append", "pack", "argmax", "attention"])
+def test_operator_microbench_small(op):
+    from hayate_b200.microbench import run_op
+    r = run_op(op, iters=2, n_decode=16, prefill=True, tokens=16 + 512)
+    assert r["op"] == op and r["ms_mean"] > 0 and r["bytes"] > 0

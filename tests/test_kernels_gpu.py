@@ -178,6 +178,64 @@ def test_kv_append_bit_exact(dt):
     assert np.array_equal(cache.float().cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_kv_append_many_tokens(dt):
+    """More rows than one pass of the grid: every lane group loops."""
+    T, Hkv, NB = 9000, 8, 600
+    k = torch.randn(T, Hkv, 128, device=dev).to(dt)
+    v = torch.randn(T, Hkv, 128, device=dev).to(dt)
+    slots = torch.randperm(NB * 16, device=dev)[:T].int()
+    slots[::97] = -1
+    cache = torch.zeros(NB, 2, Hkv, 16, 128, dtype=dt, device=dev)
+    K.kv_append(k, v, slots, cache, NB)
+    want = np.zeros((NB, 2, Hkv, 16, 128), np.float32)
+    PS.kv_append(want, k.float().cpu().numpy(), v.float().cpu().numpy(), slots.cpu().numpy())
+    torch.cuda.synchronize()
+    assert np.array_equal(cache.float().cpu().numpy(), want)
+
+
+def test_qk_norm_rope_bf16_many_tokens_vs_oracle():
+    """bf16 path over more tokens than CTAs (each CTA walks several tokens),
+    against the oracle's torch ops on the CPU: at most one bf16 ulp."""
+    T, Hq, Hkv, NB = 2500, 32, 8, 200
+    g = torch.Generator(device=dev).manual_seed(5)
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * 128, device=dev, generator=g).to(torch.bfloat16)
+    wq = (1 + 0.1 * torch.randn(128, device=dev, generator=g)).to(torch.bfloat16)
+    wk = (1 + 0.1 * torch.randn(128, device=dev, generator=g)).to(torch.bfloat16)
+    cos, sin = R.rope_tables(128, QWEN3_4B.rope_theta, QWEN3_4B.max_position_embeddings)
+    cos64, sin64 = cos[:, :64].contiguous().to(dev), sin[:, :64].contiguous().to(dev)
+    pos = torch.randint(0, 40960, (T,), device=dev, generator=g).int()
+    slots = torch.randperm(NB * 16, device=dev, generator=g)[:T].int()
+    q_out = torch.empty(T, Hq, 128, dtype=torch.bfloat16, device=dev)
+    cache = torch.zeros(NB, 2, Hkv, 16, 128, dtype=torch.bfloat16, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    K.qk_norm_rope(qkv, Hq, Hkv, pos, wq, wk, cos64, sin64, QWEN3_4B.rms_norm_eps, q_out=q_out,
+                   kv_cache_layer=cache, slot_mapping=slots, num_blocks=NB, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    c = qkv.cpu()
+    q, k = c[:, :Hq * 128].view(T, Hq, 128), c[:, Hq * 128:(Hq + Hkv) * 128].view(T, Hkv, 128)
+    vv = c[:, (Hq + Hkv) * 128:].view(T, Hkv, 128)
+    wq_out, wk_out = R.qk_norm_rope(q, k, wq.cpu(), wk.cpu(), cos, sin, pos.cpu(),
+                                    QWEN3_4B.rms_norm_eps)
+    # One bf16 ulp of a normed element (magnitude < 8: ulp <= 2^-5) moves an
+    # output by at most two such ulps with the roundings of the products and the
+    # sum, also where y*cos and y'*sin cancel and the ulp distance of the tiny
+    # result says little; most elements are identical.
+    def close(got, want):
+        d = (got.float() - want.float()).abs()
+        assert d.max().item() <= 2 ** -4
+        assert (got.view(torch.int16) != want.view(torch.int16)).float().mean().item() < 0.02
+    close(q_out.cpu(), wq_out)
+    sl = slots.cpu().long()
+    blk, j = sl // 16, sl % 16
+    cc = cache.cpu()
+    got_k = cc[blk, 0, :, j]                      # (T, Hkv, 128)
+    got_v = cc[blk, 1, :, j]
+    close(got_k, wk_out)
+    assert torch.equal(got_v, vv)
+
+
 # ------------------------------------------------------------------ attention
 def _run_attention(b, dt, kv_heads, bt_row=None, max_seqs=None, max_tokens=None):
     S, T = b["S"], b["T"]
@@ -204,6 +262,9 @@ CASES = {
     "decode_long_split": ([1] * 3, [16384, 5000, 70]),
     "prefill_only": ([37, 64, 16, 3], [37, 164, 16, 1027]),
     "mixed": ([1, 512, 1, 5, 1, 129, 1], [1000, 4096, 33, 12, 2049, 129, 7]),
+    # 376 prefill items (several per CTA), ragged 64-token tiles, prefixes
+    "prefill_many": ([65, 127, 128, 200, 512, 512, 512, 512, 300, 1],
+                     [65, 227, 1128, 200, 512, 1024, 2048, 600, 3000, 50]),
 }
 
 
@@ -266,6 +327,54 @@ def test_argmax_first_index_ties(dt):
     torch.cuda.synchronize()
     assert torch.equal(out, want)
     assert out[1].item() == 5 and out[2].item() == 0
+
+
+@pytest.mark.parametrize("rows", [1, 10, 260, 1300])
+def test_argmax_cluster_split_rows(rows):
+    """Rows split over clusters of 8, 8, 4 and 1 CTAs: ties placed in different
+    chunks resolve to the lower index; NaN wins (first NaN); a row of equal values gives 0."""
+    V = 151936
+    g = torch.Generator(device=dev).manual_seed(rows)
+    x = torch.randn(rows, V, device=dev, generator=g).to(torch.bfloat16)
+    r = rows - 1
+    x[r, 3 * V // 4 + 5] = 40.0                 # tie in the last chunk ...
+    x[r, V // 8 - 1] = 40.0                     # ... and in the first: lower index wins
+    if rows > 1:
+        x[0, 100] = float("nan")
+        x[0, 90000] = float("nan")
+        x[0, 5] = float("inf")
+    if rows > 2:
+        x[1, :] = -3.0
+    if rows > 3:                                # -0 and +0 are equal: the first zero wins
+        x[2, :] = -1.0
+        x[2, 7] = -0.0
+        x[2, 9] = 0.0
+    out = torch.empty(rows, dtype=torch.int32, device=dev)
+    K.argmax(x, out)
+    want = torch.argmax(x.float().cpu(), dim=-1).int()
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), want)
+    assert out[r].item() == V // 8 - 1
+    if rows > 1:
+        assert out[0].item() == 100
+    if rows > 2:
+        assert out[1].item() == 0
+    if rows > 3:
+        assert out[2].item() == 7
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_argmax_odd_vocab_and_unaligned_rows(dt):
+    rows, V = 12, 1001
+    base = torch.randn(rows, V + 1, device=dev).to(dt)
+    for n, x in enumerate((base[:, :V], base[:, 1:])):   # aligned rows with a tail; unaligned
+        x[2, V - 1] = 99.0 + 100 * n
+        out = torch.empty(rows, dtype=torch.int32, device=dev)
+        K.argmax(x, out)
+        want = torch.argmax(x.float().cpu(), dim=-1).int()
+        torch.cuda.synchronize()
+        assert torch.equal(out.cpu(), want)
+        assert out[2].item() == V - 1
 
 
 # --------------------------------------------------------- RMSNorm, SiLU*up
