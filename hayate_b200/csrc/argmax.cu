@@ -16,96 +16,86 @@ constexpr int AM_THREADS = 256;
 constexpr int AM_UNROLL = 4;
 constexpr int AM_MAX_CLUSTER = 8;         // portable cluster size
 
-// Elements are compared through order-preserving unsigned keys: a float's bit
-// pattern with the sign bit flipped (non-negative) or all bits flipped
-// (negative), -0 taken as +0, and every NaN mapped to the largest key, so that
-// NaN beats every number as in torch.argmax.  A thread scans its elements in increasing index
-// order and replaces its best only on a strictly larger key, keeping the first
-// index of a tie; the merges across threads compare (key, index).
-HY_DEVICE uint32_t key_f32(float f) {
-  uint32_t b = __float_as_uint(f);
-  if ((b & 0x7fffffffu) > 0x7f800000u) return 0xffffffffu;
-  if ((b & 0x7fffffffu) == 0u) b = 0u;
-  return b ^ ((b & 0x80000000u) ? 0xffffffffu : 0x80000000u);
+// (v, i) beats (a, j): NaN beats every number (torch.argmax propagates NaN),
+// otherwise the larger value; equal values (-0 == +0, NaN and NaN) go to the
+// lower index.
+HY_DEVICE bool better(float av, int ai, float bv, int bi) {
+  const bool an = isnan(av), bn = isnan(bv);
+  if (an || bn) return bn && (!an || bi < ai);
+  return bv > av || (bv == av && bi < ai);
 }
 
-// Keys of the two bf16 in a 32-bit word, as two 16-bit lanes.
-HY_DEVICE uint32_t key2_bf16(uint32_t w) {
-  w &= ~(__vcmpeq2(w & 0x7fff7fffu, 0u) & 0x80008000u);               // -0 -> +0
-  const uint32_t neg = ((w >> 15) & 0x00010001u) * 0xffffu;           // 0xffff where negative
-  const uint32_t k = w ^ (neg | 0x80008000u);
-  return k | __vcmpgtu2(w & 0x7fff7fffu, 0x7f807f80u);               // NaN -> 0xffff
-}
-
-HY_DEVICE bool better(uint32_t ak, int ai, uint32_t bk, int bi) {
-  return bk > ak || (bk == ak && bi < ai);
-}
-
-// Reduce (key, index) over the CTA; the result is valid in thread 0.
-HY_DEVICE void cta_best(uint32_t& bk, int& bi) {
+// Reduce (value, index) over the CTA; the result is valid in thread 0.
+HY_DEVICE void cta_best(float& bv, int& bi) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const uint32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (better(bk, bi, ok, oi)) { bk = ok; bi = oi; }
+    if (better(bv, bi, ov, oi)) { bv = ov; bi = oi; }
   }
-  __shared__ uint32_t sk[AM_THREADS / 32];
+  __shared__ float sv[AM_THREADS / 32];
   __shared__ int si[AM_THREADS / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) { sk[warp] = bk; si[warp] = bi; }
+  if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
   __syncthreads();
   if (warp == 0) {
-    bk = lane < AM_THREADS / 32 ? sk[lane] : 0u;
+    bv = lane < AM_THREADS / 32 ? sv[lane] : -INFINITY;
     bi = lane < AM_THREADS / 32 ? si[lane] : 0x7fffffff;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      const uint32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (better(bk, bi, ok, oi)) { bk = ok; bi = oi; }
+      if (better(bv, bi, ov, oi)) { bv = ov; bi = oi; }
     }
   }
 }
 
 template <typename T> struct Scan;
 
-// bf16: 16-byte vectors of 8 elements; a batch of AM_UNROLL vectors is reduced
-// with packed 16-bit maxima and searched for its first maximum only when it
-// beats the thread's best.
+// bf16: 16-byte vectors of 8 elements.  A batch of AM_UNROLL vectors is reduced
+// with packed bf16x2 maxima that propagate NaN; only a batch whose maximum beats
+// the thread's best (rare after the first few) is searched for the first index
+// holding it.  A thread's batches come in increasing index order, so a strictly
+// better batch maximum keeps first-index ties.
 template <> struct Scan<__nv_bfloat16> {
   static constexpr int N = 8;
-  static HY_DEVICE void run(const __nv_bfloat16* x, int v0, int v1, uint32_t& bk, int& bi) {
+  static HY_DEVICE void run(const __nv_bfloat16* x, int v0, int v1, float& bv, int& bi) {
     for (int base = v0 + threadIdx.x; base < v1; base += AM_THREADS * AM_UNROLL) {
       uint4 w[AM_UNROLL];
 #pragma unroll
       for (int u = 0; u < AM_UNROLL; ++u) {
         const int vi = base + u * AM_THREADS;
-        w[u] = vi < v1 ? __ldg(reinterpret_cast<const uint4*>(x) + vi) : make_uint4(0u, 0u, 0u, 0u);
+        // -inf pairs (0xff80) for vectors past the chunk: they never win
+        w[u] = vi < v1 ? __ldg(reinterpret_cast<const uint4*>(x) + vi)
+                       : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
       }
-      uint32_t k[AM_UNROLL][4];
-      uint32_t m = 0u;
+      __nv_bfloat162 m = *reinterpret_cast<const __nv_bfloat162*>(&w[0].x);
 #pragma unroll
       for (int u = 0; u < AM_UNROLL; ++u) {
-        const bool valid = base + u * AM_THREADS < v1;
-        k[u][0] = valid ? key2_bf16(w[u].x) : 0u;
-        k[u][1] = valid ? key2_bf16(w[u].y) : 0u;
-        k[u][2] = valid ? key2_bf16(w[u].z) : 0u;
-        k[u][3] = valid ? key2_bf16(w[u].w) : 0u;
-        m = __vmaxu2(m, __vmaxu2(__vmaxu2(k[u][0], k[u][1]), __vmaxu2(k[u][2], k[u][3])));
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w[u]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) m = __hmax2_nan(m, h[q]);
       }
-      const uint32_t bm = max(m & 0xffffu, m >> 16);
-      if (bm > bk) {                                  // first element of the batch with key bm
+      const float m0 = __low2float(m), m1 = __high2float(m);
+      const float bm = (isnan(m0) || m1 != m1) ? NAN : fmaxf(m0, m1);
+      // the thread's first batch, or a strictly better value (NaN beats numbers)
+      const bool take = bi == 0x7fffffff || (isnan(bm) ? !isnan(bv) : bm > bv);
+      if (take) {
         bool found = false;
 #pragma unroll
-        for (int u = 0; u < AM_UNROLL; ++u)
+        for (int u = 0; u < AM_UNROLL; ++u) {
+          const __nv_bfloat16* e8 = reinterpret_cast<const __nv_bfloat16*>(&w[u]);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const uint32_t ke = (k[u][e >> 1] >> (16 * (e & 1))) & 0xffffu;
-            if (!found && ke == bm) {
+            const float f = __bfloat162float(e8[e]);
+            const bool hit = isnan(bm) ? isnan(f) : (f == bm);
+            if (!found && hit) {
               found = true;
-              bk = bm;
+              bv = f;
               bi = (base + u * AM_THREADS) * 8 + e;
             }
           }
+        }
       }
     }
   }
@@ -113,23 +103,16 @@ template <> struct Scan<__nv_bfloat16> {
 
 template <> struct Scan<float> {
   static constexpr int N = 4;
-  static HY_DEVICE void run(const float* x, int v0, int v1, uint32_t& bk, int& bi) {
+  static HY_DEVICE void run(const float* x, int v0, int v1, float& bv, int& bi) {
     for (int vi = v0 + threadIdx.x; vi < v1; vi += AM_THREADS) {
       const float4 f = __ldg(reinterpret_cast<const float4*>(x) + vi);
       const float e4[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const uint32_t k = key_f32(e4[e]);
-        if (k > bk) { bk = k; bi = vi * 4 + e; }
-      }
+      for (int e = 0; e < 4; ++e)
+        if (better(bv, bi, e4[e], vi * 4 + e)) { bv = e4[e]; bi = vi * 4 + e; }
     }
   }
 };
-
-HY_DEVICE uint32_t key_of(float v) { return key_f32(v); }
-HY_DEVICE uint32_t key_of(__nv_bfloat16 v) {
-  return key2_bf16((uint32_t)__bfloat16_as_ushort(v)) & 0xffffu;
-}
 
 // A row is split over the C CTAs of one thread-block cluster (C = 1..8, chosen
 // on the host so that rows x C CTAs fill the SMs): CTA r scans the contiguous
@@ -142,48 +125,50 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(
     const T* __restrict__ logits, long ld, int V, int32_t* __restrict__ out) {
   using S = Scan<T>;
   constexpr int N = S::N;
+  hy_grid_wait();
+  hy_grid_trigger();
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.num_blocks();
   const int rank = (int)cluster.block_rank();
   const int row = blockIdx.x / C;
   const T* x = logits + (size_t)row * ld;
-  uint32_t bk = 0u;                                   // below every element's key
+  float bv = -INFINITY;
   int bi = 0x7fffffff;
   const bool vec_ok = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
   const int nvec = V / N;
   const int per = (nvec + C - 1) / C;                 // vectors per CTA
   const int v0 = min(nvec, rank * per), v1 = min(nvec, v0 + per);
   if (vec_ok) {
-    S::run(x, v0, v1, bk, bi);
+    S::run(x, v0, v1, bv, bi);
   } else {
     for (int i = v0 * N + threadIdx.x; i < v1 * N; i += AM_THREADS) {
-      const uint32_t k = key_of(x[i]);
-      if (k > bk) { bk = k; bi = i; }
+      const float v = ElemTraits<T>::to_f(x[i]);
+      if (better(bv, bi, v, i)) { bv = v; bi = i; }
     }
   }
   if (rank == C - 1)                                  // elements past the last whole vector
     for (int i = nvec * N + threadIdx.x; i < V; i += AM_THREADS) {
-      const uint32_t k = key_of(x[i]);
-      if (k > bk) { bk = k; bi = i; }
+      const float v = ElemTraits<T>::to_f(x[i]);
+      if (better(bv, bi, v, i)) { bv = v; bi = i; }
     }
-  cta_best(bk, bi);
-  __shared__ uint32_t best_k;
+  cta_best(bv, bi);
+  __shared__ float best_v;
   __shared__ int best_i;
-  if (threadIdx.x == 0) { best_k = bk; best_i = bi; }
+  if (threadIdx.x == 0) { best_v = bv; best_i = bi; }
   cluster.sync();                                     // partials visible cluster-wide
   if (rank == 0 && threadIdx.x < 32) {
     const int lane = threadIdx.x;
-    uint32_t k = 0u;
+    float v = -INFINITY;
     int i = 0x7fffffff;
     if (lane < C) {
-      k = *cluster.map_shared_rank(&best_k, lane);
+      v = *cluster.map_shared_rank(&best_v, lane);
       i = *cluster.map_shared_rank(&best_i, lane);
     }
 #pragma unroll
     for (int o = 4; o > 0; o >>= 1) {                 // C <= 8
-      const uint32_t ok = __shfl_xor_sync(0xffffffffu, k, o);
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
       const int oi = __shfl_xor_sync(0xffffffffu, i, o);
-      if (better(k, i, ok, oi)) { k = ok; i = oi; }
+      if (better(v, i, ov, oi)) { v = ov; i = oi; }
     }
     if (lane == 0) out[row] = i == 0x7fffffff ? 0 : i;
   }
@@ -203,13 +188,15 @@ cudaError_t hy_launch_argmax(int dtype, const void* logits, long ld, int rows, i
   cfg.gridDim = dim3((unsigned)(rows * C));
   cfg.blockDim = dim3(AM_THREADS);
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = C;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = hy_pdl_enabled() ? 2 : 1;
   if (dtype == 0)
     return cudaLaunchKernelEx(&cfg, argmax_kernel<__nv_bfloat16>,
                               static_cast<const __nv_bfloat16*>(logits), ld, V, out);

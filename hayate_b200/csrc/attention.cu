@@ -135,6 +135,8 @@ HY_DEVICE int mul_div(int a, int b, int c) {
 __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
     const int32_t* __restrict__ cu_q, const int32_t* __restrict__ seq_lens_k, int S,
     int kv_heads, int warp_slots, PlanView v, int32_t* err) {
+  hy_grid_wait();
+  hy_grid_trigger();
   __shared__ int ws[32];
   __shared__ int s_total, s_cpre, s_cdec, s_bad;
   if (threadIdx.x == 0) { s_total = 0; s_cpre = 0; s_cdec = 0; s_bad = 0; }
@@ -749,18 +751,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     mbar_init(&sh.tc_drain, 1);
     fence_mbar_init();
   }
-  const int n_pre = v.header[0], n_dec = v.header[1];
-  // TMEM for the tcgen05 prefill items: only the first n_pre CTAs take prefill
-  // items, and only they allocate
-  const bool use_tmem = (int)blockIdx.x < n_pre;
-  if (use_tmem && warp == 0) {
+  // set-up that reads nothing an earlier kernel wrote runs before the wait: the
+  // barriers above, the tensor-map prefetch and the TMEM columns of the
+  // tcgen05 prefill items (every CTA allocates; one CTA per SM holds them)
+  if (warp == 0) {
     tmem_alloc(&sh.tmem_base, TC_TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = use_tmem ? sh.tmem_base : 0u;
+  const uint32_t tmem = sh.tmem_base;
+  hy_grid_wait();
+  hy_grid_trigger();
+  const int n_pre = v.header[0], n_dec = v.header[1];
+  const bool use_tmem = (int)blockIdx.x < n_pre;      // the first n_pre CTAs take prefill items
   uint32_t dec_phase = 0, tile_ctr = 0;
   bool ok = true;
   int* grab = v.grab + GRAB_INTS * (a.layer & 63);
@@ -806,13 +811,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
       }
     }
   }
-  if (use_tmem) {
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-      tc_fence_after();
-      tmem_dealloc(tmem, TC_TMEM_COLS);
-    }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TC_TMEM_COLS);
   }
 }
 
@@ -940,9 +943,8 @@ static PlanView make_view(void* ws, const PlanDims& d) {
 cudaError_t hy_launch_attn_plan(const int32_t* cu_q, const int32_t* seq_lens_k, int S,
                                 int kv_heads, const PlanDims& d, void* ws, int32_t* err,
                                 int dev, cudaStream_t st) {
-  plan_kernel<<<1, PLAN_THREADS, 0, st>>>(cu_q, seq_lens_k, S, kv_heads,
-                                          hy_attn_warp_slots(dev), make_view(ws, d), err);
-  return cudaGetLastError();
+  return hy_launch(plan_kernel, dim3(1), dim3(PLAN_THREADS), 0, st, cu_q, seq_lens_k, S,
+                   kv_heads, hy_attn_warp_slots(dev), make_view(ws, d), err);
 }
 
 cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* q, void* out, int q_heads,
@@ -980,8 +982,7 @@ cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* q, void* out
   a.err = err;
   const PlanView v = make_view(ws, d);
   const int grid = device_sms(dev) * g_ctas_per_sm[dev < 64 && dev >= 0 ? dev : 0];
-  attn_main_kernel<<<grid, ATT_THREADS, SMEM_BYTES, st>>>(map, a, v);
-  return cudaGetLastError();
+  return hy_launch(attn_main_kernel, dim3(grid), dim3(ATT_THREADS), SMEM_BYTES, st, map, a, v);
 }
 
 cudaError_t hy_launch_attn_fp32(const float* q, float* out, int T, int q_heads, int kv_heads,

@@ -1,6 +1,8 @@
 // C-ABI layer: argument checks, tensor-map cache, error reporting.
 #include "hayate_b200.h"
 #include "common.cuh"
+
+#include <stdlib.h>
 #include "attention.cuh"
 
 #include <mutex>
@@ -135,6 +137,14 @@ int hy_attention_kv_map(int dev, const void* base, long rows, CUtensorMap* out) 
 }
 
 void hy_set_error(const char* msg) { snprintf(g_last_error, sizeof(g_last_error), "%s", msg); }
+
+bool hy_pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("HY_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
 
 extern "C" {
 

@@ -39,6 +39,35 @@ HY_DEVICE uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ------------------------------------------------- programmatic dependent launch
+// Kernels of the step are launched with hy_launch: with programmatic stream
+// serialisation a kernel's CTAs may start while the previous kernel on the
+// stream is still running.  Such a kernel does its set-up first and calls
+// hy_grid_wait() before it reads anything an earlier kernel wrote (the wait
+// returns once the previous grid has completed and its writes are visible; it
+// is a no-op for a kernel launched without the attribute).  hy_grid_trigger()
+// lets the next kernel's CTAs start early.
+HY_DEVICE void hy_grid_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+HY_DEVICE void hy_grid_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool hy_pdl_enabled();   // false when the environment sets HY_PDL=0
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t hy_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = hy_pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ---------------------------------------------------------------- mbarrier
 HY_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");

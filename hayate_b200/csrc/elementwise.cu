@@ -67,11 +67,17 @@ __global__ void __launch_bounds__(RN_THREADS) add_rms_norm_kernel(
   T* xr = x + r * ldx;
   float v[RN_VEC][N], wv[RN_VEC][N];
 #pragma unroll
+  for (int k = 0; k < RN_VEC; ++k) {          // the weights are no earlier kernel's output
+    const int vi = threadIdx.x + RN_THREADS * k;
+    if (vi < nvec) V::load(w + vi * N, wv[k]);
+  }
+  hy_grid_wait();
+  hy_grid_trigger();
+#pragma unroll
   for (int k = 0; k < RN_VEC; ++k) {
     const int vi = threadIdx.x + RN_THREADS * k;
     if (vi < nvec) {
       V::load(xr + vi * N, v[k]);
-      V::load(w + vi * N, wv[k]);
       if (delta != nullptr) {
         float dv[N];
         V::load(delta + r * ldd + vi * N, dv);
@@ -116,6 +122,8 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(
     const T* __restrict__ gu, long ld, int rows, int inter, T* __restrict__ y, long ldy) {
   using V = Vec<T>;
   constexpr int N = V::N;
+  hy_grid_wait();
+  hy_grid_trigger();
   const int nvec = inter / N;
   const long total = (long)rows * nvec;
   const long stride = (long)gridDim.x * blockDim.x;
@@ -141,13 +149,11 @@ cudaError_t hy_launch_add_rms_norm(int dtype, void* x, long ldx, const void* del
                                    long ldy, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   if (dtype == 0)
-    add_rms_norm_kernel<__nv_bfloat16><<<rows, RN_THREADS, 0, st>>>(
-        (__nv_bfloat16*)x, ldx, (const __nv_bfloat16*)delta, ldd, cols,
-        (const __nv_bfloat16*)w, eps, (__nv_bfloat16*)y, ldy);
-  else
-    add_rms_norm_kernel<float><<<rows, RN_THREADS, 0, st>>>(
-        (float*)x, ldx, (const float*)delta, ldd, cols, (const float*)w, eps, (float*)y, ldy);
-  return cudaGetLastError();
+    return hy_launch(add_rms_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(RN_THREADS), 0, st,
+                     (__nv_bfloat16*)x, ldx, (const __nv_bfloat16*)delta, ldd, cols,
+                     (const __nv_bfloat16*)w, eps, (__nv_bfloat16*)y, ldy);
+  return hy_launch(add_rms_norm_kernel<float>, dim3(rows), dim3(RN_THREADS), 0, st, (float*)x,
+                   ldx, (const float*)delta, ldd, cols, (const float*)w, eps, (float*)y, ldy);
 }
 
 cudaError_t hy_launch_silu_mul(int dtype, const void* gu, long ld, int rows, int inter, void* y,
@@ -157,10 +163,8 @@ cudaError_t hy_launch_silu_mul(int dtype, const void* gu, long ld, int rows, int
   long blocks = (vecs + 255) / 256;
   if (blocks > 148L * 32) blocks = 148L * 32;
   if (dtype == 0)
-    silu_mul_kernel<__nv_bfloat16><<<(int)blocks, 256, 0, st>>>(
-        (const __nv_bfloat16*)gu, ld, rows, inter, (__nv_bfloat16*)y, ldy);
-  else
-    silu_mul_kernel<float><<<(int)blocks, 256, 0, st>>>((const float*)gu, ld, rows, inter,
-                                                        (float*)y, ldy);
-  return cudaGetLastError();
+    return hy_launch(silu_mul_kernel<__nv_bfloat16>, dim3((int)blocks), dim3(256), 0, st,
+                     (const __nv_bfloat16*)gu, ld, rows, inter, (__nv_bfloat16*)y, ldy);
+  return hy_launch(silu_mul_kernel<float>, dim3((int)blocks), dim3(256), 0, st, (const float*)gu,
+                   ld, rows, inter, (float*)y, ldy);
 }

@@ -62,6 +62,8 @@ __global__ void __launch_bounds__(PACK_THREADS) pack_kernel(
   __shared__ int warp_sums[32];
   __shared__ int s_top0, s_carry_q, s_carry_n, s_carry_s, s_bad;
   __shared__ int s_cu[PACK_SMEM_SEQS + 1];      // cu_seqlens_q, for token -> sequence
+  hy_grid_wait();
+  hy_grid_trigger();
   const int32_t* s_slot = sched;
   const int32_t* s_start = sched + S;
   const int32_t* s_qlen = sched + 2 * S;
@@ -227,6 +229,8 @@ __global__ void commit_kernel(const int32_t* __restrict__ next_tokens, int n_sam
                               const int32_t* __restrict__ sched, int S,
                               int32_t* __restrict__ req_tokens, int tok_pitch, int max_reqs,
                               int32_t* err) {
+  hy_grid_wait();
+  hy_grid_trigger();
   const int k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= n_sample) return;
   const int i = sample_seq[k];
@@ -263,11 +267,10 @@ cudaError_t hy_launch_pack(const int32_t* sched, int S, int T, const int32_t* re
                            int32_t* slot_mapping, int32_t* cu_q, int32_t* seq_lens_k,
                            int32_t* sample_rows, int32_t* sample_seq, int32_t* err,
                            cudaStream_t st) {
-  pack_kernel<<<1, PACK_THREADS, 0, st>>>(sched, S, T, req_tokens, tok_pitch, max_reqs,
-                                          block_tables, bt_pitch, req_nblk, free_stack, free_top,
-                                          num_blocks, input_ids, positions, slot_mapping, cu_q,
-                                          seq_lens_k, sample_rows, sample_seq, err);
-  return cudaGetLastError();
+  return hy_launch(pack_kernel, dim3(1), dim3(PACK_THREADS), 0, st, sched, S, T, req_tokens,
+                   tok_pitch, max_reqs, block_tables, bt_pitch, req_nblk, free_stack, free_top,
+                   num_blocks, input_ids, positions, slot_mapping, cu_q, seq_lens_k, sample_rows,
+                   sample_seq, err);
 }
 
 cudaError_t hy_launch_free(const int32_t* slots, int n, int max_reqs, int32_t* block_tables,
@@ -283,7 +286,7 @@ cudaError_t hy_launch_commit(const int32_t* next_tokens, int n_sample, const int
                              int max_reqs, int32_t* err, cudaStream_t st) {
   if (n_sample <= 0) return cudaSuccess;
   const int threads = 128;
-  commit_kernel<<<(n_sample + threads - 1) / threads, threads, 0, st>>>(
-      next_tokens, n_sample, sample_seq, sched, S, req_tokens, tok_pitch, max_reqs, err);
-  return cudaGetLastError();
+  return hy_launch(commit_kernel, dim3((n_sample + threads - 1) / threads), dim3(threads), 0, st,
+                   next_tokens, n_sample, sample_seq, sched, S, req_tokens, tok_pitch, max_reqs,
+                   err);
 }

@@ -53,6 +53,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     float eps, T* __restrict__ q_out, T* __restrict__ k_out,
     T* __restrict__ cache, const int32_t* __restrict__ slot_mapping, int num_blocks,
     int32_t* err) {
+  hy_grid_wait();
+  hy_grid_trigger();
   using P = Pair<T>;
   const int lane = threadIdx.x & 31;
   const int heads = q_heads + 2 * kv_heads;
@@ -159,6 +161,8 @@ __global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
     const float* __restrict__ rope_sin, int max_pos, float eps, __nv_bfloat16* __restrict__ q_out,
     __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ cache,
     const int32_t* __restrict__ slot_mapping, int num_blocks, int32_t* err) {
+  hy_grid_wait();
+  hy_grid_trigger();
   using B = __nv_bfloat16;
   const int grp = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int heads = q_heads + 2 * kv_heads;
@@ -259,6 +263,8 @@ __global__ void __launch_bounds__(KVA_THREADS) kv_append_kernel(
     const T* __restrict__ k, const T* __restrict__ v, int T_tokens, int kv_heads,
     const int32_t* __restrict__ slot_mapping, T* __restrict__ cache, int num_blocks,
     int32_t* err) {
+  hy_grid_wait();
+  hy_grid_trigger();
   constexpr int E = 16 / (int)sizeof(T);           // elements per lane
   constexpr int LPR = HY_HEAD_DIM / E;             // lanes per row
   constexpr int G = KVA_THREADS / LPR;             // rows per CTA pass
@@ -307,10 +313,10 @@ cudaError_t hy_launch_qk_norm_rope(int dtype, const void* qkv, int ld, int T, in
     using B = __nv_bfloat16;
     const long units = (long)T * ((q_heads + 2 * kv_heads + QNR_GROUPS - 1) / QNR_GROUPS);
     const int grid = (int)(units < 148L * 8 ? units : 148L * 8);   // up to 8 CTAs per SM
-    qk_norm_rope_bf16_kernel<<<grid, QNR_THREADS, 0, st>>>(
-        (const B*)qkv, ld, T, q_heads, kv_heads, positions, (const B*)q_w, (const B*)k_w,
-        rope_cos, rope_sin, max_pos, eps, (B*)q_out, (B*)k_out, (B*)cache, slot_mapping,
-        num_blocks, err);
+    return hy_launch(qk_norm_rope_bf16_kernel, dim3(grid), dim3(QNR_THREADS), 0, st,
+                     (const B*)qkv, (int)ld, T, q_heads, kv_heads, positions, (const B*)q_w,
+                     (const B*)k_w, rope_cos, rope_sin, max_pos, eps, (B*)q_out, (B*)k_out,
+                     (B*)cache, slot_mapping, num_blocks, err);
   } else {
     const int grid = grid_for((long)T * (q_heads + 2 * kv_heads));
     qk_norm_rope_kernel<float><<<grid, 256, 0, st>>>(
@@ -331,8 +337,8 @@ cudaError_t hy_launch_kv_append(int dtype, const void* k, const void* v, int T, 
   const int grid = (int)(blocks < 148L * 8 ? (blocks > 0 ? blocks : 1) : 148L * 8);
   if (dtype == 0) {
     using B = __nv_bfloat16;
-    kv_append_kernel<B><<<grid, KVA_THREADS, 0, st>>>((const B*)k, (const B*)v, T, kv_heads,
-                                              slot_mapping, (B*)cache, num_blocks, err);
+    return hy_launch(kv_append_kernel<B>, dim3(grid), dim3(KVA_THREADS), 0, st, (const B*)k,
+                     (const B*)v, T, kv_heads, slot_mapping, (B*)cache, num_blocks, err);
   } else {
     kv_append_kernel<float><<<grid, KVA_THREADS, 0, st>>>((const float*)k, (const float*)v, T, kv_heads,
                                                   slot_mapping, (float*)cache, num_blocks, err);

@@ -10,7 +10,9 @@ qk_norm_rope / kv_append / pack / argmax: the same batch (2304 query tokens:
 256 decode rows + 4 x 512 prefill rows) through the fused QK-norm+RoPE+append
 kernel, the standalone KV append, the packing kernel and the greedy argmax over
 the 256+4 sampled rows (vocab 151936).  These inputs fit in L2, so each timed
-launch is preceded by an L2 flush (a 256 MiB write outside the timed window).
+launch is preceded by an L2 flush outside the timed window: a read of 256 MiB,
+which evicts the op's data without leaving dirty lines whose write-back the
+timed launch would pay.
 ``--tokens`` raises the token count of the append kernels (prefill-sized
 batches).  Every op reports its algorithmic bytes; packing is latency-bound,
 so its microseconds are the figure of merit.
@@ -90,17 +92,22 @@ def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True):
 L2_FLUSH_BYTES = 256 << 20
 
 
+def _flusher():
+    buf = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    return lambda: buf.sum()
+
+
 def _time(launch, iters: int, flush: bool):
     """CUDA-event time of each launch (ms), after 3 warm-up launches; an L2
     flush precedes every timed launch when ``flush``."""
-    buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda") if flush else None
+    flush_l2 = _flusher() if flush else None
     for _ in range(3):
         launch()
     torch.cuda.synchronize()
     ms = []
     for _ in range(iters):
-        if buf is not None:
-            buf.zero_()
+        if flush_l2 is not None:
+            flush_l2()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         launch()
@@ -227,10 +234,10 @@ def pack_micro(iters: int = 20, n_decode: int = 256, tokens: int = 2304):
         bt.copy_(bt0); nblk.copy_(nblk0); free.copy_(free0); top.copy_(top0)
 
     ms = []
-    buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush_l2 = _flusher()
     for i in range(iters + 3):
         reset()
-        buf.zero_()
+        flush_l2()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         launch()

@@ -349,6 +349,8 @@ def test_argmax_cluster_split_rows(rows):
         x[2, :] = -1.0
         x[2, 7] = -0.0
         x[2, 9] = 0.0
+    if rows > 4:                                # all -inf: index 0
+        x[3, :] = float("-inf")
     out = torch.empty(rows, dtype=torch.int32, device=dev)
     K.argmax(x, out)
     want = torch.argmax(x.float().cpu(), dim=-1).int()
@@ -361,6 +363,8 @@ def test_argmax_cluster_split_rows(rows):
         assert out[1].item() == 0
     if rows > 3:
         assert out[2].item() == 7
+    if rows > 4:
+        assert out[3].item() == 0
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
