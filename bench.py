@@ -48,6 +48,23 @@ def log(*a):
 
 
 # ---------------------------------------------------------------------- dist
+class stdout_to_stderr:
+    """File descriptor 1 points at stderr inside the block (output of native
+    libraries included)."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+        return False
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -56,8 +73,12 @@ def dist_setup():
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
+        # the communicator is created here and by the first collective; NCCL may
+        # print its version on stdout then, which must carry only the JSON line
+        with stdout_to_stderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", local))
+            barrier(world, local)
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local

@@ -41,9 +41,10 @@ namespace {
 #define HY_DEC_STAGES 3
 #endif
 constexpr int ATT_WARPS = HY_ATT_WARPS;                          // 8 decode / softmax warps
-constexpr int TC_MMA_WARP = ATT_WARPS;                           // prefill: tcgen05 issue
+constexpr int TC_MMA_WARP = ATT_WARPS;                           // prefill: tcgen05 issue, tile 0
 constexpr int TC_LOAD_WARP = ATT_WARPS + 1;                      // prefill: TMA issue
-constexpr int ATT_THREADS = (ATT_WARPS + 2) * 32;                // 320
+constexpr int TC_MMA_WARP1 = ATT_WARPS + 2;                      // prefill: tcgen05 issue, tile 1
+constexpr int ATT_THREADS = (ATT_WARPS + 3) * 32;                // 352
 constexpr int DEC_STAGES = HY_DEC_STAGES;                        // TMA ring per decode warp
 constexpr int DEC_TILE_BYTES = 2 * HY_BLOCK * HY_HEAD_DIM * 2;   // K+V of one block: 8 KB
 constexpr int DEC_WARP_BYTES = DEC_STAGES * DEC_TILE_BYTES;      // 24 KB
@@ -64,8 +65,14 @@ constexpr uint32_t TM_S = 0, TM_O = 128, TM_P = 384;
 constexpr int SMEM_PAYLOAD = ATT_WARPS * DEC_WARP_BYTES > TC_SMEM ? ATT_WARPS * DEC_WARP_BYTES
                                                                    : TC_SMEM;
 constexpr int SMEM_BYTES = SMEM_PAYLOAD + 1024;                  // + alignment slack
-constexpr int MIN_SPLIT = 4;                                     // blocks per decode item
-constexpr int ITEMS_PER_WARP = 3;                                // decode items aimed at per warp
+#ifndef HY_MIN_SPLIT
+#define HY_MIN_SPLIT 4
+#endif
+#ifndef HY_ITEMS_PER_WARP
+#define HY_ITEMS_PER_WARP 3
+#endif
+constexpr int MIN_SPLIT = HY_MIN_SPLIT;                          // blocks per decode item, at least
+constexpr int ITEMS_PER_WARP = HY_ITEMS_PER_WARP;                // decode items aimed at per warp
 constexpr int GRAB_INTS = 4;                                     // per layer: decode item, CTAs
                                                                  // done, prefill item, spare
 constexpr float NEG_INF = -INFINITY;
@@ -81,13 +88,13 @@ struct Shared {
   // per-sub-tile ones once per key tile.
   uint64_t tc_kfull[TC_NS];  // K tile landed (TMA transaction bytes)
   uint64_t tc_vfull[TC_NS];  // V tile landed
-  uint64_t tc_kfree[TC_NS];  // both S MMAs that read the K slot are done
-  uint64_t tc_vfree[TC_NS];  // both PV MMAs that read the V slot are done
+  uint64_t tc_kfree[TC_NS];  // both S MMAs that read the K slot are done (2 commits)
+  uint64_t tc_vfree[TC_NS];  // both PV MMAs that read the V slot are done (2 commits)
   uint64_t tc_sfull[2];      // S_X = Q_X K^T complete
   uint64_t tc_sfree[2];      // S_X read out by the 4 softmax warps of X
   uint64_t tc_pfull[2];      // P_X written to TMEM by the 4 softmax warps of X
   uint64_t tc_odone[2];      // O_X += P_X V complete
-  uint64_t tc_drain;         // error path: all issued MMAs complete
+  uint64_t tc_drain[2];      // error path: all MMAs an issuing warp issued are complete
   uint32_t tmem_base;        // TMEM columns from tcgen05.alloc
   int pre_item;              // prefill item handed to this CTA
 };
@@ -228,6 +235,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
 
 // ------------------------------------------------------------------ decode item
 struct MainArgs {
+  const __nv_bfloat16* cache;   // the whole cache: tensor-map row r starts at cache + 128 r
   const __nv_bfloat16* q;
   __nv_bfloat16* out;
   int q_heads, kv_heads;
@@ -524,97 +532,91 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const
   __syncthreads();
 
   if (warp == TC_LOAD_WARP) {
+    // lane 0 waits for the slot and posts the byte count; lanes 0-7 then issue
+    // the tile's 8 boxes (block lane / 2, column half lane % 2) side by side.
+    // (The TMA unit takes a 2 KB box about every 90 cycles, which bounds the
+    // K/V supply; 16-byte cp.async copies from one warp measured slower.)
     const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
     const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
     int ids = -1;                               // lane i: block 32 (t / 8) + i of the sequence
-    int issued = 0;
+    int issued[2] = {0, 0};                     // tiles whose K / V loads were issued
     for (int t = 0; t < ntiles && ok; ++t) {
       if ((t & 7) == 0) {
         const int b = 4 * t + lane;
         ids = (b < nblk && b < a.bt_pitch) ? bt[b] : -1;
       }
-      int id[4];
-#pragma unroll
-      for (int jb = 0; jb < 4; ++jb) id[jb] = __shfl_sync(0xffffffffu, ids, (4 * t + jb) & 31);
-      if (lane == 0) {
-        const uint32_t c = c0 + t, slot = c % TC_NS, use = c / TC_NS;
+      const int id = __shfl_sync(0xffffffffu, ids, (4 * t + (lane >> 1)) & 31);
+      const uint32_t c = c0 + t, slot = c % TC_NS, use = c / TC_NS;
 #pragma unroll 1
-        for (int kv = 0; kv < 2 && ok; ++kv) {
-          if (!mbar_wait(kv ? &sh.tc_vfree[slot] : &sh.tc_kfree[slot], (use & 1) ^ 1, a.err)) {
-            ok = false;
-            break;
-          }
-          uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
-          mbar_arrive_expect_tx(full, TC_KV_BYTES);
-          uint8_t* dst = payload + (kv ? TC_V_OFF : TC_K_OFF) + slot * TC_KV_BYTES;
-#pragma unroll
-          for (int jb = 0; jb < 4; ++jb) {
-            int r = a.oob_row;                  // past the end: zero fill
-            if (id[jb] >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
-            else if (id[jb] >= 0) r = kv_row(a, id[jb], kv, g);
-            tma_load_2d(dst + jb * 2048, map, 0, r, full);
-            tma_load_2d(dst + TC_HALF + jb * 2048, map, 64, r, full);
-          }
+      for (int kv = 0; kv < 2; ++kv) {
+        bool w_ok = true;
+        if (lane == 0)
+          w_ok = mbar_wait(kv ? &sh.tc_vfree[slot] : &sh.tc_kfree[slot], (use & 1) ^ 1, a.err);
+        if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) { ok = false; break; }
+        uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
+        if (lane == 0) mbar_arrive_expect_tx(full, TC_KV_BYTES);
+        if (lane < 8) {
+          const int jb = lane >> 1, hf = lane & 1;
+          int r = a.oob_row;                    // past the end: zero fill
+          if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
+          else if (id >= 0) r = kv_row(a, id, kv, g);
+          tma_load_2d(payload + (kv ? TC_V_OFF : TC_K_OFF) + slot * TC_KV_BYTES + hf * TC_HALF +
+                          jb * 2048, map, 64 * hf, r, full);
         }
-        if (ok) issued = t + 1;
+        issued[kv] = t + 1;
       }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     }
     if (!ok && lane == 0) {                     // loads still in flight must land first
-      for (int t = max(0, issued - TC_NS); t < issued; ++t) {
-        const uint32_t c = c0 + t;
-        mbar_wait(&sh.tc_kfull[c % TC_NS], (c / TC_NS) & 1, nullptr);
-        mbar_wait(&sh.tc_vfull[c % TC_NS], (c / TC_NS) & 1, nullptr);
-      }
+      for (int kv = 0; kv < 2; ++kv)
+        for (int t = max(0, issued[kv] - TC_NS); t < issued[kv]; ++t) {
+          const uint32_t c = c0 + t;
+          mbar_wait(kv ? &sh.tc_vfull[c % TC_NS] : &sh.tc_kfull[c % TC_NS], (c / TC_NS) & 1,
+                    nullptr);
+        }
     }
-  } else if (warp == TC_MMA_WARP) {
+  } else if (warp == TC_MMA_WARP || warp == TC_MMA_WARP1) {
+    // one MMA warp per sub-tile X: its lane 0 issues S_X(t), then O_X += P_X(t-1)
+    // V_{t-1}; both warps commit to the K and V slots' free barriers (count 2)
+    const int X = warp == TC_MMA_WARP ? 0 : 1;
     if (lane == 0) {
       constexpr uint32_t ID_S = tc_idesc_bf16(128, TC_KEYS, false);
       constexpr uint32_t ID_O = tc_idesc_bf16(128, HY_HEAD_DIM, true);
+      const uint64_t dQ = tc_desc_sw128(sbase + X * TC_Q_BYTES, 16, 1024);
       for (int t = 0; t <= ntiles && ok; ++t) {
         if (t < ntiles) {                       // S_X(t) = Q_X K_t^T
           const uint32_t c = c0 + t, slot = c % TC_NS;
-          ok = mbar_wait(&sh.tc_kfull[slot], (c / TC_NS) & 1, a.err);
-          const uint64_t dK = tc_desc_sw128(sbase + TC_K_OFF + slot * TC_KV_BYTES, 16, 1024);
-#pragma unroll 1
-          for (int X = 0; X < 2 && ok; ++X) {
-            ok = mbar_wait(&sh.tc_sfree[X], (c & 1) ^ 1, a.err);   // S_X(t-1) read out
-            if (!ok) break;
-            tc_fence_after();
-            const uint64_t dQ = tc_desc_sw128(sbase + X * TC_Q_BYTES, 16, 1024);
-#pragma unroll
-            for (int kk = 0; kk < HY_HEAD_DIM / 16; ++kk)
-              tc_mma_bf16(tmem + TM_S + 64 * X,
-                          dQ + (uint64_t)((((kk >> 2) * (TC_Q_BYTES / 2)) + (kk & 3) * 32) >> 4),
-                          dK + (uint64_t)((((kk >> 2) * TC_HALF) + (kk & 3) * 32) >> 4), ID_S,
-                          kk > 0);
-            tc_commit(&sh.tc_sfull[X]);
-          }
+          ok = mbar_wait(&sh.tc_kfull[slot], (c / TC_NS) & 1, a.err) &&
+               mbar_wait(&sh.tc_sfree[X], (c & 1) ^ 1, a.err);     // S_X(t-1) read out
           if (!ok) break;
+          tc_fence_after();
+          const uint64_t dK = tc_desc_sw128(sbase + TC_K_OFF + slot * TC_KV_BYTES, 16, 1024);
+#pragma unroll
+          for (int kk = 0; kk < HY_HEAD_DIM / 16; ++kk)
+            tc_mma_bf16(tmem + TM_S + 64 * X,
+                        dQ + (uint64_t)((((kk >> 2) * (TC_Q_BYTES / 2)) + (kk & 3) * 32) >> 4),
+                        dK + (uint64_t)((((kk >> 2) * TC_HALF) + (kk & 3) * 32) >> 4), ID_S,
+                        kk > 0);
+          tc_commit(&sh.tc_sfull[X]);
           tc_commit(&sh.tc_kfree[slot]);
         }
         if (t > 0) {                            // O_X += P_X(t-1) V_{t-1}
           const uint32_t c = c0 + t - 1, slot = c % TC_NS;
-          ok = mbar_wait(&sh.tc_vfull[slot], (c / TC_NS) & 1, a.err);
-          const uint64_t dV = tc_desc_sw128(sbase + TC_V_OFF + slot * TC_KV_BYTES, TC_HALF, 1024);
-#pragma unroll 1
-          for (int X = 0; X < 2 && ok; ++X) {
-            ok = mbar_wait(&sh.tc_pfull[X], c & 1, a.err);
-            if (!ok) break;
-            tc_fence_after();
-#pragma unroll
-            for (int kk = 0; kk < TC_KEYS / 16; ++kk)
-              tc_mma_bf16_ta(tmem + TM_O + 128 * X, tmem + TM_P + 32 * X + 8 * kk,
-                             dV + (uint64_t)((kk * 2048) >> 4), ID_O, (t > 1 || kk > 0));
-            tc_commit(&sh.tc_odone[X]);
-          }
+          ok = mbar_wait(&sh.tc_vfull[slot], (c / TC_NS) & 1, a.err) &&
+               mbar_wait(&sh.tc_pfull[X], c & 1, a.err);
           if (!ok) break;
+          tc_fence_after();
+          const uint64_t dV = tc_desc_sw128(sbase + TC_V_OFF + slot * TC_KV_BYTES, TC_HALF, 1024);
+#pragma unroll
+          for (int kk = 0; kk < TC_KEYS / 16; ++kk)
+            tc_mma_bf16_ta(tmem + TM_O + 128 * X, tmem + TM_P + 32 * X + 8 * kk,
+                           dV + (uint64_t)((kk * 2048) >> 4), ID_O, (t > 1 || kk > 0));
+          tc_commit(&sh.tc_odone[X]);
           tc_commit(&sh.tc_vfree[slot]);
         }
       }
       if (!ok) {                                // let every issued MMA finish
-        tc_commit(&sh.tc_drain);
-        mbar_wait(&sh.tc_drain, 0, nullptr);
+        tc_commit(&sh.tc_drain[X]);
+        mbar_wait(&sh.tc_drain[X], 0, nullptr);
       }
     }
     __syncwarp();
@@ -739,8 +741,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     for (int s = 0; s < TC_NS; ++s) {
       mbar_init(&sh.tc_kfull[s], 1);
       mbar_init(&sh.tc_vfull[s], 1);
-      mbar_init(&sh.tc_kfree[s], 1);
-      mbar_init(&sh.tc_vfree[s], 1);
+      mbar_init(&sh.tc_kfree[s], 2);            // one commit per MMA warp
+      mbar_init(&sh.tc_vfree[s], 2);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&sh.tc_sfull[x], 1);
@@ -748,7 +750,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
       mbar_init(&sh.tc_pfull[x], 4);
       mbar_init(&sh.tc_odone[x], 1);
     }
-    mbar_init(&sh.tc_drain, 1);
+    mbar_init(&sh.tc_drain[0], 1);
+    mbar_init(&sh.tc_drain[1], 1);
     fence_mbar_init();
   }
   // set-up that reads nothing an earlier kernel wrote runs before the wait: the
@@ -947,7 +950,8 @@ cudaError_t hy_launch_attn_plan(const int32_t* cu_q, const int32_t* seq_lens_k, 
                    kv_heads, hy_attn_warp_slots(dev), make_view(ws, d), err);
 }
 
-cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* q, void* out, int q_heads,
+cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* cache, const void* q, void* out,
+                                int q_heads,
                                 int kv_heads, int layer_row_base, int oob_row, int num_blocks,
                                 const int32_t* block_tables, int bt_pitch,
                                 const int32_t* seq_bt_row, const int32_t* cu_q,
@@ -965,6 +969,7 @@ cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* q, void* out
     attr_set[dev] = true;
   }
   MainArgs a;
+  a.cache = static_cast<const __nv_bfloat16*>(cache);
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.out = static_cast<__nv_bfloat16*>(out);
   a.q_heads = q_heads;

@@ -34,7 +34,8 @@ size_t hy_attn_workspace_bytes(const PlanDims& d);
 cudaError_t hy_launch_attn_plan(const int32_t* cu_q, const int32_t* seq_lens_k, int S,
                                 int kv_heads, const PlanDims& d, void* ws, int32_t* err,
                                 int dev, cudaStream_t st);
-cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* q, void* out, int q_heads,
+cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* cache, const void* q, void* out,
+                                int q_heads,
                                 int kv_heads, int layer_row_base, int oob_row, int num_blocks,
                                 const int32_t* block_tables, int bt_pitch,
                                 const int32_t* seq_bt_row, const int32_t* cu_q,

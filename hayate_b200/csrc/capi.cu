@@ -308,7 +308,7 @@ int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tok
   int rc = kv_map_for(dev, kv_cache, rows, &map);
   if (rc) return rc;
   return cuda_result(
-      hy_launch_attn_bf16(map, q, out, q_heads, kv_heads, (int)(layer * layer_rows), (int)rows,
+      hy_launch_attn_bf16(map, kv_cache, q, out, q_heads, kv_heads, (int)(layer * layer_rows), (int)rows,
                           num_blocks, block_tables, bt_pitch, seq_bt_row, cu_seqlens_q,
                           seq_lens_k, num_seqs, scale, d, workspace, err, dev, as_stream(stream)),
       "hy_varlen_attention(bf16)");

@@ -19,16 +19,6 @@
 namespace {
 
 template <typename T> struct Pair;
-template <> struct Pair<__nv_bfloat16> {
-  using V = __nv_bfloat162;
-  static HY_DEVICE float2 load(const __nv_bfloat16* p) {
-    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
-  }
-  static HY_DEVICE void store(__nv_bfloat16* p, float a, float b) {
-    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
-  }
-  static HY_DEVICE float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
-};
 template <> struct Pair<float> {
   static HY_DEVICE float2 load(const float* p) { return *reinterpret_cast<const float2*>(p); }
   static HY_DEVICE void store(float* p, float a, float b) {
@@ -45,6 +35,8 @@ HY_DEVICE T* cache_ptr(T* layer_base, int slot, int kv, int head, int kv_heads) 
   return layer_base + ((((size_t)blk * 2 + kv) * kv_heads + head) * HY_BLOCK + j) * HY_HEAD_DIM;
 }
 
+// fp32 path (the parity build of the model): one warp per (token, head), each
+// lane holding elements (2 lane, 2 lane + 1) and their RoPE partners 64 apart.
 template <typename T>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const T* __restrict__ qkv, int ld, int T_tokens, int q_heads, int kv_heads,

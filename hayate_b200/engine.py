@@ -36,6 +36,32 @@ from .config import EngineConfig, ModelConfig, QWEN3_4B, TINY
 from .model import Runner
 from .scheduler import SAMPLE, Scheduler, StepPlan, graph_bucket
 
+
+class _NoRange:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NO_RANGE = _NoRange()
+
+
+class _Range:
+    """An NVTX range (torch.cuda.nvtx) as a context manager."""
+
+    def __init__(self, name: str):
+        self.name = name
+
+    def __enter__(self):
+        torch.cuda.nvtx.range_push(self.name)
+        return self
+
+    def __exit__(self, *exc):
+        torch.cuda.nvtx.range_pop()
+        return False
+
 MODEL_CONFIGS = {"Qwen/Qwen3-4B": QWEN3_4B, "qwen3-4b": QWEN3_4B, "tiny": TINY}
 
 
@@ -121,6 +147,7 @@ class Engine:
         del embed, layers
         self.scheduler = Scheduler(self.ecfg, self.runner.num_blocks, self.runner.max_reqs)
         self.use_graphs = bool(compile or self.ecfg.cuda_graphs)
+        self.trace = bool(self.ecfg.trace or os.environ.get("HY_NVTX") == "1")
         self._graphs: Dict[int, torch.cuda.CUDAGraph] = {}
         self._graph_pool = None
         S = self.ecfg.max_num_seqs
@@ -170,25 +197,31 @@ class Engine:
         on the device) and then reads back the previous step's tokens, so the
         host's bookkeeping overlaps the GPU's work.  Requests therefore report
         completion one call after their last token is sampled."""
-        self._drain_pool()
-        sch = self.scheduler
-        for r in sch.admit():
-            self._upload_prompt(r)
+        rng = self._range
+        with rng("admit"):
+            self._drain_pool()
+            sch = self.scheduler
+            for r in sch.admit():
+                self._upload_prompt(r)
         launched = False
         if sch.running:
-            plan = sch.schedule()
+            with rng("schedule"):
+                plan = sch.schedule()
             if plan.num_seqs:
                 prev = self._inflight
-                self._inflight = self._launch(plan)
+                with rng("launch"):
+                    self._inflight = self._launch(plan)
                 launched = True
                 if prev is not None:
-                    self._collect(*prev)
+                    with rng("collect"):
+                        self._collect(*prev)
         if not launched:
             if self._inflight is None:
                 self.current_batch = [r for r in sch.running if not r.is_completed]
                 return bool(sch.running)
             prev, self._inflight = self._inflight, None
-            self._collect(*prev)
+            with rng("collect"):
+                self._collect(*prev)
         self.current_batch = [r for r in sch.running if not r.is_completed]
         return True
 
@@ -208,6 +241,9 @@ class Engine:
         return requests[0] if len(requests) == 1 else requests
 
     # ------------------------------------------------------------------ internals
+    def _range(self, name: str):
+        return _Range(name) if self.trace else _NO_RANGE
+
     def _drain_pool(self):
         while not self.pool.empty():
             r = self.pool.get()

@@ -30,11 +30,13 @@ import numpy as np
 import torch
 
 
-def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True):
-    """The ragged attention operator case: returns timing + algorithmic bytes."""
+def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True,
+                    ctx_lo: int = 256, ctx_hi: int = 16384):
+    """The ragged attention operator case: returns timing + algorithmic bytes.
+    ``ctx_lo``/``ctx_hi`` bound the log-uniform decode contexts."""
     from hayate_b200 import kernels as K
     from hayate_b200.workloads import attn_micro
-    w = attn_micro(seed=0, n_decode=n_decode)
+    w = attn_micro(seed=0, n_decode=n_decode, lo=ctx_lo, hi=ctx_hi)
     if not prefill:
         w.prefill_prior = []
     q_lens, kv_lens = w.q_lens(), w.seq_lens_k()
@@ -271,9 +273,10 @@ def argmax_micro(iters: int = 20, rows: int = 260, vocab: int = 151936):
 OPS = ("attention", "qk_norm_rope", "kv_append", "pack", "argmax")
 
 
-def run_op(op: str, iters: int, n_decode: int = 256, prefill: bool = True, tokens: int = 2304):
+def run_op(op: str, iters: int, n_decode: int = 256, prefill: bool = True, tokens: int = 2304,
+           ctx_lo: int = 256, ctx_hi: int = 16384):
     if op == "attention":
-        r = attention_micro(iters, n_decode, prefill)
+        r = attention_micro(iters, n_decode, prefill, ctx_lo, ctx_hi)
         r["op"] = op
         r["gbs"] = r["bytes"] / (r["ms_mean"] * 1e-3) / 1e9
         return r
@@ -295,10 +298,13 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="attention: decode sequences only")
     ap.add_argument("--tokens", type=int, default=2304,
                     help="query tokens of the batch for the append, pack and argmax ops")
+    ap.add_argument("--ctx-lo", type=int, default=256, help="attention: shortest decode context")
+    ap.add_argument("--ctx-hi", type=int, default=16384, help="attention: longest decode context")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     for op in (OPS if a.op == "all" else (a.op,)):
-        print(json.dumps(run_op(op, a.iters, a.decode, not a.no_prefill, a.tokens)), flush=True)
+        print(json.dumps(run_op(op, a.iters, a.decode, not a.no_prefill, a.tokens, a.ctx_lo,
+                                a.ctx_hi)), flush=True)
 
 
 if __name__ == "__main__":

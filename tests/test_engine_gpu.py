@@ -81,6 +81,16 @@ def test_engine_api_shapes():
     assert s.prompt_tokens == list(b"hi") and s.response is not None
 
 
+def test_trace_ranges_leave_tokens_unchanged():
+    """NVTX ranges around the step phases change nothing the engine computes."""
+    sc = TINY_GOLD["scenarios"][sorted(TINY_GOLD["scenarios"])[0]]
+    plain = run_scenario(tiny_engine(torch.float32, True), sc)
+    eng = tiny_engine(torch.float32, True)
+    eng.trace = True
+    traced = run_scenario(eng, sc)
+    assert [r.tokens for r in traced] == [r.tokens for r in plain]
+
+
 FULL = json.load(open(os.path.join(GOLDEN, "full_greedy.json")))
 
 
