@@ -124,9 +124,15 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 // shuffle.  Rounding points and the order of the products are those of the
 // kernel above; only the order of the sum of squares differs (8 in-lane terms,
 // then a 16-lane butterfly).
+#ifndef HY_QNR_UNROLL
+#define HY_QNR_UNROLL 1
+#endif
+#ifndef HY_QNR_MIN_CTAS
+#define HY_QNR_MIN_CTAS 1
+#endif
 constexpr int QNR_THREADS = 256;
 constexpr int QNR_GROUPS = QNR_THREADS / 16;        // head rows per unit
-constexpr int QNR_UNROLL = 2;                       // units in flight per CTA
+constexpr int QNR_UNROLL = HY_QNR_UNROLL;           // units in flight per CTA
 
 HY_DEVICE void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -146,7 +152,7 @@ HY_DEVICE uint4 f32_to_bf16x8(const float (&f)[8]) {
   return u;
 }
 
-__global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
+__global__ void __launch_bounds__(QNR_THREADS, HY_QNR_MIN_CTAS) qk_norm_rope_bf16_kernel(
     const __nv_bfloat16* __restrict__ qkv, int ld, int T_tokens, int q_heads, int kv_heads,
     const int32_t* __restrict__ positions, const __nv_bfloat16* __restrict__ q_w,
     const __nv_bfloat16* __restrict__ k_w, const float* __restrict__ rope_cos,
@@ -247,8 +253,11 @@ __global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
 // vector per lane of a lane group (16 lanes for bf16, 32 for fp32); item
 // i = token * 2 * kv_heads + row (K rows, then V rows); KVA_UNROLL items'
 // loads are in flight per lane before the stores.
+#ifndef HY_KVA_UNROLL
+#define HY_KVA_UNROLL 4
+#endif
 constexpr int KVA_THREADS = 256;
-constexpr int KVA_UNROLL = 4;
+constexpr int KVA_UNROLL = HY_KVA_UNROLL;
 
 template <typename T>
 __global__ void __launch_bounds__(KVA_THREADS) kv_append_kernel(

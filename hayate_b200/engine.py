@@ -34,7 +34,7 @@ from . import kernels as K
 from . import weights as Wt
 from .config import EngineConfig, ModelConfig, QWEN3_4B, TINY
 from .model import Runner
-from .scheduler import SAMPLE, Scheduler, StepPlan, graph_bucket
+from .scheduler import SAMPLE, Scheduler, StepPlan, graph_bucket, graph_buckets
 
 
 class _NoRange:
@@ -378,6 +378,28 @@ class Engine:
             r.launch_step(Sp, Sp, Sp)
         self._graphs[Sp] = g
         return g
+
+    def capture_graphs(self, sizes: Optional[List[int]] = None) -> int:
+        """Capture the decode-step graphs of the given batch buckets (all of them by
+        default) ahead of use, so that no capture happens inside a timed run.  The
+        graphs record launches over the step buffers; here every row is the padding
+        slot, and a replay reads the real schedule.  Call while no step is in
+        flight; returns how many graphs were captured."""
+        if not self.use_graphs:
+            return 0
+        if self._inflight is not None:
+            raise RuntimeError("capture_graphs: a step is still in flight")
+        self._ensure_pad_slot()
+        pad = self.scheduler.pad_slot
+        n = 0
+        for Sp in (sizes or graph_buckets(self.ecfg.max_num_seqs)):
+            if Sp in self._graphs:
+                continue
+            self._write_sched([(pad, 0, 1, SAMPLE)] * Sp, self._step_idx & 1)
+            self._capture(Sp)
+            torch.cuda.current_stream().synchronize()  # the host schedule buffer is reused
+            n += 1
+        return n
 
     # ------------------------------------------------------------------ info
     def check_device_errors(self) -> int:

@@ -137,7 +137,7 @@ def _batch_rows(n_decode: int, tokens: int):
     pre = [0, 512, 1536, 3584]
     k = 0
     while sum(q) + 512 <= tokens:
-        prior.append(pre[k % 4] + 4096 * (k // 4))
+        prior.append(pre[k % 4] + 4096 * ((k // 4) % 8))   # positions stay < 32768 + 512
         q.append(512)
         k += 1
     return prior, q

@@ -48,12 +48,15 @@ def _replica_main(rank, factory, factory_kwargs, in_q, out_q, heartbeat):
     """Replica process: feed requests into the engine, step it, report results."""
     from .engine import Request
     eng = factory(rank, **factory_kwargs)
+    capture = getattr(eng, "capture_graphs", None)
+    if capture is not None:              # decode graphs for every batch size, before timing
+        capture()
     live: Dict[int, object] = {}
     heartbeat[rank] = time.time()
     out_q.put(("ready", rank, None, None))
     while True:
-        try:
-            msg = in_q.get(timeout=0.05 if live else 0.5)
+        try:                             # never block while requests are in flight
+            msg = in_q.get_nowait() if live else in_q.get(timeout=0.5)
         except queue.Empty:
             msg = None
         while msg is not None:

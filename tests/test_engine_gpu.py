@@ -91,6 +91,18 @@ def test_trace_ranges_leave_tokens_unchanged():
     assert [r.tokens for r in traced] == [r.tokens for r in plain]
 
 
+def test_graphs_captured_ahead_give_the_same_tokens():
+    """Decode graphs captured up front (padding-slot schedules) replay real steps."""
+    name = sorted(TINY_GOLD["scenarios"])[-1]
+    sc = TINY_GOLD["scenarios"][name]
+    eng = tiny_engine(torch.float32, True)
+    assert eng.capture_graphs() == len(eng._graphs) > 0
+    got = run_scenario(eng, sc)
+    want = [r["tokens"] for r in sc["requests"]]
+    assert [r.tokens for r in got] == want
+    assert eng.check_device_errors() == 0
+
+
 FULL = json.load(open(os.path.join(GOLDEN, "full_greedy.json")))
 
 
