@@ -223,6 +223,30 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
     __syncthreads();
   }
   if (threadIdx.x < 64 * GRAB_INTS) v.grab[threadIdx.x] = 0;
+  // Prefill items ordered by their key tiles, most first (a counting sort over
+  // PLAN_THREADS cost bins), so that CTAs pulling them in order start the
+  // longest ones first whatever the order of the sequences in the batch.
+  __syncthreads();                              // the items above are written
+  const int np = s_bad ? 0 : min(s_cpre, v.max_pre);
+  __shared__ int bins[PLAN_THREADS];
+  auto cost_bin = [&](int4 it) {                // bin 0 = most key tiles
+    const int q = cu_q[it.x + 1] - cu_q[it.x], kv = seq_lens_k[it.x];
+    const int tiles = (kv - q + it.z + min(PRE_QROWS, q - it.z) + TC_KEYS - 1) / TC_KEYS;
+    return PLAN_THREADS - 1 - min(max(tiles, 0), PLAN_THREADS - 1);
+  };
+  bins[threadIdx.x] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < np; i += PLAN_THREADS) atomicAdd(&bins[cost_bin(v.pre[i])], 1);
+  __syncthreads();
+  int nbin_total;
+  const int start = plan_scan(bins[threadIdx.x], ws, nbin_total);
+  __syncthreads();
+  bins[threadIdx.x] = start;
+  __syncthreads();
+  for (int i = threadIdx.x; i < np; i += PLAN_THREADS) {
+    const int4 it = v.pre[i];
+    v.pre_sorted[atomicAdd(&bins[cost_bin(it)], 1)] = it;
+  }
   if (threadIdx.x == 0) {
     const bool bad = s_bad != 0;
     v.header[0] = bad ? 0 : min(s_cpre, v.max_pre);
@@ -500,7 +524,7 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const
                                 int item, uint8_t* payload, Shared& sh, uint32_t tmem,
                                 uint32_t& ctr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int4 it = v.pre[item];
+  const int4 it = v.pre_sorted[item];
   const int seq = it.x, g = it.y, t0 = it.z;
   const int row0 = a.cu_q[seq];
   const int q_len = a.cu_q[seq + 1] - row0;
@@ -772,8 +796,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   uint32_t dec_phase = 0, tile_ctr = 0;
   bool ok = true;
   int* grab = v.grab + GRAB_INTS * (a.layer & 63);
-  // prefill items: CTA-wide, heaviest first (within a sequence later tiles see
-  // more keys; sequences with longer prefixes come later in a batch)
+  // prefill items: CTA-wide, in the plan's order (most key tiles first)
   if (use_tmem) {
     while (ok) {
       if (threadIdx.x == 0) sh.pre_item = atomicAdd(&grab[2], 1);
@@ -781,7 +804,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
       const int k = sh.pre_item;
       __syncthreads();                          // read before thread 0 writes the next one
       if (k >= n_pre) break;
-      ok = prefill_item_tc(&kv_map, a, v, n_pre - 1 - k, payload, sh, tmem, tile_ctr);
+      ok = prefill_item_tc(&kv_map, a, v, k, payload, sh, tmem, tile_ctr);
     }
   }
   // decode items (warps 0..ATT_WARPS-1): each warp takes the next one from this
@@ -909,6 +932,7 @@ static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 size_t hy_attn_workspace_bytes(const PlanDims& d) {
   size_t off = 256;                                         // header
   off = align256(off + (size_t)d.max_pre * sizeof(int4));
+  off = align256(off + (size_t)d.max_pre * sizeof(int4));  // sorted prefill items
   off = align256(off + (size_t)d.max_dec * sizeof(int4));
   off = align256(off + (size_t)d.max_seqs * sizeof(int2));
   off = align256(off + (size_t)d.max_dec * HY_GROUP * HY_HEAD_DIM * sizeof(float));
@@ -925,6 +949,8 @@ static PlanView make_view(void* ws, const PlanDims& d) {
   v.header = reinterpret_cast<int*>(p);
   off = 256;
   v.pre = reinterpret_cast<int4*>(p + off);
+  off = align256(off + (size_t)d.max_pre * sizeof(int4));
+  v.pre_sorted = reinterpret_cast<int4*>(p + off);
   off = align256(off + (size_t)d.max_pre * sizeof(int4));
   v.dec = reinterpret_cast<int4*>(p + off);
   off = align256(off + (size_t)d.max_dec * sizeof(int4));

@@ -17,7 +17,8 @@ struct PlanDims {
 // Device view of a workspace (see attention.cu for the layout).
 struct PlanView {
   int* header;        // n_pre, n_dec, split, status
-  int4* pre;
+  int4* pre;          // prefill items by sequence (plan scratch)
+  int4* pre_sorted;   // the same items, most key tiles first (what the kernel runs)
   int4* dec;
   int2* seqinfo;      // per sequence: first decode item, number of splits
   float* part_o;      // [max_dec][4][128]
