@@ -6,10 +6,11 @@ contexts 0, 512, 1536, 3584), 32 query / 8 KV heads, head_dim 128, bf16 Q/K/V
 ~ N(0,1), paged KV in 16-token blocks behind a randomly permuted block table,
 one layer.  Its KV (~4 GB) is far larger than L2, so launches need no flush.
 
-qk_norm_rope / kv_append / pack / argmax: the same batch (2304 query tokens:
-256 decode rows + 4 x 512 prefill rows) through the fused QK-norm+RoPE+append
-kernel, the standalone KV append, the packing kernel and the greedy argmax over
-the 256+4 sampled rows (vocab 151936).  These inputs fit in L2, so each timed
+qk_norm_rope / kv_append / pack / argmax / add_rms_norm / silu_mul: the same
+batch (2304 query tokens: 256 decode rows + 4 x 512 prefill rows) through the
+fused QK-norm+RoPE+append kernel, the standalone KV append, the packing kernel,
+the greedy argmax over the 256+4 sampled rows (vocab 151936), and the residual
+add + RMSNorm (hidden 2560) and SiLU(gate)*up (9728) on its rows.  These inputs fit in L2, so each timed
 launch is preceded by an L2 flush outside the timed window: a read of 256 MiB,
 which evicts the op's data without leaving dirty lines whose write-back the
 timed launch would pay.
@@ -17,7 +18,8 @@ timed launch would pay.
 batches).  Every op reports its algorithmic bytes; packing is latency-bound,
 so its microseconds are the figure of merit.
 
-``python -m hayate_b200.microbench [--op attention|qk_norm_rope|kv_append|pack|argmax|all]
+``python -m hayate_b200.microbench [--op attention|qk_norm_rope|kv_append|pack|argmax|
+add_rms_norm|silu_mul|all]
 [--iters N]`` prints one JSON line per op.
 """
 from __future__ import annotations
@@ -270,7 +272,30 @@ def argmax_micro(iters: int = 20, rows: int = 260, vocab: int = 151936):
     return _summary("argmax", ms, rows * vocab * 2 + rows * 4, rows=rows)
 
 
-OPS = ("attention", "qk_norm_rope", "kv_append", "pack", "argmax")
+def rowwise_micro(op: str, iters: int = 20, rows: int = 2304, hidden: int = 2560,
+                  inter: int = 9728):
+    """Residual add + RMSNorm over [rows][hidden] (``add_rms_norm``) or SiLU(gate) * up
+    over [rows][2 inter] (``silu_mul``), bf16, Qwen3-4B widths."""
+    from hayate_b200 import kernels as K
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    if op == "add_rms_norm":
+        x = torch.randn(rows, hidden, device=dev, dtype=torch.bfloat16, generator=g)
+        d = torch.randn(rows, hidden, device=dev, dtype=torch.bfloat16, generator=g)
+        w = torch.ones(hidden, device=dev, dtype=torch.bfloat16)
+        y = torch.empty_like(x)
+        launch = lambda: K.add_rms_norm(x, w, 1e-6, delta=d, out=y)
+        nbytes = rows * hidden * 2 * 4 + hidden * 2            # x, delta in; x, y out; weights
+    else:
+        gu = torch.randn(rows, 2 * inter, device=dev, dtype=torch.bfloat16, generator=g)
+        y = torch.empty(rows, inter, device=dev, dtype=torch.bfloat16)
+        launch = lambda: K.silu_mul(gu, y)
+        nbytes = rows * inter * 2 * 3                           # gate, up in; product out
+    ms = _time(launch, iters, flush=True)
+    return _summary(op, ms, nbytes, rows=rows)
+
+
+OPS = ("attention", "qk_norm_rope", "kv_append", "pack", "argmax", "add_rms_norm", "silu_mul")
 
 
 def run_op(op: str, iters: int, n_decode: int = 256, prefill: bool = True, tokens: int = 2304,
@@ -286,6 +311,8 @@ def run_op(op: str, iters: int, n_decode: int = 256, prefill: bool = True, token
         return pack_micro(iters, n_decode, tokens)
     if op == "argmax":
         return argmax_micro(iters, rows=max(1, n_decode + max(0, tokens - n_decode) // 512))
+    if op in ("add_rms_norm", "silu_mul"):
+        return rowwise_micro(op, iters, rows=max(1, tokens))
     raise ValueError(f"unknown op {op!r}; one of {OPS} or 'all'")
 
 

@@ -20,7 +20,8 @@ def test_benchmark_modes_small():
     assert rows[1][1]["generated_tokens"] == 24
 
 
-@pytest.mark.parametrize("op", ["qk_norm_rope", "kv_append", "pack", "argmax", "attention"])
+@pytest.mark.parametrize("op", ["qk_norm_rope", "kv_append", "pack", "argmax", "attention",
+                                "add_rms_norm", "silu_mul"])
 def test_operator_microbench_small(op):
     from hayate_b200.microbench import run_op
     r = run_op(op, iters=2, n_decode=16, prefill=True, tokens=16 + 512)

@@ -103,6 +103,35 @@ def test_graphs_captured_ahead_give_the_same_tokens():
     assert eng.check_device_errors() == 0
 
 
+_PDL_SCRIPT = """
+import json, sys, torch
+sys.path.insert(0, {tests!r})
+from test_engine_gpu import tiny_engine, run_scenario, TINY_GOLD
+sc = TINY_GOLD["scenarios"][{name!r}]
+eng = tiny_engine(torch.bfloat16, True)
+print(json.dumps([r.tokens for r in run_scenario(eng, sc)]))
+"""
+
+
+def test_programmatic_launch_changes_no_token():
+    """The step's kernels start early under programmatic dependent launch and wait
+    for their inputs on the device; the same bf16 run without it (HY_PDL=0, read
+    once per process) gives the same tokens."""
+    import subprocess
+    import sys
+    name = sorted(TINY_GOLD["scenarios"])[-1]
+    here = os.path.dirname(os.path.abspath(__file__))
+    with_pdl = [r.tokens for r in run_scenario(tiny_engine(torch.bfloat16, True),
+                                               TINY_GOLD["scenarios"][name])]
+    env = dict(os.environ, HY_PDL="0")
+    out = subprocess.run([sys.executable, "-c", _PDL_SCRIPT.format(tests=here, name=name)],
+                         env=env, capture_output=True, text=True, timeout=600,
+                         cwd=os.path.dirname(here))
+    assert out.returncode == 0, out.stderr[-2000:]
+    without = json.loads(out.stdout.strip().splitlines()[-1])
+    assert with_pdl == without
+
+
 FULL = json.load(open(os.path.join(GOLDEN, "full_greedy.json")))
 
 
