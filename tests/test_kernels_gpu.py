@@ -387,7 +387,7 @@ def _ulp_diff_bf16(a, b):
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("cols", [2560, 256])
+@pytest.mark.parametrize("cols", [2560, 256, 4096, 1000])
 @pytest.mark.parametrize("residual", [False, True])
 def test_add_rms_norm_vs_reference(dt, cols, residual):
     x = (torch.randn(37, cols, device=dev) * 3).to(dt)
