@@ -119,20 +119,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 // Work unit = (token, pass of 16 head rows): a CTA's 16 half-warps take one
 // pass each, so a batch of T tokens spreads over T x ceil(heads / 16) CTAs (a
 // decode step of a few tokens still fills many SMs); with more units than CTAs
-// each CTA walks units QNR_UNROLL at a time, their loads issued together.  The
+// each CTA walks them one at a time, loading the next unit's position ahead.  The
 // RoPE partner of element d (d +- 64) sits 8 lanes away and comes over a
 // shuffle.  Rounding points and the order of the products are those of the
 // kernel above; only the order of the sum of squares differs (8 in-lane terms,
 // then a 16-lane butterfly).
-#ifndef HY_QNR_UNROLL
-#define HY_QNR_UNROLL 1
-#endif
-#ifndef HY_QNR_MIN_CTAS
-#define HY_QNR_MIN_CTAS 1
-#endif
 constexpr int QNR_THREADS = 256;
 constexpr int QNR_GROUPS = QNR_THREADS / 16;        // head rows per unit
-constexpr int QNR_UNROLL = HY_QNR_UNROLL;           // units in flight per CTA
 
 HY_DEVICE void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -152,7 +145,7 @@ HY_DEVICE uint4 f32_to_bf16x8(const float (&f)[8]) {
   return u;
 }
 
-__global__ void __launch_bounds__(QNR_THREADS, HY_QNR_MIN_CTAS) qk_norm_rope_bf16_kernel(
+__global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
     const __nv_bfloat16* __restrict__ qkv, int ld, int T_tokens, int q_heads, int kv_heads,
     const int32_t* __restrict__ positions, const __nv_bfloat16* __restrict__ q_w,
     const __nv_bfloat16* __restrict__ k_w, const float* __restrict__ rope_cos,
@@ -169,82 +162,76 @@ __global__ void __launch_bounds__(QNR_THREADS, HY_QNR_MIN_CTAS) qk_norm_rope_bf1
   const int d0 = l * 8;                    // this lane's 8 elements of a row
   const int c0 = (l & 7) * 8;              // ... and their RoPE table columns
   const bool upper = l >= 8;               // elements 64..127: partner is d - 64
-  for (long u0 = blockIdx.x; u0 < units; u0 += (long)gridDim.x * QNR_UNROLL) {
-    int tok[QNR_UNROLL], hh[QNR_UNROLL];
-    uint4 raw[QNR_UNROLL];
-#pragma unroll
-    for (int u = 0; u < QNR_UNROLL; ++u) {           // the rows' loads first
-      const long unit = u0 + (long)u * gridDim.x;
-      const bool uv = unit < units;
-      tok[u] = uv ? (int)(unit / npass) : -1;
-      hh[u] = uv ? (int)(unit % npass) * QNR_GROUPS + grp : heads;
-      raw[u] = hh[u] < heads ? *reinterpret_cast<const uint4*>(
-                                   qkv + (size_t)tok[u] * ld + (size_t)hh[u] * HY_HEAD_DIM + d0)
-                             : make_uint4(0u, 0u, 0u, 0u);
+  const long step = gridDim.x;
+  long unit = blockIdx.x;
+  // the position of the next unit is loaded one unit ahead, so that a unit's
+  // cos/sin rows, its head row and its slot are all requested at once
+  int pos_next = unit < units ? positions[(int)(unit / npass)] : 0;
+  for (; unit < units; unit += step) {              // uniform over the CTA
+    const int t = (int)(unit / npass), h = (int)(unit % npass) * QNR_GROUPS + grp;
+    const bool valid = h < heads;                  // uniform over the warp's half-warps
+    int pos = pos_next;
+    const long nu = unit + step;
+    pos_next = nu < units ? positions[(int)(nu / npass)] : 0;
+    if (pos < 0 || pos >= max_pos) { hy_flag(err, HY_ERR_BOUNDS); pos = 0; }
+    const uint4 raw = valid ? *reinterpret_cast<const uint4*>(
+                                  qkv + (size_t)t * ld + (size_t)h * HY_HEAD_DIM + d0)
+                            : make_uint4(0u, 0u, 0u, 0u);
+    int slot = -1;
+    if (cache != nullptr && valid && h >= q_heads) {
+      slot = slot_mapping[t];
+      if (slot >= (long)num_blocks * HY_BLOCK) { hy_flag(err, HY_ERR_BOUNDS); slot = -1; }
     }
+    if (valid && h >= q_heads + kv_heads) {        // value head: cache copy only
+      if (slot >= 0)
+        *reinterpret_cast<uint4*>(cache_ptr(cache, slot, 1, h - q_heads - kv_heads, kv_heads) + d0) = raw;
+    }
+    float cs[8], sn[8];
+    {
+      const float4* cp = reinterpret_cast<const float4*>(rope_cos + (size_t)pos * 64 + c0);
+      const float4* sp = reinterpret_cast<const float4*>(rope_sin + (size_t)pos * 64 + c0);
+      const float4 a = cp[0], b = cp[1], e = sp[0], f = sp[1];
+      cs[0] = a.x; cs[1] = a.y; cs[2] = a.z; cs[3] = a.w; cs[4] = b.x; cs[5] = b.y; cs[6] = b.z; cs[7] = b.w;
+      sn[0] = e.x; sn[1] = e.y; sn[2] = e.z; sn[3] = e.w; sn[4] = f.x; sn[5] = f.y; sn[6] = f.z; sn[7] = f.w;
+    }
+    // every lane of the warp takes part in the shuffles below
+    float x[8];
+    bf16x8_to_f32(raw, x);
+    float ss = 0.f;
 #pragma unroll
-    for (int u = 0; u < QNR_UNROLL; ++u) {
-      const int t = tok[u], h = hh[u];
-      const bool valid = h < heads;                  // uniform over the warp's half-warps
-      if (t < 0) continue;                           // uniform over the CTA
-      int pos = positions[t];
-      if (pos < 0 || pos >= max_pos) { hy_flag(err, HY_ERR_BOUNDS); pos = 0; }
-      int slot = -1;
-      if (cache != nullptr && valid && h >= q_heads) {
-        slot = slot_mapping[t];
-        if (slot >= (long)num_blocks * HY_BLOCK) { hy_flag(err, HY_ERR_BOUNDS); slot = -1; }
-      }
-      if (valid && h >= q_heads + kv_heads) {        // value head: cache copy only
-        if (slot >= 0)
-          *reinterpret_cast<uint4*>(cache_ptr(cache, slot, 1, h - q_heads - kv_heads, kv_heads) + d0) = raw[u];
-      }
-      float cs[8], sn[8];
-      {
-        const float4* cp = reinterpret_cast<const float4*>(rope_cos + (size_t)pos * 64 + c0);
-        const float4* sp = reinterpret_cast<const float4*>(rope_sin + (size_t)pos * 64 + c0);
-        const float4 a = cp[0], b = cp[1], e = sp[0], f = sp[1];
-        cs[0] = a.x; cs[1] = a.y; cs[2] = a.z; cs[3] = a.w; cs[4] = b.x; cs[5] = b.y; cs[6] = b.z; cs[7] = b.w;
-        sn[0] = e.x; sn[1] = e.y; sn[2] = e.z; sn[3] = e.w; sn[4] = f.x; sn[5] = f.y; sn[6] = f.z; sn[7] = f.w;
-      }
-      // every lane of the warp takes part in the shuffles below
-      float x[8];
-      bf16x8_to_f32(raw[u], x);
-      float ss = 0.f;
+    for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
+    for (int o = 8; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    // mean = ss / 128 exactly (a power of two)
+    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / HY_HEAD_DIM), eps)));
+    float w[8];
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(((h < q_heads) ? q_w : k_w) + d0), w);
+    float y[8];
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-      // mean = ss / 128 exactly (a power of two)
-      const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / HY_HEAD_DIM), eps)));
-      float w[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(((h < q_heads) ? q_w : k_w) + d0), w);
-      float y[8];
+    for (int e = 0; e < 8; ++e)
+      y[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], rstd), w[e])));
+    const uint4 yb = f32_to_bf16x8(y);          // exact: y is already bf16-valued
+    uint4 pb;
+    pb.x = __shfl_xor_sync(0xffffffffu, yb.x, 8);
+    pb.y = __shfl_xor_sync(0xffffffffu, yb.y, 8);
+    pb.z = __shfl_xor_sync(0xffffffffu, yb.z, 8);
+    pb.w = __shfl_xor_sync(0xffffffffu, yb.w, 8);
+    float p[8];
+    bf16x8_to_f32(pb, p);
+    float o[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        y[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], rstd), w[e])));
-      const uint4 yb = f32_to_bf16x8(y);          // exact: y is already bf16-valued
-      uint4 pb;
-      pb.x = __shfl_xor_sync(0xffffffffu, yb.x, 8);
-      pb.y = __shfl_xor_sync(0xffffffffu, yb.y, 8);
-      pb.z = __shfl_xor_sync(0xffffffffu, yb.z, 8);
-      pb.w = __shfl_xor_sync(0xffffffffu, yb.w, 8);
-      float p[8];
-      bf16x8_to_f32(pb, p);
-      float o[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {               // lower: y*cos + (-y[d+64])*sin; upper: y*cos + y[d-64]*sin
-        const float pe = upper ? p[e] : -p[e];
-        o[e] = __fadd_rn(__fmul_rn(y[e], cs[e]), __fmul_rn(pe, sn[e]));
-      }
-      if (!valid || h >= q_heads + kv_heads) continue;
-      const uint4 ob = f32_to_bf16x8(o);
-      if (h < q_heads) {
-        if (q_out) *reinterpret_cast<uint4*>(q_out + ((size_t)t * q_heads + h) * HY_HEAD_DIM + d0) = ob;
-      } else {
-        const int kh = h - q_heads;
-        if (k_out) *reinterpret_cast<uint4*>(k_out + ((size_t)t * kv_heads + kh) * HY_HEAD_DIM + d0) = ob;
-        if (slot >= 0) *reinterpret_cast<uint4*>(cache_ptr(cache, slot, 0, kh, kv_heads) + d0) = ob;
-      }
+    for (int e = 0; e < 8; ++e) {               // lower: y*cos + (-y[d+64])*sin; upper: y*cos + y[d-64]*sin
+      const float pe = upper ? p[e] : -p[e];
+      o[e] = __fadd_rn(__fmul_rn(y[e], cs[e]), __fmul_rn(pe, sn[e]));
+    }
+    if (!valid || h >= q_heads + kv_heads) continue;
+    const uint4 ob = f32_to_bf16x8(o);
+    if (h < q_heads) {
+      if (q_out) *reinterpret_cast<uint4*>(q_out + ((size_t)t * q_heads + h) * HY_HEAD_DIM + d0) = ob;
+    } else {
+      const int kh = h - q_heads;
+      if (k_out) *reinterpret_cast<uint4*>(k_out + ((size_t)t * kv_heads + kh) * HY_HEAD_DIM + d0) = ob;
+      if (slot >= 0) *reinterpret_cast<uint4*>(cache_ptr(cache, slot, 0, kh, kv_heads) + d0) = ob;
     }
   }
 }
