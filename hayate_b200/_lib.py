@@ -30,6 +30,8 @@ SIGNATURES = {
     "hy_pack_batch": (C.c_int, [P, I32, I32, P, I32, I32, P, I32, P, P, P, I32, P, P, P, P, P,
                                 P, P, P, P]),
     "hy_free_blocks": (C.c_int, [P, I32, I32, P, I32, P, P, P, I32, P, P]),
+    "hy_free_blocks_from": (C.c_int, [P, P, I32, I32, P, I32, P, P, P, I32, P, P]),
+    "hy_push_blocks": (C.c_int, [P, I32, P, P, I32, P, P]),
     "hy_commit_tokens": (C.c_int, [P, I32, P, P, I32, P, I32, I32, P, P]),
     "hy_qk_norm_rope": (C.c_int, [I32, P, I64, I32, I32, I32, P, P, P, P, P, I32, F32, P, P, P,
                                   P, I32, P, P]),

@@ -88,6 +88,9 @@ class EngineConfig:
     cuda_graphs: bool = True
     # Treat eos as an ordinary token (fixed-length generation).
     ignore_eos: bool = False
+    # Share the KV of identical prompt prefixes (full 16-token blocks) between
+    # requests; off by default.
+    prefix_caching: bool = False
     # NVTX ranges around each step's phases (admit, schedule, launch, collect),
     # for Nsight timelines; also on when the environment sets HY_NVTX=1.
     trace: bool = False

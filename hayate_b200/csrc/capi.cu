@@ -14,8 +14,9 @@ cudaError_t hy_launch_pool_init(int32_t*, int32_t*, int, cudaStream_t);
 cudaError_t hy_launch_pack(const int32_t*, int, int, const int32_t*, int, int, int32_t*, int,
                            int32_t*, int32_t*, int32_t*, int, int32_t*, int32_t*, int32_t*,
                            int32_t*, int32_t*, int32_t*, int32_t*, int32_t*, cudaStream_t);
-cudaError_t hy_launch_free(const int32_t*, int, int, int32_t*, int, int32_t*, int32_t*,
-                           int32_t*, int, int32_t*, cudaStream_t);
+cudaError_t hy_launch_push(const int32_t*, int, int32_t*, int32_t*, int, int32_t*, cudaStream_t);
+cudaError_t hy_launch_free(const int32_t*, const int32_t*, int, int, int32_t*, int, int32_t*,
+                           int32_t*, int32_t*, int, int32_t*, cudaStream_t);
 cudaError_t hy_launch_commit(const int32_t*, int, const int32_t*, const int32_t*, int, int32_t*,
                              int, int, int32_t*, cudaStream_t);
 cudaError_t hy_launch_qk_norm_rope(int, const void*, int, int, int, int, const int32_t*,
@@ -187,9 +188,34 @@ int hy_free_blocks(const int32_t* slots, int32_t n, int32_t max_reqs, int32_t* b
   if (!slots || !block_tables || !req_num_blocks || !free_stack || !free_top || n < 0 ||
       max_reqs <= 0 || bt_pitch <= 0 || num_blocks <= 0)
     return fail(HY_E_INVALID, "hy_free_blocks: bad argument");
-  return cuda_result(hy_launch_free(slots, n, max_reqs, block_tables, bt_pitch, req_num_blocks,
-                                    free_stack, free_top, num_blocks, err, as_stream(stream)),
+  return cuda_result(hy_launch_free(slots, nullptr, n, max_reqs, block_tables, bt_pitch,
+                                    req_num_blocks, free_stack, free_top, num_blocks, err,
+                                    as_stream(stream)),
                      "hy_free_blocks");
+}
+
+int hy_free_blocks_from(const int32_t* slots, const int32_t* first_block, int32_t n,
+                        int32_t max_reqs, int32_t* block_tables, int32_t bt_pitch,
+                        int32_t* req_num_blocks, int32_t* free_stack, int32_t* free_top,
+                        int32_t num_blocks, int32_t* err, void* stream) {
+  if (n == 0) return HY_OK;
+  if (!slots || !first_block || !block_tables || !req_num_blocks || !free_stack || !free_top ||
+      n < 0 || max_reqs <= 0 || bt_pitch <= 0 || num_blocks <= 0)
+    return fail(HY_E_INVALID, "hy_free_blocks_from: bad argument");
+  return cuda_result(hy_launch_free(slots, first_block, n, max_reqs, block_tables, bt_pitch,
+                                    req_num_blocks, free_stack, free_top, num_blocks, err,
+                                    as_stream(stream)),
+                     "hy_free_blocks_from");
+}
+
+int hy_push_blocks(const int32_t* block_ids, int32_t n, int32_t* free_stack, int32_t* free_top,
+                   int32_t num_blocks, int32_t* err, void* stream) {
+  if (n == 0) return HY_OK;
+  if (!block_ids || !free_stack || !free_top || n < 0 || num_blocks <= 0)
+    return fail(HY_E_INVALID, "hy_push_blocks: bad argument");
+  return cuda_result(hy_launch_push(block_ids, n, free_stack, free_top, num_blocks, err,
+                                    as_stream(stream)),
+                     "hy_push_blocks");
 }
 
 int hy_commit_tokens(const int32_t* next_tokens, int32_t n_sample, const int32_t* sample_seq,

@@ -179,10 +179,12 @@ __global__ void __launch_bounds__(PACK_THREADS) pack_kernel(
   }
 }
 
-// Return every block of the listed slots to the free stack, slot by slot in
-// list order and block by block in position order.
+// Return the blocks of the listed slots to the free stack, slot by slot in
+// list order and block by block in position order: all of them, or (first
+// given) those from position first[i] on -- the blocks before it stay with
+// their other owner (a prefix cache).
 __global__ void __launch_bounds__(PACK_THREADS) free_kernel(
-    const int32_t* __restrict__ slots, int n, int max_reqs,
+    const int32_t* __restrict__ slots, const int32_t* __restrict__ first, int n, int max_reqs,
     int32_t* __restrict__ block_tables, int bt_pitch, int32_t* __restrict__ req_nblk,
     int32_t* __restrict__ free_stack, int32_t* __restrict__ free_top, int num_blocks,
     int32_t* err) {
@@ -192,13 +194,15 @@ __global__ void __launch_bounds__(PACK_THREADS) free_kernel(
   __syncthreads();
   for (int base = 0; base < n; base += PACK_THREADS) {
     const int i = base + threadIdx.x;
-    int slot = -1, nb = 0;
+    int slot = -1, nb = 0, f = 0;
     if (i < n) {
       slot = slots[i];
       if (slot < 0 || slot >= max_reqs) { atomicOr(&s_bad, 1); slot = -1; }
       else {
-        nb = req_nblk[slot];
-        if (nb < 0 || nb > bt_pitch) { atomicOr(&s_bad, 1); nb = 0; }
+        const int have = req_nblk[slot];
+        f = first ? first[i] : 0;
+        if (have < 0 || have > bt_pitch || f < 0 || f > have) { atomicOr(&s_bad, 1); f = 0; }
+        else nb = have - f;
       }
     }
     int tot;
@@ -207,7 +211,7 @@ __global__ void __launch_bounds__(PACK_THREADS) free_kernel(
     if (slot >= 0) {
       for (int j = 0; j < nb; ++j) {
         const int dst = top + off + j;
-        if (dst < num_blocks) free_stack[dst] = block_tables[(size_t)slot * bt_pitch + j];
+        if (dst < num_blocks) free_stack[dst] = block_tables[(size_t)slot * bt_pitch + f + j];
         else atomicOr(&s_bad, 4);
       }
       req_nblk[slot] = 0;
@@ -220,6 +224,30 @@ __global__ void __launch_bounds__(PACK_THREADS) free_kernel(
     *free_top = s_top;
     if (s_bad & 1) hy_flag(err, HY_ERR_BOUNDS);
     if (s_bad & 4) hy_flag(err, HY_ERR_POOL);
+  }
+}
+
+// Push a list of block ids (in list order) onto the free stack.  All ids are
+// checked first: one outside [0, num_blocks) or a stack without room for all
+// of them pushes nothing and sets the error bit.
+__global__ void __launch_bounds__(PACK_THREADS) push_kernel(
+    const int32_t* __restrict__ ids, int n, int32_t* __restrict__ free_stack,
+    int32_t* __restrict__ free_top, int num_blocks, int32_t* err) {
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += PACK_THREADS)
+    if (ids[i] < 0 || ids[i] >= num_blocks) atomicOr(&s_bad, 1);
+  __syncthreads();
+  const int top = *free_top;
+  if (!s_bad && top + n > num_blocks) s_bad = 4;   // read by thread 0 only below
+  __syncthreads();
+  if (s_bad == 0)
+    for (int i = threadIdx.x; i < n; i += PACK_THREADS) free_stack[top + i] = ids[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (s_bad == 0) *free_top = top + n;
+    else hy_flag(err, (s_bad & 1) ? HY_ERR_BOUNDS : HY_ERR_POOL);
   }
 }
 
@@ -273,11 +301,18 @@ cudaError_t hy_launch_pack(const int32_t* sched, int S, int T, const int32_t* re
                    sample_seq, err);
 }
 
-cudaError_t hy_launch_free(const int32_t* slots, int n, int max_reqs, int32_t* block_tables,
-                           int bt_pitch, int32_t* req_nblk, int32_t* free_stack,
-                           int32_t* free_top, int num_blocks, int32_t* err, cudaStream_t st) {
-  free_kernel<<<1, PACK_THREADS, 0, st>>>(slots, n, max_reqs, block_tables, bt_pitch, req_nblk,
-                                          free_stack, free_top, num_blocks, err);
+cudaError_t hy_launch_free(const int32_t* slots, const int32_t* first, int n, int max_reqs,
+                           int32_t* block_tables, int bt_pitch, int32_t* req_nblk,
+                           int32_t* free_stack, int32_t* free_top, int num_blocks, int32_t* err,
+                           cudaStream_t st) {
+  free_kernel<<<1, PACK_THREADS, 0, st>>>(slots, first, n, max_reqs, block_tables, bt_pitch,
+                                          req_nblk, free_stack, free_top, num_blocks, err);
+  return cudaGetLastError();
+}
+
+cudaError_t hy_launch_push(const int32_t* ids, int n, int32_t* free_stack, int32_t* free_top,
+                           int num_blocks, int32_t* err, cudaStream_t st) {
+  push_kernel<<<1, PACK_THREADS, 0, st>>>(ids, n, free_stack, free_top, num_blocks, err);
   return cudaGetLastError();
 }
 

@@ -34,6 +34,7 @@ from . import kernels as K
 from . import weights as Wt
 from .config import EngineConfig, ModelConfig, QWEN3_4B, TINY
 from .model import Runner
+from .prefix_cache import PrefixCache, cacheable_blocks
 from .scheduler import SAMPLE, Scheduler, StepPlan, graph_bucket, graph_buckets
 
 
@@ -89,6 +90,13 @@ class Request:
     _pending: int = 0             # sampled tokens launched, not yet read back
     _inflight: int = 0            # launched steps containing this request, not yet read back
     _last_launched: bool = False  # the step that samples its last token is launched
+    # prefix caching: chain hashes of the prompt's cacheable blocks, how many of
+    # its leading blocks the cache holds, the adopted block ids, and a pending
+    # read-back of the block ids its prefill wrote
+    _hashes: List[int] = field(default_factory=list)
+    _shared: int = 0
+    _shared_blocks: List[int] = field(default_factory=list)
+    _offer: Optional[tuple] = None
 
 
 class ByteTokenizer:
@@ -145,7 +153,9 @@ class Engine:
             raise ValueError(f"unknown weights source {weights!r}")
         self.runner = Runner(self.cfg, self.ecfg, dtype, self.device, embed, layers, norms)
         del embed, layers
-        self.scheduler = Scheduler(self.ecfg, self.runner.num_blocks, self.runner.max_reqs)
+        self.prefix_cache = PrefixCache() if self.ecfg.prefix_caching else None
+        self.scheduler = Scheduler(self.ecfg, self.runner.num_blocks, self.runner.max_reqs,
+                                   cache=self.prefix_cache)
         self.use_graphs = bool(compile or self.ecfg.cuda_graphs)
         self.trace = bool(self.ecfg.trace or os.environ.get("HY_NVTX") == "1")
         self._graphs: Dict[int, torch.cuda.CUDAGraph] = {}
@@ -166,6 +176,7 @@ class Engine:
         self.d2h_bytes = 0
         self.steps = 0
         self.graph_steps = 0
+        self.prompt_tokens_computed = 0     # prompt tokens that went through the model
 
     @staticmethod
     def _load_tokenizer(model_name):
@@ -203,6 +214,13 @@ class Engine:
             sch = self.scheduler
             for r in sch.admit():
                 self._upload_prompt(r)
+                if r._shared_blocks:
+                    self._adopt_blocks(r)
+            evicted = sch.take_evicted()
+            if evicted:                             # cache blocks back to the device pool
+                ids = torch.tensor(evicted, dtype=torch.int32).pin_memory()
+                self.runner.push_blocks(ids.to(self.device, non_blocking=True))
+                self.h2d_bytes += 4 * len(evicted)
         launched = False
         if sch.running:
             with rng("schedule"):
@@ -268,6 +286,17 @@ class Engine:
         self.runner.req_tokens[r.slot, :t.numel()].copy_(t, non_blocking=True)
         self.h2d_bytes += t.numel() * 4
 
+    def _adopt_blocks(self, r: Request):
+        """The request's leading blocks are the cache's: its block-table row starts
+        with them and the pack kernel allocates only what follows."""
+        k = len(r._shared_blocks)
+        ids = torch.tensor(r._shared_blocks, dtype=torch.int32).pin_memory()
+        cnt = torch.tensor([k], dtype=torch.int32).pin_memory()
+        self.runner.block_tables[r.slot, :k].copy_(ids, non_blocking=True)
+        self.runner.req_nblk[r.slot:r.slot + 1].copy_(cnt, non_blocking=True)
+        r._adopt_pinned = (ids, cnt)                # alive until the copies land
+        self.h2d_bytes += 4 * (k + 1)
+
     def _ensure_pad_slot(self):
         """The padding row of graph batches owns one block and one token."""
         if self._pad_ready:
@@ -314,10 +343,16 @@ class Engine:
         self._out_host[buf][:1 + n_read].copy_(self.runner.out_buf[:1 + n_read],
                                                 non_blocking=True)
         self.d2h_bytes += 4 * (1 + n_read)
+        if self.prefix_cache is not None:            # prefills this step completes
+            for e in plan.entries:
+                if e.flags & SAMPLE and e.req.is_prefill:
+                    self._read_prompt_blocks(e.req, plan)
         self._events[buf].record()
         # host state advances at launch: the next schedule builds on this step
         for e in plan.entries:
             r = e.req
+            if r.is_prefill:
+                self.prompt_tokens_computed += e.q_len
             r.cache_pos = e.start + e.q_len
             r._inflight += 1
             if e.flags & SAMPLE:
@@ -327,6 +362,18 @@ class Engine:
                     r._last_launched = True
         return plan, buf
 
+    def _read_prompt_blocks(self, r: Request, plan: StepPlan):
+        """With the step that ends a prefill: copy the ids of the prompt blocks it
+        wrote (past those the cache gave) to the host, for the cache to take once
+        the step is collected."""
+        n = cacheable_blocks(len(r.prompt_tokens), self.ecfg.block_size)
+        if n <= r._shared:
+            return
+        host = torch.empty(n - r._shared, dtype=torch.int32).pin_memory()
+        host.copy_(self.runner.block_tables[r.slot, r._shared:n], non_blocking=True)
+        r._offer = (r._shared, n, host, plan)
+        self.d2h_bytes += 4 * (n - r._shared)
+
     def _collect(self, plan: StepPlan, buf: int):
         """Wait for a launched step, then apply its tokens and stop conditions."""
         self._events[buf].synchronize()
@@ -334,6 +381,14 @@ class Engine:
         err = int(toks[0])
         if err:
             raise K._lib.HayateError(f"device error word {err}: {K.describe_error(err)}")
+        if self.prefix_cache is not None:
+            for e in plan.entries:
+                r = e.req
+                if r._offer is not None and r._offer[3] is plan:
+                    lo, hi, host, _ = r._offer
+                    r._offer = None
+                    taken = self.prefix_cache.offer(r._hashes[lo:hi], host.tolist())
+                    self.scheduler.offered(r, taken)
         k = 0
         for e in plan.entries:
             r = e.req
@@ -356,8 +411,12 @@ class Engine:
                 r._pinned = None
             slots = torch.tensor([r.slot for r in done], dtype=torch.int32).pin_memory()
             dslots = slots.to(self.device, non_blocking=True)
-            self.runner.free_slots(dslots)
-            self.h2d_bytes += 4 * len(done)
+            first = None
+            if self.prefix_cache is not None:        # the cache keeps the leading blocks
+                f = torch.tensor([r._shared for r in done], dtype=torch.int32).pin_memory()
+                first = f.to(self.device, non_blocking=True)
+            self.runner.free_slots(dslots, first)
+            self.h2d_bytes += 4 * len(done) * (2 if first is not None else 1)
 
     def _capture(self, Sp: int) -> torch.cuda.CUDAGraph:
         r = self.runner

@@ -77,12 +77,33 @@ def pack_batch(sched: torch.Tensor, num_seqs: int, num_tokens: int, req_tokens: 
 
 
 def free_blocks(slots: torch.Tensor, block_tables: torch.Tensor, req_num_blocks: torch.Tensor,
-                free_stack: torch.Tensor, free_top: torch.Tensor, err: torch.Tensor) -> None:
+                free_stack: torch.Tensor, free_top: torch.Tensor, err: torch.Tensor,
+                first_block: Optional[torch.Tensor] = None) -> None:
+    """Return the listed slots' blocks to the pool (from position first_block[i]
+    on, when given: the earlier blocks stay with a prefix cache)."""
     _i32(slots, "slots")
-    check(_lib.load().hy_free_blocks(
-        _ptr(slots), slots.numel(), block_tables.shape[0], _ptr(block_tables),
+    if first_block is None:
+        check(_lib.load().hy_free_blocks(
+            _ptr(slots), slots.numel(), block_tables.shape[0], _ptr(block_tables),
+            block_tables.shape[1], _ptr(req_num_blocks), _ptr(free_stack), _ptr(free_top),
+            free_stack.numel(), _ptr(err), _stream()), "hy_free_blocks")
+        return
+    _i32(first_block, "first_block")
+    if first_block.numel() != slots.numel():
+        raise ValueError("first_block needs one entry per slot")
+    check(_lib.load().hy_free_blocks_from(
+        _ptr(slots), _ptr(first_block), slots.numel(), block_tables.shape[0], _ptr(block_tables),
         block_tables.shape[1], _ptr(req_num_blocks), _ptr(free_stack), _ptr(free_top),
-        free_stack.numel(), _ptr(err), _stream()), "hy_free_blocks")
+        free_stack.numel(), _ptr(err), _stream()), "hy_free_blocks_from")
+
+
+def push_blocks(block_ids: torch.Tensor, free_stack: torch.Tensor, free_top: torch.Tensor,
+                err: torch.Tensor) -> None:
+    """Push block ids onto the free stack (blocks a prefix cache gives up)."""
+    _i32(block_ids, "block_ids")
+    check(_lib.load().hy_push_blocks(_ptr(block_ids), block_ids.numel(), _ptr(free_stack),
+                                     _ptr(free_top), free_stack.numel(), _ptr(err), _stream()),
+          "hy_push_blocks")
 
 
 def commit_tokens(next_tokens: torch.Tensor, n_sample: int, sample_seq: torch.Tensor,

@@ -193,9 +193,13 @@ class Runner:
             launches += 2
         self.kernel_launches += launches
 
-    def free_slots(self, slots: torch.Tensor) -> None:
+    def free_slots(self, slots: torch.Tensor, first_block: Optional[torch.Tensor] = None) -> None:
         K.free_blocks(slots, self.block_tables, self.req_nblk, self.free_stack, self.free_top,
-                      self.error_word)
+                      self.error_word, first_block=first_block)
+        self.kernel_launches += 1
+
+    def push_blocks(self, block_ids: torch.Tensor) -> None:
+        K.push_blocks(block_ids, self.free_stack, self.free_top, self.error_word)
         self.kernel_launches += 1
 
     # our kernels per layer: 2 add+RMSNorm, QK-norm+RoPE, attention, SiLU*up

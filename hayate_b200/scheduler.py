@@ -9,14 +9,21 @@ groups of 8 and a separate decode forward.
 Admission reserves a request's worst-case KV blocks (prompt + max_tokens) so
 the device block pool can never run dry mid-flight; no preemption is needed.
 Slot ``max_reqs - 1`` is kept for the padding rows of CUDA-graph batches.
+
+With a prefix cache, a request first takes the longest cached prefix of its
+prompt's full blocks (its prefill then starts after them) and reserves only the
+rest; blocks the cache holds are not free, and unreferenced ones are evicted
+(oldest first) when an admission needs their room.  The scheduler only counts;
+the engine moves the evicted block ids back to the device pool.
 """
 from __future__ import annotations
 
 from collections import deque
 from dataclasses import dataclass, field
-from typing import Deque, List, Tuple
+from typing import Deque, List, Optional, Tuple
 
 from .config import EngineConfig
+from .prefix_cache import PrefixCache, block_hashes, cacheable_blocks
 
 # sched flags
 SAMPLE = 1
@@ -56,15 +63,19 @@ def blocks_for(tokens: int, block_size: int) -> int:
 
 
 class Scheduler:
-    def __init__(self, cfg: EngineConfig, num_blocks: int, max_reqs: int):
+    def __init__(self, cfg: EngineConfig, num_blocks: int, max_reqs: int,
+                 cache: Optional[PrefixCache] = None):
         if cfg.max_num_seqs > cfg.max_batched_tokens:
             raise ValueError("max_num_seqs must not exceed max_batched_tokens")
         self.cfg = cfg
         self.pad_slot = max_reqs - 1
         self.free_slots: Deque[int] = deque(range(max_reqs - 1))
-        self.free_blocks = num_blocks - 1          # one block for the padding slot
+        self.total_blocks = num_blocks - 1         # one block for the padding slot
+        self.free_blocks = self.total_blocks
         self.waiting: Deque = deque()
         self.running: List = []
+        self.cache = cache
+        self.evicted: List[int] = []               # cache blocks for the device pool
 
     # ---------------------------------------------------------------- admission
     def reserve_for(self, req) -> int:
@@ -78,33 +89,60 @@ class Scheduler:
         if n + 1 > self.cfg.max_model_len:
             raise ValueError(f"request {req.id}: prompt of {n} tokens exceeds max_model_len "
                              f"{self.cfg.max_model_len}")
-        if self.reserve_for(req) > self.free_blocks + self._reserved():
+        if self.reserve_for(req) > self.total_blocks:
             raise ValueError(f"request {req.id}: needs more KV blocks than the cache holds")
-
-    def _reserved(self) -> int:
-        return sum(r._blocks for r in self.running)
 
     def admit(self) -> List:
         """Move waiting requests into the running set (FIFO, stop at the first misfit)."""
         admitted = []
         while self.waiting and len(self.running) < self.cfg.max_num_seqs and self.free_slots:
             req = self.waiting[0]
-            need = self.reserve_for(req)
+            hashes, shared = [], []
+            if self.cache is not None:
+                bs = self.cfg.block_size
+                hashes = block_hashes(req.prompt_tokens, bs,
+                                      cacheable_blocks(len(req.prompt_tokens), bs))
+                shared = self.cache.match(hashes)
+            need = self.reserve_for(req) - len(shared)
+            if need > self.free_blocks and self.cache is not None:
+                # evict idle cache blocks, never those this request is about to use
+                self.cache.acquire(hashes[:len(shared)])
+                got = self.cache.evict(need - self.free_blocks)
+                self.cache.release(hashes[:len(shared)])
+                self.evicted += got
+                self.free_blocks += len(got)
             if need > self.free_blocks:
                 break
             self.waiting.popleft()
             req.slot = self.free_slots.popleft()
             req._blocks = need
+            req._hashes = hashes
+            req._shared_blocks = list(shared)       # adopted cache blocks, in order
+            req._shared = len(shared)               # leading blocks the cache holds
+            if shared:
+                self.cache.acquire(hashes[:len(shared)])
+                req.cache_pos = len(shared) * self.cfg.block_size
             self.free_blocks -= need
             self.running.append(req)
             admitted.append(req)
         return admitted
+
+    def offered(self, req, n: int) -> None:
+        """n more of the request's prompt blocks now belong to the cache."""
+        req._shared += n
+        req._blocks -= n
 
     def release(self, req) -> None:
         self.running.remove(req)
         self.free_slots.append(req.slot)
         self.free_blocks += req._blocks
         req._blocks = 0
+        if self.cache is not None and req._shared:
+            self.cache.release(req._hashes[:req._shared])
+
+    def take_evicted(self) -> List[int]:
+        out, self.evicted = self.evicted, []
+        return out
 
     # ---------------------------------------------------------------- one step
     def schedule(self) -> StepPlan:

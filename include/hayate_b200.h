@@ -81,6 +81,23 @@ int hy_free_blocks(const int32_t* slots, int32_t n, int32_t max_reqs, int32_t* b
                    int32_t bt_pitch, int32_t* req_num_blocks, int32_t* free_stack,
                    int32_t* free_top, int32_t num_blocks, int32_t* err, void* stream);
 
+/* As hy_free_blocks, but slot slots[i] gives back only its blocks from
+ * position first_block[i] on; the blocks before it stay allocated for their
+ * other owner (a prefix cache holding them for later requests).  No reference
+ * counterpart: the reference has no block pool (its README lists prefix
+ * caching as future work, README.md:70). */
+int hy_free_blocks_from(const int32_t* slots, const int32_t* first_block, int32_t n,
+                        int32_t max_reqs, int32_t* block_tables, int32_t bt_pitch,
+                        int32_t* req_num_blocks, int32_t* free_stack, int32_t* free_top,
+                        int32_t num_blocks, int32_t* err, void* stream);
+
+/* Push n block ids onto the free stack, in order (a prefix cache evicting the
+ * blocks it held).  Nothing is pushed, and an error bit is set, if an id is
+ * outside [0, num_blocks) or the stack has no room for all of them.  No
+ * reference counterpart (see hy_free_blocks_from). */
+int hy_push_blocks(const int32_t* block_ids, int32_t n, int32_t* free_stack, int32_t* free_top,
+                   int32_t num_blocks, int32_t* err, void* stream);
+
 /* Append each sampled token to its request's token row.
  * Replaces: the device->host .item() and list append of
  * Engine._finalize_generated_token (engine.py:73-78, 178-194). */

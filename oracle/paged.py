@@ -15,7 +15,7 @@ match it bit for bit.  Its link to the reference:
 """
 from __future__ import annotations
 
-from typing import Dict, List, Sequence
+from typing import Dict, List, Optional, Sequence
 
 import numpy as np
 
@@ -89,14 +89,24 @@ def commit(st: PagedState, next_tokens: np.ndarray, sample_seq: np.ndarray,
         st.req_tokens[s, sched[1, i] + sched[2, i]] = next_tokens[k]
 
 
-def free(st: PagedState, slots: Sequence[int]) -> None:
+def free(st: PagedState, slots: Sequence[int], first: Optional[Sequence[int]] = None) -> None:
+    """Blocks of each slot (from position first[i] on, if given) back onto the
+    stack, slot by slot in list order, blocks in position order."""
     top = st.free_top
-    for s in slots:
-        n = int(st.req_nblk[s])
-        st.free_stack[top:top + n] = st.block_tables[s, :n]
+    for i, s in enumerate(slots):
+        f = 0 if first is None else int(first[i])
+        n = int(st.req_nblk[s]) - f
+        st.free_stack[top:top + n] = st.block_tables[s, f:f + n]
         top += n
         st.req_nblk[s] = 0
     st.free_top = top
+
+
+def push(st: PagedState, ids: Sequence[int]) -> None:
+    """Block ids back onto the stack in list order (a prefix cache evicting)."""
+    n = len(ids)
+    st.free_stack[st.free_top:st.free_top + n] = np.asarray(ids, np.int32)
+    st.free_top += n
 
 
 def kv_append(cache_layer: np.ndarray, k: np.ndarray, v: np.ndarray,

@@ -132,6 +132,55 @@ def test_programmatic_launch_changes_no_token():
     assert with_pdl == without
 
 
+def _tiny_cached(prefix_caching, num_kv_blocks=512, max_model_len=1024):
+    ecfg = EngineConfig(max_num_seqs=8, max_batched_tokens=256, prefill_chunk=64,
+                        num_kv_blocks=num_kv_blocks, max_model_len=max_model_len,
+                        cuda_graphs=True, prefix_caching=prefix_caching)
+    hw = W.exact_seeded(TINY, 0, std=TINY_GOLD["std"])
+    return Engine("tiny", model_config=TINY, engine_config=ecfg, dtype=torch.float32, weights=hw)
+
+
+def test_prefix_caching_shares_blocks_and_keeps_tokens():
+    """Prompts sharing a 100-token prefix: once the first has run, the others take
+    its 6 full blocks from the cache, compute 96 prompt tokens fewer each, and
+    produce the tokens of an engine without the cache."""
+    import random
+    rng = random.Random(7)
+    prefix = [rng.randrange(TINY.vocab_size) for _ in range(100)]
+    prompts = [prefix + [rng.randrange(TINY.vocab_size) for _ in range(rng.randint(1, 30))]
+               for _ in range(6)]
+    runs = {}
+    for on in (False, True):
+        eng = _tiny_cached(on)
+        first = eng.generate_text(prompts[0], max_tokens=8)
+        rest = eng.generate_text(prompts[1:], max_tokens=8)
+        assert eng.check_device_errors() == 0
+        runs[on] = ([first.tokens] + [r.tokens for r in rest], eng.prompt_tokens_computed, eng)
+    assert runs[True][0] == runs[False][0]
+    assert runs[False][1] - runs[True][1] == 5 * 96
+    assert runs[True][2].prefix_cache.held >= 6
+
+
+def test_prefix_caching_evicts_when_the_pool_is_short():
+    """Waves of distinct prompts fill a small pool with cached blocks; admissions
+    evict the idle ones and the tokens stay those of an engine without the cache."""
+    import random
+    rng = random.Random(11)
+    waves = [[[rng.randrange(TINY.vocab_size) for _ in range(rng.randint(60, 120))]
+              for _ in range(3)] for _ in range(5)]
+    out = {}
+    for on in (False, True):
+        eng = _tiny_cached(on, num_kv_blocks=40, max_model_len=200)
+        toks = []
+        for w in waves:
+            toks += [r.tokens for r in eng.generate_text(w, max_tokens=6)]
+        assert eng.check_device_errors() == 0
+        out[on] = toks
+        if on:
+            assert eng.prefix_cache.held <= 39
+    assert out[True] == out[False]
+
+
 FULL = json.load(open(os.path.join(GOLDEN, "full_greedy.json")))
 
 

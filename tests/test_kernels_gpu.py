@@ -108,6 +108,37 @@ def test_pack_commit_free_bit_exact():
     assert int(ds.err.item()) == 0
 
 
+def test_free_from_and_push_bit_exact():
+    """Prefix-cache moves of the pool: slots give back only their blocks past a
+    shared prefix, and the held prefix blocks are pushed back later in a list."""
+    rng = np.random.default_rng(3)
+    st = PS.PagedState(12, 400, 32, 200)
+    st.req_tokens[:] = rng.integers(0, 1000, size=st.req_tokens.shape)
+    ds = DeviceState(st)
+    lens = [37, 150, 16, 300, 5, 90]
+    sched = PS.make_sched(list(range(len(lens))), [0] * len(lens), lens, [1] * len(lens))
+    _pack_step(ds, st, sched, int(sum(lens)))
+    slots = [4, 1, 3, 0]
+    first = [0, 5, 2, 3]                             # blocks before these stay held
+    held = [int(b) for s, f in zip(slots, first) for b in st.block_tables[s, :f]]
+    K.free_blocks(i32(slots), ds.block_tables, ds.req_nblk, ds.free_stack, ds.free_top, ds.err,
+                  first_block=i32(first))
+    PS.free(st, slots, first)
+    order = list(rng.permutation(len(held)))
+    K.push_blocks(i32([held[i] for i in order]), ds.free_stack, ds.free_top, ds.err)
+    PS.push(st, [held[i] for i in order])
+    torch.cuda.synchronize()
+    assert int(ds.err.item()) == 0
+    assert int(ds.free_top.item()) == st.free_top
+    assert np.array_equal(ds.free_stack.cpu().numpy()[:st.free_top], st.free_stack[:st.free_top])
+    assert np.array_equal(ds.req_nblk.cpu().numpy(), st.req_nblk)
+    # a bad id pushes nothing and is reported
+    top = int(ds.free_top.item())
+    K.push_blocks(i32([3, 999]), ds.free_stack, ds.free_top, ds.err)
+    torch.cuda.synchronize()
+    assert int(ds.free_top.item()) == top and int(ds.err.item()) & K.DEV_BOUNDS
+
+
 def test_pack_reports_pool_exhaustion():
     st = PS.PagedState(4, 200, 16, 3)
     ds = DeviceState(st)
