@@ -9,8 +9,9 @@ tok/s, total tok/s, where total counts prompt + generated tokens as
 benchmark.py:187,228,296 do).  Prompts are uniform-random token ids of the
 requested lengths (no tokenizer offline).  Two more modes cover the other
 benchmark configurations: ``poisson`` (exponential inter-arrival gaps,
-log-uniform prompts, chunked prefill mixed into decodes) and ``replicas``
-(requests spread over N GPU replicas by ``router.Router``).
+log-uniform prompts, chunked prefill mixed into decodes), ``replicas``
+(requests spread over N GPU replicas by ``router.Router``) and ``shared_prefix``
+(requests with a common 1024-token prefix, without and with the prefix cache).
 
 ``python -m hayate_b200.benchmark 10 [--repetitions 5] [--max-tokens 256]
 [--seed 1337] [--arrival-gap-ms 25] [--min-prompt-tokens 160]
@@ -168,6 +169,37 @@ def bench_poisson(engine, seed, reps):
     return out
 
 
+def bench_shared_prefix(n_requests, seed, reps, prefix_caching, prefix_len=1024, max_tokens=128):
+    """Requests sharing a ``prefix_len``-token prefix (a common system prompt) with
+    unique suffixes of U[16,128] tokens, all submitted at once, on an engine with
+    or without the prefix cache.  The first request runs alone beforehand, as an
+    earlier user of the same prefix would have."""
+    rng = random.Random(seed)
+    g = torch.Generator().manual_seed(seed)
+    prefix = torch.randint(0, workloads.VOCAB, (prefix_len,), generator=g).tolist()
+    reqs = [prefix + torch.randint(0, workloads.VOCAB, (rng.randint(16, 128),),
+                                   generator=g).tolist() for _ in range(n_requests)]
+    ecfg = default_engine_config(max_tokens, prefix_len + 128).with_(prefix_caching=prefix_caching)
+    eng = Engine("Qwen/Qwen3-4B", engine_config=ecfg)
+    eng.capture_graphs()
+    eng.generate_text(reqs[0], max_tokens=max_tokens)
+    out = _result([], 0.0, 0, 0)
+    for _ in range(reps):
+        sync()
+        t0 = time.perf_counter()
+        res = eng.generate_text(reqs, max_tokens=max_tokens)
+        sync()
+        dt = time.perf_counter() - t0
+        out["latencies"].append(dt)
+        out["elapsed"] += dt
+        out["generated_tokens"] += sum(len(r.tokens) for r in res)
+        out["total_tokens"] += sum(len(p) for p in reqs) + sum(len(r.tokens) for r in res)
+    out["prompt_tokens_computed"] = eng.prompt_tokens_computed
+    del eng
+    torch.cuda.empty_cache()
+    return out
+
+
 def bench_replicas(n_gpus, seed, n_requests, engine_kwargs):
     """Requests U[512,4096] prompts, 256 tokens, spread over n_gpus replicas."""
     from .router import Router
@@ -210,7 +242,8 @@ def main(argv=None):
     ap.add_argument("--min-prompt-tokens", type=int, default=DEFAULT_PROMPT_TOKENS_MIN)
     ap.add_argument("--max-prompt-tokens", type=int, default=DEFAULT_PROMPT_TOKENS_MAX)
     ap.add_argument("--modes", default="single,upfront,staggered",
-                    help="comma list of single, upfront, staggered, poisson, replicas")
+                    help="comma list of single, upfront, staggered, poisson, replicas, "
+                         "shared_prefix")
     ap.add_argument("--gpus", type=int, default=1, help="replicas mode: GPU count")
     ap.add_argument("--replica-requests", type=int, default=2048)
     ap.add_argument("--verbose", action="store_true")
@@ -239,6 +272,10 @@ def main(argv=None):
             rows.append(("poisson arrivals", bench_poisson(eng, a.seed, a.repetitions)))
         del eng
         torch.cuda.empty_cache()
+    if "shared_prefix" in modes:
+        for on in (False, True):
+            rows.append((f"shared prefix, cache {'on' if on else 'off'}",
+                         bench_shared_prefix(64, a.seed, a.repetitions, on)))
     if "replicas" in modes:
         kw = {"engine_config": default_engine_config(256, 4096)}
         rows.append((f"replicas x{a.gpus}", bench_replicas(a.gpus, a.seed, a.replica_requests, kw)))

@@ -16,9 +16,9 @@
 // layer:
 //   * prefill items -- (seq, kv_head, 64-token tile): one CTA, warp-specialised:
 //     two M=128 tcgen05 tiles (two query heads x 64 tokens each) share every
-//     64-key K/V tile a load warp stages by TMA in 4-slot rings; an MMA warp
-//     issues S = Q K^T and O += P V with S, P and O in TMEM; two softmax
-//     warpgroups run one thread per query row;
+//     64-key K/V tile a load warp stages by TMA in 4-slot rings; one MMA warp
+//     per tile issues its S = Q K^T and O += P V with S, P and O in TMEM; two
+//     softmax warpgroups run one thread per query row;
 //   * decode items  -- (seq, kv_head, block range): one warp with its own TMA
 //     ring of K/V block tiles, mma.sync for QK^T and PV, an online softmax;
 //     for a sequence split over several items, the last item to finish (an

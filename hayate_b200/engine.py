@@ -97,6 +97,7 @@ class Request:
     _shared: int = 0
     _shared_blocks: List[int] = field(default_factory=list)
     _offer: Optional[tuple] = None
+    _adopt_pinned: Optional[tuple] = None   # host buffers of the adopted-block upload
 
 
 class ByteTokenizer:
