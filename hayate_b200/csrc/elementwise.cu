@@ -65,35 +65,34 @@ __global__ void __launch_bounds__(RN_THREADS) add_rms_norm_kernel(
   const long r = blockIdx.x;
   const int nvec = cols / N;
   T* xr = x + r * ldx;
-  float v[RN_VEC][N], wv[RN_VEC][N];
+  // rows and weights stay as their 16-byte vectors (the stored residual is in
+  // the model dtype anyway) and are unpacked where used: fewer registers, more
+  // rows in flight per SM
+  uint4 xv[RN_VEC], wv[RN_VEC];
 #pragma unroll
   for (int k = 0; k < RN_VEC; ++k) {          // the weights are no earlier kernel's output
     const int vi = threadIdx.x + RN_THREADS * k;
-    if (vi < nvec) V::load(w + vi * N, wv[k]);
+    if (vi < nvec) wv[k] = *reinterpret_cast<const uint4*>(w + vi * N);
   }
   hy_grid_wait();
   hy_grid_trigger();
-#pragma unroll
-  for (int k = 0; k < RN_VEC; ++k) {
-    const int vi = threadIdx.x + RN_THREADS * k;
-    if (vi < nvec) {
-      V::load(xr + vi * N, v[k]);
-      if (delta != nullptr) {
-        float dv[N];
-        V::load(delta + r * ldd + vi * N, dv);
-#pragma unroll
-        for (int e = 0; e < N; ++e) v[k][e] = V::round(__fadd_rn(dv[e], v[k][e]));
-        V::store(xr + vi * N, v[k]);
-      }
-    }
-  }
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < RN_VEC; ++k) {
     const int vi = threadIdx.x + RN_THREADS * k;
     if (vi < nvec) {
+      float v[N];
+      V::load(xr + vi * N, v);
+      if (delta != nullptr) {
+        float dv[N];
+        V::load(delta + r * ldd + vi * N, dv);
 #pragma unroll
-      for (int e = 0; e < N; ++e) ss = __fadd_rn(ss, __fmul_rn(v[k][e], v[k][e]));
+        for (int e = 0; e < N; ++e) v[e] = V::round(__fadd_rn(dv[e], v[e]));
+        V::store(xr + vi * N, v);
+      }
+#pragma unroll
+      for (int e = 0; e < N; ++e) ss = __fadd_rn(ss, __fmul_rn(v[e], v[e]));
+      V::store(reinterpret_cast<T*>(&xv[k]), v);          // exact: v is in T already
     }
   }
 #pragma unroll
@@ -109,9 +108,11 @@ __global__ void __launch_bounds__(RN_THREADS) add_rms_norm_kernel(
   for (int k = 0; k < RN_VEC; ++k) {
     const int vi = threadIdx.x + RN_THREADS * k;
     if (vi < nvec) {
-      float o[N];
+      float v[N], g[N], o[N];
+      V::load(reinterpret_cast<const T*>(&xv[k]), v);
+      V::load(reinterpret_cast<const T*>(&wv[k]), g);
 #pragma unroll
-      for (int e = 0; e < N; ++e) o[e] = __fmul_rn(__fmul_rn(v[k][e], rstd), wv[k][e]);
+      for (int e = 0; e < N; ++e) o[e] = __fmul_rn(__fmul_rn(v[e], rstd), g[e]);
       V::store(yr + vi * N, o);
     }
   }
@@ -135,7 +136,14 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(
     V::load(gu + r * ld + inter + c, u);
 #pragma unroll
     for (int e = 0; e < N; ++e) {
-      const float s = V::round(__fdiv_rn(g[e], __fadd_rn(1.0f, expf(-g[e]))));
+      float s;
+      if constexpr (N == 8) {
+        // bf16: SiLU is rounded to bf16 right away, so the fast exp and divide
+        // (errors near 1e-7 relative) leave it within one bf16 ulp
+        s = V::round(__fdividef(g[e], 1.0f + __expf(-g[e])));
+      } else {
+        s = V::round(__fdiv_rn(g[e], __fadd_rn(1.0f, expf(-g[e]))));
+      }
       o[e] = __fmul_rn(s, u[e]);
     }
     V::store(y + r * ldy + c, o);
