@@ -165,10 +165,11 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
   // Pass 2: item counts, offsets, items.
   for (int base = 0; base < S; base += PLAN_THREADS) {
     const int i = base + threadIdx.x;
-    int npre = 0, ndec = 0, ns = 0, ntile = 0, nblk = 0;
+    int npre = 0, ndec = 0, ns = 0, ntile = 0, nblk = 0, row = 0, kv = 0;
     if (i < S) {
-      const int q = cu_q[i + 1] - cu_q[i];
-      const int kv = seq_lens_k[i];
+      row = cu_q[i];
+      const int q = cu_q[i + 1] - row;
+      kv = seq_lens_k[i];
       if (q < 0 || kv < q) atomicOr(&s_bad, HY_ERR_BOUNDS);
       else if (q == 1) {
         nblk = (kv + HY_BLOCK - 1) / HY_BLOCK;
@@ -207,11 +208,13 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
       const int ji = __shfl_sync(0xffffffffu, i, j);
       const int jp0 = __shfl_sync(0xffffffffu, p0, j), jd0 = __shfl_sync(0xffffffffu, d0, j);
       const int jns = __shfl_sync(0xffffffffu, ns, j), jnb = __shfl_sync(0xffffffffu, nblk, j);
+      const int jrow = __shfl_sync(0xffffffffu, row, j), jkv = __shfl_sync(0xffffffffu, kv, j);
       const int jnt = __shfl_sync(0xffffffffu, ntile, j);
       for (int k = lane; k < kv_heads * jns; k += 32) {   // splits differ by at most one block
         const int g = k / jns, sp = k - g * jns;
         const int lo = mul_div(sp, jnb, jns), hi = mul_div(sp + 1, jnb, jns);
-        v.dec[jd0 + k] = make_int4(ji, g, lo, hi);
+        v.dec[2 * (jd0 + k)] = make_int4(ji, g, lo, hi);
+        v.dec[2 * (jd0 + k) + 1] = make_int4(jrow, jkv, jns, 0);
       }
       for (int k = lane; k < kv_heads * jnt; k += 32) {
         const int g = k / jnt, t = k - g * jnt;
@@ -285,11 +288,10 @@ HY_DEVICE int kv_row(const MainArgs& a, int blk, int kv, int g) {
 __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
                             int item, uint8_t* ring, uint64_t* bars, uint32_t& phase) {
   const int lane = threadIdx.x & 31;
-  const int4 it = v.dec[item];
+  const int4 it = v.dec[2 * item];                // one 32-byte record
+  const int4 info = v.dec[2 * item + 1];
   const int seq = it.x, g = it.y, b0 = it.z, b1 = it.w;
-  const int kv_len = a.seq_lens_k[seq];
-  const int tok = a.cu_q[seq];
-  const int ns = v.seqinfo[seq].y;
+  const int tok = info.x, kv_len = info.y, ns = info.z;
   const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
   const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
   const int n = b1 - b0;
@@ -313,10 +315,17 @@ __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const Pla
     tma_load_2d(st + 6144, map, 64, rv, &bars[s]);
   };
 
+  // the ring's first blocks and the one after: one id per lane, loaded together
+  const int idl = (lane <= DEC_STAGES && lane < n) ? bt[b0 + lane] : 0;
+  int first_ids[DEC_STAGES + 1];
+#pragma unroll
+  for (int s = 0; s <= DEC_STAGES; ++s) first_ids[s] = __shfl_sync(0xffffffffu, idl, s);
   if (lane == 0) {
-    for (int s = 0; s < DEC_STAGES && s < n; ++s) issue(s, bt[b0 + s]);
+#pragma unroll
+    for (int s = 0; s < DEC_STAGES; ++s)
+      if (s < n) issue(s, first_ids[s]);
   }
-  int next_id = (lane == 0 && DEC_STAGES < n) ? bt[b0 + DEC_STAGES] : 0;
+  int next_id = (lane == 0 && DEC_STAGES < n) ? first_ids[DEC_STAGES] : 0;
 
   // Query fragments: rows 0..3 are the group's 4 heads; rows 4..15 are zero.
   const int r = lane >> 2, c = 2 * (lane & 3);
@@ -933,7 +942,7 @@ size_t hy_attn_workspace_bytes(const PlanDims& d) {
   size_t off = 256;                                         // header
   off = align256(off + (size_t)d.max_pre * sizeof(int4));
   off = align256(off + (size_t)d.max_pre * sizeof(int4));  // sorted prefill items
-  off = align256(off + (size_t)d.max_dec * sizeof(int4));
+  off = align256(off + (size_t)d.max_dec * 2 * sizeof(int4));
   off = align256(off + (size_t)d.max_seqs * sizeof(int2));
   off = align256(off + (size_t)d.max_dec * HY_GROUP * HY_HEAD_DIM * sizeof(float));
   off = align256(off + (size_t)d.max_dec * HY_GROUP * sizeof(float2));
@@ -953,7 +962,7 @@ static PlanView make_view(void* ws, const PlanDims& d) {
   v.pre_sorted = reinterpret_cast<int4*>(p + off);
   off = align256(off + (size_t)d.max_pre * sizeof(int4));
   v.dec = reinterpret_cast<int4*>(p + off);
-  off = align256(off + (size_t)d.max_dec * sizeof(int4));
+  off = align256(off + (size_t)d.max_dec * 2 * sizeof(int4));
   v.seqinfo = reinterpret_cast<int2*>(p + off);
   off = align256(off + (size_t)d.max_seqs * sizeof(int2));
   v.part_o = reinterpret_cast<float*>(p + off);

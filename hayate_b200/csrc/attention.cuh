@@ -19,7 +19,8 @@ struct PlanView {
   int* header;        // n_pre, n_dec, split, status
   int4* pre;          // prefill items by sequence (plan scratch)
   int4* pre_sorted;   // the same items, most key tiles first (what the kernel runs)
-  int4* dec;
+  int4* dec;          // per decode item: (seq, kv head, first block, end block), then
+                      // (query row, key length, splits of its sequence, 0)
   int2* seqinfo;      // per sequence: first decode item, number of splits
   float* part_o;      // [max_dec][4][128]
   float2* part_ml;    // [max_dec][4]  (running max in log2 units, sum)
