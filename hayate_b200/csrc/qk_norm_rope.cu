@@ -158,21 +158,23 @@ __global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
   const int grp = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int heads = q_heads + 2 * kv_heads;
   const int npass = (heads + QNR_GROUPS - 1) / QNR_GROUPS;
-  const long units = (long)T_tokens * npass;
   const int d0 = l * 8;                    // this lane's 8 elements of a row
   const int c0 = (l & 7) * 8;              // ... and their RoPE table columns
   const bool upper = l >= 8;               // elements 64..127: partner is d - 64
-  const long step = gridDim.x;
-  long unit = blockIdx.x;
-  // the position of the next unit is loaded one unit ahead, so that a unit's
-  // cos/sin rows, its head row and its slot are all requested at once
-  int pos_next = unit < units ? positions[(int)(unit / npass)] : 0;
-  for (; unit < units; unit += step) {              // uniform over the CTA
-    const int t = (int)(unit / npass), h = (int)(unit % npass) * QNR_GROUPS + grp;
+  // unit = t * npass + p walks the grid stride as (token, pass) pairs, with no
+  // division in the loop; the position of the next unit is loaded one unit
+  // ahead, so a unit's cos/sin rows, head row and slot are requested together
+  const int dt = (int)(gridDim.x / npass), dp = (int)(gridDim.x % npass);
+  int t = (int)(blockIdx.x / npass), p = (int)(blockIdx.x % npass), tn = 0, pn = 0;
+  int pos_next = t < T_tokens ? positions[t] : 0;
+  for (; t < T_tokens; t = tn, p = pn) {            // uniform over the CTA
+    tn = t + dt;                                    // the unit one grid stride on
+    pn = p + dp;
+    if (pn >= npass) { pn -= npass; ++tn; }
+    const int h = p * QNR_GROUPS + grp;
     const bool valid = h < heads;                  // uniform over the warp's half-warps
     int pos = pos_next;
-    const long nu = unit + step;
-    pos_next = nu < units ? positions[(int)(nu / npass)] : 0;
+    pos_next = tn < T_tokens ? positions[tn] : 0;
     if (pos < 0 || pos >= max_pos) { hy_flag(err, HY_ERR_BOUNDS); pos = 0; }
     const uint4 raw = valid ? *reinterpret_cast<const uint4*>(
                                   qkv + (size_t)t * ld + (size_t)h * HY_HEAD_DIM + d0)
@@ -186,6 +188,9 @@ __global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
       if (slot >= 0)
         *reinterpret_cast<uint4*>(cache_ptr(cache, slot, 1, h - q_heads - kv_heads, kv_heads) + d0) = raw;
     }
+    // a warp with no query or key row left (both half-warps value heads or past
+    // the end) skips the norm; otherwise all its lanes run it for the shuffles
+    if (__all_sync(0xffffffffu, !valid || h >= q_heads + kv_heads)) continue;
     float cs[8], sn[8];
     {
       const float4* cp = reinterpret_cast<const float4*>(rope_cos + (size_t)pos * 64 + c0);
