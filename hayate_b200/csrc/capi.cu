@@ -27,7 +27,7 @@ cudaError_t hy_launch_kv_append(int, const void*, const void*, int, int, const i
                                 int, int32_t*, cudaStream_t);
 cudaError_t hy_launch_argmax(int, const void*, long, int, int, int32_t*, cudaStream_t);
 cudaError_t hy_launch_add_rms_norm(int, void*, long, const void*, long, int, int, const void*,
-                                   float, void*, long, cudaStream_t);
+                                   float, void*, long, const float*, int, long, cudaStream_t);
 cudaError_t hy_launch_silu_mul(int, const void*, long, int, int, void*, long, cudaStream_t);
 
 namespace {
@@ -358,8 +358,30 @@ int hy_add_rms_norm(int32_t dtype, void* x, int64_t ldx, const void* delta, int6
       !vec_aligned(w, cols, dtype, cols) || (delta && !vec_aligned(delta, ldd, dtype, cols)))
     return fail(HY_E_INVALID, "hy_add_rms_norm: rows must be 16-byte aligned vectors");
   return cuda_result(hy_launch_add_rms_norm(dtype, x, (long)ldx, delta, (long)ldd, rows, cols, w,
-                                            eps, y, (long)ldy, as_stream(stream)),
+                                            eps, y, (long)ldy, nullptr, 0, 0, as_stream(stream)),
                      "hy_add_rms_norm");
+}
+
+int hy_add_rms_norm_splitk(int32_t dtype, void* x, int64_t ldx, const float* parts,
+                           int32_t nparts, int64_t part_stride, int64_t ldp, int32_t rows,
+                           int32_t cols, const void* w, float eps, void* y, int64_t ldy,
+                           void* stream) {
+  if (!dtype_ok(dtype)) return fail(HY_E_INVALID, "hy_add_rms_norm_splitk: dtype must be 0 or 1");
+  if (rows == 0) return HY_OK;
+  const int maxc = 4096;
+  if (!x || !parts || !w || !y || rows < 0 || cols <= 0 || cols > maxc || ldx < cols ||
+      ldy < cols || ldp < cols || nparts < 1 || nparts > 64 ||
+      (nparts > 1 && part_stride < (int64_t)rows * ldp))
+    return fail(HY_E_INVALID, "hy_add_rms_norm_splitk: bad argument (cols must be in 1..4096, "
+                              "1..64 parts that do not overlap)");
+  if (!vec_aligned(x, ldx, dtype, cols) || !vec_aligned(y, ldy, dtype, cols) ||
+      !vec_aligned(w, cols, dtype, cols) || !vec_aligned(parts, ldp, HY_DTYPE_FP32, cols) ||
+      (part_stride & 3))
+    return fail(HY_E_INVALID, "hy_add_rms_norm_splitk: rows must be 16-byte aligned vectors");
+  return cuda_result(hy_launch_add_rms_norm(dtype, x, (long)ldx, nullptr, (long)ldp, rows, cols,
+                                            w, eps, y, (long)ldy, parts, nparts,
+                                            (long)part_stride, as_stream(stream)),
+                     "hy_add_rms_norm_splitk");
 }
 
 int hy_silu_mul(int32_t dtype, const void* gu, int64_t ld, int32_t rows, int32_t inter, void* y,

@@ -53,11 +53,14 @@ template <> struct Vec<float> {
 constexpr int RN_THREADS = 128;
 
 // x <- round(x + delta) (when delta is given: the residual add of block.py:24,30),
-// y <- RMSNorm(x) * w.
-template <typename T>
+// y <- RMSNorm(x) * w.  With split-K partials instead of delta, delta is first
+// round(sum of the nparts fp32 partials, in order), i.e. the projection's
+// output as its GEMM would have rounded it.
+template <typename T, bool PARTS>
 __global__ void __launch_bounds__(RN_THREADS) add_rms_norm_kernel(
     T* __restrict__ x, long ldx, const T* __restrict__ delta, long ldd, int cols,
-    const T* __restrict__ w, float eps, T* __restrict__ y, long ldy) {
+    const T* __restrict__ w, float eps, T* __restrict__ y, long ldy,
+    const float* __restrict__ parts, int nparts, long pstride) {
   using V = Vec<T>;
   constexpr int N = V::N;
   constexpr int RN_VEC = 32 / N;
@@ -83,11 +86,52 @@ __global__ void __launch_bounds__(RN_THREADS) add_rms_norm_kernel(
     if (vi < nvec) {
       float v[N];
       V::load(xr + vi * N, v);
-      if (delta != nullptr) {
+      if (!PARTS && delta != nullptr) {
         float dv[N];
         V::load(delta + r * ldd + vi * N, dv);
 #pragma unroll
         for (int e = 0; e < N; ++e) v[e] = V::round(__fadd_rn(dv[e], v[e]));
+        V::store(xr + vi * N, v);
+      } else if (PARTS) {
+        // the loads of the first PMAX partials are all issued before the sum
+        // uses any of them (one L2 round trip, not one per partial)
+        constexpr int PMAX = 8;
+        float dv[N];
+        const float* pp = parts + r * ldd + vi * N;
+        float4 pb[PMAX][N / 4];
+#pragma unroll
+        for (int p = 0; p < PMAX; ++p)
+          if (p < nparts)
+#pragma unroll
+            for (int e = 0; e < N / 4; ++e)
+              pb[p][e] = __ldcg(reinterpret_cast<const float4*>(pp + p * pstride + 4 * e));
+#pragma unroll
+        for (int e = 0; e < N / 4; ++e) {
+          dv[4 * e] = pb[0][e].x; dv[4 * e + 1] = pb[0][e].y;
+          dv[4 * e + 2] = pb[0][e].z; dv[4 * e + 3] = pb[0][e].w;
+        }
+#pragma unroll
+        for (int p = 1; p < PMAX; ++p)
+          if (p < nparts)
+#pragma unroll
+            for (int e = 0; e < N / 4; ++e) {
+              dv[4 * e] = __fadd_rn(dv[4 * e], pb[p][e].x);
+              dv[4 * e + 1] = __fadd_rn(dv[4 * e + 1], pb[p][e].y);
+              dv[4 * e + 2] = __fadd_rn(dv[4 * e + 2], pb[p][e].z);
+              dv[4 * e + 3] = __fadd_rn(dv[4 * e + 3], pb[p][e].w);
+            }
+        for (int p = PMAX; p < nparts; ++p) {
+#pragma unroll
+          for (int e = 0; e < N; e += 4) {
+            const float4 a = __ldcg(reinterpret_cast<const float4*>(pp + p * pstride + e));
+            dv[e] = __fadd_rn(dv[e], a.x);
+            dv[e + 1] = __fadd_rn(dv[e + 1], a.y);
+            dv[e + 2] = __fadd_rn(dv[e + 2], a.z);
+            dv[e + 3] = __fadd_rn(dv[e + 3], a.w);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < N; ++e) v[e] = V::round(__fadd_rn(V::round(dv[e]), v[e]));
         V::store(xr + vi * N, v);
       }
 #pragma unroll
@@ -152,16 +196,21 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(
 
 }  // namespace
 
+// delta (model dtype) or parts (fp32, nparts x rows, pstride apart) -- at most
+// one of them -- with row pitch ldd.
 cudaError_t hy_launch_add_rms_norm(int dtype, void* x, long ldx, const void* delta, long ldd,
                                    int rows, int cols, const void* w, float eps, void* y,
-                                   long ldy, cudaStream_t st) {
+                                   long ldy, const float* parts, int nparts, long pstride,
+                                   cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
+  using B = __nv_bfloat16;
   if (dtype == 0)
-    return hy_launch(add_rms_norm_kernel<__nv_bfloat16>, dim3(rows), dim3(RN_THREADS), 0, st,
-                     (__nv_bfloat16*)x, ldx, (const __nv_bfloat16*)delta, ldd, cols,
-                     (const __nv_bfloat16*)w, eps, (__nv_bfloat16*)y, ldy);
-  return hy_launch(add_rms_norm_kernel<float>, dim3(rows), dim3(RN_THREADS), 0, st, (float*)x,
-                   ldx, (const float*)delta, ldd, cols, (const float*)w, eps, (float*)y, ldy);
+    return hy_launch(parts ? add_rms_norm_kernel<B, true> : add_rms_norm_kernel<B, false>,
+                     dim3(rows), dim3(RN_THREADS), 0, st, (B*)x, ldx, (const B*)delta, ldd, cols,
+                     (const B*)w, eps, (B*)y, ldy, parts, nparts, pstride);
+  return hy_launch(parts ? add_rms_norm_kernel<float, true> : add_rms_norm_kernel<float, false>,
+                   dim3(rows), dim3(RN_THREADS), 0, st, (float*)x, ldx, (const float*)delta, ldd,
+                   cols, (const float*)w, eps, (float*)y, ldy, parts, nparts, pstride);
 }
 
 cudaError_t hy_launch_silu_mul(int dtype, const void* gu, long ld, int rows, int inter, void* y,

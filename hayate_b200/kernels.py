@@ -192,6 +192,24 @@ def add_rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float,
     return out
 
 
+def add_rms_norm_splitk(x: torch.Tensor, w: torch.Tensor, eps: float, parts: torch.Tensor,
+                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x += round(parts.sum(0)) in place (parts: [n, rows, cols] fp32 split-K
+    partials of the projection giving the residual's delta), then return
+    RMSNorm(x) * w."""
+    rows, cols = x.shape
+    if parts.dtype != torch.float32 or parts.dim() != 3 or parts.shape[1:] != (rows, cols):
+        raise ValueError("parts must be fp32 [n, rows, cols]")
+    if x.stride(1) != 1 or parts.stride(2) != 1:
+        raise ValueError("rows must be contiguous")
+    out = torch.empty_like(x) if out is None else out
+    check(_lib.load().hy_add_rms_norm_splitk(
+        _dt(x), _ptr(x), x.stride(0), _ptr(parts), parts.shape[0], parts.stride(0),
+        parts.stride(1), rows, cols, _ptr(w), float(eps), _ptr(out), out.stride(0), _stream()),
+        "hy_add_rms_norm_splitk")
+    return out
+
+
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float,
              out: Optional[torch.Tensor] = None) -> torch.Tensor:
     return add_rms_norm(x, w, eps, None, out)

@@ -188,6 +188,21 @@ int hy_add_rms_norm(int32_t dtype, void* x, int64_t ldx, const void* delta, int6
                     int32_t rows, int32_t cols, const void* w, float eps, void* y, int64_t ldy,
                     void* stream);
 
+/* As hy_add_rms_norm with the residual's delta given as nparts (1..64) fp32
+ * split-K partials of the projection that produced it: part p of row r at
+ * parts + p * part_stride + r * ldp (floats).  delta = round(sum of the parts in
+ * order), then x[r] <- round(x[r] + delta) and y[r] = round(RMSNorm(x[r]) * w),
+ * so the projection's output is rounded once, as its unsplit GEMM rounds it.
+ * Lets the caller run a decode-sized projection (few rows, long K) as a batched
+ * GEMM over K slices, which fills the GPU where one GEMM of a few rows cannot.
+ * Replaces: the o_proj / down_proj outputs' residual adds and the following
+ * post_attention_layernorm / input_layernorm, hayate/model/block.py:21-31,
+ * hayate/model/attention.py:66 and hayate/model/linear.py:11-14. */
+int hy_add_rms_norm_splitk(int32_t dtype, void* x, int64_t ldx, const float* parts,
+                           int32_t nparts, int64_t part_stride, int64_t ldp, int32_t rows,
+                           int32_t cols, const void* w, float eps, void* y, int64_t ldy,
+                           void* stream);
+
 /* y[r][i] = silu(gu[r][i]) * gu[r][inter + i] with the reference's two rounding
  * points (silu result, product).  `inter` a multiple of 8 (bf16) / 4 (fp32).
  * Replaces: FeedForward's silu(gate) * up, hayate/model/linear.py:11-13. */

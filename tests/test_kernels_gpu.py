@@ -437,6 +437,58 @@ def test_add_rms_norm_vs_reference(dt, cols, residual):
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("nparts,rows,cols", [(8, 16, 2560), (4, 64, 2560), (1, 5, 256),
+                                              (3, 37, 1000)])
+def test_add_rms_norm_splitk_vs_reference(dt, nparts, rows, cols):
+    """The residual's delta given as fp32 split-K partials: x gains round(sum of
+    the partials in order) exactly, as the unsplit projection's rounded output
+    would give it, and y is the reference RMSNorm of the new x."""
+    x = (torch.randn(rows, cols, device=dev) * 3).to(dt)
+    # partials in a strided [n, rows, cols] view, as a batched GEMM writes them
+    big = torch.randn(nparts, rows + 3, cols + 8, device=dev)
+    parts = big[:, 1:rows + 1, 4:cols + 4]
+    w = (1 + 0.1 * torch.randn(cols, device=dev)).to(dt)
+    acc = parts[0].clone()
+    for p in range(1, nparts):                          # fp32 sum in the kernel's order
+        acc = acc + parts[p]
+    want_x = x + acc.to(dt)                              # block.py:24,30 on the rounded output
+    want = R.rms_norm(want_x, w, 1e-6)
+    got = K.add_rms_norm_splitk(x, w, 1e-6, parts)
+    torch.cuda.synchronize()
+    assert torch.equal(x, want_x)
+    if dt == torch.bfloat16:
+        d = _ulp_diff_bf16(got, want)
+        assert d.max().item() <= 1 and (d > 0).float().mean().item() < 0.02
+    else:
+        torch.testing.assert_close(got, want, rtol=2e-6, atol=2e-6)
+
+
+def test_splitk_projection_matches_one_gemm():
+    """o_proj / down_proj as a batched GEMM over K slices + the partial sums in
+    add+RMSNorm give the residual and normed rows of one GEMM + add+RMSNorm, up
+    to the bf16 rounding of a differently ordered fp32 sum (decode step shapes)."""
+    import torch.nn.functional as F
+    from hayate_b200.model import linear_splitk
+    g = torch.Generator(device=dev).manual_seed(3)
+    for k, s in ((4096, 8), (9728, 8), (9728, 4)):
+        a = torch.randn(16, k, device=dev, generator=g).to(torch.bfloat16)
+        w = (torch.randn(2560, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        x = torch.randn(16, 2560, device=dev, generator=g).to(torch.bfloat16)
+        ln = (1 + 0.1 * torch.randn(2560, device=dev, generator=g)).to(torch.bfloat16)
+        parts = linear_splitk(a, w, s)
+        assert parts.shape == (s, 16, 2560) and parts.dtype == torch.float32
+        x1, x2 = x.clone(), x.clone()
+        y1 = K.add_rms_norm(x1, ln, 1e-6, delta=F.linear(a, w))
+        y2 = K.add_rms_norm_splitk(x2, ln, 1e-6, parts)
+        torch.cuda.synchronize()
+        # the two fp32 sums may round delta to neighbouring bf16 values (one
+        # ulp of delta, |delta| ~ 1.3-2): a few elements move by that much
+        for got, want in ((x2, x1), (y2, y1)):
+            torch.testing.assert_close(got.float(), want.float(), rtol=1e-2, atol=3e-2)
+            assert (got != want).float().mean().item() < 0.05
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
 def test_silu_mul_vs_reference(dt):
     gu = (torch.randn(19, 2 * 9728, device=dev) * 2).to(dt)
     got = K.silu_mul(gu)
