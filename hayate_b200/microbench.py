@@ -33,12 +33,16 @@ import torch
 
 
 def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True,
-                    ctx_lo: int = 256, ctx_hi: int = 16384):
+                    ctx_lo: int = 256, ctx_hi: int = 16384, priors=None):
     """The ragged attention operator case: returns timing + algorithmic bytes.
-    ``ctx_lo``/``ctx_hi`` bound the log-uniform decode contexts."""
+    ``ctx_lo``/``ctx_hi`` bound the log-uniform decode contexts; ``priors`` (a
+    list of prior context lengths, one 512-token prefill chunk each) replaces
+    the operator case's four chunks."""
     from hayate_b200 import kernels as K
     from hayate_b200.workloads import attn_micro
     w = attn_micro(seed=0, n_decode=n_decode, lo=ctx_lo, hi=ctx_hi)
+    if priors is not None:
+        w.prefill_prior = list(priors)
     if not prefill:
         w.prefill_prior = []
     q_lens, kv_lens = w.q_lens(), w.seq_lens_k()
@@ -299,11 +303,12 @@ OPS = ("attention", "qk_norm_rope", "kv_append", "pack", "argmax", "add_rms_norm
 
 
 def run_op(op: str, iters: int, n_decode: int = 256, prefill: bool = True, tokens: int = 2304,
-           ctx_lo: int = 256, ctx_hi: int = 16384):
+           ctx_lo: int = 256, ctx_hi: int = 16384, priors=None):
     if op == "attention":
-        r = attention_micro(iters, n_decode, prefill, ctx_lo, ctx_hi)
+        r = attention_micro(iters, n_decode, prefill, ctx_lo, ctx_hi, priors)
         r["op"] = op
         r["gbs"] = r["bytes"] / (r["ms_mean"] * 1e-3) / 1e9
+        r["prefill_tflops"] = r["prefill_flops"] / (r["ms_mean"] * 1e-3) / 1e12
         return r
     if op in ("qk_norm_rope", "kv_append"):
         return append_micro(iters, n_decode, tokens, fused=op == "qk_norm_rope")
@@ -327,11 +332,15 @@ def main():
                     help="query tokens of the batch for the append, pack and argmax ops")
     ap.add_argument("--ctx-lo", type=int, default=256, help="attention: shortest decode context")
     ap.add_argument("--ctx-hi", type=int, default=16384, help="attention: longest decode context")
+    ap.add_argument("--priors", default=None,
+                    help="attention: comma-separated prior lengths, one 512-token prefill "
+                         "chunk each (default: the operator case's 0,512,1536,3584)")
     a = ap.parse_args()
+    priors = None if a.priors is None else [int(x) for x in a.priors.split(",") if x]
     torch.cuda.set_device(0)
     for op in (OPS if a.op == "all" else (a.op,)):
         print(json.dumps(run_op(op, a.iters, a.decode, not a.no_prefill, a.tokens, a.ctx_lo,
-                                a.ctx_hi)), flush=True)
+                                a.ctx_hi, priors)), flush=True)
 
 
 if __name__ == "__main__":

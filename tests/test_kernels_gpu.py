@@ -296,6 +296,11 @@ CASES = {
     # 376 prefill items (several per CTA), ragged 64-token tiles, prefixes
     "prefill_many": ([65, 127, 128, 200, 512, 512, 512, 512, 300, 1],
                      [65, 227, 1128, 200, 512, 1024, 2048, 600, 3000, 50]),
+    # a chunk after 8192 cached tokens (129/130 key tiles per item); a 64-token
+    # chunk after 16384; a ragged 36-row tile after 5000 beside a short chunk
+    "prefill_long_prior": ([128, 1], [8320, 300]),
+    "prefill_longer_prior": ([64, 1], [16448, 100]),
+    "prefill_ragged_prior": ([100, 37, 1], [5100, 37, 2000]),
 }
 
 
