@@ -75,6 +75,13 @@ constexpr int MIN_SPLIT = HY_MIN_SPLIT;                          // blocks per d
 constexpr int ITEMS_PER_WARP = HY_ITEMS_PER_WARP;                // decode items aimed at per warp
 constexpr int GRAB_INTS = 4;                                     // per layer: decode item, CTAs
                                                                  // done, prefill item, spare
+// a split-K merge stages the partials of MERGE_CHUNK splits at a time (2 KB of O
+// and 32 B of (m, l) each, then their weights) in the merging warp's TMA ring
+constexpr int MERGE_CHUNK = 8;                                   // = 32 lanes / 4 heads
+constexpr int MERGE_O_BYTES = MERGE_CHUNK * HY_GROUP * HY_HEAD_DIM * 4;
+constexpr int MERGE_ML_BYTES = MERGE_CHUNK * HY_GROUP * 8;
+static_assert(MERGE_O_BYTES + MERGE_ML_BYTES + MERGE_CHUNK * HY_GROUP * 4 <= DEC_WARP_BYTES,
+              "merge staging must fit a decode warp's ring");
 constexpr float NEG_INF = -INFINITY;
 // Lazy rescaling: the running max is only raised when a new score exceeds it
 // by more than 2^RESCALE_LOG2; until then probabilities may exceed 1 by up to
@@ -214,7 +221,8 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
         const int g = k / jns, sp = k - g * jns;
         const int lo = mul_div(sp, jnb, jns), hi = mul_div(sp + 1, jnb, jns);
         v.dec[2 * (jd0 + k)] = make_int4(ji, g, lo, hi);
-        v.dec[2 * (jd0 + k) + 1] = make_int4(jrow, jkv, jns, 0);
+        v.dec[2 * (jd0 + k) + 1] = make_int4(jrow, jkv, jns, jd0 + g * jns);
+        v.dec_ids[2 * (jd0 + k)] = make_int4(-1, 0, 0, 0);
       }
       for (int k = lane; k < kv_heads * jnt; k += 32) {
         const int g = k / jnt, t = k - g * jnt;
@@ -288,12 +296,13 @@ HY_DEVICE int kv_row(const MainArgs& a, int blk, int kv, int g) {
 __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
                             int item, uint8_t* ring, uint64_t* bars, uint32_t& phase) {
   const int lane = threadIdx.x & 31;
-  const int4 it = v.dec[2 * item];                // one 32-byte record
-  const int4 info = v.dec[2 * item + 1];
+  const uint64_t keep = l2_keep_policy();
+  const int4 it = ld_keep(&v.dec[2 * item], keep);        // one 32-byte record
+  const int4 info = ld_keep(&v.dec[2 * item + 1], keep);
   const int seq = it.x, g = it.y, b0 = it.z, b1 = it.w;
-  const int tok = info.x, kv_len = info.y, ns = info.z;
-  const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
-  const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
+  const int tok = info.x, kv_len = info.y, ns = info.z, first = info.w;
+  const int4 c0 = ld_keep(&v.dec_ids[2 * item], keep);
+  const int4 c1 = ld_keep(&v.dec_ids[2 * item + 1], keep);
   const int n = b1 - b0;
 
   // Issue the K and V tiles of logical block b into ring stage s (lane 0 only).
@@ -315,11 +324,28 @@ __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const Pla
     tma_load_2d(st + 6144, map, 64, rv, &bars[s]);
   };
 
-  // the ring's first blocks and the one after: one id per lane, loaded together
-  const int idl = (lane <= DEC_STAGES && lane < n) ? bt[b0 + lane] : 0;
+  // The block-table row and the ids of the ring's first blocks and the one
+  // after: cached with the item by the plan's first attention launch (block
+  // tables do not change while a plan is in use), else loaded (one id per
+  // lane, together) and cached for the later layers.
+  static_assert(DEC_STAGES == 3, "the item cache holds DEC_STAGES + 1 = 4 block ids");
+  int bt_row;
   int first_ids[DEC_STAGES + 1];
+  if (c0.x >= 0) {                                // warp-uniform
+    bt_row = c0.x;
+    first_ids[0] = c0.y; first_ids[1] = c0.z; first_ids[2] = c0.w; first_ids[3] = c1.x;
+  } else {
+    bt_row = a.seq_bt_row ? ld_keep(a.seq_bt_row + seq, keep) : seq;
+    const int32_t* bt0 = a.block_tables + (size_t)bt_row * a.bt_pitch;
+    const int idl = (lane <= DEC_STAGES && lane < n) ? ld_keep(bt0 + b0 + lane, keep) : 0;
 #pragma unroll
-  for (int s = 0; s <= DEC_STAGES; ++s) first_ids[s] = __shfl_sync(0xffffffffu, idl, s);
+    for (int s = 0; s <= DEC_STAGES; ++s) first_ids[s] = __shfl_sync(0xffffffffu, idl, s);
+    if (lane == 0) {
+      v.dec_ids[2 * item + 1] = make_int4(first_ids[3], 0, 0, 0);
+      v.dec_ids[2 * item] = make_int4(bt_row, first_ids[0], first_ids[1], first_ids[2]);
+    }
+  }
+  const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
   if (lane == 0) {
 #pragma unroll
     for (int s = 0; s < DEC_STAGES; ++s)
@@ -415,7 +441,7 @@ __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const Pla
     __syncwarp();
     if (i + DEC_STAGES < n && lane == 0) {
       issue(s, next_id);
-      next_id = (i + DEC_STAGES + 1 < n) ? bt[b0 + i + DEC_STAGES + 1] : 0;
+      next_id = (i + DEC_STAGES + 1 < n) ? ld_keep(bt + b0 + i + DEC_STAGES + 1, keep) : 0;
     }
   }
   if (!ok) {
@@ -449,9 +475,11 @@ __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const Pla
     if (lane == 0) last = atomicAdd(&v.counters[seq * a.kv_heads + g], 1) == ns - 1;
     if (__shfl_sync(0xffffffffu, last, 0)) {
       __threadfence();
-      const int first = v.seqinfo[seq].x + g * ns;
-      // lane owns d = 4*lane..4*lane+3 of all 4 heads; partials are read through
-      // L2 (__ldcg) since other SMs wrote them during this launch.
+      // Other SMs wrote the partials during this launch, so they are read
+      // through L2: MERGE_CHUNK splits at a time are staged into this warp's
+      // idle TMA ring by cp.async (one L2 round trip per chunk).  Lane
+      // (s, h) = (lane / 4, lane % 4) then weighs split s of head h, and every
+      // lane accumulates d = 4*lane..4*lane+3 of all 4 heads from shared memory.
       float M[HY_GROUP], L[HY_GROUP];
       float4 acc[HY_GROUP];
 #pragma unroll
@@ -460,37 +488,57 @@ __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const Pla
         L[rr] = 0.f;
         acc[rr] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      for (int s0 = 0; s0 < ns; s0 += 8) {             // (m, l) of 8 splits x 4 heads per pass
-        const int sl = s0 + (lane >> 2);
-        float2 ml = make_float2(NEG_INF, 0.f);
-        if (sl < ns) ml = __ldcg(&v.part_ml[(size_t)(first + sl) * HY_GROUP + (lane & 3)]);
-        float mx = ml.x;                                // max over the 8 splits of head lane&3
+      const float* s_o = reinterpret_cast<const float*>(ring);
+      const float2* s_ml = reinterpret_cast<const float2*>(ring + MERGE_O_BYTES);
+      float* s_w = reinterpret_cast<float*>(ring + MERGE_O_BYTES + MERGE_ML_BYTES);
+      for (int s0 = 0; s0 < ns; s0 += MERGE_CHUNK) {
+        const int nsl = min(MERGE_CHUNK, ns - s0);
+        const uint8_t* g_o =
+            reinterpret_cast<const uint8_t*>(v.part_o + (size_t)(first + s0) * HY_GROUP * HY_HEAD_DIM);
+        const uint8_t* g_ml =
+            reinterpret_cast<const uint8_t*>(v.part_ml + (size_t)(first + s0) * HY_GROUP);
+        const int bytes_o = nsl * HY_GROUP * HY_HEAD_DIM * (int)sizeof(float);
+        const int bytes_ml = nsl * HY_GROUP * (int)sizeof(float2);
+        __syncwarp();                                   // the previous chunk is read
+        for (int off = lane * 16; off < bytes_o; off += 512) cp_async16(ring + off, g_o + off);
+        for (int off = lane * 16; off < bytes_ml; off += 512)
+          cp_async16(ring + MERGE_O_BYTES + off, g_ml + off);
+        cp_async_wait_all();
+        __syncwarp();
+        const int sl = lane >> 2, h = lane & 3;
+        const float2 ml = sl < nsl ? s_ml[sl * HY_GROUP + h] : make_float2(NEG_INF, 0.f);
+        float mx = ml.x;                                // max over the chunk's splits of head h
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        float m_old = M[0];
+#pragma unroll
+        for (int rr = 1; rr < HY_GROUP; ++rr) if (h == rr) m_old = M[rr];
+        const float m_new = fmaxf(m_old, mx);
+        const float w = sl < nsl ? exp2f(ml.x - m_new) : 0.f;
+        float lw = w * ml.y;                            // sum over the chunk of w * l, head h
+        lw += __shfl_xor_sync(0xffffffffu, lw, 4);
+        lw += __shfl_xor_sync(0xffffffffu, lw, 8);
+        lw += __shfl_xor_sync(0xffffffffu, lw, 16);
+        s_w[lane] = w;                                  // weight of split sl, head h
+        const float sc = exp2f(m_old - m_new);          // 0 when m_old was -inf
 #pragma unroll
         for (int rr = 0; rr < HY_GROUP; ++rr) {
-          const float mnew = fmaxf(M[rr], __shfl_sync(0xffffffffu, mx, rr));
-          const float sc = exp2f(M[rr] - mnew);
-          L[rr] *= sc;
-          acc[rr].x *= sc; acc[rr].y *= sc; acc[rr].z *= sc; acc[rr].w *= sc;
-          M[rr] = mnew;
+          const float scr = __shfl_sync(0xffffffffu, sc, rr);
+          M[rr] = __shfl_sync(0xffffffffu, m_new, rr);
+          L[rr] = L[rr] * scr + __shfl_sync(0xffffffffu, lw, rr);
+          acc[rr].x *= scr; acc[rr].y *= scr; acc[rr].z *= scr; acc[rr].w *= scr;
         }
-        const int nsl = min(8, ns - s0);
+        __syncwarp();
+#pragma unroll 1
         for (int k = 0; k < nsl; ++k) {
-          float4 po[HY_GROUP];
-#pragma unroll
-          for (int rr = 0; rr < HY_GROUP; ++rr)
-            po[rr] = __ldcg(reinterpret_cast<const float4*>(
-                v.part_o + ((size_t)(first + s0 + k) * HY_GROUP + rr) * HY_HEAD_DIM + 4 * lane));
 #pragma unroll
           for (int rr = 0; rr < HY_GROUP; ++rr) {
-            const float ms = __shfl_sync(0xffffffffu, ml.x, 4 * k + rr);
-            const float ls = __shfl_sync(0xffffffffu, ml.y, 4 * k + rr);
-            const float wgt = exp2f(ms - M[rr]);
-            L[rr] += wgt * ls;
-            acc[rr].x += wgt * po[rr].x; acc[rr].y += wgt * po[rr].y;
-            acc[rr].z += wgt * po[rr].z; acc[rr].w += wgt * po[rr].w;
+            const float wk = s_w[k * HY_GROUP + rr];
+            const float4 po =
+                *reinterpret_cast<const float4*>(s_o + (k * HY_GROUP + rr) * HY_HEAD_DIM + 4 * lane);
+            acc[rr].x += wk * po.x; acc[rr].y += wk * po.y;
+            acc[rr].z += wk * po.z; acc[rr].w += wk * po.w;
           }
         }
       }
@@ -800,7 +848,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   const uint32_t tmem = sh.tmem_base;
   hy_grid_wait();
   hy_grid_trigger();
-  const int n_pre = v.header[0], n_dec = v.header[1];
+  const uint64_t keep = l2_keep_policy();
+  const int n_pre = ld_keep(v.header, keep), n_dec = ld_keep(v.header + 1, keep);
   const bool use_tmem = (int)blockIdx.x < n_pre;      // the first n_pre CTAs take prefill items
   uint32_t dec_phase = 0, tile_ctr = 0;
   bool ok = true;
@@ -943,6 +992,7 @@ size_t hy_attn_workspace_bytes(const PlanDims& d) {
   off = align256(off + (size_t)d.max_pre * sizeof(int4));
   off = align256(off + (size_t)d.max_pre * sizeof(int4));  // sorted prefill items
   off = align256(off + (size_t)d.max_dec * 2 * sizeof(int4));
+  off = align256(off + (size_t)d.max_dec * 2 * sizeof(int4));   // cached block ids
   off = align256(off + (size_t)d.max_seqs * sizeof(int2));
   off = align256(off + (size_t)d.max_dec * HY_GROUP * HY_HEAD_DIM * sizeof(float));
   off = align256(off + (size_t)d.max_dec * HY_GROUP * sizeof(float2));
@@ -962,6 +1012,8 @@ static PlanView make_view(void* ws, const PlanDims& d) {
   v.pre_sorted = reinterpret_cast<int4*>(p + off);
   off = align256(off + (size_t)d.max_pre * sizeof(int4));
   v.dec = reinterpret_cast<int4*>(p + off);
+  off = align256(off + (size_t)d.max_dec * 2 * sizeof(int4));
+  v.dec_ids = reinterpret_cast<int4*>(p + off);
   off = align256(off + (size_t)d.max_dec * 2 * sizeof(int4));
   v.seqinfo = reinterpret_cast<int2*>(p + off);
   off = align256(off + (size_t)d.max_seqs * sizeof(int2));

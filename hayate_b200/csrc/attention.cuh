@@ -20,7 +20,11 @@ struct PlanView {
   int4* pre;          // prefill items by sequence (plan scratch)
   int4* pre_sorted;   // the same items, most key tiles first (what the kernel runs)
   int4* dec;          // per decode item: (seq, kv head, first block, end block), then
-                      // (query row, key length, splits of its sequence, 0)
+                      // (query row, key length, splits of its sequence, first item
+                      // of its sequence and KV head)
+  int4* dec_ids;      // per decode item, 2 x int4: its block-table row and first 4
+                      // block ids, cached by the first attention launch on the
+                      // plan (the plan writes row -1: not cached yet)
   int2* seqinfo;      // per sequence: first decode item, number of splits
   float* part_o;      // [max_dec][4][128]
   float2* part_ml;    // [max_dec][4]  (running max in log2 units, sum)

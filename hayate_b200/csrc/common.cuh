@@ -39,6 +39,36 @@ HY_DEVICE uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ------------------------------------------------- L2 residency of small tables
+// Loads with an L2 evict-last policy: the small per-step tables a kernel reads
+// once per layer (plan records, block tables) then stay in L2 while each layer
+// streams ~200 MB of weights through it, so the next layer's reads hit L2.
+HY_DEVICE uint64_t l2_keep_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+HY_DEVICE int ld_keep(const int* a, uint64_t pol) {
+  int v;
+  asm volatile("ld.global.L2::cache_hint.b32 %0, [%1], %2;" : "=r"(v) : "l"(a), "l"(pol));
+  return v;
+}
+HY_DEVICE int4 ld_keep(const int4* a, uint64_t pol) {
+  int4 v;
+  asm volatile("ld.global.L2::cache_hint.v4.b32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(a), "l"(pol));
+  return v;
+}
+
+// 16-byte global -> shared copy through L2 (cp.async.cg), completed by cp_async_wait_all
+HY_DEVICE void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+HY_DEVICE void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
 // ------------------------------------------------- programmatic dependent launch
 // Kernels of the step are launched with hy_launch: with programmatic stream
 // serialisation a kernel's CTAs may start while the previous kernel on the

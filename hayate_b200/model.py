@@ -208,7 +208,9 @@ class Runner:
                 h = K.add_rms_norm(x, nxt, eps, delta=F.linear(act, w.w_down))
             launches += self.LAYER_LAUNCHES + (self.ws is not None)   # + combine kernel
         if n_sample > 0:
-            logits = F.linear(h.index_select(0, self.sample_rows[:n_sample]), self.embed)
+            # every row sampled (decode steps): the sampled rows are rows 0..T-1 in order
+            hs = h if n_sample == T else h.index_select(0, self.sample_rows[:n_sample])
+            logits = F.linear(hs, self.embed)
             K.argmax(logits, self.next_tokens[:n_sample])
             K.commit_tokens(self.next_tokens[:n_sample], n_sample, self.sample_seq, sched, S,
                             self.req_tokens, err)
