@@ -146,7 +146,10 @@ int hy_attention_plan(const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, in
  * prefill and decode in one launch.  seq_bt_row (nullable) maps sequence i to
  * its block-table row.  bf16 runs the TMA + tensor-core kernel; fp32 a scalar
  * kernel for parity runs.  max_seqs/max_tokens must equal those given to
- * hy_attention_plan for the same workspace.
+ * hy_attention_plan for the same workspace.  The first bf16 call after a plan
+ * caches each decode item's block-table row and first block ids in the
+ * workspace for the later calls: block_tables and seq_bt_row must not change
+ * between a plan and the last call that uses it.
  * Replaces: cat + F.scaled_dot_product_attention(attn_mask, enable_gqa=True),
  * hayate/model/attention.py:52-64. */
 int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tokens,
