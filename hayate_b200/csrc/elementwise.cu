@@ -51,20 +51,24 @@ template <> struct Vec<float> {
 // vectors are loaded together with the row, so a row costs one memory round
 // trip plus a CTA reduction.
 constexpr int RN_THREADS = 128;
+// The split-K variant runs decode-sized batches (a few rows): 384 threads give
+// one 16-byte slot per thread at hidden size 2560, so each thread's partial
+// loads are one short batch.
+constexpr int RN_PARTS_THREADS = 384;
 
 // x <- round(x + delta) (when delta is given: the residual add of block.py:24,30),
 // y <- RMSNorm(x) * w.  With split-K partials instead of delta, delta is first
 // round(sum of the nparts fp32 partials, in order), i.e. the projection's
 // output as its GEMM would have rounded it.
-template <typename T, bool PARTS>
-__global__ void __launch_bounds__(RN_THREADS) add_rms_norm_kernel(
+template <typename T, bool PARTS, int THREADS>
+__global__ void __launch_bounds__(THREADS) add_rms_norm_kernel(
     T* __restrict__ x, long ldx, const T* __restrict__ delta, long ldd, int cols,
     const T* __restrict__ w, float eps, T* __restrict__ y, long ldy,
     const float* __restrict__ parts, int nparts, long pstride) {
   using V = Vec<T>;
   constexpr int N = V::N;
-  constexpr int RN_VEC = 32 / N;
-  __shared__ float red[RN_THREADS / 32];
+  constexpr int RN_VEC = (4096 / N + THREADS - 1) / THREADS;   // 16-byte slots per thread
+  __shared__ float red[THREADS / 32];
   const long r = blockIdx.x;
   const int nvec = cols / N;
   T* xr = x + r * ldx;
@@ -74,7 +78,7 @@ __global__ void __launch_bounds__(RN_THREADS) add_rms_norm_kernel(
   uint4 xv[RN_VEC], wv[RN_VEC];
 #pragma unroll
   for (int k = 0; k < RN_VEC; ++k) {          // the weights are no earlier kernel's output
-    const int vi = threadIdx.x + RN_THREADS * k;
+    const int vi = threadIdx.x + THREADS * k;
     if (vi < nvec) wv[k] = *reinterpret_cast<const uint4*>(w + vi * N);
   }
   hy_grid_wait();
@@ -82,7 +86,7 @@ __global__ void __launch_bounds__(RN_THREADS) add_rms_norm_kernel(
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < RN_VEC; ++k) {
-    const int vi = threadIdx.x + RN_THREADS * k;
+    const int vi = threadIdx.x + THREADS * k;
     if (vi < nvec) {
       float v[N];
       V::load(xr + vi * N, v);
@@ -145,12 +149,12 @@ __global__ void __launch_bounds__(RN_THREADS) add_rms_norm_kernel(
   __syncthreads();
   float tot = 0.f;
 #pragma unroll
-  for (int i = 0; i < RN_THREADS / 32; ++i) tot = __fadd_rn(tot, red[i]);
+  for (int i = 0; i < THREADS / 32; ++i) tot = __fadd_rn(tot, red[i]);
   const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)cols), eps)));
   T* yr = y + r * ldy;
 #pragma unroll
   for (int k = 0; k < RN_VEC; ++k) {
-    const int vi = threadIdx.x + RN_THREADS * k;
+    const int vi = threadIdx.x + THREADS * k;
     if (vi < nvec) {
       float v[N], g[N], o[N];
       V::load(reinterpret_cast<const T*>(&xv[k]), v);
@@ -205,12 +209,19 @@ cudaError_t hy_launch_add_rms_norm(int dtype, void* x, long ldx, const void* del
   if (rows <= 0) return cudaSuccess;
   using B = __nv_bfloat16;
   if (dtype == 0)
-    return hy_launch(parts ? add_rms_norm_kernel<B, true> : add_rms_norm_kernel<B, false>,
-                     dim3(rows), dim3(RN_THREADS), 0, st, (B*)x, ldx, (const B*)delta, ldd, cols,
-                     (const B*)w, eps, (B*)y, ldy, parts, nparts, pstride);
-  return hy_launch(parts ? add_rms_norm_kernel<float, true> : add_rms_norm_kernel<float, false>,
-                   dim3(rows), dim3(RN_THREADS), 0, st, (float*)x, ldx, (const float*)delta, ldd,
-                   cols, (const float*)w, eps, (float*)y, ldy, parts, nparts, pstride);
+    return parts ? hy_launch(add_rms_norm_kernel<B, true, RN_PARTS_THREADS>, dim3(rows),
+                             dim3(RN_PARTS_THREADS), 0, st, (B*)x, ldx, (const B*)delta, ldd,
+                             cols, (const B*)w, eps, (B*)y, ldy, parts, nparts, pstride)
+                 : hy_launch(add_rms_norm_kernel<B, false, RN_THREADS>, dim3(rows),
+                             dim3(RN_THREADS), 0, st, (B*)x, ldx, (const B*)delta, ldd, cols,
+                             (const B*)w, eps, (B*)y, ldy, parts, nparts, pstride);
+  return parts ? hy_launch(add_rms_norm_kernel<float, true, RN_PARTS_THREADS>, dim3(rows),
+                           dim3(RN_PARTS_THREADS), 0, st, (float*)x, ldx, (const float*)delta,
+                           ldd, cols, (const float*)w, eps, (float*)y, ldy, parts, nparts,
+                           pstride)
+               : hy_launch(add_rms_norm_kernel<float, false, RN_THREADS>, dim3(rows),
+                           dim3(RN_THREADS), 0, st, (float*)x, ldx, (const float*)delta, ldd,
+                           cols, (const float*)w, eps, (float*)y, ldy, parts, nparts, pstride);
 }
 
 cudaError_t hy_launch_silu_mul(int dtype, const void* gu, long ld, int rows, int inter, void* y,
