@@ -868,11 +868,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   // decode items (warps 0..ATT_WARPS-1): each warp takes the next one from this
   // layer's counter, so warps that finish early keep pulling work.  A launch
   // whose decode items fit one round of warps (and has no prefill items)
-  // assigns them statically and skips the counters' round trips.
+  // assigns them statically and skips the counters' round trips; item i goes
+  // to CTA i % grid, so that a small batch spreads its TMA boxes over every
+  // SM (an SM's TMA unit takes a 2 KB box about every 100 cycles).
   const int lane = threadIdx.x & 31;
   const int nw = (int)gridDim.x * ATT_WARPS;
   if (n_pre == 0 && n_dec <= nw) {
-    const int item = (int)blockIdx.x * ATT_WARPS + warp;
+    const int item = warp * (int)gridDim.x + (int)blockIdx.x;
     if (warp < ATT_WARPS && item < n_dec && ok)
       ok = decode_item(&kv_map, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
                        dec_phase);
