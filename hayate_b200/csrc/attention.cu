@@ -293,7 +293,7 @@ HY_DEVICE int kv_row(const MainArgs& a, int blk, int kv, int g) {
 }
 
 // Returns false if a wait ran out (the caller stops).
-__device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
+__device__ bool decode_item(const CUtensorMap* tiles, const MainArgs& a, const PlanView& v,
                             int item, uint8_t* ring, uint64_t* bars, uint32_t& phase) {
   const int lane = threadIdx.x & 31;
   const uint64_t keep = l2_keep_policy();
@@ -318,10 +318,8 @@ __device__ bool decode_item(const CUtensorMap* map, const MainArgs& a, const Pla
     uint8_t* st = ring + s * DEC_TILE_BYTES;
     fence_proxy_async();
     mbar_arrive_expect_tx(&bars[s], DEC_TILE_BYTES);
-    tma_load_2d(st, map, 0, rk, &bars[s]);
-    tma_load_2d(st + 2048, map, 64, rk, &bars[s]);
-    tma_load_2d(st + 4096, map, 0, rv, &bars[s]);
-    tma_load_2d(st + 6144, map, 64, rv, &bars[s]);
+    tma_load_3d(st, tiles, 0, rk, 0, &bars[s]);            // K: both halves, one box
+    tma_load_3d(st + 4096, tiles, 0, rv, 0, &bars[s]);     // V
   };
 
   // The block-table row and the ids of the ring's first blocks and the one
@@ -810,13 +808,15 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const
 }
 
 __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
-    const __grid_constant__ CUtensorMap kv_map, MainArgs a, PlanView v) {
+    const __grid_constant__ CUtensorMap kv_map, const __grid_constant__ CUtensorMap kv_tiles,
+    MainArgs a, PlanView v) {
   __shared__ Shared sh;
   extern __shared__ uint8_t dyn_smem[];
   uint8_t* payload = payload_base(dyn_smem);
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     prefetch_tmap(&kv_map);
+    prefetch_tmap(&kv_tiles);
     for (int w = 0; w < ATT_WARPS; ++w)
       for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&sh.dec_bar[w][s], 1);
     for (int s = 0; s < TC_NS; ++s) {
@@ -876,7 +876,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   if (n_pre == 0 && n_dec <= nw) {
     const int item = warp * (int)gridDim.x + (int)blockIdx.x;
     if (warp < ATT_WARPS && item < n_dec && ok)
-      ok = decode_item(&kv_map, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
+      ok = decode_item(&kv_tiles, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
                        dec_phase);
   } else {
     while (ok && warp < ATT_WARPS) {
@@ -884,7 +884,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
       if (lane == 0) item = atomicAdd(&grab[0], 1);
       item = __shfl_sync(0xffffffffu, item, 0);
       if (item >= n_dec) break;
-      ok = decode_item(&kv_map, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
+      ok = decode_item(&kv_tiles, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
                        dec_phase);
     }
     __syncthreads();
@@ -1039,7 +1039,7 @@ cudaError_t hy_launch_attn_plan(const int32_t* cu_q, const int32_t* seq_lens_k, 
                    kv_heads, hy_attn_warp_slots(dev), make_view(ws, d), err);
 }
 
-cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* cache, const void* q, void* out,
+cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const void* cache, const void* q, void* out,
                                 int q_heads,
                                 int kv_heads, int layer_row_base, int oob_row, int num_blocks,
                                 const int32_t* block_tables, int bt_pitch,
@@ -1076,7 +1076,8 @@ cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* cache, const
   a.err = err;
   const PlanView v = make_view(ws, d);
   const int grid = device_sms(dev) * g_ctas_per_sm[dev < 64 && dev >= 0 ? dev : 0];
-  return hy_launch(attn_main_kernel, dim3(grid), dim3(ATT_THREADS), SMEM_BYTES, st, map, a, v);
+  return hy_launch(attn_main_kernel, dim3(grid), dim3(ATT_THREADS), SMEM_BYTES, st, maps.halves,
+                   maps.tiles, a, v);
 }
 
 cudaError_t hy_launch_attn_fp32(const float* q, float* out, int T, int q_heads, int kv_heads,

@@ -6,6 +6,16 @@
 #include <stddef.h>
 #include <stdint.h>
 
+// Tensor maps over the bf16 KV cache viewed as rows of 128 elements (256 B):
+//   halves: 2-D, box = 16 rows x 64 columns (one half of a block's head tile)
+//   tiles:  3-D (64 columns, rows, 2 halves 128 B apart), box = 16 rows x both
+//           halves: one (block, K or V, head) tile, landing in shared memory as
+//           the two half boxes would (half h at +2 KB h, 128-byte swizzle)
+struct KvMaps {
+  CUtensorMap halves;
+  CUtensorMap tiles;
+};
+
 // Capacities of one attention workspace.
 struct PlanDims {
   int max_pre;     // prefill items (kv_head x 16-token tile)
@@ -40,7 +50,7 @@ size_t hy_attn_workspace_bytes(const PlanDims& d);
 cudaError_t hy_launch_attn_plan(const int32_t* cu_q, const int32_t* seq_lens_k, int S,
                                 int kv_heads, const PlanDims& d, void* ws, int32_t* err,
                                 int dev, cudaStream_t st);
-cudaError_t hy_launch_attn_bf16(const CUtensorMap& map, const void* cache, const void* q, void* out,
+cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const void* cache, const void* q, void* out,
                                 int q_heads,
                                 int kv_heads, int layer_row_base, int oob_row, int num_blocks,
                                 const int32_t* block_tables, int bt_pitch,

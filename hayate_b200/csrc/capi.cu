@@ -60,7 +60,7 @@ struct MapEntry {
   int dev;
   const void* base;
   long rows;
-  CUtensorMap map;
+  KvMaps maps;
 };
 
 std::mutex g_map_mu;
@@ -80,28 +80,36 @@ int get_encoder() {
   return HY_OK;
 }
 
-// 2-D view of the cache: rows of 128 bf16 (256 B); a box is 16 rows x 64
-// columns (one half of a block's head tile), swizzled 128 B in shared memory.
-int kv_map_for(int dev, const void* base, long rows, CUtensorMap* out) {
+// The cache's tensor maps (KvMaps): rows of 128 bf16 (256 B), 16-row boxes,
+// 128-byte swizzle in shared memory.
+int kv_map_for(int dev, const void* base, long rows, KvMaps* out) {
   std::lock_guard<std::mutex> lk(g_map_mu);
   for (int i = 0; i < g_nmaps; ++i)
     if (g_maps[i].dev == dev && g_maps[i].base == base && g_maps[i].rows == rows) {
-      *out = g_maps[i].map;
+      *out = g_maps[i].maps;
       return HY_OK;
     }
   int rc = get_encoder();
   if (rc) return rc;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
     return fail(HY_E_INVALID, "kv_cache must be 16-byte aligned");
-  CUtensorMap m;
-  cuuint64_t dims[2] = {HY_HEAD_DIM, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {HY_HEAD_DIM * 2};
-  cuuint32_t box[2] = {64, HY_BLOCK};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  KvMaps m;
+  cuuint64_t dims2[2] = {HY_HEAD_DIM, (cuuint64_t)rows};
+  cuuint64_t strides2[1] = {HY_HEAD_DIM * 2};
+  cuuint32_t box2[2] = {64, HY_BLOCK};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(&m.halves, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                        dims2, strides2, box2, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_SUCCESS) {
+    cuuint64_t dims3[3] = {64, (cuuint64_t)rows, 2};
+    cuuint64_t strides3[2] = {HY_HEAD_DIM * 2, 128};         // row: 256 B, half: 128 B
+    cuuint32_t box3[3] = {64, HY_BLOCK, 2};
+    r = g_encode(&m.tiles, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims3,
+                 strides3, box3, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) {
     char buf[64];
     snprintf(buf, sizeof(buf), "%d", (int)r);
@@ -133,7 +141,7 @@ __global__ void wait_timeout_probe_kernel(int32_t* err, uint64_t timeout_ns, int
 }
 
 // Shared with other translation units of the library (not part of the C ABI).
-int hy_attention_kv_map(int dev, const void* base, long rows, CUtensorMap* out) {
+int hy_attention_kv_map(int dev, const void* base, long rows, KvMaps* out) {
   return kv_map_for(dev, base, rows, out);
 }
 
@@ -330,7 +338,7 @@ int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tok
   const PlanDims d = hy_attn_plan_dims(max_seqs, max_tokens, kv_heads, dev);
   if (workspace_bytes < hy_attn_workspace_bytes(d))
     return fail(HY_E_INVALID, "hy_varlen_attention: workspace too small for max_seqs/max_tokens");
-  CUtensorMap map;
+  KvMaps map;
   int rc = kv_map_for(dev, kv_cache, rows, &map);
   if (rc) return rc;
   return cuda_result(

@@ -32,7 +32,7 @@
 // address comes from cudaGetSymbolAddress (see scratch_for).
 static __device__ __align__(256) uint8_t g_noalloc_scratch[HY_NOALLOC_SCRATCH_BYTES];
 
-int hy_attention_kv_map(int dev, const void* base, long rows, CUtensorMap* out);  // capi.cu
+int hy_attention_kv_map(int dev, const void* base, long rows, KvMaps* out);  // capi.cu
 void hy_set_error(const char* msg);                                              // capi.cu
 
 namespace {
@@ -109,7 +109,7 @@ extern "C" int hy_varlen_attention_noalloc(
   }
   void* ws = scratch_for(dev);
   if (ws == nullptr) return HY_E_CUDA;
-  CUtensorMap map;
+  KvMaps map;
   int rc = hy_attention_kv_map(dev, kv_cache, rows, &map);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
