@@ -1,0 +1,101 @@
+"""Critical path of graph-replayed decode steps, per kernel.
+
+``python -m hayate_b200.steptrace [--steps 10]`` runs the upfront workload's 10
+requests (bf16 Qwen3-4B, random weights) into their decode phase, records
+``--steps`` decode steps with the torch profiler (CUPTI kernel timestamps, no
+ncu) and charges each kernel only for the time it extends the step: its end
+minus the later of its own start and the previous kernel's end.  Kernels that
+programmatic dependent launch starts early (before the previous kernel ends)
+are therefore not charged for the overlap, which plain per-kernel durations are.
+"""
+from __future__ import annotations
+
+import argparse
+import collections
+
+import torch
+
+# kernel-name fragments -> row label, first match wins
+LABELS = (
+    ("attn_main", "attention"),
+    ("add_rms_norm_kernel<__nv_bfloat16, true", "add+RMSNorm, split-K partials"),
+    ("add_rms_norm", "add+RMSNorm"),
+    ("qk_norm_rope", "QK-norm+RoPE (+KV append)"),
+    ("silu_mul", "SiLU*up"),
+    ("nvjet_tss_192x16", "cuBLAS o/down (batched over K slices)"),
+    ("nvjet_tst_192x16", "cuBLAS gate/up"),
+    ("nvjet_tst_128x8", "cuBLAS qkv"),
+    ("nvjet_tst_384x16", "cuBLAS LM head"),
+    ("indexSelect", "embedding"),
+    ("plan_kernel", "attention plan"),
+    ("pack_kernel", "pack"),
+    ("argmax", "argmax"),
+    ("commit", "commit"),
+    ("Memcpy", "memcpy"),
+)
+
+
+def label(name: str) -> str:
+    for frag, lab in LABELS:
+        if frag in name:
+            return lab
+    return name[:48]
+
+
+def critical_path(events):
+    """events: (name, start_us, end_us) sorted by start -> (per-label exclusive
+    time, duration, count), total span, gaps between kernels."""
+    excl = collections.defaultdict(float)
+    dur = collections.defaultdict(float)
+    cnt = collections.Counter()
+    prev_end, gaps = None, 0.0
+    for name, s, t in events:
+        lab = label(name)
+        base = s if prev_end is None else max(prev_end, s)
+        if prev_end is not None and s > prev_end:
+            gaps += s - prev_end
+        excl[lab] += max(0.0, t - base)
+        dur[lab] += t - s
+        cnt[lab] += 1
+        prev_end = t if prev_end is None else max(prev_end, t)
+    span = events[-1][2] - events[0][1] if events else 0.0
+    return excl, dur, cnt, span, gaps
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--steps", type=int, default=10)
+    args = ap.parse_args()
+    from torch.profiler import ProfilerActivity, profile
+
+    from .config import EngineConfig
+    from .engine import Engine, Request
+    from .workloads import upfront
+    ecfg = EngineConfig(max_num_seqs=16, max_batched_tokens=8192, prefill_chunk=512,
+                        num_kv_blocks=1024, max_model_len=1024, cuda_graphs=True,
+                        ignore_eos=True)
+    eng = Engine("Qwen/Qwen3-4B", engine_config=ecfg, weights="device")
+    prompts = [r.prompt for r in upfront(seed=0)]
+    eng.generate_text(prompts, max_tokens=64)            # warm-up: graphs captured
+    for p in prompts:
+        eng.add_request(Request(id=eng.request_id, prompt=p, max_tokens=args.steps + 50))
+        eng.request_id += 1
+    eng.generate()                                      # prefill
+    eng.generate()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(args.steps):
+            eng.generate()
+        torch.cuda.synchronize()
+    ev = sorted(((e.name, e.time_range.start, e.time_range.end) for e in prof.events()
+                 if e.device_type == torch.autograd.DeviceType.CUDA), key=lambda x: x[1])
+    excl, dur, cnt, span, gaps = critical_path(ev)
+    print(f"{args.steps} decode steps of 10 sequences: {span / args.steps:.1f} us per step, "
+          f"gaps between kernels {gaps / args.steps:.1f} us per step")
+    for lab, x in sorted(excl.items(), key=lambda kv: -kv[1]):
+        print(f"{lab:40s} {cnt[lab] / args.steps:6.1f}/step  {x / cnt[lab]:7.2f} us excl "
+              f"({100 * x / span:4.1f}%)  {dur[lab] / cnt[lab]:7.2f} us duration")
+
+
+if __name__ == "__main__":
+    main()

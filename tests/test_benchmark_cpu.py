@@ -25,3 +25,33 @@ def test_workloads_are_seeded_and_shaped():
     assert all(512 <= len(x.prompt) <= 4096 for x in r)
     reqs = benchmark.make_requests(4, 7, 1337, 160, 320)
     assert len(reqs) == 4 and all(160 <= len(x["prompt"]) <= 320 for x in reqs)
+
+
+def test_step_trace_charges_only_the_time_a_kernel_extends_the_step():
+    """A kernel started early by programmatic dependent launch (the second one
+    below starts at 8 while the first runs to 10) is charged from the first's end;
+    idle time between kernels is counted as gaps, not charged to either."""
+    from hayate_b200.steptrace import critical_path, label
+    ev = [("nvjet_tst_128x8_64x12", 0.0, 10.0), ("attn_main_kernel", 8.0, 20.0),
+          ("silu_mul_kernel", 25.0, 30.0)]
+    excl, dur, cnt, span, gaps = critical_path(ev)
+    assert excl[label("nvjet_tst_128x8_64x12")] == 10.0
+    assert excl["attention"] == 10.0 and dur["attention"] == 12.0
+    assert excl["SiLU*up"] == 5.0
+    assert span == 30.0 and gaps == 5.0 and sum(cnt.values()) == 3
+
+
+def test_splitk_slices_for_decode_sized_bf16_steps_only():
+    """o_proj (K 4096) and down_proj (K 9728) split into 8 K slices up to 32 rows
+    and 4 up to 128; larger steps, fp32 runs and K that the slices do not divide
+    into 8-element multiples keep one GEMM."""
+    from types import SimpleNamespace
+    import torch
+    from hayate_b200.model import Runner
+    bf16, fp32 = SimpleNamespace(dtype=torch.bfloat16), SimpleNamespace(dtype=torch.float32)
+    assert Runner.splitk_parts(bf16, 16, 4096) == 8
+    assert Runner.splitk_parts(bf16, 32, 9728) == 8
+    assert Runner.splitk_parts(bf16, 64, 9728) == 4
+    assert Runner.splitk_parts(bf16, 129, 4096) == 1
+    assert Runner.splitk_parts(fp32, 16, 4096) == 1
+    assert Runner.splitk_parts(bf16, 16, 4100) == 1
