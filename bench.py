@@ -2,43 +2,56 @@
 
 ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hayate|reference]``
 
-A *step* is one complete run of the "submit all upfront" workload through the
-engine: 10 requests with prompt lengths U[64,512] (uniform random token ids),
-256 greedy tokens each, Qwen3-4B architecture in bf16 with random N(0,0.02)
-weights (seed 0), continuous batching until every request finishes.  Under
-torchrun every rank is an independent replica on its own GPU with its own
-requests (seed = rank): request-level data parallelism, no collective on the
-data path (weak scaling).  ``value`` is total output tokens of all ranks over
-the slowest rank's device time; ``e2e`` is the same metric through
-``Engine.generate_text`` with host token lists in and out.
+Workload: the request-level data-parallel configuration the output-tok/s metric
+is quoted on -- N x 256 requests, prompt lengths U[512,4096] (uniform-random
+token ids), 256 greedy tokens each (fixed length, eos ignored), Qwen3-4B
+architecture in bf16 with random N(0,0.02) weights.  The request set is split
+over the N GPUs by the router's least-outstanding-work rule
+(``router.least_work_assignment``), computed identically on every rank; each
+rank is an independent engine replica on its own GPU (no collective on the
+data path).  At N=8 the set is the 2048-request configuration; at N=1 it is the
+256-request load one of its replicas carries.
+
+A *step* is one complete run of the rank's share through the engine: every
+request submitted at once, continuous batching (512-token prefill chunks mixed
+into decode steps, paged KV) until all finish.  ``value`` is total output
+tokens of all ranks over the slowest rank's device time; ``e2e`` is the same
+metric through ``Engine.generate_text`` with host token lists in and out.
 
 The line also carries the ragged-attention roofline (the operator case of 256
 decode sequences with contexts log-uniform in [256,16384] plus 4 prefill
-chunks of 512 tokens, one layer, paged KV in 16-token blocks) and, at N=1, a
-CPU baseline: the reference algorithm (``oracle.reference``) timed on this
-host's cores.  ``--impl reference`` times only that CPU path.
+chunks of 512 tokens, one layer, paged KV in 16-token blocks), the 10-request
+"submit all upfront" run (prompts U[64,512]) as a secondary figure, and, at
+N=1, a CPU baseline: the reference algorithm (``oracle.reference``) timed on
+this host's cores.  ``--impl reference`` times only that CPU path.
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
 import sys
 import time
 
-import numpy as np
 import torch
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
-WORKLOAD = ("upfront: 10 requests/GPU, prompt lengths U[64,512], uniform-random ids, 256 greedy "
-            "tokens each, all submitted at once; Qwen3-4B arch (36 layers, hidden 2560, 32/8 "
-            "heads, MLP 9728, vocab 151936) bf16 random-init N(0,0.02) seed 0")
-N_REQ, MAX_TOKENS = 10, 256
+PER_GPU = 256                      # requests per replica
+MAX_TOKENS = 256
+PROMPT_LO, PROMPT_HI = 512, 4096
+WORKLOAD = ("replica share of N x 256 requests (the 2048-request set at N=8), prompt lengths "
+            "U[512,4096], uniform-random ids, 256 greedy tokens each (eos ignored), split over "
+            "the N GPUs by least outstanding work (prompt + max_tokens), every request of a "
+            "share submitted at once; Qwen3-4B arch (36 layers, hidden 2560, 32/8 heads, "
+            "head_dim 128, MLP 9728, vocab 151936) bf16")
+WEIGHTS = ("random-init N(0,0.02) drawn on the GPU (torch.cuda generator, seed 0); the parity "
+           "fixtures use the CPU recipe of the same distribution, and throughput does not "
+           "depend on the values")
+REF_BATCH = 20                     # the reference engine's MAX_BATCH_SIZE (engine.py:13)
 PEAKS_FILE = os.path.join(REPO, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
 
@@ -160,11 +173,26 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------- engine arm
-def make_engine(device):
+def rank_share(world: int, rank: int, seed: int = 0):
+    """This rank's requests of the world x 256 request set (least outstanding
+    work, the router's rule for requests that arrive together)."""
+    from hayate_b200.router import least_work_assignment
+    from hayate_b200.workloads import replicas
+    ws = replicas(seed=seed, n=PER_GPU * world, lo=PROMPT_LO, hi=PROMPT_HI, max_tokens=MAX_TOKENS)
+    owner = least_work_assignment([len(w.prompt) + w.max_tokens for w in ws], world)
+    return [w for w, o in zip(ws, owner) if o == rank]
+
+
+def make_engine(device, share):
+    """An engine sized so the whole share is admitted at once (every request's
+    worst-case KV blocks reserved)."""
     from hayate_b200.config import EngineConfig
     from hayate_b200.engine import Engine
-    ecfg = EngineConfig(max_num_seqs=16, max_batched_tokens=8192, prefill_chunk=512,
-                        num_kv_blocks=1024, max_model_len=1024, cuda_graphs=True,
+    from hayate_b200.scheduler import blocks_for
+    blocks = sum(blocks_for(len(w.prompt) + w.max_tokens, 16) for w in share) + 64
+    ecfg = EngineConfig(max_num_seqs=max(PER_GPU, len(share)), max_batched_tokens=8192,
+                        prefill_chunk=512, num_kv_blocks=blocks,
+                        max_model_len=PROMPT_HI + MAX_TOKENS + 16, cuda_graphs=True,
                         ignore_eos=True)
     return Engine("Qwen/Qwen3-4B", engine_config=ecfg, dtype=torch.bfloat16, weights="device",
                   seed=0, device=device)
@@ -212,13 +240,19 @@ def profile_traffic():
 
 
 # ---------------------------------------------------------------------- CPU arm
+CPU_SAMPLE = ("decode steps of the reference step loop restated on CPU (oracle/reference.py, "
+              "engine.py:184-217) over its full batch of 20 requests (MAX_BATCH_SIZE) taken from "
+              "the rank-0 share of this workload, bf16, their caches pre-filled with random "
+              "values at their prompt lengths (a decode step's cost does not depend on them); "
+              "prefill is not timed -- it is ~90% of this workload's tokens, so the CPU figure "
+              "is an upper bound on the reference's throughput here")
+
+
 def cpu_reference_decode(steps: int, warmup: int, seed: int = 0):
     """The reference step loop (oracle.reference.RefEngine) on this host's CPU
-    cores: decode steps of the 10-request upfront batch at its prompt lengths,
-    bf16, caches pre-filled with random values (a decode step's cost does not
-    depend on them).  Returns (output tok/s, seconds per step, threads)."""
+    cores: decode steps of a 20-request batch of the workload.  Returns
+    (output tok/s, seconds per step, threads)."""
     from hayate_b200.config import QWEN3_4B as cfg
-    from hayate_b200.workloads import upfront
     from oracle import reference as R
     from hayate_b200 import weights as Wt
     threads = os.cpu_count() or 1
@@ -230,7 +264,8 @@ def cpu_reference_decode(steps: int, warmup: int, seed: int = 0):
     # the seed-0 weights of the parity fixtures, filled block-parallel
     Wr = R.RefWeights.from_host(Wt.exact_seeded(cfg, seed), torch.bfloat16)
     eng = R.RefEngine(Wr)
-    for sr in upfront(seed=seed):
+    batch = rank_share(1, 0, seed)[:REF_BATCH]
+    for sr in batch:
         r = eng.add(sr.prompt, 10 ** 6)
         L = len(sr.prompt)
         r.k = rnd(cfg.num_layers, cfg.num_kv_heads, L, cfg.head_dim)
@@ -242,7 +277,7 @@ def cpu_reference_decode(steps: int, warmup: int, seed: int = 0):
     for _ in range(steps):
         eng.step()
     dt = (time.perf_counter() - t0) / steps
-    return N_REQ / dt, dt, threads
+    return len(batch) / dt, dt, threads
 
 
 def reference_arm(args, world, rank):
@@ -254,13 +289,11 @@ def reference_arm(args, world, rank):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "requests_per_gpu": N_REQ, "max_tokens": MAX_TOKENS},
+        "config": {"workload": WORKLOAD, "requests_per_gpu": PER_GPU, "max_tokens": MAX_TOKENS,
+                   "step": "one decode step of the reference engine over 20 requests",
+                   "left_out": "prefill (not timed on the CPU)"},
         "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": "one step = one decode step of the 10-request upfront batch "
-                                   "through the reference step loop restated on CPU "
-                                   "(oracle/reference.py, engine.py:184-217), bf16, caches at "
-                                   "the prompt lengths pre-filled with random values; prefill "
-                                   "not timed"},
+                         "sample": CPU_SAMPLE},
         "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -268,6 +301,9 @@ def reference_arm(args, world, rank):
 
 
 # ---------------------------------------------------------------------- main
+E2E_RUNS = 3        # end-to-end runs (host lists in and out), after the device-resident ones
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -287,10 +323,12 @@ def main():
     from hayate_b200.workloads import upfront
 
     device = torch.device("cuda", local)
-    eng = make_engine(device)
-    reqs = upfront(seed=rank)
-    host_prompts = [r.prompt for r in reqs]
+    share = rank_share(world, rank)
+    eng = make_engine(device, share)
+    eng.capture_graphs()                       # every decode bucket, before any timing
+    host_prompts = [w.prompt for w in share]
     dev_prompts = [torch.tensor(p, dtype=torch.int32, device=device) for p in host_prompts]
+    prompt_tokens = sum(len(p) for p in host_prompts)
 
     def device_run():
         return run_workload(eng, dev_prompts, MAX_TOKENS)
@@ -311,17 +349,26 @@ def main():
     ms_max = max_over_ranks(ms, world)
     toks_all = sum_over_ranks(toks, world)
 
+    e2e_steps = max(1, min(args.steps, E2E_RUNS))
     h0, d0 = eng.h2d_bytes, eng.d2h_bytes
     barrier(world, local)
-    ems, etoks, ewall = timed(eng, e2e_run, args.steps)
+    ems, etoks, ewall = timed(eng, e2e_run, e2e_steps)
     barrier(world, local)
     ems_max = max_over_ranks(ems, world)
     etoks_all = sum_over_ranks(etoks, world)
-    h2d = (eng.h2d_bytes - h0) / args.steps
-    d2h = (eng.d2h_bytes - d0) / args.steps
+    h2d = (eng.h2d_bytes - h0) / e2e_steps
+    d2h = (eng.d2h_bytes - d0) / e2e_steps
+
+    # secondary: the 10-request "submit all upfront" run on the same engine
+    c2 = [torch.tensor(r.prompt, dtype=torch.int32, device=device) for r in upfront(seed=rank)]
+    run_workload(eng, c2, 256)
+    c2_ms, c2_toks, _ = timed(eng, lambda: run_workload(eng, c2, 256), 3)
     err = eng.check_device_errors()
     if err:
         raise RuntimeError(f"device error word {err}")
+    c2_line = {"workload": "10 requests, prompts U[64,512], 256 tokens each, all at once",
+               "value": c2_toks / (c2_ms * 1e-3), "unit": "tok/s", "ms_per_run": c2_ms / 3,
+               "runs": 3}
 
     # ragged-attention roofline (every rank runs it; rank 0 reports)
     del eng
@@ -335,33 +382,36 @@ def main():
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         tok_s, dt, threads = cpu_reference_decode(steps=3, warmup=1)
         cpu = {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": "3 decode steps (after 1 warm-up) of the 10-request upfront batch "
-                         "through the reference step loop restated on CPU (oracle/reference.py), "
-                         "bf16, caches at the prompt lengths pre-filled with random values; "
-                         "prefill not timed"}
+               "sample": "3 " + CPU_SAMPLE + " (after 1 warm-up step)"}
     if rank == 0:
-        emit_line(args, world, toks_all, ms_max, wall_ms, etoks_all, ems_max, h2d, d2h, launches,
-                  am, achieved, peak, peak_kind, cpu, clocks)
+        emit_line(args, world, toks_all, ms_max, wall_ms, etoks_all, ems_max, e2e_steps, h2d, d2h,
+                  launches, am, achieved, peak, peak_kind, cpu, clocks, c2_line,
+                  len(share), prompt_tokens)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
 
 
-def emit_line(args, world, toks_all, ms_max, wall_ms, etoks_all, ems_max, h2d, d2h, launches,
-              am, achieved, peak, peak_kind, cpu, clocks):
+def emit_line(args, world, toks_all, ms_max, wall_ms, etoks_all, ems_max, e2e_steps, h2d, d2h,
+              launches, am, achieved, peak, peak_kind, cpu, clocks, c2_line, n_share,
+              prompt_tokens):
     line = {
         "metric": "total output tok/s", "value": toks_all / (ms_max * 1e-3), "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (uniform-random token ids, random-init weights)",
-        "config": {"workload": WORKLOAD, "requests_per_gpu": N_REQ, "max_tokens": MAX_TOKENS,
-                   "parallelism": f"request-level replicas x{world}",
-                   "step": "one full run of the workload (prefill + 256 decode steps)",
-                   "l2": "no flush: every decode step streams 8 GB of weights (> 126 MB L2)",
+        "config": {"workload": WORKLOAD, "weights": WEIGHTS, "requests_per_gpu": PER_GPU,
+                   "requests_rank0": n_share, "prompt_tokens_rank0": prompt_tokens,
+                   "max_tokens": MAX_TOKENS,
+                   "parallelism": f"request-level replicas x{world} (no collective on the data path)",
+                   "engine": "max_num_seqs 256, 8192 tokens per step, 512-token prefill chunks, "
+                             "16-token KV blocks, CUDA-graph decode steps",
+                   "step": "one full run of the rank's share (prefill + 256 decode tokens each)",
+                   "l2": "no flush: every engine step streams 8 GB of weights (> 126 MB L2)",
                    "wall_ms_per_step": wall_ms / args.steps},
         "e2e": {"value": etoks_all / (ems_max * 1e-3), "unit": "tok/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "api": "Engine.generate_text(host token lists) -> Request.tokens"},
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -373,6 +423,7 @@ def emit_line(args, world, toks_all, ms_max, wall_ms, etoks_all, ems_max, h2d, d
                                  "16-token blocks, permuted block table, one layer",
                      "algorithmic_bytes": am["bytes"], "ms_per_launch": am["ms_mean"],
                      "prefill_flops": am["prefill_flops"]},
+        "secondary": {"upfront10": c2_line},
         "cpu_baseline": cpu,
         "clocks": clocks,
     }

@@ -43,6 +43,8 @@ SIGNATURES = {
     "hy_add_rms_norm": (C.c_int, [I32, P, I64, P, I64, I32, I32, P, F32, P, I64, P]),
     "hy_add_rms_norm_splitk": (C.c_int, [I32, P, I64, P, I32, I64, I64, I32, I32, P, F32, P,
                                          I64, P]),
+    "hy_gather_add_rms_norm": (C.c_int, [I32, P, I64, P, I32, P, I64, P, I32, I64, I32, I32, P,
+                                         F32, P, I64, P, I64, P, P]),
     "hy_silu_mul": (C.c_int, [I32, P, I64, I32, I32, P, I64, P]),
     "hy_argmax": (C.c_int, [I32, P, I64, I32, I32, P, P]),
     "hy_selftest_wait_timeout": (C.c_int, [P, I32, P, P]),

@@ -27,7 +27,9 @@ cudaError_t hy_launch_kv_append(int, const void*, const void*, int, int, const i
                                 int, int32_t*, cudaStream_t);
 cudaError_t hy_launch_argmax(int, const void*, long, int, int, int32_t*, cudaStream_t);
 cudaError_t hy_launch_add_rms_norm(int, void*, long, const void*, long, int, int, const void*,
-                                   float, void*, long, const float*, int, long, cudaStream_t);
+                                   float, void*, long, const float*, int, long, cudaStream_t,
+                                   const int32_t* = nullptr, int = 0, void* = nullptr, long = 0,
+                                   int32_t* = nullptr);
 cudaError_t hy_launch_silu_mul(int, const void*, long, int, int, void*, long, cudaStream_t);
 
 namespace {
@@ -390,6 +392,33 @@ int hy_add_rms_norm_splitk(int32_t dtype, void* x, int64_t ldx, const float* par
                                             w, eps, y, (long)ldy, parts, nparts,
                                             (long)part_stride, as_stream(stream)),
                      "hy_add_rms_norm_splitk");
+}
+
+int hy_gather_add_rms_norm(int32_t dtype, const void* x, int64_t ldx, const int32_t* x_rows,
+                           int32_t x_nrows, const void* delta, int64_t ldd, const float* parts,
+                           int32_t nparts, int64_t part_stride, int32_t rows, int32_t cols,
+                           const void* w, float eps, void* x_out, int64_t ldxo, void* y,
+                           int64_t ldy, int32_t* err, void* stream) {
+  if (!dtype_ok(dtype)) return fail(HY_E_INVALID, "hy_gather_add_rms_norm: dtype must be 0 or 1");
+  if (rows == 0) return HY_OK;
+  const int maxc = 4096;
+  if (!x || !x_rows || !w || !y || rows < 0 || x_nrows <= 0 || cols <= 0 || cols > maxc ||
+      ldx < cols || ldy < cols || (x_out && ldxo < cols) || (delta && parts) ||
+      ((delta || parts) && ldd < cols) || (parts && (nparts < 1 || nparts > 64)) ||
+      (parts && nparts > 1 && part_stride < (int64_t)rows * ldd))
+    return fail(HY_E_INVALID, "hy_gather_add_rms_norm: bad argument (cols must be in 1..4096, "
+                              "at most one of delta and parts)");
+  if (!vec_aligned(x, ldx, dtype, cols) || !vec_aligned(y, ldy, dtype, cols) ||
+      !vec_aligned(w, cols, dtype, cols) || (delta && !vec_aligned(delta, ldd, dtype, cols)) ||
+      (x_out && !vec_aligned(x_out, ldxo, dtype, cols)) ||
+      (parts && (!vec_aligned(parts, ldd, HY_DTYPE_FP32, cols) || (part_stride & 3))))
+    return fail(HY_E_INVALID, "hy_gather_add_rms_norm: rows must be 16-byte aligned vectors");
+  return cuda_result(hy_launch_add_rms_norm(dtype, const_cast<void*>(x), (long)ldx, delta,
+                                            (long)ldd, rows, cols, w, eps, y, (long)ldy, parts,
+                                            parts ? nparts : 0, (long)part_stride,
+                                            as_stream(stream), x_rows, x_nrows, x_out, (long)ldxo,
+                                            err),
+                     "hy_gather_add_rms_norm");
 }
 
 int hy_silu_mul(int32_t dtype, const void* gu, int64_t ld, int32_t rows, int32_t inter, void* y,

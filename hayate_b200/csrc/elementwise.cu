@@ -60,18 +60,23 @@ constexpr int RN_PARTS_THREADS = 384;
 // y <- RMSNorm(x) * w.  With split-K partials instead of delta, delta is first
 // round(sum of the nparts fp32 partials, in order), i.e. the projection's
 // output as its GEMM would have rounded it.
-template <typename T, bool PARTS, int THREADS>
+// GATHER: output row r takes residual row x_rows[r] of x (a step's sampled
+// tokens); the updated residual goes to row r of x_out (nullable) instead of
+// back into x, and a row index outside [0, x_nrows) sets HY_ERR_BOUNDS and
+// leaves the output row unwritten.
+template <typename T, bool PARTS, bool GATHER, int THREADS>
 __global__ void __launch_bounds__(THREADS) add_rms_norm_kernel(
     T* __restrict__ x, long ldx, const T* __restrict__ delta, long ldd, int cols,
     const T* __restrict__ w, float eps, T* __restrict__ y, long ldy,
-    const float* __restrict__ parts, int nparts, long pstride) {
+    const float* __restrict__ parts, int nparts, long pstride,
+    const int32_t* __restrict__ x_rows, int x_nrows, T* __restrict__ x_out, long ldxo,
+    int32_t* err) {
   using V = Vec<T>;
   constexpr int N = V::N;
   constexpr int RN_VEC = (4096 / N + THREADS - 1) / THREADS;   // 16-byte slots per thread
   __shared__ float red[THREADS / 32];
   const long r = blockIdx.x;
   const int nvec = cols / N;
-  T* xr = x + r * ldx;
   // rows and weights stay as their 16-byte vectors (the stored residual is in
   // the model dtype anyway) and are unpacked where used: fewer registers, more
   // rows in flight per SM
@@ -83,6 +88,17 @@ __global__ void __launch_bounds__(THREADS) add_rms_norm_kernel(
   }
   hy_grid_wait();
   hy_grid_trigger();
+  T* xr = x + r * ldx;                        // residual row read
+  T* xw = xr;                                 // residual row written (nullable)
+  if constexpr (GATHER) {
+    const int src = x_rows[r];                // the same for the whole CTA
+    if (src < 0 || src >= x_nrows) {
+      if (threadIdx.x == 0) hy_flag(err, HY_ERR_BOUNDS);
+      return;
+    }
+    xr = x + (long)src * ldx;
+    xw = x_out ? x_out + r * ldxo : nullptr;
+  }
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < RN_VEC; ++k) {
@@ -95,7 +111,9 @@ __global__ void __launch_bounds__(THREADS) add_rms_norm_kernel(
         V::load(delta + r * ldd + vi * N, dv);
 #pragma unroll
         for (int e = 0; e < N; ++e) v[e] = V::round(__fadd_rn(dv[e], v[e]));
-        V::store(xr + vi * N, v);
+        if (xw) V::store(xw + vi * N, v);
+      } else if (GATHER && !PARTS) {
+        if (xw) V::store(xw + vi * N, v);
       } else if (PARTS) {
         // the loads of the first PMAX partials are all issued before the sum
         // uses any of them (one L2 round trip, not one per partial)
@@ -136,7 +154,7 @@ __global__ void __launch_bounds__(THREADS) add_rms_norm_kernel(
         }
 #pragma unroll
         for (int e = 0; e < N; ++e) v[e] = V::round(__fadd_rn(V::round(dv[e]), v[e]));
-        V::store(xr + vi * N, v);
+        if (xw) V::store(xw + vi * N, v);
       }
 #pragma unroll
       for (int e = 0; e < N; ++e) ss = __fadd_rn(ss, __fmul_rn(v[e], v[e]));
@@ -200,28 +218,45 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(
 
 }  // namespace
 
+template <typename T, bool GATHER>
+static cudaError_t launch_add_rms_norm(void* x, long ldx, const void* delta, long ldd, int rows,
+                                       int cols, const void* w, float eps, void* y, long ldy,
+                                       const float* parts, int nparts, long pstride,
+                                       const int32_t* x_rows, int x_nrows, void* x_out,
+                                       long ldxo, int32_t* err, cudaStream_t st) {
+  if (parts)
+    return hy_launch(add_rms_norm_kernel<T, true, GATHER, RN_PARTS_THREADS>, dim3(rows),
+                     dim3(RN_PARTS_THREADS), 0, st, (T*)x, ldx, (const T*)delta, ldd, cols,
+                     (const T*)w, eps, (T*)y, ldy, parts, nparts, pstride, x_rows, x_nrows,
+                     (T*)x_out, ldxo, err);
+  return hy_launch(add_rms_norm_kernel<T, false, GATHER, RN_THREADS>, dim3(rows),
+                   dim3(RN_THREADS), 0, st, (T*)x, ldx, (const T*)delta, ldd, cols, (const T*)w,
+                   eps, (T*)y, ldy, parts, nparts, pstride, x_rows, x_nrows, (T*)x_out, ldxo, err);
+}
+
 // delta (model dtype) or parts (fp32, nparts x rows, pstride apart) -- at most
-// one of them -- with row pitch ldd.
+// one of them -- with row pitch ldd.  With x_rows, output row r reads residual
+// row x_rows[r] (< x_nrows) and writes the updated residual to x_out.
 cudaError_t hy_launch_add_rms_norm(int dtype, void* x, long ldx, const void* delta, long ldd,
                                    int rows, int cols, const void* w, float eps, void* y,
                                    long ldy, const float* parts, int nparts, long pstride,
-                                   cudaStream_t st) {
+                                   cudaStream_t st, const int32_t* x_rows, int x_nrows,
+                                   void* x_out, long ldxo, int32_t* err) {
   if (rows <= 0) return cudaSuccess;
   using B = __nv_bfloat16;
-  if (dtype == 0)
-    return parts ? hy_launch(add_rms_norm_kernel<B, true, RN_PARTS_THREADS>, dim3(rows),
-                             dim3(RN_PARTS_THREADS), 0, st, (B*)x, ldx, (const B*)delta, ldd,
-                             cols, (const B*)w, eps, (B*)y, ldy, parts, nparts, pstride)
-                 : hy_launch(add_rms_norm_kernel<B, false, RN_THREADS>, dim3(rows),
-                             dim3(RN_THREADS), 0, st, (B*)x, ldx, (const B*)delta, ldd, cols,
-                             (const B*)w, eps, (B*)y, ldy, parts, nparts, pstride);
-  return parts ? hy_launch(add_rms_norm_kernel<float, true, RN_PARTS_THREADS>, dim3(rows),
-                           dim3(RN_PARTS_THREADS), 0, st, (float*)x, ldx, (const float*)delta,
-                           ldd, cols, (const float*)w, eps, (float*)y, ldy, parts, nparts,
-                           pstride)
-               : hy_launch(add_rms_norm_kernel<float, false, RN_THREADS>, dim3(rows),
-                           dim3(RN_THREADS), 0, st, (float*)x, ldx, (const float*)delta, ldd,
-                           cols, (const float*)w, eps, (float*)y, ldy, parts, nparts, pstride);
+  if (x_rows)
+    return dtype == 0 ? launch_add_rms_norm<B, true>(x, ldx, delta, ldd, rows, cols, w, eps, y,
+                                                     ldy, parts, nparts, pstride, x_rows,
+                                                     x_nrows, x_out, ldxo, err, st)
+                      : launch_add_rms_norm<float, true>(x, ldx, delta, ldd, rows, cols, w, eps,
+                                                         y, ldy, parts, nparts, pstride, x_rows,
+                                                         x_nrows, x_out, ldxo, err, st);
+  return dtype == 0 ? launch_add_rms_norm<B, false>(x, ldx, delta, ldd, rows, cols, w, eps, y,
+                                                    ldy, parts, nparts, pstride, nullptr, 0,
+                                                    nullptr, 0, nullptr, st)
+                    : launch_add_rms_norm<float, false>(x, ldx, delta, ldd, rows, cols, w, eps, y,
+                                                        ldy, parts, nparts, pstride, nullptr, 0,
+                                                        nullptr, 0, nullptr, st);
 }
 
 cudaError_t hy_launch_silu_mul(int dtype, const void* gu, long ld, int rows, int inter, void* y,

@@ -157,7 +157,13 @@ class Engine:
         self.prefix_cache = PrefixCache() if self.ecfg.prefix_caching else None
         self.scheduler = Scheduler(self.ecfg, self.runner.num_blocks, self.runner.max_reqs,
                                    cache=self.prefix_cache)
-        self.use_graphs = bool(compile or self.ecfg.cuda_graphs)
+        # A subclass that overrides ``sample`` (the reference's hook for the
+        # next-token choice, engine.py:69-71) gets the step's last-token logits
+        # and its choice is committed on the device; the built-in greedy choice
+        # runs the fused argmax kernel.  Decode steps are only captured in CUDA
+        # graphs for the built-in choice.
+        self._sampler = None if type(self).sample is Engine.sample else self.sample
+        self.use_graphs = bool(compile or self.ecfg.cuda_graphs) and self._sampler is None
         self.trace = bool(self.ecfg.trace or os.environ.get("HY_NVTX") == "1")
         self._graphs: Dict[int, torch.cuda.CUDAGraph] = {}
         self._graph_pool = None
@@ -195,7 +201,12 @@ class Engine:
         self.pool.put(request)
 
     def sample(self, logits: torch.Tensor) -> torch.Tensor:
-        """select the next token greedily via argmax (on-GPU kernel)"""
+        """select the next token greedily via argmax (on-GPU kernel).
+
+        Override it to choose tokens another way: the engine then calls it once
+        per step with the ``(num_sampled, vocab)`` logits of the step's last
+        tokens, on the device, and commits the ``(num_sampled, 1)`` ids it
+        returns."""
         logits = logits.contiguous()
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
         K.argmax(logits, out)
@@ -298,13 +309,15 @@ class Engine:
         r._adopt_pinned = (ids, cnt)                # alive until the copies land
         self.h2d_bytes += 4 * (k + 1)
 
-    def _ensure_pad_slot(self):
-        """The padding row of graph batches owns one block and one token."""
+    def _ensure_pad_slot(self, buf: int):
+        """The padding row of graph batches owns one block and one token.  ``buf``
+        is a host schedule buffer no launched step still reads (the one the
+        caller is about to fill)."""
         if self._pad_ready:
             return
         self._pad_ready = True
         pad = self.scheduler.pad_slot
-        self._write_sched([(pad, 0, 1, SAMPLE)], self._step_idx & 1)
+        self._write_sched([(pad, 0, 1, SAMPLE)], buf)
         self.runner.launch_step(1, 1, 1)
         torch.cuda.current_stream().synchronize()     # once, before any graph capture
 
@@ -325,7 +338,10 @@ class Engine:
         S, T, ns = plan.num_seqs, plan.num_tokens, plan.num_sample
         if self.use_graphs and plan.decode_only:
             Sp = graph_bucket(S, self.ecfg.max_num_seqs)
-            self._ensure_pad_slot()
+            # the other buffer belongs to the previous step, whose schedule copy
+            # may still be queued; this step's buffer is free (its last user was
+            # collected)
+            self._ensure_pad_slot(buf)
             pad = self.scheduler.pad_slot
             rows += [(pad, 0, 1, SAMPLE)] * (Sp - S)
             self._write_sched(rows, buf)
@@ -338,7 +354,7 @@ class Engine:
             n_read = Sp
         else:
             self._write_sched(rows, buf)
-            self.runner.launch_step(S, T, ns)
+            self.runner.launch_step(S, T, ns, sampler=self._sampler)
             n_read = ns
         self.steps += 1
         self._out_host[buf][:1 + n_read].copy_(self.runner.out_buf[:1 + n_read],
@@ -359,7 +375,7 @@ class Engine:
             if e.flags & SAMPLE:
                 r.is_prefill = False
                 r._pending += 1
-                if len(r.tokens) + r._pending >= max(r.max_tokens, 1):
+                if len(r.tokens) + r._pending >= self.scheduler.token_limit(r):
                     r._last_launched = True
         return plan, buf
 
@@ -401,7 +417,7 @@ class Engine:
                 if r.is_completed:
                     continue                    # stopped at an earlier token (eos)
                 r.tokens.append(tok)
-                if tok == self.eos_token_id or len(r.tokens) >= r.max_tokens:
+                if tok == self.eos_token_id or len(r.tokens) >= self.scheduler.token_limit(r):
                     r.is_completed = True
                     r._last_launched = True
                     r.response = self.tokenizer.decode(r.tokens, skip_special_tokens=True)
@@ -449,7 +465,7 @@ class Engine:
             return 0
         if self._inflight is not None:
             raise RuntimeError("capture_graphs: a step is still in flight")
-        self._ensure_pad_slot()
+        self._ensure_pad_slot(self._step_idx & 1)
         pad = self.scheduler.pad_slot
         n = 0
         for Sp in (sizes or graph_buckets(self.ecfg.max_num_seqs)):

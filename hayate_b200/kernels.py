@@ -210,6 +210,39 @@ def add_rms_norm_splitk(x: torch.Tensor, w: torch.Tensor, eps: float, parts: tor
     return out
 
 
+def gather_add_rms_norm(x: torch.Tensor, rows: torch.Tensor, w: torch.Tensor, eps: float,
+                        delta: Optional[torch.Tensor] = None,
+                        parts: Optional[torch.Tensor] = None,
+                        x_out: Optional[torch.Tensor] = None,
+                        out: Optional[torch.Tensor] = None,
+                        err: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Output row i: r = x[rows[i]] + delta[i] (or + round(parts[:, i].sum(0)),
+    fp32 split-K partials; or r = x[rows[i]] with neither), written to
+    x_out[i] if given; returns RMSNorm(r) * w.  x is not modified."""
+    n = rows.numel()
+    cols = x.shape[1]
+    _i32(rows, "rows")
+    if x.stride(1) != 1 or (delta is not None and delta.stride(1) != 1):
+        raise ValueError("rows must be contiguous")
+    if delta is not None and parts is not None:
+        raise ValueError("give delta or parts, not both")
+    out = torch.empty(n, cols, dtype=x.dtype, device=x.device) if out is None else out
+    if parts is not None:
+        if parts.dtype != torch.float32 or parts.dim() != 3 or parts.shape[1:] != (n, cols) \
+                or parts.stride(2) != 1:
+            raise ValueError("parts must be fp32 [k, rows, cols] with contiguous rows")
+        ldd, nparts, pstride = parts.stride(1), parts.shape[0], parts.stride(0)
+    else:
+        ldd = 0 if delta is None else delta.stride(0)
+        nparts, pstride = 0, 0
+    check(_lib.load().hy_gather_add_rms_norm(
+        _dt(x), _ptr(x), x.stride(0), _ptr(rows), x.shape[0], _ptr(delta), ldd, _ptr(parts),
+        nparts, pstride, n, cols, _ptr(w), float(eps), _ptr(x_out),
+        0 if x_out is None else x_out.stride(0), _ptr(out), out.stride(0), _ptr(err), _stream()),
+        "hy_gather_add_rms_norm")
+    return out
+
+
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float,
              out: Optional[torch.Tensor] = None) -> torch.Tensor:
     return add_rms_norm(x, w, eps, None, out)

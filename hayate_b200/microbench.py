@@ -32,15 +32,15 @@ import numpy as np
 import torch
 
 
-def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True,
-                    ctx_lo: int = 256, ctx_hi: int = 16384, priors=None):
-    """The ragged attention operator case: returns timing + algorithmic bytes.
-    ``ctx_lo``/``ctx_hi`` bound the log-uniform decode contexts; ``priors`` (a
-    list of prior context lengths, one 512-token prefill chunk each) replaces
-    the operator case's four chunks."""
-    from hayate_b200 import kernels as K
+def attention_micro_batch(n_decode: int = 256, prefill: bool = True, ctx_lo: int = 256,
+                          ctx_hi: int = 16384, priors=None, seed: int = 0):
+    """The ragged attention operator batch on the current device: 256 decode
+    sequences with contexts log-uniform in [ctx_lo, ctx_hi] plus 512-token
+    prefill chunks after ``priors`` (default 0, 512, 1536, 3584), 32 query / 8
+    KV heads, bf16 Q and cache ~ N(0,1), one layer, 16-token blocks behind a
+    randomly permuted block table.  Returns a dict of its tensors and shapes."""
     from hayate_b200.workloads import attn_micro
-    w = attn_micro(seed=0, n_decode=n_decode, lo=ctx_lo, hi=ctx_hi)
+    w = attn_micro(seed=seed, n_decode=n_decode, lo=ctx_lo, hi=ctx_hi)
     if priors is not None:
         w.prefill_prior = list(priors)
     if not prefill:
@@ -51,10 +51,9 @@ def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True,
     nblk = [-(-k // 16) for k in kv_lens]
     NB = sum(nblk) + 64
     dev = torch.device("cuda")
-    g = torch.Generator(device=dev).manual_seed(0)
+    g = torch.Generator(device=dev).manual_seed(seed)
     cache = torch.randn(1, NB, 2, Hkv, 16, D, device=dev, dtype=torch.bfloat16, generator=g)
     q = torch.randn(T, Hq, D, device=dev, dtype=torch.bfloat16, generator=g)
-    out = torch.empty_like(q)
     perm = torch.randperm(NB, device=dev, generator=g).to(torch.int32)
     maxb = max(nblk)
     bt = torch.full((S, maxb), -1, dtype=torch.int32, device=dev)
@@ -64,6 +63,24 @@ def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True,
         off += n
     cu = torch.tensor([0] + list(np.cumsum(q_lens)), dtype=torch.int32, device=dev)
     kv = torch.tensor(kv_lens, dtype=torch.int32, device=dev)
+    return {"q": q, "cache": cache, "bt": bt, "cu": cu, "kv": kv, "S": S, "T": T,
+            "q_lens": q_lens, "kv_lens": kv_lens, "nblk": nblk, "decode_seqs": len(w.decode_ctx),
+            "prefill_chunks": len(w.prefill_prior)}
+
+
+def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True,
+                    ctx_lo: int = 256, ctx_hi: int = 16384, priors=None):
+    """The ragged attention operator case: returns timing + algorithmic bytes.
+    ``ctx_lo``/``ctx_hi`` bound the log-uniform decode contexts; ``priors`` (a
+    list of prior context lengths, one 512-token prefill chunk each) replaces
+    the operator case's four chunks."""
+    from hayate_b200 import kernels as K
+    b = attention_micro_batch(n_decode, prefill, ctx_lo, ctx_hi, priors)
+    q, cache, bt, cu, kv, S, T = b["q"], b["cache"], b["bt"], b["cu"], b["kv"], b["S"], b["T"]
+    q_lens, kv_lens, nblk = b["q_lens"], b["kv_lens"], b["nblk"]
+    Hkv, Hq, D = 8, 32, 128
+    dev = q.device
+    out = torch.empty_like(q)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     ws = torch.zeros(K.attention_workspace_size(S, T, Hkv), dtype=torch.uint8, device=dev)
     K.attention_plan(cu, kv, S, Hkv, S, T, ws, err)
@@ -76,12 +93,12 @@ def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True,
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(iters)]
-    for a, b in ev:
+    for a, e in ev:
         a.record()
         launch()
-        b.record()
+        e.record()
     torch.cuda.synchronize()
-    ms = [a.elapsed_time(b) for a, b in ev]
+    ms = [a.elapsed_time(e) for a, e in ev]
     if int(err.item()) != 0:
         raise RuntimeError(f"attention micro: device error {int(err.item())}")
     kv_bytes = sum(kv_lens) * Hkv * D * 2 * 2                  # K and V, read once
@@ -90,11 +107,12 @@ def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True,
     pre_flops = sum(4 * Hq * D * (ql * (kl - ql) + ql * (ql + 1) / 2)
                     for ql, kl in zip(q_lens, kv_lens) if ql > 1)
     dec_bytes = sum(k * Hkv * D * 4 for ql, k in zip(q_lens, kv_lens) if ql == 1)
-    del cache
+    del cache, b
     torch.cuda.empty_cache()
     return {"ms_mean": statistics.mean(ms), "ms_min": min(ms), "bytes": kv_bytes + qo_bytes + bt_bytes,
             "decode_kv_bytes": dec_bytes, "prefill_flops": pre_flops, "iters": iters,
-            "decode_seqs": len(w.decode_ctx), "prefill_chunks": len(w.prefill_prior)}
+            "decode_seqs": len([x for x in q_lens if x == 1]),
+            "prefill_chunks": len([x for x in q_lens if x > 1])}
 
 
 L2_FLUSH_BYTES = 256 << 20

@@ -159,8 +159,37 @@ class Runner:
         return self.out_buf[1:]
 
     # ------------------------------------------------------------------ step
-    def launch_step(self, S: int, T: int, n_sample: int) -> None:
-        """Enqueue one step for the schedule already in ``self.sched[:4*S]``."""
+    def launch_step(self, S: int, T: int, n_sample: int, sampler=None) -> None:
+        """Enqueue one step for the schedule already in ``self.sched[:4*S]``:
+        pack, the model, the LM head on the sampled rows, the next tokens
+        (greedy argmax kernel, or ``sampler(logits) -> (n, 1) or (n,)`` token
+        ids on the device) committed to the requests' token rows."""
+        logits = self.forward_logits(S, T, n_sample)
+        if logits is None:
+            return
+        toks = self.next_tokens[:n_sample]
+        if sampler is None:
+            K.argmax(logits, toks)
+        else:
+            toks.copy_(sampler(logits).reshape(-1))
+        K.commit_tokens(toks, n_sample, self.sample_seq, self.sched[:4 * S], S, self.req_tokens,
+                        self.error_word)
+        self.kernel_launches += 2 if sampler is None else 1
+
+    def forward_logits(self, S: int, T: int, n_sample: int) -> Optional[torch.Tensor]:
+        """The model half of a step: pack the schedule in ``self.sched[:4*S]``
+        (allocating its KV blocks), run the layers (appending the step's K/V to
+        the cache), and return the logits ``(n_sample, vocab)`` of the last
+        token of each sequence that samples, in schedule order -- the reference
+        model's ``logits[:, -1, :]`` (qwen.py:46-124, engine.py:143-163), or None
+        when no sequence samples.  Nothing is committed: the caller appends the
+        chosen tokens (``launch_step`` does, or ``commit_next_tokens``).
+
+        The last layer needs every row only up to its attention (their K/V are
+        appended there); from its o_proj on it runs on the sampled rows alone,
+        gathered by ``hy_gather_add_rms_norm``, and the final norm follows on
+        those rows (the reference norms and projects every position,
+        qwen.py:122-123)."""
         cfg, ecfg = self.cfg, self.ecfg
         err = self.error_word
         Hq, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
@@ -181,41 +210,70 @@ class Runner:
         s_d = self.splitk_parts(T, cfg.intermediate_size)
         x = F.embedding(self.input_ids[:T], self.embed)
         eps = cfg.rms_norm_eps
-        I = cfg.intermediate_size
         h = K.add_rms_norm(x, self.layers[0].ln1, eps)
         launches += 1
         nl = len(self.layers)
+        gathered = n_sample < T             # the last layer's tail runs on the sampled rows
         for l, w in enumerate(self.layers):
+            last = l == nl - 1
             qkv = F.linear(h, w.w_qkv)
             K.qk_norm_rope(qkv, Hq, Hkv, pos, w.q_norm, w.k_norm, self.rope_cos, self.rope_sin,
                            eps, q_out=q, kv_cache_layer=self.kv_cache[l], slot_mapping=smap,
                            num_blocks=self.num_blocks, err=err)
+            launches += 1
+            if last and n_sample == 0:
+                break                       # K/V appended; nothing samples this step
             K.varlen_attention(q, attn, self.kv_cache, l, self.block_tables, cu_q, kv_lens, S,
                                ecfg.max_num_seqs, ecfg.max_batched_tokens, self.ws,
                                seq_bt_row=slots, err=err)
-            # x += o_proj(attn); h = post_attention_layernorm(x)
+            launches += 1
             a2 = attn.view(T, Hq * D)
+            nxt = self.final_norm if last else self.layers[l + 1].ln1
+            if last and gathered:
+                rows = self.sample_rows[:n_sample]
+                a_s = a2.index_select(0, rows)
+                xs = torch.empty(n_sample, cfg.hidden_size, dtype=self.dtype, device=self.device)
+                so = self.splitk_parts(n_sample, Hq * D)
+                if so > 1:
+                    h = K.gather_add_rms_norm(x, rows, w.ln2, eps, parts=linear_splitk(a_s, w.w_o, so),
+                                              x_out=xs, err=err)
+                else:
+                    h = K.gather_add_rms_norm(x, rows, w.ln2, eps, delta=F.linear(a_s, w.w_o),
+                                              x_out=xs, err=err)
+                act = K.silu_mul(F.linear(h, w.w_gate_up))
+                sd = self.splitk_parts(n_sample, cfg.intermediate_size)
+                if sd > 1:
+                    h = K.add_rms_norm_splitk(xs, nxt, eps, linear_splitk(act, w.w_down, sd))
+                else:
+                    h = K.add_rms_norm(xs, nxt, eps, delta=F.linear(act, w.w_down))
+                launches += 3
+                break
+            # x += o_proj(attn); h = post_attention_layernorm(x)
             if s_o > 1:
                 h = K.add_rms_norm_splitk(x, w.ln2, eps, linear_splitk(a2, w.w_o, s_o))
             else:
                 h = K.add_rms_norm(x, w.ln2, eps, delta=F.linear(a2, w.w_o))
             act = K.silu_mul(F.linear(h, w.w_gate_up))
             # x += mlp(h); h = next block's input_layernorm(x), or the final norm
-            nxt = self.layers[l + 1].ln1 if l + 1 < nl else self.final_norm
             if s_d > 1:
                 h = K.add_rms_norm_splitk(x, nxt, eps, linear_splitk(act, w.w_down, s_d))
             else:
                 h = K.add_rms_norm(x, nxt, eps, delta=F.linear(act, w.w_down))
-            launches += self.LAYER_LAUNCHES + (self.ws is not None)   # + combine kernel
-        if n_sample > 0:
-            # every row sampled (decode steps): the sampled rows are rows 0..T-1 in order
-            hs = h if n_sample == T else h.index_select(0, self.sample_rows[:n_sample])
-            logits = F.linear(hs, self.embed)
-            K.argmax(logits, self.next_tokens[:n_sample])
-            K.commit_tokens(self.next_tokens[:n_sample], n_sample, self.sample_seq, sched, S,
-                            self.req_tokens, err)
-            launches += 2
+            launches += 3
         self.kernel_launches += launches
+        if n_sample == 0:
+            return None
+        # decode steps sample every row, in order: h holds exactly those rows
+        return F.linear(h, self.embed)
+
+    def commit_next_tokens(self, tokens: torch.Tensor, S: int, n_sample: int) -> None:
+        """Append ``tokens`` (int32, one per sampled sequence, schedule order) to
+        their requests' token rows: the step after ``forward_logits`` feeds them."""
+        toks = self.next_tokens[:n_sample]
+        toks.copy_(tokens.reshape(-1))
+        K.commit_tokens(toks, n_sample, self.sample_seq, self.sched[:4 * S], S, self.req_tokens,
+                        self.error_word)
+        self.kernel_launches += 1
 
     def free_slots(self, slots: torch.Tensor, first_block: Optional[torch.Tensor] = None) -> None:
         K.free_blocks(slots, self.block_tables, self.req_nblk, self.free_stack, self.free_top,
@@ -241,9 +299,9 @@ class Runner:
                 return s
         return 1
 
-    # our kernels per layer: 2 add+RMSNorm, QK-norm+RoPE, attention, SiLU*up
-    LAYER_LAUNCHES = 5
-
     def launches_per_step(self, n_sample: bool = True) -> int:
-        per_layer = self.LAYER_LAUNCHES + (self.ws is not None)
+        """Kernels of this library one decode step (every row sampled) launches:
+        pack, plan, the first RMSNorm, per layer QK-norm+RoPE, attention, two
+        add+RMSNorm and SiLU*up, then argmax and commit."""
+        per_layer = 5
         return 2 + (self.ws is not None) + per_layer * len(self.layers) + (2 if n_sample else 0)

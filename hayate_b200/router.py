@@ -37,6 +37,21 @@ class Job:
     attempts: int = 0
 
 
+def least_work_assignment(costs: List[int], n: int) -> List[int]:
+    """Replica of each job when jobs of these costs (prompt + max_tokens tokens)
+    arrive together: each goes, in order, to the replica with the least
+    outstanding work so far (the lowest index on ties) -- ``Router._assign``'s
+    rule before any job has finished.  Deterministic, so every rank of a
+    multi-process run can compute its own share without communicating."""
+    load = [0] * n
+    out = []
+    for c in costs:
+        r = min(range(n), key=lambda k: load[k])
+        out.append(r)
+        load[r] += c
+    return out
+
+
 def default_engine_factory(rank: int, **engine_kwargs):
     import torch
     from .engine import Engine

@@ -8,6 +8,9 @@ groups of 8 and a separate decode forward.
 
 Admission reserves a request's worst-case KV blocks (prompt + max_tokens) so
 the device block pool can never run dry mid-flight; no preemption is needed.
+A request generates at most ``max_model_len - len(prompt)`` tokens: one whose
+``max_tokens`` would take it past ``max_model_len`` completes there (its token
+row and block table are sized by that length), as a length-capped request.
 Slot ``max_reqs - 1`` is kept for the padding rows of CUDA-graph batches.
 
 With a prefix cache, a request first takes the longest cached prefix of its
@@ -78,9 +81,14 @@ class Scheduler:
         self.evicted: List[int] = []               # cache blocks for the device pool
 
     # ---------------------------------------------------------------- admission
+    def token_limit(self, req) -> int:
+        """Tokens the request generates at most: its max_tokens (at least one, as
+        the reference's prefill always samples one), capped so that prompt plus
+        output stay within max_model_len."""
+        return min(max(req.max_tokens, 1), self.cfg.max_model_len - len(req.prompt_tokens))
+
     def reserve_for(self, req) -> int:
-        total = min(len(req.prompt_tokens) + max(req.max_tokens, 1), self.cfg.max_model_len)
-        return blocks_for(total, self.cfg.block_size)
+        return blocks_for(len(req.prompt_tokens) + self.token_limit(req), self.cfg.block_size)
 
     def check_request(self, req) -> None:
         n = len(req.prompt_tokens)

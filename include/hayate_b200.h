@@ -206,6 +206,24 @@ int hy_add_rms_norm_splitk(int32_t dtype, void* x, int64_t ldx, const float* par
                            int32_t cols, const void* w, float eps, void* y, int64_t ldy,
                            void* stream);
 
+/* hy_add_rms_norm over gathered rows: output row r takes residual row
+ * x_rows[r] of x (x has x_nrows rows; x itself is not written), adds delta[r]
+ * (model dtype) or round(sum of the nparts fp32 split-K partials of row r,
+ * part_stride apart) -- at most one of them, row pitch ldd -- writes the
+ * updated residual to row r of x_out (nullable) and y[r] = RMSNorm * w.  A row
+ * index outside [0, x_nrows) ORs HY_DEV_BOUNDS into err and leaves row r
+ * unwritten.  Lets the last block run its post-attention half and the final
+ * norm on the step's sampled tokens only.
+ * Replaces: the last block's residual add + post_attention_layernorm
+ * (hayate/model/block.py:24-28) and the final norm applied to every position
+ * (hayate/model/qwen.py:122-123, whose logits the engine then cuts to the last
+ * position, engine.py:163). */
+int hy_gather_add_rms_norm(int32_t dtype, const void* x, int64_t ldx, const int32_t* x_rows,
+                           int32_t x_nrows, const void* delta, int64_t ldd, const float* parts,
+                           int32_t nparts, int64_t part_stride, int32_t rows, int32_t cols,
+                           const void* w, float eps, void* x_out, int64_t ldxo, void* y,
+                           int64_t ldy, int32_t* err, void* stream);
+
 /* y[r][i] = silu(gu[r][i]) * gu[r][inter + i] with the reference's two rounding
  * points (silu result, product).  `inter` a multiple of 8 (bf16) / 4 (fp32).
  * Replaces: FeedForward's silu(gate) * up, hayate/model/linear.py:11-13. */

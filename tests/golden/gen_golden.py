@@ -1,8 +1,8 @@
 """Generate the parity fixtures under tests/golden/ by running the reference.
 
 This script is the only committed code that imports the reference
-(``hayate`` from the reference checkout, default ``/root/reference``); it runs in
-the development container, never on the GPU machine.  It writes:
+(``hayate`` from a reference checkout named by ``--ref``); it runs where that
+checkout exists, never on the GPU machine.  It writes:
 
 * ``tiny_engine.json``   -- greedy tokens (+ top-2 logit margins) from the
   reference ``Engine`` (``hayate/engine/engine.py``) driving a two-layer model
@@ -12,13 +12,24 @@ the development container, never on the GPU machine.  It writes:
   prefill call and the first decode call of one scenario;
 * ``qk_norm_rope.npz``   -- the reference QK-RMSNorm (``attention.py:23-24,40-41``)
   and RoPE (``rope.py:3-13,31-44``) on seeded inputs, bf16 and fp32;
+* ``tiny_eos.json``      -- the same two-layer model with the tokenizer's
+  ``eos_token_id`` set to a token the reference emits mid-sequence, so that
+  requests stop early (engine.py:76-77);
+* ``tiny_paged_pin.npz`` -- what the paged spec is pinned to: the position ids
+  each forward call of the reference passes to its blocks (qwen.py:66-77,
+  recorded at the first block) with the call's token ids, and every request's
+  compacted cache after its last step (engine.py:118-141; layer 0, the first
+  4 of 128 dimensions, K and V);
 * ``full_greedy.json``   -- greedy tokens and margins of the full-size model
   (fp32, seeded random init) for the single-request case and the first 64
   tokens of the 10-request upfront case, plus a weight fingerprint;
+* ``full_chunked.json``  -- the same for the first 6 requests of the Poisson
+  workload (prompts of 1330, 1861, 1125, 345, 280 and 256 tokens, three of
+  them longer than one 512-token prefill chunk), 32 tokens each;
 * ``hayate_b200/data/rng_ckpt_*.npz`` -- generator checkpoints for the exact
   block-parallel weight fill.
 
-Usage: ``python tests/golden/gen_golden.py [--part tiny|full|all] [--ref PATH]``
+Usage: ``python tests/golden/gen_golden.py --ref PATH [--part tiny|eos|paged|full|chunked|all]``
 """
 from __future__ import annotations
 
@@ -49,8 +60,10 @@ TINY_STD = 0.15
 
 class FakeTokenizer:
     """Identity tokenizer: prompts are token-id lists."""
-    eos_token_id = None
     pad_token_id = 0
+
+    def __init__(self, eos_token_id=None):
+        self.eos_token_id = eos_token_id
 
     def encode(self, prompt):
         return list(prompt)
@@ -100,14 +113,14 @@ def build_ref_model(ref, cfg: ModelConfig, w: W.HostWeights, dtype):
     return m
 
 
-def build_ref_engine(ref, model):
+def build_ref_engine(ref, model, eos_token_id=None):
     Engine = ref["Engine"]
     eng = Engine.__new__(Engine)
     eng.model = model
     eng.num_layers = model.num_layers
     eng.num_kv_groups = model.num_kv_groups
     eng.head_dim = model.head_dim
-    eng.tokenizer = FakeTokenizer()
+    eng.tokenizer = FakeTokenizer(eos_token_id)
     eng.pool = Queue()
     eng.current_batch = []
     eng.request_id = 0
@@ -277,10 +290,139 @@ def gen_tiny_ckpt():
     W.save_checkpoints(TINY, 0, states)
 
 
+# eos ids chosen from the reference's own greedy output without eos (batch5:
+# 462 ends two requests at tokens 3 and 8, 254 two at tokens 10 and 18;
+# staggered25: 349 recurs in several requests)
+EOS_CASES = (("batch5_eos462", "batch5", 462), ("batch5_eos254", "batch5", 254),
+             ("staggered25_eos349", "staggered25", 349))
+
+
+def gen_eos(ref):
+    cfg = TINY
+    w = W.sequential_seeded(cfg, 0, std=TINY_STD)
+    scen = tiny_scenarios(cfg)
+    out = {"config": cfg.__dict__, "seed": 0, "std": TINY_STD, "scenarios": {}}
+    for name, base, eos in EOS_CASES:
+        sc = scen[base]
+        eng = build_ref_engine(ref, build_ref_model(ref, cfg, w, torch.float32), eos_token_id=eos)
+        if sc["kind"] == "upfront":
+            res = run_upfront(ref, eng, sc["prompts"], sc["max_tokens"])
+        else:
+            res = run_staggered(ref, eng, sc["arrivals"])
+        early = sum(1 for r in res if len(r["tokens"]) < r["max_tokens"])
+        assert early > 0, f"{name}: eos {eos} stops no request early"
+        out["scenarios"][name] = {"kind": sc["kind"], "eos_token_id": eos, "requests": res}
+        print(f"eos {name}: {early} of {len(res)} requests stop at eos", flush=True)
+    with open(os.path.join(HERE, "tiny_eos.json"), "w") as f:
+        json.dump(out, f)
+
+
+PIN_DIMS = 4           # leading head dimensions kept of each cached K/V row
+
+
+def gen_paged_pin(ref):
+    """Record the reference's position ids per forward call and its compacted
+    per-request caches after the run (two-layer model, fp32), for the
+    scenarios that mix padded prefill groups, decodes and a 700-token prompt."""
+    cfg = TINY
+    w = W.sequential_seeded(cfg, 0, std=TINY_STD)
+    scen = tiny_scenarios(cfg)
+    arrays = {}
+    for name in ("batch5", "long_prompt", "staggered25"):
+        sc = scen[name]
+        model = build_ref_model(ref, cfg, w, torch.float32)
+        calls = []
+        blk0 = model.layers[0]
+        orig_blk = blk0.forward
+
+        def blk_forward(x, attn_mask, cos, sin, position_ids, prev_k, prev_v, _o=orig_blk):
+            calls.append(position_ids.clone())
+            return _o(x, attn_mask, cos, sin, position_ids, prev_k, prev_v)
+
+        blk0.forward = blk_forward
+        eng = build_ref_engine(ref, model)
+        toks = []                                  # the token ids of each call, by request
+        orig_fp = eng._forward_pass
+
+        def fp(tokens, requests, pad_lengths_py=None, _o=orig_fp):
+            toks.append((tokens.clone(), [r.id for r in requests],
+                         list(pad_lengths_py) if pad_lengths_py is not None else None,
+                         [r.cache_pos for r in requests]))
+            return _o(tokens, requests, pad_lengths_py=pad_lengths_py)
+
+        eng._forward_pass = fp
+        Request = ref["Request"]
+        if sc["kind"] == "upfront":
+            reqs = []
+            for p in sc["prompts"]:
+                r = Request(id=eng.request_id, prompt=list(p), max_tokens=sc["max_tokens"])
+                eng.request_id += 1
+                eng.add_request(r)
+                reqs.append(r)
+            while eng.generate():
+                pass
+        else:
+            reqs = []
+            pending = sorted(sc["arrivals"], key=lambda a: a[0])
+            step = 0
+            while pending or eng.current_batch or not eng.pool.empty():
+                while pending and pending[0][0] <= step:
+                    _, prompt, mt = pending.pop(0)
+                    r = Request(id=eng.request_id, prompt=list(prompt), max_tokens=mt)
+                    eng.request_id += 1
+                    eng.add_request(r)
+                    reqs.append(r)
+                eng.generate()
+                step += 1
+        assert len(calls) == len(toks)
+        for i, (pos, (tk, ids, pads, cpos)) in enumerate(zip(calls, toks)):
+            arrays[f"{name}_call{i}_positions"] = pos.numpy()
+            arrays[f"{name}_call{i}_tokens"] = tk.numpy()
+            arrays[f"{name}_call{i}_ids"] = np.array(ids)
+            arrays[f"{name}_call{i}_pads"] = np.array(pads if pads is not None else [0] * len(ids))
+            arrays[f"{name}_call{i}_cache_pos"] = np.array(cpos)
+        arrays[f"{name}_ncalls"] = np.array(len(calls))
+        for r in reqs:
+            arrays[f"{name}_req{r.id}_prompt"] = np.array(r.prompt)
+            arrays[f"{name}_req{r.id}_tokens"] = np.array(r.tokens)
+            arrays[f"{name}_req{r.id}_k"] = r.kv_cache.k[0, :, :, :PIN_DIMS].numpy()
+            arrays[f"{name}_req{r.id}_v"] = r.kv_cache.v[0, :, :, :PIN_DIMS].numpy()
+        arrays[f"{name}_nreq"] = np.array(len(reqs))
+        print(f"paged pin {name}: {len(calls)} forward calls, {len(reqs)} requests", flush=True)
+    np.savez_compressed(os.path.join(HERE, "tiny_paged_pin.npz"), **arrays)
+
+
+def gen_chunked(ref, n_req: int = 6, ntok: int = 32):
+    """Full-size model, fp32: the first requests of the Poisson workload, whose
+    long prompts the engine splits into 512-token chunks."""
+    cfg = QWEN3_4B
+    t0 = time.time()
+    w = W.exact_seeded(cfg, 0)
+    with open(os.path.join(HERE, "full_greedy.json")) as f:
+        fp_want = json.load(f)["fingerprint"]
+    assert W.fingerprint(w) == fp_want, "weights differ from the full_greedy fixture's"
+    print(f"full weights in {time.time() - t0:.0f}s", flush=True)
+    model = build_ref_model(ref, cfg, w, torch.float32)
+    del w
+    eng = build_ref_engine(ref, model)
+    ws = workloads.poisson(seed=0)[:n_req]
+    t0 = time.time()
+    res = run_upfront(ref, eng, [r.prompt for r in ws], ntok)
+    print(f"chunked slice: {time.time() - t0:.1f}s", flush=True)
+    out = {"config": cfg.__dict__, "seed": 0, "fingerprint": fp_want,
+           "workload": f"poisson(seed=0)[:{n_req}], {ntok} tokens each, submitted upfront",
+           "requests": res}
+    with open(os.path.join(HERE, "full_chunked.json"), "w") as f:
+        json.dump(out, f)
+
+
+PARTS = ("tiny", "eos", "paged", "full", "chunked")
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--part", default="all", choices=["tiny", "full", "all"])
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--part", default="all", choices=list(PARTS) + ["all"])
+    ap.add_argument("--ref", required=True, help="path of the reference checkout")
     ap.add_argument("--c2-tokens", type=int, default=64)
     args = ap.parse_args()
     sys.dont_write_bytecode = True
@@ -293,12 +435,19 @@ def main():
                TransformerBlock=TransformerBlock, compute_rope_params=compute_rope_params,
                apply_rope_vectorized=apply_rope_vectorized)
     torch.set_num_threads(os.cpu_count() or 8)
-    if args.part in ("tiny", "all"):
+    parts = PARTS if args.part == "all" else (args.part,)
+    if "tiny" in parts:
         gen_tiny(ref)
         gen_qk_norm_rope(ref)
         gen_tiny_ckpt()
-    if args.part in ("full", "all"):
+    if "eos" in parts:
+        gen_eos(ref)
+    if "paged" in parts:
+        gen_paged_pin(ref)
+    if "full" in parts:
         gen_full(ref, args.c2_tokens)
+    if "chunked" in parts:
+        gen_chunked(ref)
 
 
 if __name__ == "__main__":

@@ -2,6 +2,7 @@
 import json
 import os
 
+import numpy as np
 import pytest
 import torch
 
@@ -15,11 +16,27 @@ pytestmark = pytest.mark.gpu
 TINY_GOLD = json.load(open(os.path.join(GOLDEN, "tiny_engine.json")))
 
 
-def tiny_engine(dtype, graphs, chunk=64, max_seqs=32):
+def tiny_engine(dtype, graphs, chunk=64, max_seqs=32, tokenizer=None, max_model_len=1024,
+                engine_cls=Engine):
     ecfg = EngineConfig(max_num_seqs=max_seqs, max_batched_tokens=256, prefill_chunk=chunk,
-                        num_kv_blocks=512, max_model_len=1024, cuda_graphs=graphs)
+                        num_kv_blocks=512, max_model_len=max_model_len, cuda_graphs=graphs)
     hw = W.exact_seeded(TINY, 0, std=TINY_GOLD["std"])
-    return Engine("tiny", model_config=TINY, engine_config=ecfg, dtype=dtype, weights=hw)
+    return engine_cls("tiny", model_config=TINY, engine_config=ecfg, dtype=dtype, weights=hw,
+                      tokenizer=tokenizer)
+
+
+class IdTokenizer:
+    """Token-id prompts; ``eos_token_id`` as the reference's tokenizer has one."""
+    pad_token_id = 0
+
+    def __init__(self, eos_token_id=None):
+        self.eos_token_id = eos_token_id
+
+    def encode(self, prompt):
+        return list(prompt)
+
+    def decode(self, ids, skip_special_tokens=True):
+        return " ".join(map(str, ids))
 
 
 def run_scenario(eng, sc):
@@ -54,6 +71,80 @@ def test_tiny_fp32_tokens_equal_reference(name, graphs):
     assert eng.check_device_errors() == 0
     if graphs and name in ("batch5", "staggered25"):
         assert eng.graph_steps > 0
+
+
+EOS_GOLD = json.load(open(os.path.join(GOLDEN, "tiny_eos.json")))
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+@pytest.mark.parametrize("name", sorted(EOS_GOLD["scenarios"]))
+def test_tiny_fp32_stops_at_eos_like_reference(name, graphs):
+    """With the tokenizer's eos id set, a request completes on the step that
+    samples eos (engine.py:76-77): the same tokens as the reference, eos last,
+    nothing after it, and its slot freed for the requests behind it."""
+    sc = EOS_GOLD["scenarios"][name]
+    eos = sc["eos_token_id"]
+    eng = tiny_engine(torch.float32, graphs, tokenizer=IdTokenizer(eos))
+    reqs = run_scenario(eng, sc)
+    early = 0
+    for r, want in zip(reqs, sc["requests"]):
+        assert r.is_completed and r.tokens == want["tokens"], (r.id, r.tokens, want["tokens"])
+        if len(r.tokens) < want["max_tokens"]:
+            assert r.tokens[-1] == eos and eos not in r.tokens[:-1]
+            assert r.response is not None
+            early += 1
+    assert early > 0
+    assert not eng.scheduler.running and eng.check_device_errors() == 0
+
+
+def test_output_capped_at_max_model_len():
+    """max_tokens past max_model_len: the request ends at the length limit with
+    no device error (its token row and block table hold exactly that much)."""
+    eng = tiny_engine(torch.bfloat16, True, max_model_len=64)
+    r = eng.generate_text(list(range(1, 41)), max_tokens=100)
+    assert r.is_completed and len(r.tokens) == 24
+    rs = eng.generate_text([list(range(1, 60)), [7] * 10], max_tokens=30)
+    assert [len(x.tokens) for x in rs] == [5, 30]
+    assert eng.check_device_errors() == 0
+
+
+class LogitsEngine(Engine):
+    """Overrides ``sample`` as the reference's hook (engine.py:69-71): receives
+    each step's last-token logits and picks greedily with torch."""
+
+    def __init__(self, *a, **kw):
+        super().__init__(*a, **kw)
+        self.seen = []
+
+    def sample(self, logits):
+        self.seen.append(logits.detach().clone())
+        return torch.argmax(logits, dim=-1, keepdim=True)
+
+
+def test_model_boundary_returns_the_reference_last_token_logits():
+    """The model half of a step returns the logits of each sampled sequence's
+    last token: equal (fp32) to the reference model's ``logits[:, -1, :]`` for
+    its first prefill call and its first decode call (qwen.py:46-59,
+    engine.py:143-163), and the tokens a custom ``sample`` picks are committed."""
+    f = np.load(os.path.join(GOLDEN, "tiny_forward.npz"))
+    lens = f["prompt_lens"].tolist()
+    flat = f["prompts_flat"].tolist()
+    prompts, o = [], 0
+    for n in lens:
+        prompts.append(flat[o:o + n])
+        o += n
+    eng = tiny_engine(torch.float32, True, engine_cls=LogitsEngine)
+    assert not eng.use_graphs                    # a custom sampler is not captured
+    reqs = eng.generate_text(prompts, max_tokens=3)
+    assert len(eng.seen) == 3                   # prefill, then two decode steps
+    for step, key in ((0, "c0_logits"), (1, "c1_logits")):
+        want = torch.from_numpy(f[key][:, -1, :])
+        got = eng.seen[step].float().cpu()
+        assert got.shape == want.shape
+        torch.testing.assert_close(got, want, rtol=1e-4, atol=1e-4)
+    plain = tiny_engine(torch.float32, True).generate_text(prompts, max_tokens=3)
+    assert [r.tokens for r in reqs] == [r.tokens for r in plain]
+    assert eng.check_device_errors() == 0
 
 
 def test_tiny_bf16_first_tokens_where_margin_is_clear():
@@ -199,16 +290,41 @@ def full_fp32_engine():
     torch.cuda.empty_cache()
 
 
-@pytest.mark.parametrize("case,ntok", [("single", 32), ("upfront", 32)])
-def test_qwen3_4b_fp32_greedy_matches_reference(full_fp32_engine, case, ntok):
-    eng = full_fp32_engine
-    want = FULL["cases"][case]
-    reqs = eng.generate_text([r["prompt"] for r in want], max_tokens=ntok)
-    reqs = reqs if isinstance(reqs, list) else [reqs]
+def _tokens_match(reqs, want, ntok):
     for r, w in zip(reqs, want):
         got, exp = r.tokens[:ntok], w["tokens"][:ntok]
         if got != exp:
             i = next(j for j in range(ntok) if got[j] != exp[j])
             pytest.fail(f"request {r.id}: first divergence at token {i} "
                         f"(reference top-2 margin there {w['margins'][i]:.3g})")
+
+
+@pytest.mark.parametrize("case,ntok", [("single", 32), ("upfront", 32)])
+def test_qwen3_4b_fp32_greedy_matches_reference(full_fp32_engine, case, ntok):
+    eng = full_fp32_engine
+    want = FULL["cases"][case]
+    reqs = eng.generate_text([r["prompt"] for r in want], max_tokens=ntok)
+    reqs = reqs if isinstance(reqs, list) else [reqs]
+    _tokens_match(reqs, want, ntok)
+    assert eng.check_device_errors() == 0
+
+
+CHUNKED = json.load(open(os.path.join(GOLDEN, "full_chunked.json")))
+
+
+def test_qwen3_4b_fp32_chunked_prefill_matches_reference(full_fp32_engine):
+    """The first 6 requests of the Poisson workload (prompts of 1330, 1861,
+    1125, 345, 280 and 256 tokens): the engine splits the three long prompts
+    into 512-token chunks, runs them in steps beside the short requests'
+    decodes, and must give the reference's fp32 greedy tokens (its one padded
+    prefill of all 6, then decodes) for the first 32 tokens of each."""
+    eng = full_fp32_engine
+    want = CHUNKED["requests"]
+    chunk = eng.ecfg.prefill_chunk
+    assert sum(len(w["prompt"]) > chunk for w in want) >= 3
+    steps0, tok0 = eng.steps, eng.prompt_tokens_computed
+    reqs = eng.generate_text([w["prompt"] for w in want], max_tokens=32)
+    assert eng.prompt_tokens_computed - tok0 == sum(len(w["prompt"]) for w in want)
+    assert eng.steps - steps0 > 32              # chunked prefill took extra mixed steps
+    _tokens_match(reqs, want, 32)
     assert eng.check_device_errors() == 0

@@ -339,6 +339,36 @@ def test_attention_micro_shape_reduced():
     assert (got.float() - want).abs().max().item() <= 2e-2
 
 
+def test_attention_operator_case_full_size():
+    """The ragged attention operator case exactly as the bench times it (256
+    decode sequences, contexts log-uniform in [256,16384], 4 prefill chunks of
+    512 after 0/512/1536/3584 cached tokens, permuted block table, one plan as
+    the bench makes it): every output row within 2e-2 of fp32 SDPA with the
+    reference's causal mask."""
+    from hayate_b200.microbench import attention_micro_batch
+    b = attention_micro_batch()
+    S, T = b["S"], b["T"]
+    out = torch.full_like(b["q"], float("nan"))
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = torch.zeros(K.attention_workspace_size(S, T, 8), dtype=torch.uint8, device=dev)
+    K.attention_plan(b["cu"], b["kv"], S, 8, S, T, ws, err)
+    for _ in range(2):                  # the second call runs on the cached block ids
+        K.varlen_attention(b["q"], out, b["cache"], 0, b["bt"], b["cu"], b["kv"], S, S, T, ws,
+                           err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, K.describe_error(int(err.item()))
+    cu = b["cu"].tolist()
+    worst = 0.0
+    for i in range(S):
+        L, nb = b["kv_lens"][i], b["nblk"][i]
+        blocks = b["cache"][0, b["bt"][i, :nb].long()]           # (nb, 2, 8, 16, 128)
+        k = blocks[:, 0].permute(0, 2, 1, 3).reshape(-1, 8, 128)[:L]
+        v = blocks[:, 1].permute(0, 2, 1, 3).reshape(-1, 8, 128)[:L]
+        want = R.varlen_attention(b["q"][cu[i]:cu[i + 1]], [0, cu[i + 1] - cu[i]], [k], [v])
+        worst = max(worst, (out[cu[i]:cu[i + 1]].float() - want).abs().max().item())
+    assert worst <= 2e-2, f"max abs err {worst}"
+
+
 @pytest.mark.parametrize("name", ["decode_edges", "mixed"])
 def test_attention_fp32_vs_reference(name):
     q_lens, kv_lens = CASES[name]
@@ -466,6 +496,57 @@ def test_add_rms_norm_splitk_vs_reference(dt, nparts, rows, cols):
         assert d.max().item() <= 1 and (d > 0).float().mean().item() < 0.02
     else:
         torch.testing.assert_close(got, want, rtol=2e-6, atol=2e-6)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("mode", ["delta", "parts", "none"])
+def test_gather_add_rms_norm_vs_reference(dt, mode):
+    """Rows gathered by index (repeats allowed), the residual's delta added (a
+    tensor, fp32 split-K partials, or none), the updated rows written to x_out
+    and normed; the source rows are left untouched.  An index out of range sets
+    the bounds bit and leaves its output row unwritten."""
+    g = torch.Generator(device=dev).manual_seed(17)
+    cols = 2560
+    src = (torch.randn(50, cols, device=dev, generator=g) * 3).to(dt)
+    keep = src.clone()
+    idx = [49, 3, 3, 17, 0, 21]
+    rows = i32(idx)
+    n = len(idx)
+    w = (1 + 0.1 * torch.randn(cols, device=dev, generator=g)).to(dt)
+    delta = parts = None
+    base = src[torch.tensor(idx, device=dev).long()]
+    if mode == "delta":
+        delta = (torch.randn(n, cols, device=dev, generator=g) * 3).to(dt)
+        want_x = base + delta
+    elif mode == "parts":
+        big = torch.randn(4, n + 2, cols + 8, device=dev, generator=g)
+        parts = big[:, 1:n + 1, 4:cols + 4]
+        acc = parts[0].clone()
+        for p in range(1, 4):
+            acc = acc + parts[p]
+        want_x = base + acc.to(dt)
+    else:
+        want_x = base
+    want = R.rms_norm(want_x, w, 1e-6)
+    x_out = torch.full((n, cols), 7.0, dtype=dt, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    got = K.gather_add_rms_norm(src, rows, w, 1e-6, delta=delta, parts=parts, x_out=x_out, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(src, keep)
+    assert torch.equal(x_out, want_x)
+    if dt == torch.bfloat16:
+        d = _ulp_diff_bf16(got, want)
+        assert d.max().item() <= 1 and (d > 0).float().mean().item() < 0.02
+    else:
+        torch.testing.assert_close(got, want, rtol=2e-6, atol=2e-6)
+    bad = i32([2, 50, -1])
+    out = torch.zeros(3, cols, dtype=dt, device=dev)
+    K.gather_add_rms_norm(src, bad, w, 1e-6, out=out, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & K.DEV_BOUNDS
+    assert torch.equal(out[1:], torch.zeros_like(out[1:]))
+    torch.testing.assert_close(out[0].float(), R.rms_norm(src[2:3], w, 1e-6)[0].float())
 
 
 def test_splitk_projection_matches_one_gemm():

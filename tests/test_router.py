@@ -37,3 +37,17 @@ def test_router_requeues_work_of_a_failed_replica(mode):
         _run(r, work)
         assert r.failures == [1]
         assert any(j.attempts > 1 for j in r.jobs.values())
+
+
+def test_static_assignment_is_the_routers_rule_for_a_burst():
+    """Jobs submitted together land where least_work_assignment puts them (the
+    bench computes each rank's share with it, without communicating)."""
+    from hayate_b200.router import least_work_assignment
+    work = _workload(40, seed=3)
+    with Router(3, fake_factory) as r:
+        for p, m in work:
+            r.submit(p, m)
+        got = [r.jobs[j].replica for j in sorted(r.jobs)]
+        r.wait_all(timeout=120)
+    assert got == least_work_assignment([len(p) + m for p, m in work], 3)
+    assert least_work_assignment([5, 1, 1, 1, 1, 1], 2) == [0, 1, 1, 1, 1, 1]

@@ -72,3 +72,18 @@ def test_graph_buckets_cover_every_batch():
     for n in range(1, 257):
         b = graph_bucket(n, 256)
         assert b >= n and b in bs
+
+
+def test_output_is_capped_at_max_model_len():
+    """A request whose max_tokens would run past max_model_len generates up to
+    the length limit: its reservation covers exactly that many tokens."""
+    cfg = EngineConfig(max_num_seqs=4, max_batched_tokens=64, max_model_len=64)
+    s = Scheduler(cfg, num_blocks=20, max_reqs=5)
+    long_out = req(0, 40, max_tokens=100)
+    s.check_request(long_out)                       # admitted, not rejected
+    assert s.token_limit(long_out) == 24
+    assert s.reserve_for(long_out) == 4             # 64 tokens = 4 blocks
+    short = req(1, 40, max_tokens=5)
+    assert s.token_limit(short) == 5 and s.reserve_for(short) == 3
+    edge = req(2, 63, max_tokens=0)                 # one token always, as the reference
+    assert s.token_limit(edge) == 1 and s.reserve_for(edge) == 4
