@@ -176,26 +176,17 @@ class ClockSampler:
 def rank_share(world: int, rank: int, seed: int = 0):
     """This rank's requests of the world x 256 request set (least outstanding
     work, the router's rule for requests that arrive together)."""
-    from hayate_b200.router import least_work_assignment
-    from hayate_b200.workloads import replicas
-    ws = replicas(seed=seed, n=PER_GPU * world, lo=PROMPT_LO, hi=PROMPT_HI, max_tokens=MAX_TOKENS)
-    owner = least_work_assignment([len(w.prompt) + w.max_tokens for w in ws], world)
-    return [w for w, o in zip(ws, owner) if o == rank]
+    from hayate_b200.workloads import replica_share
+    return replica_share(world, rank, seed, PER_GPU)
 
 
 def make_engine(device, share):
     """An engine sized so the whole share is admitted at once (every request's
     worst-case KV blocks reserved)."""
-    from hayate_b200.config import EngineConfig
+    from hayate_b200.benchmark import replica_engine_config
     from hayate_b200.engine import Engine
-    from hayate_b200.scheduler import blocks_for
-    blocks = sum(blocks_for(len(w.prompt) + w.max_tokens, 16) for w in share) + 64
-    ecfg = EngineConfig(max_num_seqs=max(PER_GPU, len(share)), max_batched_tokens=8192,
-                        prefill_chunk=512, num_kv_blocks=blocks,
-                        max_model_len=PROMPT_HI + MAX_TOKENS + 16, cuda_graphs=True,
-                        ignore_eos=True)
-    return Engine("Qwen/Qwen3-4B", engine_config=ecfg, dtype=torch.bfloat16, weights="device",
-                  seed=0, device=device)
+    return Engine("Qwen/Qwen3-4B", engine_config=replica_engine_config(share),
+                  dtype=torch.bfloat16, weights="device", seed=0, device=device)
 
 
 def run_workload(eng, prompts, max_tokens):

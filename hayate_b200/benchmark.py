@@ -227,6 +227,18 @@ def summarize(rows, verbose=False):
               f"{r['total_tokens'] / r['elapsed']:>11.2f}")
 
 
+def replica_engine_config(share) -> EngineConfig:
+    """Engine of one replica sized so that its whole share is admitted at once:
+    a seat per request (at least 256) and every request's worst-case KV blocks
+    (prompt + max_tokens) in the pool; 8192 tokens per step, 512-token chunks."""
+    from .scheduler import blocks_for
+    blocks = sum(blocks_for(len(w.prompt) + w.max_tokens, 16) for w in share) + 64
+    longest = max(len(w.prompt) + w.max_tokens for w in share)
+    return EngineConfig(max_num_seqs=max(256, len(share)), max_batched_tokens=8192,
+                        prefill_chunk=512, num_kv_blocks=blocks, max_model_len=longest + 16,
+                        cuda_graphs=True, ignore_eos=True)
+
+
 def default_engine_config(max_tokens, max_prompt):
     return EngineConfig(max_num_seqs=256, max_batched_tokens=8192, prefill_chunk=512,
                         max_model_len=max_prompt + max_tokens + 16, ignore_eos=True)

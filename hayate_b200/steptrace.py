@@ -1,4 +1,4 @@
-"""Critical path of graph-replayed decode steps, per kernel.
+"""Critical path of the engine's steps, per kernel.
 
 ``python -m hayate_b200.steptrace [--steps 10]`` runs the upfront workload's 10
 requests (bf16 Qwen3-4B, random weights) into their decode phase, records
@@ -7,6 +7,10 @@ ncu) and charges each kernel only for the time it extends the step: its end
 minus the later of its own start and the previous kernel's end.  Kernels that
 programmatic dependent launch starts early (before the previous kernel ends)
 are therefore not charged for the overlap, which plain per-kernel durations are.
+
+``python -m hayate_b200.steptrace --replica-share`` does the same over one
+complete run of a replica's share of the 2048-request workload (256 requests,
+prompts U[512,4096], 256 tokens each; one warm-up run first).
 """
 from __future__ import annotations
 
@@ -26,7 +30,9 @@ LABELS = (
     ("nvjet_tst_192x16", "cuBLAS gate/up"),
     ("nvjet_tst_128x8", "cuBLAS qkv"),
     ("nvjet_tst_384x16", "cuBLAS LM head"),
-    ("indexSelect", "embedding"),
+    ("nvjet", "cuBLAS (other shapes)"),
+    ("gemm", "cuBLAS (other shapes)"),
+    ("indexSelect", "embedding / row gather"),
     ("plan_kernel", "attention plan"),
     ("pack_kernel", "pack"),
     ("argmax", "argmax"),
@@ -62,15 +68,49 @@ def critical_path(events):
     return excl, dur, cnt, span, gaps
 
 
+def report(ev, title, per):
+    excl, dur, cnt, span, gaps = critical_path(ev)
+    print(f"{title}: {span / per:.1f} us per {'step' if per > 1 else 'run'}, gaps between "
+          f"kernels {gaps / per:.1f} us")
+    for lab, x in sorted(excl.items(), key=lambda kv: -kv[1]):
+        print(f"{lab:40s} {cnt[lab] / per:8.1f}/{'step' if per > 1 else 'run'}  "
+              f"{x / cnt[lab]:8.2f} us excl ({100 * x / span:4.1f}%)  "
+              f"{dur[lab] / cnt[lab]:8.2f} us duration")
+
+
+def _cuda_events(prof):
+    return sorted(((e.name, e.time_range.start, e.time_range.end) for e in prof.events()
+                   if e.device_type == torch.autograd.DeviceType.CUDA), key=lambda x: x[1])
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--replica-share", action="store_true",
+                    help="profile one full run of a replica's 256-request share")
     args = ap.parse_args()
     from torch.profiler import ProfilerActivity, profile
 
     from .config import EngineConfig
     from .engine import Engine, Request
     from .workloads import upfront
+    if args.replica_share:
+        from .benchmark import replica_engine_config
+        from .workloads import replica_share
+        share = replica_share(1, 0)
+        eng = Engine("Qwen/Qwen3-4B", engine_config=replica_engine_config(share),
+                     weights="device")
+        eng.capture_graphs()
+        prompts = [torch.tensor(w.prompt, dtype=torch.int32, device=eng.device) for w in share]
+        eng.generate_text(prompts, max_tokens=256)          # warm-up run
+        torch.cuda.synchronize()
+        s0 = eng.steps
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            eng.generate_text(prompts, max_tokens=256)
+            torch.cuda.synchronize()
+        report(_cuda_events(prof), f"one run of {len(share)} requests, {eng.steps - s0} engine "
+               f"steps ({eng.graph_steps} graph-replayed in all runs)", 1)
+        return
     ecfg = EngineConfig(max_num_seqs=16, max_batched_tokens=8192, prefill_chunk=512,
                         num_kv_blocks=1024, max_model_len=1024, cuda_graphs=True,
                         ignore_eos=True)
@@ -87,14 +127,7 @@ def main():
         for _ in range(args.steps):
             eng.generate()
         torch.cuda.synchronize()
-    ev = sorted(((e.name, e.time_range.start, e.time_range.end) for e in prof.events()
-                 if e.device_type == torch.autograd.DeviceType.CUDA), key=lambda x: x[1])
-    excl, dur, cnt, span, gaps = critical_path(ev)
-    print(f"{args.steps} decode steps of 10 sequences: {span / args.steps:.1f} us per step, "
-          f"gaps between kernels {gaps / args.steps:.1f} us per step")
-    for lab, x in sorted(excl.items(), key=lambda kv: -kv[1]):
-        print(f"{lab:40s} {cnt[lab] / args.steps:6.1f}/step  {x / cnt[lab]:7.2f} us excl "
-              f"({100 * x / span:4.1f}%)  {dur[lab] / cnt[lab]:7.2f} us duration")
+    report(_cuda_events(prof), f"{args.steps} decode steps of 10 sequences", args.steps)
 
 
 if __name__ == "__main__":

@@ -15,7 +15,9 @@ seeds, in the shapes of the five benchmark configurations:
 * ``attn_micro`` -- the ragged attention operator case: 256 decode sequences
   with contexts log-uniform in [256,16384] plus 4 prefill chunks of 512 tokens
   with prior contexts {0, 512, 1536, 3584};
-* ``replicas``   -- 2048 requests, prompt lengths U[512,4096], 256 tokens each.
+* ``replicas``   -- 2048 requests, prompt lengths U[512,4096], 256 tokens each;
+  ``replica_share`` is one GPU's part of the N x 256-request version of it,
+  split by the router's least-outstanding-work rule.
 """
 from __future__ import annotations
 
@@ -77,6 +79,21 @@ def replicas(seed: int = 0, vocab: int = VOCAB, n: int = 2048, lo: int = 512,
     lens = [rng.randint(lo, hi) for _ in range(n)]
     g = torch.Generator().manual_seed(seed)
     return [SyntheticRequest(_ids(g, L, vocab), max_tokens) for L in lens]
+
+
+REPLICA_PER_GPU = 256
+
+
+def replica_share(world: int, rank: int, seed: int = 0,
+                  per_gpu: int = REPLICA_PER_GPU) -> List[SyntheticRequest]:
+    """Rank ``rank``'s requests of the ``world * per_gpu`` replica workload
+    (prompts U[512,4096], 256 tokens), assigned as the router assigns requests
+    that arrive together (least outstanding work); the same on every rank, so
+    no communication is needed.  At world=8 the set is the 2048-request one."""
+    from .router import least_work_assignment
+    ws = replicas(seed=seed, n=per_gpu * world)
+    owner = least_work_assignment([len(w.prompt) + w.max_tokens for w in ws], world)
+    return [w for w, o in zip(ws, owner) if o == rank]
 
 
 @dataclass
