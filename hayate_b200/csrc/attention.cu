@@ -51,6 +51,9 @@ constexpr int DEC_WARP_BYTES = DEC_STAGES * DEC_TILE_BYTES;      // 24 KB
 constexpr int PRE_QROWS = 64;                                    // query tokens per prefill item
 // tcgen05 prefill: sub-tile X (0, 1) = 128 rows r: query head 4g + 2X + r / 64,
 // token t0 + r % 64; KV tiles of 64 keys (4 blocks) in rings of TC_NS slots.
+// A K slot holds the two 64-column halves outermost ([half][64 keys][64], the
+// K-major operand of S = Q K^T); a V slot holds each block's 4 KB tile as one
+// TMA box lands it ([block][half][16 keys][64], the MN-major operand of P V).
 constexpr int TC_KEYS = 64;
 constexpr int TC_NS = 4;                                         // K and V ring slots
 constexpr int TC_KV_BYTES = TC_KEYS * HY_HEAD_DIM * 2;          // K or V of one tile: 16 KB
@@ -59,9 +62,11 @@ constexpr int TC_Q_BYTES = 128 * HY_HEAD_DIM * 2;                // Q of one sub
 constexpr int TC_K_OFF = 2 * TC_Q_BYTES;                         // K ring
 constexpr int TC_V_OFF = TC_K_OFF + TC_NS * TC_KV_BYTES;         // V ring
 constexpr int TC_SMEM = TC_V_OFF + TC_NS * TC_KV_BYTES;          // 192 KB
-// TMEM columns: S_X at 64 X, O_X at 128 + 128 X, P_X (bf16 pairs) at 384 + 32 X
+// TMEM columns: two S buffers per sub-tile, S_X[b] at 64 (2X + b), P_X[b] (bf16
+// pairs) written over the first 32 columns of S_X[b]; O_X at 256 + 128 X.
 constexpr uint32_t TC_TMEM_COLS = 512;
-constexpr uint32_t TM_S = 0, TM_O = 128, TM_P = 384;
+constexpr uint32_t TM_O = 256;
+HY_DEVICE uint32_t tm_s(int X, uint32_t b) { return 64u * (2u * X + b); }
 constexpr int SMEM_PAYLOAD = ATT_WARPS * DEC_WARP_BYTES > TC_SMEM ? ATT_WARPS * DEC_WARP_BYTES
                                                                    : TC_SMEM;
 constexpr int SMEM_BYTES = SMEM_PAYLOAD + 1024;                  // + alignment slack
@@ -97,10 +102,9 @@ struct Shared {
   uint64_t tc_vfull[TC_NS];  // V tile landed
   uint64_t tc_kfree[TC_NS];  // both S MMAs that read the K slot are done (2 commits)
   uint64_t tc_vfree[TC_NS];  // both PV MMAs that read the V slot are done (2 commits)
-  uint64_t tc_sfull[2];      // S_X = Q_X K^T complete
-  uint64_t tc_sfree[2];      // S_X read out by the 4 softmax warps of X
-  uint64_t tc_pfull[2];      // P_X written to TMEM by the 4 softmax warps of X
-  uint64_t tc_odone[2];      // O_X += P_X V complete
+  uint64_t tc_sfull[2][2];   // S_X[b] = Q_X K^T complete (once per use of buffer b)
+  uint64_t tc_pfull[2][2];   // P_X[b] written over S_X[b] by the 4 softmax warps of X
+  uint64_t tc_odone[2];      // O_X += P_X V complete (once per key tile)
   uint64_t tc_drain[2];      // error path: all MMAs an issuing warp issued are complete
   uint32_t tmem_base;        // TMEM columns from tcgen05.alloc
   int pre_item;              // prefill item handed to this CTA
@@ -561,23 +565,34 @@ __device__ bool decode_item(const CUtensorMap* tiles, const MainArgs& a, const P
 // M=128 sub-tiles X of the same tokens (query heads 4g+2X, 4g+2X+1), which see
 // the same keys and masks, so each 64-key K/V tile is loaded once for both.
 //   warps 0-3 / 4-7  softmax of sub-tile 0 / 1: thread = row = TMEM lane, so a
-//                    row's max and sum stay in one thread.  Per key tile: S_X
+//                    row's max and sum stay in one thread.  Per key tile: S_X[b]
 //                    from TMEM, causal mask, online softmax with lazy rescaling
-//                    of O_X, P_X (bf16 pairs) back into TMEM;
-//   warp 8, lane 0   issues S_X(t) = Q_X K_t^T for both X, then
-//                    O_X += P_X(t-1) V_{t-1} (A operand read from TMEM), each
-//                    followed by tcgen05.commit to the barrier its consumer waits on;
-//   warp 9, lane 0   loads K_t and V_t (8 TMA boxes each: 4 paged blocks x two
-//                    64-column halves) into ring slot c % TC_NS once the MMAs of
-//                    the slot's previous use are done.
-// c = c0 + t counts key tiles over all items of the launch; every barrier
-// completes exactly once per tile (sub-tile barriers) or per use of its slot
-// (ring barriers), so a wait is always on the current or the previous phase.
-// Returns false if a wait ran out; the roles then drain their own asynchronous
-// work before the item ends.
-__device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
-                                int item, uint8_t* payload, Shared& sh, uint32_t tmem,
-                                uint32_t& ctr) {
+//                    of O_X, P_X (bf16 pairs) written back over S_X[b];
+//   warp 8 / 10,     one per sub-tile: issues S_X(t) = Q_X K_t^T into buffer
+//   lane 0           b = t % 2, then O_X += P_X(t-1) V_{t-1} (A operand read from
+//                    TMEM), each followed by tcgen05.commit to the barrier its
+//                    consumer waits on;
+//   warp 9, lane 0   loads K_t (8 TMA boxes: 4 paged blocks x two 64-column
+//                    halves) and V_t (4 boxes: one whole 4 KB block tile each) into
+//                    ring slot c % TC_NS once the MMAs of the slot's previous use
+//                    are done.
+// With two S buffers the MMA warp issues S(t+1) while the softmax works on
+// S(t), so the softmax never waits for its scores once the pipeline is full.
+// S(t) may overwrite buffer b only after PV(t-2) has read P(t-2) from it: the
+// issuing thread issued PV(t-2) before S(t), and tcgen05.mma operations of one
+// thread execute in issue order (as the K-step accumulation into one D relies
+// on).  The softmax writes P(t) over S(t) after reading S(t), which completed
+// after PV(t-2); it need not wait for PV(t-1) (the other buffer) except to
+// rescale O.
+// c = c0 + t counts key tiles over all items of the launch; each barrier
+// completes exactly once per tile (odone), per use of its buffer (sfull, pfull:
+// every second tile) or per use of its slot (ring barriers), and no role can
+// run a full phase ahead of the role that waits on it, so a wait is always on
+// the current or the previous phase.  Returns false if a wait ran out; the
+// roles then drain their own asynchronous work before the item ends.
+__device__ bool prefill_item_tc(const CUtensorMap* map, const CUtensorMap* tiles,
+                                const MainArgs& a, const PlanView& v, int item, uint8_t* payload,
+                                Shared& sh, uint32_t tmem, uint32_t& ctr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int4 it = v.pre_sorted[item];
   const int seq = it.x, g = it.y, t0 = it.z;
@@ -612,9 +627,8 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const
 
   if (warp == TC_LOAD_WARP) {
     // lane 0 waits for the slot and posts the byte count; lanes 0-7 then issue
-    // the tile's 8 boxes (block lane / 2, column half lane % 2) side by side.
-    // (The TMA unit takes a 2 KB box about every 90 cycles, which bounds the
-    // K/V supply; 16-byte cp.async copies from one warp measured slower.)
+    // the K tile's 8 half boxes (block lane / 2, column half lane % 2), lanes
+    // 0-3 the V tile's 4 block boxes, side by side.
     const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
     const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
     int ids = -1;                               // lane i: block 32 (t / 8) + i of the sequence
@@ -624,7 +638,6 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const
         const int b = 4 * t + lane;
         ids = (b < nblk && b < a.bt_pitch) ? bt[b] : -1;
       }
-      const int id = __shfl_sync(0xffffffffu, ids, (4 * t + (lane >> 1)) & 31);
       const uint32_t c = c0 + t, slot = c % TC_NS, use = c / TC_NS;
 #pragma unroll 1
       for (int kv = 0; kv < 2; ++kv) {
@@ -634,13 +647,17 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const
         if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) { ok = false; break; }
         uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
         if (lane == 0) mbar_arrive_expect_tx(full, TC_KV_BYTES);
-        if (lane < 8) {
-          const int jb = lane >> 1, hf = lane & 1;
+        const int jb = kv ? lane : (lane >> 1);
+        const int id = __shfl_sync(0xffffffffu, ids, (4 * t + jb) & 31);
+        if (lane < (kv ? 4 : 8)) {
           int r = a.oob_row;                    // past the end: zero fill
           if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
           else if (id >= 0) r = kv_row(a, id, kv, g);
-          tma_load_2d(payload + (kv ? TC_V_OFF : TC_K_OFF) + slot * TC_KV_BYTES + hf * TC_HALF +
-                          jb * 2048, map, 64 * hf, r, full);
+          if (kv)
+            tma_load_3d(payload + TC_V_OFF + slot * TC_KV_BYTES + jb * 4096, tiles, 0, r, 0, full);
+          else
+            tma_load_2d(payload + TC_K_OFF + slot * TC_KV_BYTES + (lane & 1) * TC_HALF + jb * 2048,
+                        map, 64 * (lane & 1), r, full);
         }
         issued[kv] = t + 1;
       }
@@ -662,33 +679,34 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const
       constexpr uint32_t ID_O = tc_idesc_bf16(128, HY_HEAD_DIM, true);
       const uint64_t dQ = tc_desc_sw128(sbase + X * TC_Q_BYTES, 16, 1024);
       for (int t = 0; t <= ntiles && ok; ++t) {
-        if (t < ntiles) {                       // S_X(t) = Q_X K_t^T
+        if (t < ntiles) {                       // S_X(t) = Q_X K_t^T into buffer c % 2
           const uint32_t c = c0 + t, slot = c % TC_NS;
-          ok = mbar_wait(&sh.tc_kfull[slot], (c / TC_NS) & 1, a.err) &&
-               mbar_wait(&sh.tc_sfree[X], (c & 1) ^ 1, a.err);     // S_X(t-1) read out
+          ok = mbar_wait(&sh.tc_kfull[slot], (c / TC_NS) & 1, a.err);
           if (!ok) break;
           tc_fence_after();
           const uint64_t dK = tc_desc_sw128(sbase + TC_K_OFF + slot * TC_KV_BYTES, 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < HY_HEAD_DIM / 16; ++kk)
-            tc_mma_bf16(tmem + TM_S + 64 * X,
+            tc_mma_bf16(tmem + tm_s(X, c & 1),
                         dQ + (uint64_t)((((kk >> 2) * (TC_Q_BYTES / 2)) + (kk & 3) * 32) >> 4),
                         dK + (uint64_t)((((kk >> 2) * TC_HALF) + (kk & 3) * 32) >> 4), ID_S,
                         kk > 0);
-          tc_commit(&sh.tc_sfull[X]);
+          tc_commit(&sh.tc_sfull[X][c & 1]);
           tc_commit(&sh.tc_kfree[slot]);
         }
         if (t > 0) {                            // O_X += P_X(t-1) V_{t-1}
           const uint32_t c = c0 + t - 1, slot = c % TC_NS;
           ok = mbar_wait(&sh.tc_vfull[slot], (c / TC_NS) & 1, a.err) &&
-               mbar_wait(&sh.tc_pfull[X], c & 1, a.err);
+               mbar_wait(&sh.tc_pfull[X][c & 1], (c >> 1) & 1, a.err);
           if (!ok) break;
           tc_fence_after();
-          const uint64_t dV = tc_desc_sw128(sbase + TC_V_OFF + slot * TC_KV_BYTES, TC_HALF, 1024);
+          // V slot: block kk's tile at kk x 4 KB, its column halves 2 KB apart (LBO),
+          // 8-key groups 1 KB apart (SBO)
+          const uint64_t dV = tc_desc_sw128(sbase + TC_V_OFF + slot * TC_KV_BYTES, 2048, 1024);
 #pragma unroll
           for (int kk = 0; kk < TC_KEYS / 16; ++kk)
-            tc_mma_bf16_ta(tmem + TM_O + 128 * X, tmem + TM_P + 32 * X + 8 * kk,
-                           dV + (uint64_t)((kk * 2048) >> 4), ID_O, (t > 1 || kk > 0));
+            tc_mma_bf16_ta(tmem + TM_O + 128 * X, tmem + tm_s(X, c & 1) + 8 * kk,
+                           dV + (uint64_t)((kk * 4096) >> 4), ID_O, (t > 1 || kk > 0));
           tc_commit(&sh.tc_odone[X]);
           tc_commit(&sh.tc_vfree[slot]);
         }
@@ -702,25 +720,21 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const
   } else {                                      // softmax warpgroups
     const int X = warp >> 2, r = (warp & 3) * 32 + lane, j = r & 63;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_base + TM_S + 64 * X;
     const uint32_t tO = tmem + lane_base + TM_O + 128 * X;
-    const uint32_t tP = tmem + lane_base + TM_P + 32 * X;
     const int lim = prefix + t0 + j;            // last key row r may see
     const float sl2 = a.scale_log2;
     float m = NEG_INF, l = 0.f;                 // m in scaled log2 units
     for (int t = 0; t < ntiles && ok; ++t) {
       const uint32_t c = c0 + t;
+      const uint32_t tS = tmem + lane_base + tm_s(X, c & 1);
       // waits are made warp-uniform: tcgen05.ld/st below are warp-collective
-      ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_sfull[X], c & 1, a.err));
+      ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_sfull[X][c & 1], (c >> 1) & 1, a.err));
       if (!ok) break;
       tc_fence_after();
       float s[64];
       tmem_ld32(tS, *reinterpret_cast<float(*)[32]>(&s[0]));
       tmem_ld32(tS + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sh.tc_sfree[X]);
       const int kb = t * TC_KEYS;
       if (kb + TC_KEYS - 1 > prefix + t0) {     // the tile reaches the diagonal or the end
 #pragma unroll
@@ -732,15 +746,13 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const
       for (int i = 0; i < 64; ++i) mx = fmaxf(mx, s[i]);
       mx *= sl2;
       const bool grow = mx > m + RESCALE_LOG2;
-      bool odone = false;                       // O_X += P_X V of tile t-1 is complete
       if (__any_sync(0xffffffffu, grow)) {
         const float mnew = grow ? mx : m;
-        const float alpha = exp2f(m - mnew);    // 0 when m was -inf
+        const float alpha = ex2_ftz(m - mnew);  // 0 when m was -inf
         l *= alpha;
         m = mnew;
-        if (t > 0) {                            // O holds tiles < t
+        if (t > 0) {                            // O holds tiles < t: wait for PV(t-1)
           ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_odone[X], (c & 1) ^ 1, a.err));
-          odone = true;
           tc_fence_after();
 #pragma unroll 1
           for (int cc = 0; cc < 4; ++cc) {
@@ -758,21 +770,17 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const MainArgs& a, const
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float p0 = exp2f(fmaf(s[2 * i], sl2, mneg));
-        const float p1 = exp2f(fmaf(s[2 * i + 1], sl2, mneg));
+        const float p0 = ex2_ftz(fmaf(s[2 * i], sl2, mneg));
+        const float p1 = ex2_ftz(fmaf(s[2 * i + 1], sl2, mneg));
         l += p0;
         l += p1;
         pk[i] = pack_bf16(p0, p1);
       }
-      if (!odone) {                             // P_X is free once PV of tile t-1 is done
-        ok = __all_sync(0xffffffffu, ok && mbar_wait(&sh.tc_odone[X], (c & 1) ^ 1, a.err));
-        tc_fence_after();
-      }
-      tmem_st32u(tP, pk);
+      tmem_st32u(tS, pk);                       // P(t) over the first 32 columns of S(t)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sh.tc_pfull[X]);
+      if (lane == 0) mbar_arrive(&sh.tc_pfull[X][c & 1]);
     }
     if (ok) {                                   // epilogue: O_X / l -> out
       const uint32_t c = c0 + ntiles - 1;
@@ -826,9 +834,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
       mbar_init(&sh.tc_vfree[s], 2);
     }
     for (int x = 0; x < 2; ++x) {
-      mbar_init(&sh.tc_sfull[x], 1);
-      mbar_init(&sh.tc_sfree[x], 4);            // one arrival per softmax warp
-      mbar_init(&sh.tc_pfull[x], 4);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&sh.tc_sfull[x][b], 1);
+        mbar_init(&sh.tc_pfull[x][b], 4);       // one arrival per softmax warp
+      }
       mbar_init(&sh.tc_odone[x], 1);
     }
     mbar_init(&sh.tc_drain[0], 1);
@@ -862,7 +871,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
       const int k = sh.pre_item;
       __syncthreads();                          // read before thread 0 writes the next one
       if (k >= n_pre) break;
-      ok = prefill_item_tc(&kv_map, a, v, k, payload, sh, tmem, tile_ctr);
+      ok = prefill_item_tc(&kv_map, &kv_tiles, a, v, k, payload, sh, tmem, tile_ctr);
     }
   }
   // decode items (warps 0..ATT_WARPS-1): each warp takes the next one from this

@@ -210,6 +210,15 @@ HY_DEVICE void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// 2^x with the hardware approximation (PTX ex2.approx.ftz.f32): relative error
+// near 2^-22, subnormal results flushed to zero, 2^-inf = 0.  Softmax weights
+// are rounded to bf16 or summed in fp32, so neither matters there.
+HY_DEVICE float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 HY_DEVICE uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
