@@ -48,6 +48,7 @@ SIGNATURES = {
     "hy_silu_mul": (C.c_int, [I32, P, I64, I32, I32, P, I64, P]),
     "hy_argmax": (C.c_int, [I32, P, I64, I32, I32, P, P]),
     "hy_selftest_wait_timeout": (C.c_int, [P, I32, P, P]),
+    "hy_selftest_exp2_poly": (C.c_int, [P, P, I32, P]),
     "hy_varlen_attention_noalloc": (C.c_int, [P, P, I32, I32, I32, P, I32, I32, I32, P, I32, P,
                                               P, P, I32, F32, P, P]),
 }

@@ -4,7 +4,9 @@
 ``csrc/*.cu`` to an object under ``_build/`` (in parallel) and links the shared
 library next to this file.  Objects are rebuilt when their source or any header
 is newer.  ``-Xptxas -v`` output (registers, spills, shared memory) is kept in
-``_build/ptxas.log``.
+``_build/ptxas.log``.  ``HY_NVCC_DEFINES`` (e.g. ``-DHY_EXP2_POLY_EVERY=2``)
+adds preprocessor definitions to every compile, for building a tuning variant
+of a kernel constant; rebuild with ``--force`` after changing it.
 """
 from __future__ import annotations
 
@@ -52,7 +54,8 @@ def _stale(target: str, deps) -> bool:
 
 def _compile(src: str, verbose: bool):
     obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
-    cmd = [nvcc(), *ARCH, *FLAGS, "-c", src, "-o", obj]
+    defines = os.environ.get("HY_NVCC_DEFINES", "").split()
+    cmd = [nvcc(), *ARCH, *FLAGS, *defines, "-c", src, "-o", obj]
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -88,6 +88,11 @@ constexpr int MERGE_ML_BYTES = MERGE_CHUNK * HY_GROUP * 8;
 static_assert(MERGE_O_BYTES + MERGE_ML_BYTES + MERGE_CHUNK * HY_GROUP * 4 <= DEC_WARP_BYTES,
               "merge staging must fit a decode warp's ring");
 constexpr float NEG_INF = -INFINITY;
+#ifndef HY_EXP2_POLY_EVERY
+#define HY_EXP2_POLY_EVERY 4
+#endif
+// prefill softmax: 1 in EXP2_POLY_EVERY pairs of weights by exp2_poly (0: none)
+constexpr int EXP2_POLY_EVERY = HY_EXP2_POLY_EVERY;
 // Lazy rescaling: the running max is only raised when a new score exceeds it
 // by more than 2^RESCALE_LOG2; until then probabilities may exceed 1 by up to
 // that factor, which fp32 accumulators and bf16 P carry without loss of
@@ -741,9 +746,17 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const CUtensorMap* tiles
         for (int i = 0; i < 64; ++i)
           if (kb + i > lim || kb + i >= kv_len) s[i] = NEG_INF;
       }
-      float mx = NEG_INF;
+      // row max and row sum as 8 independent chains (a 64-long chain of
+      // dependent max or add instructions would expose its latency)
+      float mxs[8];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) mx = fmaxf(mx, s[i]);
+      for (int k = 0; k < 8; ++k) mxs[k] = s[k];
+#pragma unroll
+      for (int i = 8; i < 64; i += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mxs[k] = fmaxf(mxs[k], s[i + k]);
+      float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                       fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
       mx *= sl2;
       const bool grow = mx > m + RESCALE_LOG2;
       if (__any_sync(0xffffffffu, grow)) {
@@ -768,14 +781,20 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const CUtensorMap* tiles
       }
       const float mneg = (m == NEG_INF) ? 0.f : -m;
       uint32_t pk[32];
+      float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float p0 = ex2_ftz(fmaf(s[2 * i], sl2, mneg));
-        const float p1 = ex2_ftz(fmaf(s[2 * i + 1], sl2, mneg));
-        l += p0;
-        l += p1;
+        // every EXP2_POLY_EVERY-th pair of weights on the FMA pipe, the rest on
+        // the exp2 unit: the two units then share the tile's 64 exponentials
+        const bool poly = EXP2_POLY_EVERY > 0 && (i % EXP2_POLY_EVERY) == EXP2_POLY_EVERY - 1;
+        const float x0 = fmaf(s[2 * i], sl2, mneg), x1 = fmaf(s[2 * i + 1], sl2, mneg);
+        const float p0 = poly ? exp2_poly(x0) : ex2_ftz(x0);
+        const float p1 = poly ? exp2_poly(x1) : ex2_ftz(x1);
+        ls[(2 * i) & 7] += p0;
+        ls[(2 * i + 1) & 7] += p1;
         pk[i] = pack_bf16(p0, p1);
       }
+      l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
       tmem_st32u(tS, pk);                       // P(t) over the first 32 columns of S(t)
       tmem_wait_st();
       tc_fence_before();

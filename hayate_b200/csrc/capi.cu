@@ -142,6 +142,12 @@ __global__ void wait_timeout_probe_kernel(int32_t* err, uint64_t timeout_ns, int
   if (threadIdx.x == 0) *done = ok ? 2 : 1;
 }
 
+// The prefill softmax's polynomial 2^x on n inputs (one thread each).
+__global__ void exp2_poly_probe_kernel(const float* __restrict__ x, float* __restrict__ y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = exp2_poly(x[i]);
+}
+
 // Shared with other translation units of the library (not part of the C ABI).
 int hy_attention_kv_map(int dev, const void* base, long rows, KvMaps* out) {
   return kv_map_for(dev, base, rows, out);
@@ -439,6 +445,13 @@ int hy_selftest_wait_timeout(int32_t* err, int32_t timeout_ms, int32_t* done, vo
   wait_timeout_probe_kernel<<<1, 32, 0, as_stream(stream)>>>(err, (uint64_t)timeout_ms * 1000000ull,
                                                              done);
   return cuda_result(cudaGetLastError(), "hy_selftest_wait_timeout");
+}
+
+int hy_selftest_exp2_poly(const float* x, float* y, int32_t n, void* stream) {
+  if (!x || !y || n < 0) return fail(HY_E_INVALID, "hy_selftest_exp2_poly: bad argument");
+  if (n == 0) return HY_OK;
+  exp2_poly_probe_kernel<<<(n + 255) / 256, 256, 0, as_stream(stream)>>>(x, y, n);
+  return cuda_result(cudaGetLastError(), "hy_selftest_exp2_poly");
 }
 
 int hy_argmax(int32_t dtype, const void* logits, int64_t ld, int32_t rows, int32_t vocab,

@@ -219,6 +219,26 @@ HY_DEVICE float ex2_ftz(float x) {
   return y;
 }
 
+// 2^x on the FMA and integer pipes, for softmax weights the exp2 unit cannot
+// keep up with: Cody-Waite range reduction to f = x - round(x) in [-0.5, 0.5]
+// (round(x) by the 1.5 * 2^23 addition), a degree-3 polynomial for 2^f whose
+// coefficients minimise the largest relative error on that interval (fitted by
+// linear programming over 4001 points: 7.5e-5, i.e. 2^-13.7), then 2^round(x)
+// added to the exponent bits.  Valid for x <= 127; results below 2^-126 are
+// returned as 0 (x = -inf gives 0).  Used where the weight is rounded to bf16
+// (2^-9 relative) or summed in fp32.
+HY_DEVICE float exp2_poly(float x) {
+  const float xc = fmaxf(x, -126.0f);
+  const float t = __fadd_rn(xc, 12582912.0f);          // 1.5 * 2^23: round(xc) in the low bits
+  const float f = __fsub_rn(xc, __fsub_rn(t, 12582912.0f));
+  float p = fmaf(0.05517166853f, f, 0.24261112511f);
+  p = fmaf(p, f, 0.69326096773f);
+  p = fmaf(p, f, 0.99992805719f);
+  const int e = __float_as_int(t) - 0x4B400000;         // round(xc) as an integer
+  const float y = __int_as_float(__float_as_int(p) + (e << 23));
+  return x < -126.0f ? 0.0f : y;
+}
+
 HY_DEVICE uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

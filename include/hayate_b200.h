@@ -246,6 +246,14 @@ int hy_argmax(int32_t dtype, const void* logits, int64_t ld, int32_t rows, int32
  * The kernels' own waits use the same bounded wait (limit 2 s). */
 int hy_selftest_wait_timeout(int32_t* err, int32_t timeout_ms, int32_t* done, void* stream);
 
+/* Accuracy self-test of the polynomial 2^x the prefill softmax computes part of
+ * its weights with (the rest on the hardware exp2 unit): y[i] = 2^x[i] for
+ * -126 < x[i] <= 127 with relative error below 1e-4 (2e-4 at -126, whose result
+ * is subnormal); 0 for x[i] < -126 and for -inf.  No
+ * reference counterpart: the reference takes its softmax from torch SDPA
+ * (hayate/model/attention.py:58-64). */
+int hy_selftest_exp2_poly(const float* x, float* y, int32_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

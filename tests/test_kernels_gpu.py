@@ -605,3 +605,31 @@ def test_bounded_wait_gives_up_and_reports():
     out = torch.empty(3, dtype=torch.int32, device=dev)
     K.argmax(x, out)
     assert torch.equal(out, torch.argmax(x, -1).int())
+
+
+def test_exp2_poly_accuracy_against_cuda_exp2():
+    """The prefill softmax's polynomial 2^x (range reduction + a degree-3
+    minimax polynomial on the FMA pipe) against CUDA's exp2f (torch.exp2 on the
+    device): relative error below 1e-4 on (-126, 8] (weights are rounded to
+    bf16, 2^-9 relative, before the P V product) and 2e-4 at -126 (a subnormal
+    result); exactly 0 below -126 and at -inf."""
+    from hayate_b200 import _lib
+    x = torch.cat([torch.linspace(-125.99, 8.0, 200001, device=dev),
+                   torch.tensor([0.0, -0.5, 0.5, 1.0, -1.0, 7.5, -125.5], device=dev)])
+    y = torch.empty_like(x)
+    assert _lib.load().hy_selftest_exp2_poly(x.data_ptr(), y.data_ptr(), x.numel(),
+                                             torch.cuda.current_stream().cuda_stream) == 0
+    want = torch.exp2(x)
+    rel = ((y - want).abs() / want).max().item()
+    assert rel < 1e-4, rel
+    edge = torch.tensor([-126.0], device=dev)
+    ye = torch.empty_like(edge)
+    _lib.load().hy_selftest_exp2_poly(edge.data_ptr(), ye.data_ptr(), 1,
+                                      torch.cuda.current_stream().cuda_stream)
+    assert ((ye - torch.exp2(edge)).abs() / torch.exp2(edge)).item() < 2e-4
+    lo = torch.tensor([-126.5, -127.0, -200.0, float("-inf")], device=dev)
+    out = torch.full_like(lo, 5.0)
+    _lib.load().hy_selftest_exp2_poly(lo.data_ptr(), out.data_ptr(), lo.numel(),
+                                      torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert torch.equal(out, torch.zeros_like(lo))
