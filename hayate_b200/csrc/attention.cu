@@ -78,6 +78,15 @@ constexpr int SMEM_BYTES = SMEM_PAYLOAD + 1024;                  // + alignment 
 #endif
 constexpr int MIN_SPLIT = HY_MIN_SPLIT;                          // blocks per decode item, at least
 constexpr int ITEMS_PER_WARP = HY_ITEMS_PER_WARP;                // decode items aimed at per warp
+// Per-CTA decode: a step of decode sequences only, whose (sequence, KV head)
+// pairs fit one per CTA and whose contexts are at most GROUP_MAX_BLOCKS blocks,
+// gives each pair to one CTA; its decode warps split the pair's blocks and
+// merge their partials in shared memory.
+#ifndef HY_GROUP_MAX_BLOCKS
+#define HY_GROUP_MAX_BLOCKS 128
+#endif
+constexpr int GROUP_MAX_BLOCKS = HY_GROUP_MAX_BLOCKS;
+constexpr int MERGE_BAR = 1;                                     // named barrier of the decode warps
 constexpr int GRAB_INTS = 4;                                     // per layer: decode item, CTAs
                                                                  // done, prefill item, spare
 // a split-K merge stages the partials of MERGE_CHUNK splits at a time (2 KB of O
@@ -161,22 +170,41 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
   hy_grid_wait();
   hy_grid_trigger();
   __shared__ int ws[32];
-  __shared__ int s_total, s_cpre, s_cdec, s_bad;
-  if (threadIdx.x == 0) { s_total = 0; s_cpre = 0; s_cdec = 0; s_bad = 0; }
+  __shared__ int s_total, s_cpre, s_cdec, s_bad, s_maxblk, s_anypre;
+  if (threadIdx.x == 0) {
+    s_total = 0; s_cpre = 0; s_cdec = 0; s_bad = 0; s_maxblk = 0; s_anypre = 0;
+  }
   __syncthreads();
-  // Pass 1: KV blocks over all decode sequences.
-  int part = 0;
+  // Pass 1: KV blocks over all decode sequences, the longest, any prefill.
+  int part = 0, mxb = 0, pre = 0;
   for (int i = threadIdx.x; i < S; i += PLAN_THREADS) {
     const int q = cu_q[i + 1] - cu_q[i];
-    if (q == 1) part += (seq_lens_k[i] + HY_BLOCK - 1) / HY_BLOCK;
+    if (q == 1) {
+      const int nb = (seq_lens_k[i] + HY_BLOCK - 1) / HY_BLOCK;
+      part += nb;
+      mxb = max(mxb, nb);
+    } else if (q > 1) {
+      pre = 1;
+    }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-  if ((threadIdx.x & 31) == 0) atomicAdd(&s_total, part);   // 32 shared atomics, not 1024
+  for (int o = 16; o > 0; o >>= 1) {
+    part += __shfl_xor_sync(0xffffffffu, part, o);
+    mxb = max(mxb, __shfl_xor_sync(0xffffffffu, mxb, o));
+    pre |= __shfl_xor_sync(0xffffffffu, pre, o);
+  }
+  if ((threadIdx.x & 31) == 0) {                // 32 shared atomics, not 1024
+    atomicAdd(&s_total, part);
+    atomicMax(&s_maxblk, mxb);
+    atomicOr(&s_anypre, pre);
+  }
   __syncthreads();
   const long target = (long)ITEMS_PER_WARP * warp_slots;
   const long want = ((long)kv_heads * s_total + target - 1) / target;
   const int split = (int)max((long)MIN_SPLIT, want);
+  // per-CTA decode (see GROUP_MAX_BLOCKS): one item per warp, at most a CTA's warps
+  const bool group = !s_anypre && (long)S * kv_heads <= warp_slots / ATT_WARPS &&
+                     s_maxblk <= GROUP_MAX_BLOCKS;
 
   // Pass 2: item counts, offsets, items.
   for (int base = 0; base < S; base += PLAN_THREADS) {
@@ -189,7 +217,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
       if (q < 0 || kv < q) atomicOr(&s_bad, HY_ERR_BOUNDS);
       else if (q == 1) {
         nblk = (kv + HY_BLOCK - 1) / HY_BLOCK;
-        ns = (nblk + split - 1) / split;
+        ns = group ? max(1, min(ATT_WARPS, nblk)) : (nblk + split - 1) / split;
         ndec = kv_heads * ns;
       } else if (q > 1) {
         ntile = (q + PRE_QROWS - 1) / PRE_QROWS;
@@ -273,6 +301,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
     v.header[1] = bad ? 0 : min(s_cdec, v.max_dec);
     v.header[2] = split;
     v.header[3] = s_bad;
+    v.header[4] = group && !bad ? S * kv_heads : 0;   // per-CTA decode: its pair count
     if (bad) hy_flag(err, s_bad);
   }
 }
@@ -301,15 +330,24 @@ HY_DEVICE int kv_row(const MainArgs& a, int blk, int kv, int g) {
   return a.layer_row_base + ((blk * 2 + kv) * a.kv_heads + g) * HY_BLOCK;
 }
 
-// Returns false if a wait ran out (the caller stops).
-__device__ bool decode_item(const CUtensorMap* tiles, const MainArgs& a, const PlanView& v,
-                            int item, uint8_t* ring, uint64_t* bars, uint32_t& phase) {
+// The attention of one decode item over its block range: on return lane
+// (r, c) = (lane / 4, lane % 4) with r < 4 holds query head 4g + r's unnormalised
+// output in o[j][0..1] (dims 8j + 2c, 8j + 2c + 1), and every lane of row r its
+// running max m (scaled log2 units) and sum l.  Returns false if a wait ran out.
+struct DecodeItemInfo {
+  int seq, g, tok, ns, first;
+};
+
+__device__ bool decode_item_core(const CUtensorMap* tiles, const MainArgs& a, const PlanView& v,
+                                 int item, uint8_t* ring, uint64_t* bars, uint32_t& phase,
+                                 float (&o)[16][4], float& m, float& l, DecodeItemInfo& di) {
   const int lane = threadIdx.x & 31;
   const uint64_t keep = l2_keep_policy();
   const int4 it = ld_keep(&v.dec[2 * item], keep);        // one 32-byte record
   const int4 info = ld_keep(&v.dec[2 * item + 1], keep);
   const int seq = it.x, g = it.y, b0 = it.z, b1 = it.w;
-  const int tok = info.x, kv_len = info.y, ns = info.z, first = info.w;
+  const int tok = info.x, kv_len = info.y;
+  di.seq = seq; di.g = g; di.tok = tok; di.ns = info.z; di.first = info.w;
   const int4 c0 = ld_keep(&v.dec_ids[2 * item], keep);
   const int4 c1 = ld_keep(&v.dec_ids[2 * item + 1], keep);
   const int n = b1 - b0;
@@ -375,10 +413,10 @@ __device__ bool decode_item(const CUtensorMap* tiles, const MainArgs& a, const P
       }
     }
   }
-  float o[16][4];
 #pragma unroll
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float m = NEG_INF, l = 0.f;
+  m = NEG_INF;
+  l = 0.f;
 
   // Per-lane ldmatrix coordinates.
   const int mi = lane >> 3, ri = lane & 7;
@@ -456,9 +494,23 @@ __device__ bool decode_item(const CUtensorMap* tiles, const MainArgs& a, const P
     for (int s = 0; s < DEC_STAGES; ++s) mbar_wait(&bars[s], (phase >> s) & 1u, nullptr);
     return false;
   }
-
   l += __shfl_xor_sync(0xffffffffu, l, 1);
   l += __shfl_xor_sync(0xffffffffu, l, 2);
+  return true;
+}
+
+// One decode item whose split-K partners may run on other SMs: a sole item
+// writes its output; otherwise the partial goes to the workspace and the last
+// of the (seq, head)'s items to finish (an atomic count) merges all of them.
+__device__ bool decode_item(const CUtensorMap* tiles, const MainArgs& a, const PlanView& v,
+                            int item, uint8_t* ring, uint64_t* bars, uint32_t& phase) {
+  const int lane = threadIdx.x & 31;
+  float o[16][4];
+  float m, l;
+  DecodeItemInfo di;
+  if (!decode_item_core(tiles, a, v, item, ring, bars, phase, o, m, l, di)) return false;
+  const int seq = di.seq, g = di.g, tok = di.tok, ns = di.ns, first = di.first;
+  const int r = lane >> 2, c = 2 * (lane & 3);
   if (r < HY_GROUP) {
     if (ns <= 1) {
       const float inv = 1.f / l;
@@ -562,6 +614,70 @@ __device__ bool decode_item(const CUtensorMap* tiles, const MainArgs& a, const P
       if (lane == 0) v.counters[seq * a.kv_heads + g] = 0;   // ready for the next layer
     }
   }
+  return true;
+}
+
+// Per-CTA decode of one (sequence, KV head) pair: warp w < ns runs the pair's
+// item w; the partials meet in shared memory (each warp's own TMA ring, idle
+// once its item is done) and the CTA's decode warps merge them, one output
+// pair of head dimensions per thread.  No workspace round trip, fence or
+// atomic count.  All ATT_WARPS decode warps of the CTA call this.
+__device__ bool decode_pair_cta(const CUtensorMap* tiles, const MainArgs& a, const PlanView& v,
+                                int pair, uint8_t* payload, uint64_t (*bars)[DEC_STAGES],
+                                uint32_t& phase) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int seq = pair / a.kv_heads, g = pair - seq * a.kv_heads;
+  const int2 si = v.seqinfo[seq];               // first decode item of the sequence, items per head
+  const int ns = si.y, first = si.x + g * ns;
+  uint8_t* ring = payload + warp * DEC_WARP_BYTES;
+  float* part_o = reinterpret_cast<float*>(ring);                        // [4][128]
+  float2* part_ml = reinterpret_cast<float2*>(ring + HY_GROUP * HY_HEAD_DIM * 4);
+  bool ok = true;
+  if (warp < ns) {
+    float o[16][4];
+    float m, l;
+    DecodeItemInfo di;
+    ok = decode_item_core(tiles, a, v, first + warp, ring, bars[warp], phase, o, m, l, di);
+    const int r = lane >> 2, c = 2 * (lane & 3);
+    if (ok && r < HY_GROUP) {
+      if (ns == 1) {                            // the only split: final output
+        const float inv = 1.f / l;
+        __nv_bfloat16* op =
+            a.out + ((size_t)di.tok * a.q_heads + g * HY_GROUP + r) * HY_HEAD_DIM;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          *reinterpret_cast<uint32_t*>(op + 8 * j + c) = pack_bf16(o[j][0] * inv, o[j][1] * inv);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          *reinterpret_cast<float2*>(part_o + r * HY_HEAD_DIM + 8 * j + c) =
+              make_float2(o[j][0], o[j][1]);
+        if ((lane & 3) == 0) part_ml[r] = make_float2(m, l);
+      }
+    }
+  }
+  if (named_sync_or(MERGE_BAR, ATT_WARPS * 32, !ok)) return false;
+  if (ns <= 1) return true;
+  const int t = threadIdx.x, r = t >> 6, d = 2 * (t & 63);
+  const int tok = v.dec[2 * first + 1].x;
+  float M = NEG_INF;
+  for (int w = 0; w < ns; ++w)
+    M = fmaxf(M, reinterpret_cast<const float2*>(payload + w * DEC_WARP_BYTES +
+                                                 HY_GROUP * HY_HEAD_DIM * 4)[r].x);
+  float L = 0.f, a0 = 0.f, a1 = 0.f;
+  for (int w = 0; w < ns; ++w) {
+    const uint8_t* rw = payload + w * DEC_WARP_BYTES;
+    const float2 ml = reinterpret_cast<const float2*>(rw + HY_GROUP * HY_HEAD_DIM * 4)[r];
+    const float2 po = *reinterpret_cast<const float2*>(
+        reinterpret_cast<const float*>(rw) + r * HY_HEAD_DIM + d);
+    const float wt = ex2_ftz(ml.x - M);
+    L = fmaf(wt, ml.y, L);
+    a0 = fmaf(wt, po.x, a0);
+    a1 = fmaf(wt, po.y, a1);
+  }
+  const float inv = 1.f / L;
+  *reinterpret_cast<uint32_t*>(a.out + ((size_t)tok * a.q_heads + g * HY_GROUP + r) * HY_HEAD_DIM +
+                               d) = pack_bf16(a0 * inv, a1 * inv);
   return true;
 }
 
@@ -878,6 +994,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   hy_grid_trigger();
   const uint64_t keep = l2_keep_policy();
   const int n_pre = ld_keep(v.header, keep), n_dec = ld_keep(v.header + 1, keep);
+  const int n_pairs = ld_keep(v.header + 4, keep);    // per-CTA decode when > 0
   const bool use_tmem = (int)blockIdx.x < n_pre;      // the first n_pre CTAs take prefill items
   uint32_t dec_phase = 0, tile_ctr = 0;
   bool ok = true;
@@ -901,7 +1018,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   // SM (an SM's TMA unit takes a 2 KB box about every 100 cycles).
   const int lane = threadIdx.x & 31;
   const int nw = (int)gridDim.x * ATT_WARPS;
-  if (n_pre == 0 && n_dec <= nw) {
+  if (n_pairs > 0) {                            // one (sequence, KV head) pair per CTA
+    if (warp < ATT_WARPS && (int)blockIdx.x < n_pairs)
+      ok = decode_pair_cta(&kv_tiles, a, v, blockIdx.x, payload, sh.dec_bar, dec_phase);
+  } else if (n_pre == 0 && n_dec <= nw) {
     const int item = warp * (int)gridDim.x + (int)blockIdx.x;
     if (warp < ATT_WARPS && item < n_dec && ok)
       ok = decode_item(&kv_tiles, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],

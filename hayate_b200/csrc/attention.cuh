@@ -26,7 +26,8 @@ struct PlanDims {
 
 // Device view of a workspace (see attention.cu for the layout).
 struct PlanView {
-  int* header;        // n_pre, n_dec, split, status
+  int* header;        // n_pre, n_dec, split, status, (sequence, KV head) pairs of a
+                      // per-CTA decode step (0: decode items split over all warps)
   int4* pre;          // prefill items by sequence (plan scratch)
   int4* pre_sorted;   // the same items, most key tiles first (what the kernel runs)
   int4* dec;          // per decode item: (seq, kv head, first block, end block), then

@@ -301,6 +301,15 @@ CASES = {
     "prefill_long_prior": ([128, 1], [8320, 300]),
     "prefill_longer_prior": ([64, 1], [16448, 100]),
     "prefill_ragged_prior": ([100, 37, 1], [5100, 37, 2000]),
+    # decode only, 18 x 8 (sequence, KV head) pairs <= 148 CTAs and contexts of at
+    # most 128 blocks: one pair per CTA, partials merged in shared memory
+    "decode_per_cta": ([1] * 18, [1, 16, 17, 33, 100, 128, 129, 500, 777, 1000, 1023, 1024,
+                                  1025, 1500, 2000, 2047, 2048, 64]),
+    # 19 x 8 pairs > 148: the split-K path with its workspace merge
+    "decode_per_cta_over": ([1] * 19, [1, 16, 17, 33, 100, 128, 129, 500, 777, 1000, 1023, 1024,
+                                       1025, 1500, 2000, 2047, 2048, 64, 3]),
+    # a context past 128 blocks: the split-K path as well
+    "decode_per_cta_long": ([1] * 3, [2049, 30, 700]),
 }
 
 
