@@ -184,6 +184,9 @@ class Engine:
         self.steps = 0
         self.graph_steps = 0
         self.prompt_tokens_computed = 0     # prompt tokens that went through the model
+        # when a list: one (num_seqs, num_tokens, num_sampled, decode_only, key
+        # tokens) record per launched step, for profiling
+        self.step_log: Optional[list] = None
 
     @staticmethod
     def _load_tokenizer(model_name):
@@ -357,6 +360,9 @@ class Engine:
             self.runner.launch_step(S, T, ns, sampler=self._sampler)
             n_read = ns
         self.steps += 1
+        if self.step_log is not None:
+            self.step_log.append((S, T, ns, plan.decode_only,
+                                  sum(e.start + e.q_len for e in plan.entries)))
         self._out_host[buf][:1 + n_read].copy_(self.runner.out_buf[:1 + n_read],
                                                 non_blocking=True)
         self.d2h_bytes += 4 * (1 + n_read)

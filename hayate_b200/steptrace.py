@@ -78,6 +78,36 @@ def report(ev, title, per):
               f"{dur[lab] / cnt[lab]:8.2f} us duration")
 
 
+def attention_by_step(events, log, cfg):
+    """Attention launches grouped by engine step (in launch order; a step whose
+    sequences sample nothing skips the last layer's): time and the KV bytes of
+    decode-only steps (every key of every sequence read once per layer)."""
+    att = [(s, t) for n, s, t in events if "attn_main" in n]
+    L = cfg.num_layers
+    kv_token_layer = 2 * cfg.num_kv_heads * cfg.head_dim * 2        # K and V, bf16
+    k = 0
+    dec_us = dec_bytes = mix_us = 0.0
+    n_dec = n_mix = 0
+    for S, T, ns, decode_only, keys in log:
+        n = L if ns > 0 else L - 1
+        us = sum(t - s for s, t in att[k:k + n])
+        k += n
+        if decode_only:
+            dec_us += us
+            dec_bytes += keys * kv_token_layer * n
+            n_dec += 1
+        else:
+            mix_us += us
+            n_mix += 1
+    if k != len(att):
+        print(f"(attention launches {len(att)} != {k} expected from the step log)")
+    if n_dec:
+        print(f"decode-only steps: {n_dec}, attention {dec_us / 1e3:.1f} ms for "
+              f"{dec_bytes / 1e9:.1f} GB of K/V = {dec_bytes / (dec_us * 1e-6) / 1e9:.0f} GB/s")
+    if n_mix:
+        print(f"steps with prefill chunks: {n_mix}, attention {mix_us / 1e3:.1f} ms")
+
+
 def _cuda_events(prof):
     return sorted(((e.name, e.time_range.start, e.time_range.end) for e in prof.events()
                    if e.device_type == torch.autograd.DeviceType.CUDA), key=lambda x: x[1])
@@ -105,11 +135,14 @@ def main():
         eng.generate_text(prompts, max_tokens=256)          # warm-up run
         torch.cuda.synchronize()
         s0 = eng.steps
+        eng.step_log = []
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
             eng.generate_text(prompts, max_tokens=256)
             torch.cuda.synchronize()
-        report(_cuda_events(prof), f"one run of {len(share)} requests, {eng.steps - s0} engine "
+        ev = _cuda_events(prof)
+        report(ev, f"one run of {len(share)} requests, {eng.steps - s0} engine "
                f"steps ({eng.graph_steps} graph-replayed in all runs)", 1)
+        attention_by_step(ev, eng.step_log, eng.cfg)
         return
     ecfg = EngineConfig(max_num_seqs=16, max_batched_tokens=8192, prefill_chunk=512,
                         num_kv_blocks=1024, max_model_len=1024, cuda_graphs=True,
