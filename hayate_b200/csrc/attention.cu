@@ -98,9 +98,13 @@ static_assert(MERGE_O_BYTES + MERGE_ML_BYTES + MERGE_CHUNK * HY_GROUP * 4 <= DEC
               "merge staging must fit a decode warp's ring");
 constexpr float NEG_INF = -INFINITY;
 #ifndef HY_EXP2_POLY_EVERY
-#define HY_EXP2_POLY_EVERY 4
+#define HY_EXP2_POLY_EVERY 0
 #endif
-// prefill softmax: 1 in EXP2_POLY_EVERY pairs of weights by exp2_poly (0: none)
+// prefill softmax: 1 in EXP2_POLY_EVERY pairs of weights by exp2_poly (0: none).
+// Off: with the row max and sum as independent chains the exp2 unit is not
+// the limit, and the polynomial's extra instructions cost issue slots (4
+// prefill chunks of 512 / 16 chunks: 94.8 / 339.5 us with none, 98.1 / 352.3
+// with 1 in 8, 103.7 / 371.5 with 1 in 4, 112.3 / 403.7 with 1 in 2).
 constexpr int EXP2_POLY_EVERY = HY_EXP2_POLY_EVERY;
 // Lazy rescaling: the running max is only raised when a new score exceeds it
 // by more than 2^RESCALE_LOG2; until then probabilities may exceed 1 by up to
