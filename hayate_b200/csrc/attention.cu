@@ -41,10 +41,9 @@ namespace {
 #define HY_DEC_STAGES 3
 #endif
 constexpr int ATT_WARPS = HY_ATT_WARPS;                          // 8 decode / softmax warps
-constexpr int TC_S_WARP = ATT_WARPS;                             // prefill: S = Q K^T issue (leader)
-constexpr int TC_PV_WARP = ATT_WARPS + 2;                        // prefill: O += P V issue (leader)
-constexpr int TC_SOFTMAX_WARPS = 4;                              // prefill: warps 0-3, a row each
-constexpr int TC_LOAD_WARP0 = 4;                                 // prefill: warps 4-7 load K and V
+constexpr int TC_MMA_WARP = ATT_WARPS;                           // prefill: tcgen05 issue (leader)
+constexpr int TC_KLOAD_WARP = ATT_WARPS + 1;                     // prefill: K half-tiles by TMA
+constexpr int TC_VLOAD_WARP = ATT_WARPS + 2;                     // prefill: V half-tiles by TMA
 constexpr int ATT_THREADS = (ATT_WARPS + 3) * 32;                // 352
 constexpr int DEC_STAGES = HY_DEC_STAGES;                        // TMA ring per decode warp
 constexpr int DEC_TILE_BYTES = 2 * HY_BLOCK * HY_HEAD_DIM * 2;   // K+V of one block: 8 KB
@@ -123,18 +122,20 @@ struct Shared {
   // MMA issuers wait there); the others in both CTAs (the leader's commits
   // arrive on both).  Ring barriers complete once per use of their slot, the
   // buffer ones once per use of their S buffer (every second key tile).
-  uint64_t tc_kfull[TC_NS];  // leader: both CTAs' K halves landed (2 loader arrivals + bytes)
+  uint64_t tc_kfull[TC_NS];  // leader: both CTAs' K halves landed (its loader's arrival + bytes)
   uint64_t tc_vfull[TC_NS];  // leader: both CTAs' V halves landed
   uint64_t tc_kfree[TC_NS];  // the S MMAs that read the K slot are done
   uint64_t tc_vfree[TC_NS];  // the PV MMAs that read the V slot are done
   uint64_t tc_sfull[2];      // S[b] = Q K^T complete
-  uint64_t tc_pfull[2];      // leader: P[b] written by the 4 softmax warps of both CTAs
+  uint64_t tc_pfull[2];      // leader: P[b] written by the 8 softmax warps of both CTAs
   uint64_t tc_odone[2];      // O += P[b] V complete
   uint64_t tc_drain[2];      // error path: all MMAs an issuing thread issued are complete
   uint32_t tmem_base;        // TMEM columns from tcgen05.alloc
   int pre_item;              // prefill item handed to this pair (the leader writes both)
   int pair_bad;              // leader: a wait of the pair's last item ran out
   int peer_bad;              // leader: written by the peer
+  float xrow[3][2][128];     // softmax: partial row max by key-tile parity ([0], [1]) and
+                             // partial row sum ([2]), by column half
 };
 
 HY_DEVICE uint8_t* payload_base(uint8_t* dyn) {
@@ -697,28 +698,27 @@ __device__ bool decode_pair_cta(const CUtensorMap* tiles, const MainArgs& a, con
 // ------------------------------------------------------------------ prefill item
 // tcgen05 on a CTA pair, warp-specialised (all warps of both CTAs call this
 // for the same item):
-//   warps 0-3        softmax: thread = row = TMEM lane, so a row's max and sum
-//                    stay in one thread.  Per key tile: S[b] from TMEM (two
-//                    passes of 4 x 32 columns: the row max, then the weights),
-//                    causal mask, online softmax with lazy rescaling of O, P[b]
-//                    (bf16 pairs) written over S[b] 16 columns at a time;
-//   warps 4-7        load this CTA's half of K_t (warps 4, 5: two blocks each,
-//                    both 64-column halves) and of V_t (warps 6, 7: four blocks
-//                    each, this CTA's 64 columns) into ring slot c % TC_NS, the
-//                    bytes counted on the leader's full barrier;
-//   warp 8, lane 0   (leader) issues S(t) = Q K_t^T into buffer b = t % 2 once
-//                    both K halves landed and PV(t-2), the last reader of P[b],
-//                    is done;
-//   warp 10, lane 0  (leader) issues O += P(t) V_t once both V halves landed and
-//                    both CTAs' softmax wrote P(t).
-// Each issue is followed by tcgen05.commit to the barriers its consumers wait
-// on, in both CTAs.  With two S buffers S(t+1) runs while the softmax works on
-// S(t).  c = c0 + t counts key tiles over the pair's items of the launch (the
-// same in both CTAs); each barrier completes once per use of its slot or
-// buffer, and no role can run a full phase ahead of the role that waits on it,
-// so a wait is always on the current or the previous phase.  Returns false if a
-// wait ran out; the roles drain their own asynchronous work, and the pair
-// stops taking items.
+//   warps 0-7        softmax: warps w and w + 4 share rows 32 (w % 4).. (TMEM
+//                    lane = row) and split the key tile's 128 columns in
+//                    halves; per key tile: S[b] half from TMEM, causal mask,
+//                    the row max completed with the partner's through shared
+//                    memory, online softmax with lazy rescaling of this warp's
+//                    64 O columns, P[b] (bf16 pairs) over S[b];
+//   warp 8, lane 0   (leader) issues S(t) = Q K_t^T into buffer b = t % 2, then
+//                    O += P(t-1) V_{t-1}, each followed by tcgen05.commit to the
+//                    barriers its consumers wait on, in both CTAs;
+//   warp 9 / 10      load this CTA's half of K_t (its 64 keys, both 64-column
+//                    halves) / of V_t (its 64 columns of all 128 keys) into ring
+//                    slot c % TC_NS, the bytes counted on the leader's barrier.
+// S(t) overwrites buffer b after PV(t-2), the last reader of P[b], because one
+// thread issues both in that order and tcgen05.mma operations of a thread
+// execute in issue order (as the K-step accumulation into one D relies on).
+// With two S buffers S(t+1) runs while the softmax works on S(t).  c = c0 + t
+// counts key tiles over the pair's items of the launch (the same in both CTAs);
+// each barrier completes once per use of its slot or buffer, and no role can
+// run a full phase ahead of the role that waits on it, so a wait is always on
+// the current or the previous phase.  Returns false if a wait ran out; the
+// roles drain their own asynchronous work, and the pair stops taking items.
 __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
                                   int item, uint8_t* payload, Shared& sh, uint32_t tmem,
                                   uint32_t rank, uint32_t& ctr) {
@@ -754,10 +754,10 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
   }
   cluster_sync();                               // both CTAs' Q rows are in place
 
-  if (warp >= TC_LOAD_WARP0 && warp < TC_LOAD_WARP0 + 4) {
-    // loader lw: lw 0, 1 = K blocks 4 rank + 2 lw, +1 of the tile (keys of this
-    // CTA's half), lw 2, 3 = V blocks 4 (lw - 2) .. +3 (this CTA's columns)
-    const int lw = warp - TC_LOAD_WARP0, kv = lw >> 1;
+  if (warp == TC_KLOAD_WARP || warp == TC_VLOAD_WARP) {
+    // K: blocks 4 rank .. 4 rank + 3 of the tile, both 64-column halves;
+    // V: blocks 0 .. 7 of the tile, this CTA's 64 columns
+    const int kv = warp == TC_VLOAD_WARP;
     const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
     const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
     int issued = 0;
@@ -767,33 +767,25 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
         ok = mbar_wait(kv ? &sh.tc_vfree[slot] : &sh.tc_kfree[slot], (use & 1) ^ 1, a.err);
         if (!ok) break;
         uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
-        if (rank == 0) mbar_arrive_expect_tx(full, 2 * 4 * 2048);   // this warp's and the peer's
+        if (rank == 0) mbar_arrive_expect_tx(full, 2 * TC_KV_BYTES);   // this CTA's and the peer's
         const uint32_t lbar = smem_in_cta(smem_u32(full), 0);
-        const int nb = kv ? 4 : 2;
-        int ids[4];
+        int ids[8];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int b = 8 * t + (kv ? 4 * (lw - 2) + k : 4 * (int)rank + 2 * lw + k);
-          ids[k] = (k < nb && b < nblk && b < a.bt_pitch) ? bt[b] : -1;
+        for (int k = 0; k < 8; ++k) {
+          const int b = kv ? 8 * t + k : 8 * t + 4 * (int)rank + (k >> 1);
+          ids[k] = ((kv || (k & 1) == 0) && b < nblk && b < a.bt_pitch) ? bt[b] : -1;
         }
+        uint8_t* sl = payload + (kv ? TC_V_OFF : TC_K_OFF) + slot * TC_KV_BYTES;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          if (k >= nb) break;
-          const int id = ids[k];
-          if (kv) {                             // V block 4 (lw - 2) + k, this CTA's 64 columns
-            int r = a.oob_row;                  // past the end: zero fill
-            if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
-            else if (id >= 0) r = kv_row(a, id, 1, g);
-            tma_load_2d_pair(payload + TC_V_OFF + slot * TC_KV_BYTES + (4 * (lw - 2) + k) * 2048,
-                             map, 64 * (int)rank, r, lbar);
-          } else {                              // K block 2 lw + k of this CTA's half, both halves
-            int r = a.oob_row;
-            if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
-            else if (id >= 0) r = kv_row(a, id, 0, g);
-            uint8_t* dst = payload + TC_K_OFF + slot * TC_KV_BYTES + (2 * lw + k) * 2048;
-            tma_load_2d_pair(dst, map, 0, r, lbar);
-            tma_load_2d_pair(dst + TC_HALF, map, 64, r, lbar);
-          }
+        for (int k = 0; k < 8; ++k) {
+          const int id = kv ? ids[k] : ids[k & ~1];
+          int r = a.oob_row;                    // past the end: zero fill
+          if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
+          else if (id >= 0) r = kv_row(a, id, kv, g);
+          if (kv)                               // V block k, this CTA's 64 columns
+            tma_load_2d_pair(sl + k * 2048, map, 64 * (int)rank, r, lbar);
+          else                                  // K block k / 2, column half k % 2
+            tma_load_2d_pair(sl + (k & 1) * TC_HALF + (k >> 1) * 2048, map, 64 * (k & 1), r, lbar);
         }
         issued = t + 1;
       }
@@ -806,16 +798,15 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
       }
     }
     __syncwarp();
-  } else if (rank == 0 && (warp == TC_S_WARP || warp == TC_PV_WARP)) {
-    if (lane == 0) {
-      const bool is_s = warp == TC_S_WARP;
-      if (is_s) {
-        constexpr uint32_t ID_S = tc_idesc_bf16(256, TC_KEYS, false);
-        const uint64_t dQ = tc_desc_sw128(sbase, 16, 1024);
-        for (int t = 0; t < ntiles && ok; ++t) {  // S(t) = Q K_t^T into buffer c % 2
+  } else if (warp == TC_MMA_WARP) {
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t ID_S = tc_idesc_bf16(256, TC_KEYS, false);
+      constexpr uint32_t ID_O = tc_idesc_bf16(256, HY_HEAD_DIM, true);
+      const uint64_t dQ = tc_desc_sw128(sbase, 16, 1024);
+      for (int t = 0; t <= ntiles && ok; ++t) {
+        if (t < ntiles) {                       // S(t) = Q K_t^T into buffer c % 2
           const uint32_t c = c0 + t, slot = c % TC_NS, b = c & 1;
-          ok = mbar_wait(&sh.tc_kfull[slot], (c / TC_NS) & 1, a.err) &&
-               mbar_wait(&sh.tc_odone[b], ((c >> 1) & 1) ^ 1, a.err);   // PV(c-2) read P[b]
+          ok = mbar_wait(&sh.tc_kfull[slot], (c / TC_NS) & 1, a.err);
           if (!ok) break;
           tc_fence_after();
           const uint64_t dK = tc_desc_sw128(sbase + TC_K_OFF + slot * TC_KV_BYTES, 16, 1024);
@@ -828,10 +819,8 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
           pair_commit_both(&sh.tc_sfull[b]);
           pair_commit_both(&sh.tc_kfree[slot]);
         }
-      } else {
-        constexpr uint32_t ID_O = tc_idesc_bf16(256, HY_HEAD_DIM, true);
-        for (int t = 0; t < ntiles && ok; ++t) {  // O += P(t) V_t
-          const uint32_t c = c0 + t, slot = c % TC_NS, b = c & 1;
+        if (t > 0) {                            // O += P(t-1) V_{t-1}
+          const uint32_t c = c0 + t - 1, slot = c % TC_NS, b = c & 1;
           ok = mbar_wait(&sh.tc_vfull[slot], (c / TC_NS) & 1, a.err) &&
                mbar_wait(&sh.tc_pfull[b], (c >> 1) & 1, a.err);
           if (!ok) break;
@@ -841,58 +830,65 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
 #pragma unroll
           for (int kk = 0; kk < TC_KEYS / 16; ++kk)
             pair_mma_bf16_ta(tmem + TM_O, tmem + tm_s(b) + 8 * kk,
-                             dV + (uint64_t)((kk * 2048) >> 4), ID_O, (t > 0 || kk > 0));
+                             dV + (uint64_t)((kk * 2048) >> 4), ID_O, (t > 1 || kk > 0));
           pair_commit_both(&sh.tc_odone[b]);
           pair_commit_both(&sh.tc_vfree[slot]);
         }
       }
       if (!ok) {                                // let every issued MMA finish
-        const int d = is_s ? 0 : 1;
-        pair_commit_local(&sh.tc_drain[d]);
-        mbar_wait(&sh.tc_drain[d], 0, nullptr);
+        pair_commit_local(&sh.tc_drain[0]);
+        mbar_wait(&sh.tc_drain[0], 0, nullptr);
       }
     }
     __syncwarp();
-  } else if (warp < TC_SOFTMAX_WARPS) {         // softmax: one row per thread
-    const int r = warp * 32 + lane, j = r & 63;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const uint32_t tO = tmem + lane_base + TM_O;
+  } else if (warp < ATT_WARPS) {                // softmax: row (w % 4) * 32 + lane, column half w / 4
+    const int q = warp & 3, hf = warp >> 2;
+    const int r = q * 32 + lane, j = r & 63;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const uint32_t tO = tmem + lane_base + TM_O + 64 * hf;        // this warp's 64 O columns
     const int lim = prefix + t0 + j;            // last key row r may see
     const float sl2 = a.scale_log2;
     const uint32_t pfull0 = smem_in_cta(smem_u32(&sh.tc_pfull[0]), 0);
     const uint32_t pfull1 = smem_in_cta(smem_u32(&sh.tc_pfull[1]), 0);
-    float m = NEG_INF, l = 0.f;                 // m in scaled log2 units
-    for (int t = 0; t < ntiles && ok; ++t) {
+    float m = NEG_INF, l = 0.f;                 // m in scaled log2 units; l: this half's sum
+    // The partner warps w and w + 4 meet once per key tile at named barrier
+    // 1 + w % 4 and once in the epilogue; every decision to stop is taken from
+    // the barrier's combined flag, so both always run the same barriers.
+    for (int t = 0; t < ntiles; ++t) {
       const uint32_t c = c0 + t, b = c & 1;
-      const uint32_t tS = tmem + lane_base + tm_s(b);
+      const uint32_t tS = tmem + lane_base + tm_s(b) + 64 * hf;
       // waits are made warp-uniform: tcgen05.ld/st below are warp-collective
-      ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_sfull[b], (c >> 1) & 1, a.err));
-      if (!ok) break;
-      tc_fence_after();
-      const int kb = t * TC_KEYS;
-      const bool edge = kb + TC_KEYS - 1 > prefix + t0;   // the tile reaches the diagonal or the end
-      // pass 1: the row maximum over the tile's 128 scores
-      float mxs[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mxs[k] = NEG_INF;
-#pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        float s[32];
-        tmem_ld32(tS + 32 * ch, s);
+      const bool w_ok =
+          ok && __all_sync(0xffffffffu, mbar_wait(&sh.tc_sfull[b], (c >> 1) & 1, a.err));
+      float s[64];
+      float mx = NEG_INF;
+      if (w_ok) {
+        tc_fence_after();
+        tmem_ld32(tS, *reinterpret_cast<float(*)[32]>(&s[0]));
+        tmem_ld32(tS + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
         tmem_wait_ld();
-        if (edge) {
+        const int kb = t * TC_KEYS + 64 * hf;
+        if (kb + 63 > prefix + t0) {            // the half reaches the diagonal or the end
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int key = kb + 32 * ch + i;
-            if (key > lim || key >= kv_len) s[i] = NEG_INF;
-          }
+          for (int i = 0; i < 64; ++i)
+            if (kb + i > lim || kb + i >= kv_len) s[i] = NEG_INF;
         }
+        float mxs[8];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mxs[i & 7] = fmaxf(mxs[i & 7], s[i]);
+        for (int k = 0; k < 8; ++k) mxs[k] = s[k];
+#pragma unroll
+        for (int i = 8; i < 64; i += 8)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) mxs[k] = fmaxf(mxs[k], s[i + k]);
+        mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                   fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
       }
-      float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                       fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
-      mx *= sl2;
+      // the row max over both halves: exchange with the partner warp (slots by
+      // tile parity, so a write of tile t+1 cannot meet a read of tile t); past
+      // this barrier both warps have read their S columns, so P may overwrite them
+      sh.xrow[b][hf][r] = mx;
+      if (named_sync_or(1 + q, 64, !w_ok)) { ok = false; break; }
+      mx = fmaxf(mx, sh.xrow[b][hf ^ 1][r]) * sl2;
       const bool grow = mx > m + RESCALE_LOG2;
       if (__any_sync(0xffffffffu, grow)) {
         const float mnew = grow ? mx : m;
@@ -904,7 +900,7 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
           ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_odone[cp & 1], (cp >> 1) & 1, a.err));
           tc_fence_after();
 #pragma unroll 1
-          for (int cc = 0; cc < 4; ++cc) {
+          for (int cc = 0; cc < 2 && ok; ++cc) {
             float o[32];
             tmem_ld32(tO + 32 * cc, o);
             tmem_wait_ld();
@@ -915,42 +911,32 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
           tmem_wait_st();
         }
       }
-      // pass 2: weights, row sum, P over the columns already read
       const float mneg = (m == NEG_INF) ? 0.f : -m;
+      uint32_t pk[32];
       float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        float s[32];
-        tmem_ld32(tS + 32 * ch, s);
-        tmem_wait_ld();
-        if (edge) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int key = kb + 32 * ch + i;
-            if (key > lim || key >= kv_len) s[i] = NEG_INF;
-          }
-        }
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const bool poly = EXP2_POLY_EVERY > 0 && (i % EXP2_POLY_EVERY) == EXP2_POLY_EVERY - 1;
-          const float x0 = fmaf(s[2 * i], sl2, mneg), x1 = fmaf(s[2 * i + 1], sl2, mneg);
-          const float p0 = poly ? exp2_poly(x0) : ex2_ftz(x0);
-          const float p1 = poly ? exp2_poly(x1) : ex2_ftz(x1);
-          ls[(2 * i) & 7] += p0;
-          ls[(2 * i + 1) & 7] += p1;
-          pk[i] = pack_bf16(p0, p1);
-        }
-        // P columns 16 ch .. 16 ch + 15 lie in S columns this pass has read
-        tmem_st16u(tS + 16 * ch, pk);
+      for (int i = 0; i < 32; ++i) {
+        const bool poly = EXP2_POLY_EVERY > 0 && (i % EXP2_POLY_EVERY) == EXP2_POLY_EVERY - 1;
+        const float x0 = fmaf(s[2 * i], sl2, mneg), x1 = fmaf(s[2 * i + 1], sl2, mneg);
+        const float p0 = poly ? exp2_poly(x0) : ex2_ftz(x0);
+        const float p1 = poly ? exp2_poly(x1) : ex2_ftz(x1);
+        ls[(2 * i) & 7] += p0;
+        ls[(2 * i + 1) & 7] += p1;
+        pk[i] = pack_bf16(p0, p1);
       }
       l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+      // P columns 32 hf .. 32 hf + 31 of buffer b (keys 64 hf .. 64 hf + 63)
+      tmem_st32u(tmem + lane_base + tm_s(b) + 32 * hf, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(b ? pfull1 : pfull0);
     }
-    if (ok) {                                   // epilogue: O / l -> out
+    // epilogue: the row sum over both halves, then this warp's 64 columns of O / l
+    sh.xrow[2][hf][r] = l;
+    if (named_sync_or(1 + q, 64, !ok)) ok = false;
+    l += sh.xrow[2][hf ^ 1][r];
+    if (ok) {
       const uint32_t c = c0 + ntiles - 1;
       ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_odone[c & 1], (c >> 1) & 1, a.err));
       tc_fence_after();
@@ -958,9 +944,9 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
       const bool store = ok && j < nrows;
       const float inv = 1.f / l;
       __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP +
-                                   2 * (int)rank + (r >> 6)) * HY_HEAD_DIM;
+                                   2 * (int)rank + (r >> 6)) * HY_HEAD_DIM + 64 * hf;
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
+      for (int cc = 0; cc < 2; ++cc) {
         float o[32];
         tmem_ld32(tO + 32 * cc, o);
         tmem_wait_ld();
@@ -1001,14 +987,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     for (int w = 0; w < ATT_WARPS; ++w)
       for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&sh.dec_bar[w][s], 1);
     for (int s = 0; s < TC_NS; ++s) {
-      mbar_init(&sh.tc_kfull[s], 2);            // the leader's two K loader warps
-      mbar_init(&sh.tc_vfull[s], 2);
+      mbar_init(&sh.tc_kfull[s], 1);            // the leader's K loader
+      mbar_init(&sh.tc_vfull[s], 1);
       mbar_init(&sh.tc_kfree[s], 1);
       mbar_init(&sh.tc_vfree[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sh.tc_sfull[b], 1);
-      mbar_init(&sh.tc_pfull[b], 2 * TC_SOFTMAX_WARPS);   // softmax warps of both CTAs
+      mbar_init(&sh.tc_pfull[b], 2 * ATT_WARPS);          // softmax warps of both CTAs
       mbar_init(&sh.tc_odone[b], 1);
     }
     mbar_init(&sh.tc_drain[0], 1);
