@@ -415,9 +415,13 @@ HY_DEVICE uint32_t smem_in_cta(uint32_t smem_addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
   return r;
 }
+// Arrive on a barrier of another CTA of the cluster, with the default (CTA-scope)
+// release: what the waiter reads through this barrier is TMEM written by
+// tcgen05.st, ordered by tcgen05.fence::before_thread_sync on this side and
+// ::after_thread_sync on the waiter's, so no cluster-scope fence is needed
+// (one per key tile measured as the kernel's largest stall).
 HY_DEVICE void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
 }
 HY_DEVICE void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" :: "r"(cluster_addr), "r"(v) : "memory");
