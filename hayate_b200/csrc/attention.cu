@@ -760,41 +760,57 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
     const int kv = warp == TC_VLOAD_WARP;
     const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
     const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
+    // block ids 32 at a time (4 key tiles), lane i holding block 32 n + i, the
+    // next batch requested one batch ahead so no tile waits on the table
+    auto batch = [&](int n) {
+      const int bb = 32 * n + lane;
+      return (bb < nblk && bb < a.bt_pitch) ? bt[bb] : -1;
+    };
+    int ids = batch(0), ids_next = batch(1);
     int issued = 0;
-    if (lane == 0) {
-      for (int t = 0; t < ntiles && ok; ++t) {
-        const uint32_t c = c0 + t, slot = c % TC_NS, use = c / TC_NS;
-        ok = mbar_wait(kv ? &sh.tc_vfree[slot] : &sh.tc_kfree[slot], (use & 1) ^ 1, a.err);
-        if (!ok) break;
-        uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
-        if (rank == 0) mbar_arrive_expect_tx(full, 2 * TC_KV_BYTES);   // this CTA's and the peer's
-        const uint32_t lbar = smem_in_cta(smem_u32(full), 0);
-        int ids[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int b = kv ? 8 * t + k : 8 * t + 4 * (int)rank + (k >> 1);
-          ids[k] = ((kv || (k & 1) == 0) && b < nblk && b < a.bt_pitch) ? bt[b] : -1;
-        }
-        uint8_t* sl = payload + (kv ? TC_V_OFF : TC_K_OFF) + slot * TC_KV_BYTES;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int id = kv ? ids[k] : ids[k & ~1];
-          int r = a.oob_row;                    // past the end: zero fill
-          if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
-          else if (id >= 0) r = kv_row(a, id, kv, g);
-          if (kv)                               // V block k, this CTA's 64 columns
-            tma_load_2d_pair(sl + k * 2048, map, 64 * (int)rank, r, lbar);
-          else                                  // K block k / 2, column half k % 2
-            tma_load_2d_pair(sl + (k & 1) * TC_HALF + (k >> 1) * 2048, map, 64 * (k & 1), r, lbar);
-        }
-        issued = t + 1;
+    for (int t = 0; t < ntiles && ok; ++t) {
+      if (t > 0 && (t & 3) == 0) {
+        ids = ids_next;
+        ids_next = batch((t >> 2) + 1);
       }
-      if (!ok && rank == 0) {                   // loads still in flight must land first
-        for (int t = max(0, issued - TC_NS); t < issued; ++t) {
-          const uint32_t c = c0 + t;
-          mbar_wait(kv ? &sh.tc_vfull[c % TC_NS] : &sh.tc_kfull[c % TC_NS], (c / TC_NS) & 1,
-                    nullptr);
+      const uint32_t c = c0 + t, slot = c % TC_NS, use = c / TC_NS;
+      // this tile's 8 block ids (V: blocks 8t .. 8t+7; K: this CTA's 4)
+      int id8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int src = 8 * (t & 3) + (kv ? k : 4 * (int)rank + (k >> 1));
+        id8[k] = __shfl_sync(0xffffffffu, ids, src);
+      }
+      bool w_ok = true;
+      if (lane == 0) {
+        w_ok = mbar_wait(kv ? &sh.tc_vfree[slot] : &sh.tc_kfree[slot], (use & 1) ^ 1, a.err);
+        if (w_ok) {
+          uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
+          if (rank == 0) mbar_arrive_expect_tx(full, 2 * TC_KV_BYTES);   // this CTA's and the peer's
+          const uint32_t lbar = smem_in_cta(smem_u32(full), 0);
+          uint8_t* sl = payload + (kv ? TC_V_OFF : TC_K_OFF) + slot * TC_KV_BYTES;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int id = id8[k];
+            int r = a.oob_row;                  // past the end: zero fill
+            if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
+            else if (id >= 0) r = kv_row(a, id, kv, g);
+            if (kv)                             // V block k, this CTA's 64 columns
+              tma_load_2d_pair(sl + k * 2048, map, 64 * (int)rank, r, lbar);
+            else                                // K block k / 2, column half k % 2
+              tma_load_2d_pair(sl + (k & 1) * TC_HALF + (k >> 1) * 2048, map, 64 * (k & 1), r,
+                               lbar);
+          }
         }
+      }
+      ok = __shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0) != 0;
+      if (ok) issued = t + 1;
+    }
+    if (!ok && rank == 0 && lane == 0) {        // loads still in flight must land first
+      for (int t = max(0, issued - TC_NS); t < issued; ++t) {
+        const uint32_t c = c0 + t;
+        mbar_wait(kv ? &sh.tc_vfull[c % TC_NS] : &sh.tc_kfull[c % TC_NS], (c / TC_NS) & 1,
+                  nullptr);
       }
     }
     __syncwarp();
