@@ -42,9 +42,9 @@ namespace {
 #endif
 constexpr int ATT_WARPS = HY_ATT_WARPS;                          // 8 decode / softmax warps
 constexpr int TC_MMA_WARP = ATT_WARPS;                           // prefill: tcgen05 issue (leader)
-constexpr int TC_KLOAD_WARP = ATT_WARPS + 1;                     // prefill: K half-tiles by TMA
-constexpr int TC_VLOAD_WARP = ATT_WARPS + 2;                     // prefill: V half-tiles by TMA
-constexpr int ATT_THREADS = (ATT_WARPS + 3) * 32;                // 352
+constexpr int TC_LOAD_WARP0 = ATT_WARPS + 1;                     // prefill: 4 TMA loader warps
+constexpr int TC_LOAD_WARPS = 4;
+constexpr int ATT_THREADS = (ATT_WARPS + 1 + TC_LOAD_WARPS) * 32; // 416
 constexpr int DEC_STAGES = HY_DEC_STAGES;                        // TMA ring per decode warp
 constexpr int DEC_TILE_BYTES = 2 * HY_BLOCK * HY_HEAD_DIM * 2;   // K+V of one block: 8 KB
 constexpr int DEC_WARP_BYTES = DEC_STAGES * DEC_TILE_BYTES;      // 24 KB
@@ -122,7 +122,7 @@ struct Shared {
   // MMA issuers wait there); the others in both CTAs (the leader's commits
   // arrive on both).  Ring barriers complete once per use of their slot, the
   // buffer ones once per use of their S buffer (every second key tile).
-  uint64_t tc_kfull[TC_NS];  // leader: both CTAs' K halves landed (its loader's arrival + bytes)
+  uint64_t tc_kfull[TC_NS];  // leader: both CTAs' K halves landed (its 2 loaders' arrivals + bytes)
   uint64_t tc_vfull[TC_NS];  // leader: both CTAs' V halves landed
   uint64_t tc_kfree[TC_NS];  // the S MMAs that read the K slot are done
   uint64_t tc_vfree[TC_NS];  // the PV MMAs that read the V slot are done
@@ -707,9 +707,10 @@ __device__ bool decode_pair_cta(const CUtensorMap* tiles, const MainArgs& a, con
 //   warp 8, lane 0   (leader) issues S(t) = Q K_t^T into buffer b = t % 2, then
 //                    O += P(t-1) V_{t-1}, each followed by tcgen05.commit to the
 //                    barriers its consumers wait on, in both CTAs;
-//   warp 9 / 10      load this CTA's half of K_t (its 64 keys, both 64-column
-//                    halves) / of V_t (its 64 columns of all 128 keys) into ring
-//                    slot c % TC_NS, the bytes counted on the leader's barrier.
+//   warps 9-12       load this CTA's half of K_t (its 64 keys, both 64-column
+//                    halves: warps 9, 10) and of V_t (its 64 columns of all 128
+//                    keys: warps 11, 12) into ring slot c % TC_NS, the bytes
+//                    counted on the leader's barrier.
 // S(t) overwrites buffer b after PV(t-2), the last reader of P[b], because one
 // thread issues both in that order and tcgen05.mma operations of a thread
 // execute in issue order (as the K-step accumulation into one D relies on).
@@ -754,10 +755,12 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
   }
   cluster_sync();                               // both CTAs' Q rows are in place
 
-  if (warp == TC_KLOAD_WARP || warp == TC_VLOAD_WARP) {
-    // K: blocks 4 rank .. 4 rank + 3 of the tile, both 64-column halves;
-    // V: blocks 0 .. 7 of the tile, this CTA's 64 columns
-    const int kv = warp == TC_VLOAD_WARP;
+  if (warp >= TC_LOAD_WARP0 && warp < TC_LOAD_WARP0 + TC_LOAD_WARPS) {
+    // lw 0, 1: K blocks 4 rank + 2 lw, +1 of the tile (this CTA's keys), both
+    // 64-column halves; lw 2, 3: V blocks 4 (lw - 2) .. +3, this CTA's 64 columns.
+    // An SM's TMA unit takes about one box per 90 cycles when several warps
+    // issue; one warp alone is slower, so the tile's 16 boxes are split four ways.
+    const int lw = warp - TC_LOAD_WARP0, kv = lw >> 1;
     const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
     const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
     // block ids 32 at a time (4 key tiles), lane i holding block 32 n + i, the
@@ -774,32 +777,34 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
         ids_next = batch((t >> 2) + 1);
       }
       const uint32_t c = c0 + t, slot = c % TC_NS, use = c / TC_NS;
-      // this tile's 8 block ids (V: blocks 8t .. 8t+7; K: this CTA's 4)
-      int id8[8];
+      // this warp's 4 boxes of the tile: V blocks 4 (lw - 2) + k; K block
+      // 4 rank + 2 lw + k / 2, column half k % 2
+      int id4[4];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int src = 8 * (t & 3) + (kv ? k : 4 * (int)rank + (k >> 1));
-        id8[k] = __shfl_sync(0xffffffffu, ids, src);
+      for (int k = 0; k < 4; ++k) {
+        const int src = 8 * (t & 3) + (kv ? 4 * (lw - 2) + k : 4 * (int)rank + 2 * lw + (k >> 1));
+        id4[k] = __shfl_sync(0xffffffffu, ids, src);
       }
       bool w_ok = true;
       if (lane == 0) {
         w_ok = mbar_wait(kv ? &sh.tc_vfree[slot] : &sh.tc_kfree[slot], (use & 1) ^ 1, a.err);
         if (w_ok) {
           uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
-          if (rank == 0) mbar_arrive_expect_tx(full, 2 * TC_KV_BYTES);   // this CTA's and the peer's
+          // this warp's and the peer's counterpart: 2 x 4 boxes of 2 KB
+          if (rank == 0) mbar_arrive_expect_tx(full, 2 * 4 * 2048);
           const uint32_t lbar = smem_in_cta(smem_u32(full), 0);
           uint8_t* sl = payload + (kv ? TC_V_OFF : TC_K_OFF) + slot * TC_KV_BYTES;
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int id = id8[k];
+          for (int k = 0; k < 4; ++k) {
+            const int id = id4[k];
             int r = a.oob_row;                  // past the end: zero fill
             if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
             else if (id >= 0) r = kv_row(a, id, kv, g);
-            if (kv)                             // V block k, this CTA's 64 columns
-              tma_load_2d_pair(sl + k * 2048, map, 64 * (int)rank, r, lbar);
-            else                                // K block k / 2, column half k % 2
-              tma_load_2d_pair(sl + (k & 1) * TC_HALF + (k >> 1) * 2048, map, 64 * (k & 1), r,
-                               lbar);
+            if (kv)                             // V block 4 (lw - 2) + k, this CTA's 64 columns
+              tma_load_2d_pair(sl + (4 * (lw - 2) + k) * 2048, map, 64 * (int)rank, r, lbar);
+            else                                // K block 2 lw + k / 2 of this CTA's 4, half k % 2
+              tma_load_2d_pair(sl + (k & 1) * TC_HALF + (2 * lw + (k >> 1)) * 2048, map,
+                               64 * (k & 1), r, lbar);
           }
         }
       }
@@ -1003,8 +1008,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     for (int w = 0; w < ATT_WARPS; ++w)
       for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&sh.dec_bar[w][s], 1);
     for (int s = 0; s < TC_NS; ++s) {
-      mbar_init(&sh.tc_kfull[s], 1);            // the leader's K loader
-      mbar_init(&sh.tc_vfull[s], 1);
+      mbar_init(&sh.tc_kfull[s], 2);            // the leader's two K loader warps
+      mbar_init(&sh.tc_vfull[s], 2);
       mbar_init(&sh.tc_kfree[s], 1);
       mbar_init(&sh.tc_vfree[s], 1);
     }
