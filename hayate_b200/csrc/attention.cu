@@ -41,36 +41,33 @@ namespace {
 #define HY_DEC_STAGES 3
 #endif
 constexpr int ATT_WARPS = HY_ATT_WARPS;                          // 8 decode / softmax warps
-constexpr int TC_MMA_WARP = ATT_WARPS;                           // prefill: tcgen05 issue (leader)
-constexpr int TC_LOAD_WARP0 = ATT_WARPS + 1;                     // prefill: 4 TMA loader warps
-constexpr int TC_LOAD_WARPS = 4;
-constexpr int ATT_THREADS = (ATT_WARPS + 1 + TC_LOAD_WARPS) * 32; // 416
+constexpr int TC_MMA_WARP = ATT_WARPS;                           // prefill: tcgen05 issue, tile 0
+constexpr int TC_LOAD_WARP = ATT_WARPS + 1;                      // prefill: TMA issue, blocks 0-1
+constexpr int TC_LOAD_WARP2 = ATT_WARPS + 3;                     // prefill: TMA issue, blocks 2-3
+constexpr int TC_MMA_WARP1 = ATT_WARPS + 2;                      // prefill: tcgen05 issue, tile 1
+constexpr int ATT_THREADS = (ATT_WARPS + 4) * 32;                // 384
 constexpr int DEC_STAGES = HY_DEC_STAGES;                        // TMA ring per decode warp
 constexpr int DEC_TILE_BYTES = 2 * HY_BLOCK * HY_HEAD_DIM * 2;   // K+V of one block: 8 KB
 constexpr int DEC_WARP_BYTES = DEC_STAGES * DEC_TILE_BYTES;      // 24 KB
 constexpr int PRE_QROWS = 64;                                    // query tokens per prefill item
-// tcgen05 prefill on CTA pairs (cluster of two, cta_group::2): a pair runs an
-// item of 4 query heads x 64 tokens = 256 rows as one M = 256 tile; CTA rank r
-// holds rows r*128.. (query heads 4g + 2r, 4g + 2r + 1, row i: head + i / 64,
-// token t0 + i % 64).  Key tiles of 128 keys (8 paged blocks) in rings of
-// TC_NS slots; each CTA loads half of every tile: for S = Q K^T the keys
-// r*64..r*64+63 (the M = 256 MMA takes the B columns half from each CTA), for
-// O += P V the head dimensions r*64..r*64+63 of all 128 keys.
-// K slot of a CTA: [64-column half][64 keys][64] (K-major operand, SW128);
-// V slot: [128 keys][64] (MN-major operand, SW128), block j at j * 2 KB.
-constexpr int TC_KEYS = 128;
+// tcgen05 prefill: sub-tile X (0, 1) = 128 rows r: query head 4g + 2X + r / 64,
+// token t0 + r % 64; KV tiles of 64 keys (4 blocks) in rings of TC_NS slots.
+// A K slot holds the two 64-column halves outermost ([half][64 keys][64], the
+// K-major operand of S = Q K^T); a V slot holds each block's 4 KB tile as one
+// TMA box lands it ([block][half][16 keys][64], the MN-major operand of P V).
+constexpr int TC_KEYS = 64;
 constexpr int TC_NS = 4;                                         // K and V ring slots
-constexpr int TC_KV_BYTES = 64 * HY_HEAD_DIM * 2;               // a CTA's K or V half-tile: 16 KB
-constexpr int TC_HALF = 64 * 128;                                // K slot: one 64-column half, 8 KB
-constexpr int TC_Q_BYTES = 128 * HY_HEAD_DIM * 2;                // Q rows of a CTA: 32 KB
-constexpr int TC_K_OFF = TC_Q_BYTES;                             // K ring
+constexpr int TC_KV_BYTES = TC_KEYS * HY_HEAD_DIM * 2;          // K or V of one tile: 16 KB
+constexpr int TC_HALF = TC_KEYS * 128;                           // one 64-column half: 8 KB
+constexpr int TC_Q_BYTES = 128 * HY_HEAD_DIM * 2;                // Q of one sub-tile: 32 KB
+constexpr int TC_K_OFF = 2 * TC_Q_BYTES;                         // K ring
 constexpr int TC_V_OFF = TC_K_OFF + TC_NS * TC_KV_BYTES;         // V ring
-constexpr int TC_SMEM = TC_V_OFF + TC_NS * TC_KV_BYTES;          // 160 KB
-// TMEM columns of each CTA: two S buffers, S[b] at 128 b (P[b], bf16 pairs,
-// written over its first 64 columns), O at 256.
+constexpr int TC_SMEM = TC_V_OFF + TC_NS * TC_KV_BYTES;          // 192 KB
+// TMEM columns: two S buffers per sub-tile, S_X[b] at 64 (2X + b), P_X[b] (bf16
+// pairs) written over the first 32 columns of S_X[b]; O_X at 256 + 128 X.
 constexpr uint32_t TC_TMEM_COLS = 512;
 constexpr uint32_t TM_O = 256;
-HY_DEVICE uint32_t tm_s(uint32_t b) { return 128u * b; }
+HY_DEVICE uint32_t tm_s(int X, uint32_t b) { return 64u * (2u * X + b); }
 constexpr int SMEM_PAYLOAD = ATT_WARPS * DEC_WARP_BYTES > TC_SMEM ? ATT_WARPS * DEC_WARP_BYTES
                                                                    : TC_SMEM;
 constexpr int SMEM_BYTES = SMEM_PAYLOAD + 1024;                  // + alignment slack
@@ -118,24 +115,18 @@ constexpr float RESCALE_LOG2 = 8.0f;
 
 struct Shared {
   uint64_t dec_bar[ATT_WARPS][DEC_STAGES];
-  // tcgen05 prefill.  The full barriers and pfull live in the pair leader (the
-  // MMA issuers wait there); the others in both CTAs (the leader's commits
-  // arrive on both).  Ring barriers complete once per use of their slot, the
-  // buffer ones once per use of their S buffer (every second key tile).
-  uint64_t tc_kfull[TC_NS];  // leader: both CTAs' K halves landed (its 2 loaders' arrivals + bytes)
-  uint64_t tc_vfull[TC_NS];  // leader: both CTAs' V halves landed
-  uint64_t tc_kfree[TC_NS];  // the S MMAs that read the K slot are done
-  uint64_t tc_vfree[TC_NS];  // the PV MMAs that read the V slot are done
-  uint64_t tc_sfull[2];      // S[b] = Q K^T complete
-  uint64_t tc_pfull[2];      // leader: P[b] written by the 8 softmax warps of both CTAs
-  uint64_t tc_odone[2];      // O += P[b] V complete
-  uint64_t tc_drain[2];      // error path: all MMAs an issuing thread issued are complete
+  // tcgen05 prefill.  Ring barriers complete once per use of their slot, the
+  // per-sub-tile ones once per key tile.
+  uint64_t tc_kfull[TC_NS];  // K tile landed (TMA transaction bytes)
+  uint64_t tc_vfull[TC_NS];  // V tile landed
+  uint64_t tc_kfree[TC_NS];  // both S MMAs that read the K slot are done (2 commits)
+  uint64_t tc_vfree[TC_NS];  // both PV MMAs that read the V slot are done (2 commits)
+  uint64_t tc_sfull[2][2];   // S_X[b] = Q_X K^T complete (once per use of buffer b)
+  uint64_t tc_pfull[2][2];   // P_X[b] written over S_X[b] by the 4 softmax warps of X
+  uint64_t tc_odone[2];      // O_X += P_X V complete (once per key tile)
+  uint64_t tc_drain[2];      // error path: all MMAs an issuing warp issued are complete
   uint32_t tmem_base;        // TMEM columns from tcgen05.alloc
-  int pre_item;              // prefill item handed to this pair (the leader writes both)
-  int pair_bad;              // leader: a wait of the pair's last item ran out
-  int peer_bad;              // leader: written by the peer
-  float xrow[3][2][128];     // softmax: partial row max by key-tile parity ([0], [1]) and
-                             // partial row sum ([2]), by column half
+  int pre_item;              // prefill item handed to this CTA
 };
 
 HY_DEVICE uint8_t* payload_base(uint8_t* dyn) {
@@ -696,33 +687,38 @@ __device__ bool decode_pair_cta(const CUtensorMap* tiles, const MainArgs& a, con
 }
 
 // ------------------------------------------------------------------ prefill item
-// tcgen05 on a CTA pair, warp-specialised (all warps of both CTAs call this
-// for the same item):
-//   warps 0-7        softmax: warps w and w + 4 share rows 32 (w % 4).. (TMEM
-//                    lane = row) and split the key tile's 128 columns in
-//                    halves; per key tile: S[b] half from TMEM, causal mask,
-//                    the row max completed with the partner's through shared
-//                    memory, online softmax with lazy rescaling of this warp's
-//                    64 O columns, P[b] (bf16 pairs) over S[b];
-//   warp 8, lane 0   (leader) issues S(t) = Q K_t^T into buffer b = t % 2, then
-//                    O += P(t-1) V_{t-1}, each followed by tcgen05.commit to the
-//                    barriers its consumers wait on, in both CTAs;
-//   warps 9-12       load this CTA's half of K_t (its 64 keys, both 64-column
-//                    halves: warps 9, 10) and of V_t (its 64 columns of all 128
-//                    keys: warps 11, 12) into ring slot c % TC_NS, the bytes
-//                    counted on the leader's barrier.
-// S(t) overwrites buffer b after PV(t-2), the last reader of P[b], because one
-// thread issues both in that order and tcgen05.mma operations of a thread
-// execute in issue order (as the K-step accumulation into one D relies on).
-// With two S buffers S(t+1) runs while the softmax works on S(t).  c = c0 + t
-// counts key tiles over the pair's items of the launch (the same in both CTAs);
-// each barrier completes once per use of its slot or buffer, and no role can
+// tcgen05, warp-specialised.  Item = (seq, kv head g, 64-token tile t0): two
+// M=128 sub-tiles X of the same tokens (query heads 4g+2X, 4g+2X+1), which see
+// the same keys and masks, so each 64-key K/V tile is loaded once for both.
+//   warps 0-3 / 4-7  softmax of sub-tile 0 / 1: thread = row = TMEM lane, so a
+//                    row's max and sum stay in one thread.  Per key tile: S_X[b]
+//                    from TMEM, causal mask, online softmax with lazy rescaling
+//                    of O_X, P_X (bf16 pairs) written back over S_X[b];
+//   warp 8 / 10,     one per sub-tile: issues S_X(t) = Q_X K_t^T into buffer
+//   lane 0           b = t % 2, then O_X += P_X(t-1) V_{t-1} (A operand read from
+//                    TMEM), each followed by tcgen05.commit to the barrier its
+//                    consumer waits on;
+//   warps 9, 11      load K_t (8 TMA boxes: 4 paged blocks x two 64-column
+//                    halves) and V_t (4 boxes: one whole 4 KB block tile each) into
+//                    ring slot c % TC_NS once the MMAs of the slot's previous use
+//                    are done, each warp two of the tile's four blocks.
+// With two S buffers the MMA warp issues S(t+1) while the softmax works on
+// S(t), so the softmax never waits for its scores once the pipeline is full.
+// S(t) may overwrite buffer b only after PV(t-2) has read P(t-2) from it: the
+// issuing thread issued PV(t-2) before S(t), and tcgen05.mma operations of one
+// thread execute in issue order (as the K-step accumulation into one D relies
+// on).  The softmax writes P(t) over S(t) after reading S(t), which completed
+// after PV(t-2); it need not wait for PV(t-1) (the other buffer) except to
+// rescale O.
+// c = c0 + t counts key tiles over all items of the launch; each barrier
+// completes exactly once per tile (odone), per use of its buffer (sfull, pfull:
+// every second tile) or per use of its slot (ring barriers), and no role can
 // run a full phase ahead of the role that waits on it, so a wait is always on
 // the current or the previous phase.  Returns false if a wait ran out; the
-// roles drain their own asynchronous work, and the pair stops taking items.
-__device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, const PlanView& v,
-                                  int item, uint8_t* payload, Shared& sh, uint32_t tmem,
-                                  uint32_t rank, uint32_t& ctr) {
+// roles then drain their own asynchronous work before the item ends.
+__device__ bool prefill_item_tc(const CUtensorMap* map, const CUtensorMap* tiles,
+                                const MainArgs& a, const PlanView& v, int item, uint8_t* payload,
+                                Shared& sh, uint32_t tmem, uint32_t& ctr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int4 it = v.pre_sorted[item];
   const int seq = it.x, g = it.y, t0 = it.z;
@@ -739,177 +735,154 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
   ctr += ntiles;
   bool ok = true;
 
-  if (warp < ATT_WARPS) {                       // this CTA's 128 Q rows -> smem (SW128, K-major)
-    const int r = (warp & 3) * 32 + lane, ch0 = (warp >> 2) * 8;
-    const int h = 2 * (int)rank + (r >> 6), j = r & 63;
+  if (warp < ATT_WARPS) {                       // Q rows -> smem (128B-swizzled, K-major)
+    const int X = warp >> 2, r = (warp & 3) * 32 + lane;
+    const int h = 2 * X + (r >> 6), j = r & 63;
     const bool valid = j < nrows;
     const uint4* qp = reinterpret_cast<const uint4*>(
         a.q + ((size_t)(row0 + t0 + (valid ? j : 0)) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM);
-    uint8_t* qrow = payload + (r >> 3) * 1024 + (r & 7) * 128;
+    uint8_t* qrow = payload + X * TC_Q_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-    for (int c = ch0; c < ch0 + 8; ++c) {
+    for (int c = 0; c < 16; ++c) {
       const uint4 val = valid ? qp[c] : make_uint4(0u, 0u, 0u, 0u);
       *reinterpret_cast<uint4*>(qrow + (c >> 3) * (TC_Q_BYTES / 2) + (((c & 7) ^ (r & 7)) << 4)) = val;
     }
     fence_proxy_async();                        // generic smem writes -> async proxy
   }
-  cluster_sync();                               // both CTAs' Q rows are in place
+  __syncthreads();
 
-  if (warp >= TC_LOAD_WARP0 && warp < TC_LOAD_WARP0 + TC_LOAD_WARPS) {
-    // lw 0, 1: K blocks 4 rank + 2 lw, +1 of the tile (this CTA's keys), both
-    // 64-column halves; lw 2, 3: V blocks 4 (lw - 2) .. +3, this CTA's 64 columns.
-    // An SM's TMA unit takes about one box per 90 cycles when several warps
-    // issue; one warp alone is slower, so the tile's 16 boxes are split four ways.
-    const int lw = warp - TC_LOAD_WARP0, kv = lw >> 1;
+  if (warp == TC_LOAD_WARP || warp == TC_LOAD_WARP2) {
+    // Two load warps, lw = 0, 1, each for blocks 2 lw and 2 lw + 1 of every key
+    // tile: lane 0 waits for the slot and posts its byte count; lanes 0-3 then
+    // issue the K boxes (block 2 lw + lane / 2, column half lane % 2), lanes 0-1
+    // the V block boxes.  An SM's TMA unit takes more boxes per cycle from two
+    // issuing warps than from one (one warp issuing a tile's 12 boxes was the
+    // prefill pipeline's slowest role).
+    const int lw = warp == TC_LOAD_WARP2;
     const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
     const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
-    // block ids 32 at a time (4 key tiles), lane i holding block 32 n + i, the
-    // next batch requested one batch ahead so no tile waits on the table
-    auto batch = [&](int n) {
-      const int bb = 32 * n + lane;
-      return (bb < nblk && bb < a.bt_pitch) ? bt[bb] : -1;
-    };
-    int ids = batch(0), ids_next = batch(1);
-    int issued = 0;
+    int ids = -1;                               // lane i: block 32 (t / 8) + i of the sequence
+    int issued[2] = {0, 0};                     // tiles whose K / V loads were issued
     for (int t = 0; t < ntiles && ok; ++t) {
-      if (t > 0 && (t & 3) == 0) {
-        ids = ids_next;
-        ids_next = batch((t >> 2) + 1);
+      if ((t & 7) == 0) {
+        const int b = 4 * t + lane;
+        ids = (b < nblk && b < a.bt_pitch) ? bt[b] : -1;
       }
       const uint32_t c = c0 + t, slot = c % TC_NS, use = c / TC_NS;
-      // this warp's 4 boxes of the tile: V blocks 4 (lw - 2) + k; K block
-      // 4 rank + 2 lw + k / 2, column half k % 2
-      int id4[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int src = 8 * (t & 3) + (kv ? 4 * (lw - 2) + k : 4 * (int)rank + 2 * lw + (k >> 1));
-        id4[k] = __shfl_sync(0xffffffffu, ids, src);
-      }
-      bool w_ok = true;
-      if (lane == 0) {
-        w_ok = mbar_wait(kv ? &sh.tc_vfree[slot] : &sh.tc_kfree[slot], (use & 1) ^ 1, a.err);
-        if (w_ok) {
-          uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
-          // this warp's and the peer's counterpart: 2 x 4 boxes of 2 KB
-          if (rank == 0) mbar_arrive_expect_tx(full, 2 * 4 * 2048);
-          const uint32_t lbar = smem_in_cta(smem_u32(full), 0);
-          uint8_t* sl = payload + (kv ? TC_V_OFF : TC_K_OFF) + slot * TC_KV_BYTES;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int id = id4[k];
-            int r = a.oob_row;                  // past the end: zero fill
-            if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
-            else if (id >= 0) r = kv_row(a, id, kv, g);
-            if (kv)                             // V block 4 (lw - 2) + k, this CTA's 64 columns
-              tma_load_2d_pair(sl + (4 * (lw - 2) + k) * 2048, map, 64 * (int)rank, r, lbar);
-            else                                // K block 2 lw + k / 2 of this CTA's 4, half k % 2
-              tma_load_2d_pair(sl + (k & 1) * TC_HALF + (2 * lw + (k >> 1)) * 2048, map,
-                               64 * (k & 1), r, lbar);
-          }
+#pragma unroll 1
+      for (int kv = 0; kv < 2; ++kv) {
+        bool w_ok = true;
+        if (lane == 0)
+          w_ok = mbar_wait(kv ? &sh.tc_vfree[slot] : &sh.tc_kfree[slot], (use & 1) ^ 1, a.err);
+        if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) { ok = false; break; }
+        uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
+        if (lane == 0) mbar_arrive_expect_tx(full, TC_KV_BYTES / 2);
+        const int jb = 2 * lw + (kv ? lane : (lane >> 1));
+        const int id = __shfl_sync(0xffffffffu, ids, (4 * t + jb) & 31);
+        if (lane < (kv ? 2 : 4)) {
+          int r = a.oob_row;                    // past the end: zero fill
+          if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
+          else if (id >= 0) r = kv_row(a, id, kv, g);
+          if (kv)
+            tma_load_3d(payload + TC_V_OFF + slot * TC_KV_BYTES + jb * 4096, tiles, 0, r, 0, full);
+          else
+            tma_load_2d(payload + TC_K_OFF + slot * TC_KV_BYTES + (lane & 1) * TC_HALF + jb * 2048,
+                        map, 64 * (lane & 1), r, full);
         }
-      }
-      ok = __shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0) != 0;
-      if (ok) issued = t + 1;
-    }
-    if (!ok && rank == 0 && lane == 0) {        // loads still in flight must land first
-      for (int t = max(0, issued - TC_NS); t < issued; ++t) {
-        const uint32_t c = c0 + t;
-        mbar_wait(kv ? &sh.tc_vfull[c % TC_NS] : &sh.tc_kfull[c % TC_NS], (c / TC_NS) & 1,
-                  nullptr);
+        issued[kv] = t + 1;
       }
     }
-    __syncwarp();
-  } else if (warp == TC_MMA_WARP) {
-    if (rank == 0 && lane == 0) {
-      constexpr uint32_t ID_S = tc_idesc_bf16(256, TC_KEYS, false);
-      constexpr uint32_t ID_O = tc_idesc_bf16(256, HY_HEAD_DIM, true);
-      const uint64_t dQ = tc_desc_sw128(sbase, 16, 1024);
+    if (!ok && lane == 0) {                     // loads still in flight must land first
+      for (int kv = 0; kv < 2; ++kv)
+        for (int t = max(0, issued[kv] - TC_NS); t < issued[kv]; ++t) {
+          const uint32_t c = c0 + t;
+          mbar_wait(kv ? &sh.tc_vfull[c % TC_NS] : &sh.tc_kfull[c % TC_NS], (c / TC_NS) & 1,
+                    nullptr);
+        }
+    }
+  } else if (warp == TC_MMA_WARP || warp == TC_MMA_WARP1) {
+    // one MMA warp per sub-tile X: its lane 0 issues S_X(t), then O_X += P_X(t-1)
+    // V_{t-1}; both warps commit to the K and V slots' free barriers (count 2)
+    const int X = warp == TC_MMA_WARP ? 0 : 1;
+    if (lane == 0) {
+      constexpr uint32_t ID_S = tc_idesc_bf16(128, TC_KEYS, false);
+      constexpr uint32_t ID_O = tc_idesc_bf16(128, HY_HEAD_DIM, true);
+      const uint64_t dQ = tc_desc_sw128(sbase + X * TC_Q_BYTES, 16, 1024);
       for (int t = 0; t <= ntiles && ok; ++t) {
-        if (t < ntiles) {                       // S(t) = Q K_t^T into buffer c % 2
-          const uint32_t c = c0 + t, slot = c % TC_NS, b = c & 1;
+        if (t < ntiles) {                       // S_X(t) = Q_X K_t^T into buffer c % 2
+          const uint32_t c = c0 + t, slot = c % TC_NS;
           ok = mbar_wait(&sh.tc_kfull[slot], (c / TC_NS) & 1, a.err);
           if (!ok) break;
           tc_fence_after();
           const uint64_t dK = tc_desc_sw128(sbase + TC_K_OFF + slot * TC_KV_BYTES, 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < HY_HEAD_DIM / 16; ++kk)
-            pair_mma_bf16(tmem + tm_s(b),
-                          dQ + (uint64_t)((((kk >> 2) * (TC_Q_BYTES / 2)) + (kk & 3) * 32) >> 4),
-                          dK + (uint64_t)((((kk >> 2) * TC_HALF) + (kk & 3) * 32) >> 4), ID_S,
-                          kk > 0);
-          pair_commit_both(&sh.tc_sfull[b]);
-          pair_commit_both(&sh.tc_kfree[slot]);
+            tc_mma_bf16(tmem + tm_s(X, c & 1),
+                        dQ + (uint64_t)((((kk >> 2) * (TC_Q_BYTES / 2)) + (kk & 3) * 32) >> 4),
+                        dK + (uint64_t)((((kk >> 2) * TC_HALF) + (kk & 3) * 32) >> 4), ID_S,
+                        kk > 0);
+          tc_commit(&sh.tc_sfull[X][c & 1]);
+          tc_commit(&sh.tc_kfree[slot]);
         }
-        if (t > 0) {                            // O += P(t-1) V_{t-1}
-          const uint32_t c = c0 + t - 1, slot = c % TC_NS, b = c & 1;
+        if (t > 0) {                            // O_X += P_X(t-1) V_{t-1}
+          const uint32_t c = c0 + t - 1, slot = c % TC_NS;
           ok = mbar_wait(&sh.tc_vfull[slot], (c / TC_NS) & 1, a.err) &&
-               mbar_wait(&sh.tc_pfull[b], (c >> 1) & 1, a.err);
+               mbar_wait(&sh.tc_pfull[X][c & 1], (c >> 1) & 1, a.err);
           if (!ok) break;
           tc_fence_after();
-          // this CTA's V half: 8-key groups 1 KB apart (SBO), block kk at kk x 2 KB
-          const uint64_t dV = tc_desc_sw128(sbase + TC_V_OFF + slot * TC_KV_BYTES, TC_HALF, 1024);
+          // V slot: block kk's tile at kk x 4 KB, its column halves 2 KB apart (LBO),
+          // 8-key groups 1 KB apart (SBO)
+          const uint64_t dV = tc_desc_sw128(sbase + TC_V_OFF + slot * TC_KV_BYTES, 2048, 1024);
 #pragma unroll
           for (int kk = 0; kk < TC_KEYS / 16; ++kk)
-            pair_mma_bf16_ta(tmem + TM_O, tmem + tm_s(b) + 8 * kk,
-                             dV + (uint64_t)((kk * 2048) >> 4), ID_O, (t > 1 || kk > 0));
-          pair_commit_both(&sh.tc_odone[b]);
-          pair_commit_both(&sh.tc_vfree[slot]);
+            tc_mma_bf16_ta(tmem + TM_O + 128 * X, tmem + tm_s(X, c & 1) + 8 * kk,
+                           dV + (uint64_t)((kk * 4096) >> 4), ID_O, (t > 1 || kk > 0));
+          tc_commit(&sh.tc_odone[X]);
+          tc_commit(&sh.tc_vfree[slot]);
         }
       }
       if (!ok) {                                // let every issued MMA finish
-        pair_commit_local(&sh.tc_drain[0]);
-        mbar_wait(&sh.tc_drain[0], 0, nullptr);
+        tc_commit(&sh.tc_drain[X]);
+        mbar_wait(&sh.tc_drain[X], 0, nullptr);
       }
     }
     __syncwarp();
-  } else if (warp < ATT_WARPS) {                // softmax: row (w % 4) * 32 + lane, column half w / 4
-    const int q = warp & 3, hf = warp >> 2;
-    const int r = q * 32 + lane, j = r & 63;
-    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    const uint32_t tO = tmem + lane_base + TM_O + 64 * hf;        // this warp's 64 O columns
+  } else {                                      // softmax warpgroups
+    const int X = warp >> 2, r = (warp & 3) * 32 + lane, j = r & 63;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tO = tmem + lane_base + TM_O + 128 * X;
     const int lim = prefix + t0 + j;            // last key row r may see
     const float sl2 = a.scale_log2;
-    const uint32_t pfull0 = smem_in_cta(smem_u32(&sh.tc_pfull[0]), 0);
-    const uint32_t pfull1 = smem_in_cta(smem_u32(&sh.tc_pfull[1]), 0);
-    float m = NEG_INF, l = 0.f;                 // m in scaled log2 units; l: this half's sum
-    // The partner warps w and w + 4 meet once per key tile at named barrier
-    // 1 + w % 4 and once in the epilogue; every decision to stop is taken from
-    // the barrier's combined flag, so both always run the same barriers.
-    for (int t = 0; t < ntiles; ++t) {
-      const uint32_t c = c0 + t, b = c & 1;
-      const uint32_t tS = tmem + lane_base + tm_s(b) + 64 * hf;
+    float m = NEG_INF, l = 0.f;                 // m in scaled log2 units
+    for (int t = 0; t < ntiles && ok; ++t) {
+      const uint32_t c = c0 + t;
+      const uint32_t tS = tmem + lane_base + tm_s(X, c & 1);
       // waits are made warp-uniform: tcgen05.ld/st below are warp-collective
-      const bool w_ok =
-          ok && __all_sync(0xffffffffu, mbar_wait(&sh.tc_sfull[b], (c >> 1) & 1, a.err));
+      ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_sfull[X][c & 1], (c >> 1) & 1, a.err));
+      if (!ok) break;
+      tc_fence_after();
       float s[64];
-      float mx = NEG_INF;
-      if (w_ok) {
-        tc_fence_after();
-        tmem_ld32(tS, *reinterpret_cast<float(*)[32]>(&s[0]));
-        tmem_ld32(tS + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
-        tmem_wait_ld();
-        const int kb = t * TC_KEYS + 64 * hf;
-        if (kb + 63 > prefix + t0) {            // the half reaches the diagonal or the end
+      tmem_ld32(tS, *reinterpret_cast<float(*)[32]>(&s[0]));
+      tmem_ld32(tS + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+      tmem_wait_ld();
+      const int kb = t * TC_KEYS;
+      if (kb + TC_KEYS - 1 > prefix + t0) {     // the tile reaches the diagonal or the end
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (kb + i > lim || kb + i >= kv_len) s[i] = NEG_INF;
-        }
-        float mxs[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mxs[k] = s[k];
-#pragma unroll
-        for (int i = 8; i < 64; i += 8)
-#pragma unroll
-          for (int k = 0; k < 8; ++k) mxs[k] = fmaxf(mxs[k], s[i + k]);
-        mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                   fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+        for (int i = 0; i < 64; ++i)
+          if (kb + i > lim || kb + i >= kv_len) s[i] = NEG_INF;
       }
-      // the row max over both halves: exchange with the partner warp (slots by
-      // tile parity, so a write of tile t+1 cannot meet a read of tile t); past
-      // this barrier both warps have read their S columns, so P may overwrite them
-      sh.xrow[b][hf][r] = mx;
-      if (named_sync_or(1 + q, 64, !w_ok)) { ok = false; break; }
-      mx = fmaxf(mx, sh.xrow[b][hf ^ 1][r]) * sl2;
+      // row max and row sum as 8 independent chains (a 64-long chain of
+      // dependent max or add instructions would expose its latency)
+      float mxs[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mxs[k] = s[k];
+#pragma unroll
+      for (int i = 8; i < 64; i += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mxs[k] = fmaxf(mxs[k], s[i + k]);
+      float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                       fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+      mx *= sl2;
       const bool grow = mx > m + RESCALE_LOG2;
       if (__any_sync(0xffffffffu, grow)) {
         const float mnew = grow ? mx : m;
@@ -917,11 +890,10 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
         l *= alpha;
         m = mnew;
         if (t > 0) {                            // O holds tiles < t: wait for PV(t-1)
-          const uint32_t cp = c - 1;
-          ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_odone[cp & 1], (cp >> 1) & 1, a.err));
+          ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_odone[X], (c & 1) ^ 1, a.err));
           tc_fence_after();
 #pragma unroll 1
-          for (int cc = 0; cc < 2 && ok; ++cc) {
+          for (int cc = 0; cc < 4; ++cc) {
             float o[32];
             tmem_ld32(tO + 32 * cc, o);
             tmem_wait_ld();
@@ -937,6 +909,8 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
       float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
+        // every EXP2_POLY_EVERY-th pair of weights on the FMA pipe, the rest on
+        // the exp2 unit: the two units then share the tile's 64 exponentials
         const bool poly = EXP2_POLY_EVERY > 0 && (i % EXP2_POLY_EVERY) == EXP2_POLY_EVERY - 1;
         const float x0 = fmaf(s[2 * i], sl2, mneg), x1 = fmaf(s[2 * i + 1], sl2, mneg);
         const float p0 = poly ? exp2_poly(x0) : ex2_ftz(x0);
@@ -946,28 +920,23 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
         pk[i] = pack_bf16(p0, p1);
       }
       l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
-      // P columns 32 hf .. 32 hf + 31 of buffer b (keys 64 hf .. 64 hf + 63)
-      tmem_st32u(tmem + lane_base + tm_s(b) + 32 * hf, pk);
+      tmem_st32u(tS, pk);                       // P(t) over the first 32 columns of S(t)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(b ? pfull1 : pfull0);
+      if (lane == 0) mbar_arrive(&sh.tc_pfull[X][c & 1]);
     }
-    // epilogue: the row sum over both halves, then this warp's 64 columns of O / l
-    sh.xrow[2][hf][r] = l;
-    if (named_sync_or(1 + q, 64, !ok)) ok = false;
-    l += sh.xrow[2][hf ^ 1][r];
-    if (ok) {
+    if (ok) {                                   // epilogue: O_X / l -> out
       const uint32_t c = c0 + ntiles - 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_odone[c & 1], (c >> 1) & 1, a.err));
+      ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_odone[X], c & 1, a.err));
       tc_fence_after();
       // tcgen05.ld is warp-collective: every lane loads, only real rows store
       const bool store = ok && j < nrows;
       const float inv = 1.f / l;
-      __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP +
-                                   2 * (int)rank + (r >> 6)) * HY_HEAD_DIM + 64 * hf;
+      __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + 2 * X +
+                                   (r >> 6)) * HY_HEAD_DIM;
 #pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
+      for (int cc = 0; cc < 4; ++cc) {
         float o[32];
         tmem_ld32(tO + 32 * cc, o);
         tmem_wait_ld();
@@ -986,13 +955,8 @@ __device__ bool prefill_item_pair(const CUtensorMap* map, const MainArgs& a, con
     }
   }
   tc_fence_before();
-  const bool bad = __syncthreads_or(!ok);
-  if (bad && threadIdx.x == 0) {
-    if (rank == 0) sh.pair_bad = 1;
-    else st_cluster_u32(smem_in_cta(smem_u32(&sh.peer_bad), 0), 1u);
-  }
-  cluster_sync();                               // the pair's item is done in both CTAs
-  return !bad;
+  if (__syncthreads_or(!ok)) ok = false;
+  return ok;
 }
 
 __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
@@ -1008,33 +972,31 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     for (int w = 0; w < ATT_WARPS; ++w)
       for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&sh.dec_bar[w][s], 1);
     for (int s = 0; s < TC_NS; ++s) {
-      mbar_init(&sh.tc_kfull[s], 2);            // the leader's two K loader warps
+      mbar_init(&sh.tc_kfull[s], 2);            // one arrival per load warp
       mbar_init(&sh.tc_vfull[s], 2);
-      mbar_init(&sh.tc_kfree[s], 1);
-      mbar_init(&sh.tc_vfree[s], 1);
+      mbar_init(&sh.tc_kfree[s], 2);            // one commit per MMA warp
+      mbar_init(&sh.tc_vfree[s], 2);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sh.tc_sfull[b], 1);
-      mbar_init(&sh.tc_pfull[b], 2 * ATT_WARPS);          // softmax warps of both CTAs
-      mbar_init(&sh.tc_odone[b], 1);
+    for (int x = 0; x < 2; ++x) {
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&sh.tc_sfull[x][b], 1);
+        mbar_init(&sh.tc_pfull[x][b], 4);       // one arrival per softmax warp
+      }
+      mbar_init(&sh.tc_odone[x], 1);
     }
     mbar_init(&sh.tc_drain[0], 1);
     mbar_init(&sh.tc_drain[1], 1);
-    sh.pair_bad = 0;
-    sh.peer_bad = 0;
     fence_mbar_init();
   }
   // set-up that reads nothing an earlier kernel wrote runs before the wait: the
   // barriers above, the tensor-map prefetch and the TMEM columns of the
-  // tcgen05 prefill items (the same warp of both CTAs of the pair allocates;
-  // one CTA per SM holds them)
-  const uint32_t rank = cluster_rank();
+  // tcgen05 prefill items (every CTA allocates; one CTA per SM holds them)
   if (warp == 0) {
-    pair_tmem_alloc(&sh.tmem_base, TC_TMEM_COLS);
-    pair_tmem_relinquish();
+    tmem_alloc(&sh.tmem_base, TC_TMEM_COLS);
+    tmem_relinquish();
   }
   tc_fence_before();
-  cluster_sync();                               // barriers of both CTAs initialised
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
   hy_grid_wait();
@@ -1042,23 +1004,19 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   const uint64_t keep = l2_keep_policy();
   const int n_pre = ld_keep(v.header, keep), n_dec = ld_keep(v.header + 1, keep);
   const int n_pairs = ld_keep(v.header + 4, keep);    // per-CTA decode when > 0
+  const bool use_tmem = (int)blockIdx.x < n_pre;      // the first n_pre CTAs take prefill items
   uint32_t dec_phase = 0, tile_ctr = 0;
   bool ok = true;
   int* grab = v.grab + GRAB_INTS * (a.layer & 63);
-  // prefill items: one per CTA pair at a time, in the plan's order (most key
-  // tiles first); the leader takes the next one and hands it to its peer
-  if (n_pre > 0) {
-    const uint32_t peer_item = smem_in_cta(smem_u32(&sh.pre_item), 1);
-    while (true) {
-      if (rank == 0 && threadIdx.x == 0) {
-        const int k = (sh.pair_bad | sh.peer_bad) ? n_pre : atomicAdd(&grab[2], 1);
-        sh.pre_item = k;
-        st_cluster_u32(peer_item, (uint32_t)k);
-      }
-      cluster_sync();
+  // prefill items: CTA-wide, in the plan's order (most key tiles first)
+  if (use_tmem) {
+    while (ok) {
+      if (threadIdx.x == 0) sh.pre_item = atomicAdd(&grab[2], 1);
+      __syncthreads();
       const int k = sh.pre_item;
+      __syncthreads();                          // read before thread 0 writes the next one
       if (k >= n_pre) break;
-      if (!prefill_item_pair(&kv_map, a, v, k, payload, sh, tmem, rank, tile_ctr)) ok = false;
+      ok = prefill_item_tc(&kv_map, &kv_tiles, a, v, k, payload, sh, tmem, tile_ctr);
     }
   }
   // decode items (warps 0..ATT_WARPS-1): each warp takes the next one from this
@@ -1097,10 +1055,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     }
   }
   tc_fence_before();
-  cluster_sync();                               // both CTAs are done with TMEM
+  __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    pair_tmem_dealloc(tmem, TC_TMEM_COLS);
+    tmem_dealloc(tmem, TC_TMEM_COLS);
   }
 }
 
@@ -1274,28 +1232,9 @@ cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const void* cache, const voi
   a.scale_log2 = scale * 1.4426950408889634f;
   a.err = err;
   const PlanView v = make_view(ws, d);
-  // clusters of two CTAs: the prefill tiles run on CTA pairs
-  const int grid = (device_sms(dev) * g_ctas_per_sm[dev < 64 && dev >= 0 ? dev : 0]) & ~1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(ATT_THREADS);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  int n = 0;
-  attr[n].id = cudaLaunchAttributeClusterDimension;
-  attr[n].val.clusterDim.x = 2;
-  attr[n].val.clusterDim.y = 1;
-  attr[n].val.clusterDim.z = 1;
-  ++n;
-  if (hy_pdl_enabled()) {
-    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[n].val.programmaticStreamSerializationAllowed = 1;
-    ++n;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, attn_main_kernel, maps.halves, maps.tiles, a, v);
+  const int grid = device_sms(dev) * g_ctas_per_sm[dev < 64 && dev >= 0 ? dev : 0];
+  return hy_launch(attn_main_kernel, dim3(grid), dim3(ATT_THREADS), SMEM_BYTES, st, maps.halves,
+                   maps.tiles, a, v);
 }
 
 cudaError_t hy_launch_attn_fp32(const float* q, float* out, int T, int q_heads, int kv_heads,

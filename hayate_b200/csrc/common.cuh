@@ -377,104 +377,3 @@ HY_DEVICE void tmem_st32(uint32_t taddr, const float (&v)[32]) {
 
 HY_DEVICE void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 HY_DEVICE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// 16 consecutive 32-bit columns of this thread's TMEM lane (warp-collective).
-HY_DEVICE void tmem_st16u(uint32_t taddr, const uint32_t* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-      :: "r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
-         "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]),
-         "r"(v[14]), "r"(v[15])
-      : "memory");
-}
-
-// ---------------------------------------------------------------- CTA pairs
-// A kernel launched in clusters of two CTAs can run its tensor-core tiles on
-// the pair (cta_group::2): one thread of the even CTA (the leader) issues an
-// M = 256 MMA whose A rows 0-127 come from the leader's shared memory or TMEM
-// and rows 128-255 from its peer's (same offsets), whose B columns are split
-// in halves between the two CTAs' shared memory, and whose D rows land in each
-// CTA's own TMEM at the same address.  Every tcgen05 instruction of such a
-// kernel uses cta_group::2: TMEM is allocated and freed by the same warp of
-// both CTAs.  No TMA here carries a multicast qualifier: each CTA loads its own
-// tiles, and a load's completion may be counted on the leader's barrier.
-HY_DEVICE uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// Every thread of both CTAs arrives; returns once all have.
-HY_DEVICE void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
-               ::: "memory");
-}
-// The shared::cluster address of `smem_addr` (a shared::cta address) in CTA `rank`.
-HY_DEVICE uint32_t smem_in_cta(uint32_t smem_addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
-  return r;
-}
-// Arrive on a barrier of another CTA of the cluster, with the default (CTA-scope)
-// release: what the waiter reads through this barrier is TMEM written by
-// tcgen05.st, ordered by tcgen05.fence::before_thread_sync on this side and
-// ::after_thread_sync on the waiter's, so no cluster-scope fence is needed
-// (one per key tile measured as the kernel's largest stall).
-HY_DEVICE void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
-}
-HY_DEVICE void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;" :: "r"(cluster_addr), "r"(v) : "memory");
-}
-// 2-D tiled load into this CTA's shared memory whose bytes are counted on the
-// pair leader's barrier `leader_bar` (a shared::cluster address).  No multicast.
-HY_DEVICE void tma_load_2d_pair(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
-                                uint32_t leader_bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];"
-      :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
-         "r"(leader_bar)
-      : "memory");
-}
-HY_DEVICE void pair_tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
-               :: "r"(smem_u32(smem_dst)), "r"(ncols) : "memory");
-}
-HY_DEVICE void pair_tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-HY_DEVICE void pair_tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols)
-               : "memory");
-}
-// D[tmem] (+)= A[smem] * B[smem] on the pair (M = 256), issued by the leader.
-HY_DEVICE void pair_mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                             uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
-}
-// D[tmem] (+)= A[tmem] * B[smem] on the pair (A rows in each CTA's TMEM).
-HY_DEVICE void pair_mma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
-      :: "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
-}
-// Arrive on `bar` in both CTAs of the pair once every tcgen05 op this thread
-// issued has completed.
-HY_DEVICE void pair_commit_both(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" :: "r"(smem_u32(bar)), "h"((uint16_t)3) : "memory");
-}
-// The same, on this CTA's `bar` only.
-HY_DEVICE void pair_commit_local(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-               :: "r"(smem_u32(bar)) : "memory");
-}
