@@ -16,7 +16,8 @@
 // layer:
 //   * prefill items -- (seq, kv_head, 64-token tile): one CTA, warp-specialised:
 //     two M=128 tcgen05 tiles (two query heads x 64 tokens each) share every
-//     64-key K/V tile a load warp stages by TMA in 4-slot rings; one MMA warp
+//     64-key K/V tile, staged by TMA in 4-slot rings by two load warps (two of
+//     the tile's four blocks each: one warp issues too few boxes); one MMA warp
 //     per tile issues its S = Q K^T and O += P V with S, P and O in TMEM; two
 //     softmax warpgroups run one thread per query row;
 //   * decode items  -- (seq, kv_head, block range): one warp with its own TMA
