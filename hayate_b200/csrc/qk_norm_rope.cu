@@ -116,16 +116,20 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 // bf16 path of the same operation, laid out for bandwidth: a head row (128
 // elements, 256 bytes) is one 16-byte vector per lane of a half-warp, so every
 // load and store is a full 16-byte access and a warp moves two rows at once.
-// Work unit = (token, pass of 16 head rows): a CTA's 16 half-warps take one
-// pass each, so a batch of T tokens spreads over T x ceil(heads / 16) CTAs (a
-// decode step of a few tokens still fills many SMs); with more units than CTAs
-// each CTA walks them one at a time, loading the next unit's position ahead.  The
-// RoPE partner of element d (d +- 64) sits 8 lanes away and comes over a
+// Work unit = (token, group of NPC passes of 16 head rows): pass j of group g
+// covers head rows 16 (g NPC + j) + half-warp.  Small batches (decode steps)
+// use NPC = 1, so a few tokens still spread over many CTAs; prefill-sized
+// batches use NPC = all passes of a token, so one CTA iteration covers the
+// whole token with one load of its position, slot and cos/sin rows.  Each CTA
+// walks its units one grid stride apart and loads the next unit's head rows,
+// position and slot before it computes the current one, so two units' rows are
+// in flight per lane (the kernel is bound by bytes in flight, not by issue).
+// The RoPE partner of element d (d +- 64) sits 8 lanes away and comes over a
 // shuffle.  Rounding points and the order of the products are those of the
 // kernel above; only the order of the sum of squares differs (8 in-lane terms,
 // then a 16-lane butterfly).
 constexpr int QNR_THREADS = 256;
-constexpr int QNR_GROUPS = QNR_THREADS / 16;        // head rows per unit
+constexpr int QNR_GROUPS = QNR_THREADS / 16;        // head rows per pass
 
 HY_DEVICE void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -145,6 +149,35 @@ HY_DEVICE uint4 f32_to_bf16x8(const float (&f)[8]) {
   return u;
 }
 
+// One unit's inputs held by a lane: its NPC head-row vectors, the token's
+// position and cache slot.
+template <int NPC>
+struct QnrUnit {
+  uint4 raw[NPC];
+  int pos, slot;
+};
+
+template <int NPC>
+HY_DEVICE void qnr_load(QnrUnit<NPC>& u, int t, int g, int T_tokens, int heads, int grp, int d0,
+                        const __nv_bfloat16* __restrict__ qkv, int ld,
+                        const int32_t* __restrict__ positions,
+                        const int32_t* __restrict__ slot_mapping, bool want_slot) {
+  u.pos = 0;
+  u.slot = -1;
+#pragma unroll
+  for (int j = 0; j < NPC; ++j) u.raw[j] = make_uint4(0u, 0u, 0u, 0u);
+  if (t >= T_tokens) return;
+  u.pos = positions[t];
+  if (want_slot) u.slot = slot_mapping[t];
+#pragma unroll
+  for (int j = 0; j < NPC; ++j) {
+    const int h = (g * NPC + j) * QNR_GROUPS + grp;
+    if (h < heads)
+      u.raw[j] = *reinterpret_cast<const uint4*>(qkv + (size_t)t * ld + (size_t)h * HY_HEAD_DIM + d0);
+  }
+}
+
+template <int NPC>
 __global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
     const __nv_bfloat16* __restrict__ qkv, int ld, int T_tokens, int q_heads, int kv_heads,
     const int32_t* __restrict__ positions, const __nv_bfloat16* __restrict__ q_w,
@@ -154,43 +187,30 @@ __global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
     const int32_t* __restrict__ slot_mapping, int num_blocks, int32_t* err) {
   hy_grid_wait();
   hy_grid_trigger();
-  using B = __nv_bfloat16;
   const int grp = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int heads = q_heads + 2 * kv_heads;
   const int npass = (heads + QNR_GROUPS - 1) / QNR_GROUPS;
+  const int G = (npass + NPC - 1) / NPC;           // pass groups per token
   const int d0 = l * 8;                    // this lane's 8 elements of a row
   const int c0 = (l & 7) * 8;              // ... and their RoPE table columns
   const bool upper = l >= 8;               // elements 64..127: partner is d - 64
-  // unit = t * npass + p walks the grid stride as (token, pass) pairs, with no
-  // division in the loop; the position of the next unit is loaded one unit
-  // ahead, so a unit's cos/sin rows, head row and slot are requested together
-  const int dt = (int)(gridDim.x / npass), dp = (int)(gridDim.x % npass);
-  int t = (int)(blockIdx.x / npass), p = (int)(blockIdx.x % npass), tn = 0, pn = 0;
-  int pos_next = t < T_tokens ? positions[t] : 0;
-  for (; t < T_tokens; t = tn, p = pn) {            // uniform over the CTA
-    tn = t + dt;                                    // the unit one grid stride on
-    pn = p + dp;
-    if (pn >= npass) { pn -= npass; ++tn; }
-    const int h = p * QNR_GROUPS + grp;
-    const bool valid = h < heads;                  // uniform over the warp's half-warps
-    int pos = pos_next;
-    pos_next = tn < T_tokens ? positions[tn] : 0;
+  const bool want_slot = cache != nullptr;
+  const long slot_end = (long)num_blocks * HY_BLOCK;
+  // unit = t * G + g walks the grid stride as (token, group) pairs, with no
+  // division in the loop
+  const int dt = (int)(gridDim.x / G), dg = (int)(gridDim.x % G);
+  int t = (int)(blockIdx.x / G), g = (int)(blockIdx.x % G);
+  QnrUnit<NPC> cur;
+  qnr_load(cur, t, g, T_tokens, heads, grp, d0, qkv, ld, positions, slot_mapping, want_slot);
+  while (t < T_tokens) {                           // uniform over the CTA
+    int tn = t + dt, gn = g + dg;                  // the unit one grid stride on
+    if (gn >= G) { gn -= G; ++tn; }
+    QnrUnit<NPC> nxt;
+    qnr_load(nxt, tn, gn, T_tokens, heads, grp, d0, qkv, ld, positions, slot_mapping, want_slot);
+    int pos = cur.pos;
     if (pos < 0 || pos >= max_pos) { hy_flag(err, HY_ERR_BOUNDS); pos = 0; }
-    const uint4 raw = valid ? *reinterpret_cast<const uint4*>(
-                                  qkv + (size_t)t * ld + (size_t)h * HY_HEAD_DIM + d0)
-                            : make_uint4(0u, 0u, 0u, 0u);
-    int slot = -1;
-    if (cache != nullptr && valid && h >= q_heads) {
-      slot = slot_mapping[t];
-      if (slot >= (long)num_blocks * HY_BLOCK) { hy_flag(err, HY_ERR_BOUNDS); slot = -1; }
-    }
-    if (valid && h >= q_heads + kv_heads) {        // value head: cache copy only
-      if (slot >= 0)
-        *reinterpret_cast<uint4*>(cache_ptr(cache, slot, 1, h - q_heads - kv_heads, kv_heads) + d0) = raw;
-    }
-    // a warp with no query or key row left (both half-warps value heads or past
-    // the end) skips the norm; otherwise all its lanes run it for the shuffles
-    if (__all_sync(0xffffffffu, !valid || h >= q_heads + kv_heads)) continue;
+    int slot = cur.slot;
+    if (slot >= slot_end) { hy_flag(err, HY_ERR_BOUNDS); slot = -1; }
     float cs[8], sn[8];
     {
       const float4* cp = reinterpret_cast<const float4*>(rope_cos + (size_t)pos * 64 + c0);
@@ -199,45 +219,61 @@ __global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
       cs[0] = a.x; cs[1] = a.y; cs[2] = a.z; cs[3] = a.w; cs[4] = b.x; cs[5] = b.y; cs[6] = b.z; cs[7] = b.w;
       sn[0] = e.x; sn[1] = e.y; sn[2] = e.z; sn[3] = e.w; sn[4] = f.x; sn[5] = f.y; sn[6] = f.z; sn[7] = f.w;
     }
-    // every lane of the warp takes part in the shuffles below
-    float x[8];
-    bf16x8_to_f32(raw, x);
-    float ss = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
+    for (int j = 0; j < NPC; ++j) {
+      const int h = (g * NPC + j) * QNR_GROUPS + grp;
+      const bool valid = h < heads;                // uniform over each half-warp
+      const uint4 raw = cur.raw[j];
+      if (valid && h >= q_heads + kv_heads) {      // value head: cache copy only
+        if (slot >= 0)
+          *reinterpret_cast<uint4*>(cache_ptr(cache, slot, 1, h - q_heads - kv_heads, kv_heads) + d0) = raw;
+      }
+      // a warp with no query or key row in this pass (both half-warps value
+      // heads or past the end) skips the norm; otherwise all its lanes run it
+      // for the shuffles
+      if (__all_sync(0xffffffffu, !valid || h >= q_heads + kv_heads)) continue;
+      float x[8];
+      bf16x8_to_f32(raw, x);
+      float ss = 0.f;
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-    // mean = ss / 128 exactly (a power of two)
-    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / HY_HEAD_DIM), eps)));
-    float w[8];
-    bf16x8_to_f32(*reinterpret_cast<const uint4*>(((h < q_heads) ? q_w : k_w) + d0), w);
-    float y[8];
+      for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      y[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], rstd), w[e])));
-    const uint4 yb = f32_to_bf16x8(y);          // exact: y is already bf16-valued
-    uint4 pb;
-    pb.x = __shfl_xor_sync(0xffffffffu, yb.x, 8);
-    pb.y = __shfl_xor_sync(0xffffffffu, yb.y, 8);
-    pb.z = __shfl_xor_sync(0xffffffffu, yb.z, 8);
-    pb.w = __shfl_xor_sync(0xffffffffu, yb.w, 8);
-    float p[8];
-    bf16x8_to_f32(pb, p);
-    float o[8];
+      for (int o = 8; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      // mean = ss / 128 exactly (a power of two)
+      const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / HY_HEAD_DIM), eps)));
+      float w[8];
+      bf16x8_to_f32(*reinterpret_cast<const uint4*>(((h < q_heads) ? q_w : k_w) + d0), w);
+      float y[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {               // lower: y*cos + (-y[d+64])*sin; upper: y*cos + y[d-64]*sin
-      const float pe = upper ? p[e] : -p[e];
-      o[e] = __fadd_rn(__fmul_rn(y[e], cs[e]), __fmul_rn(pe, sn[e]));
+      for (int e = 0; e < 8; ++e)
+        y[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], rstd), w[e])));
+      const uint4 yb = f32_to_bf16x8(y);          // exact: y is already bf16-valued
+      uint4 pb;
+      pb.x = __shfl_xor_sync(0xffffffffu, yb.x, 8);
+      pb.y = __shfl_xor_sync(0xffffffffu, yb.y, 8);
+      pb.z = __shfl_xor_sync(0xffffffffu, yb.z, 8);
+      pb.w = __shfl_xor_sync(0xffffffffu, yb.w, 8);
+      float p[8];
+      bf16x8_to_f32(pb, p);
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {               // lower: y*cos + (-y[d+64])*sin; upper: y*cos + y[d-64]*sin
+        const float pe = upper ? p[e] : -p[e];
+        o[e] = __fadd_rn(__fmul_rn(y[e], cs[e]), __fmul_rn(pe, sn[e]));
+      }
+      if (!valid || h >= q_heads + kv_heads) continue;
+      const uint4 ob = f32_to_bf16x8(o);
+      if (h < q_heads) {
+        if (q_out) *reinterpret_cast<uint4*>(q_out + ((size_t)t * q_heads + h) * HY_HEAD_DIM + d0) = ob;
+      } else {
+        const int kh = h - q_heads;
+        if (k_out) *reinterpret_cast<uint4*>(k_out + ((size_t)t * kv_heads + kh) * HY_HEAD_DIM + d0) = ob;
+        if (slot >= 0) *reinterpret_cast<uint4*>(cache_ptr(cache, slot, 0, kh, kv_heads) + d0) = ob;
+      }
     }
-    if (!valid || h >= q_heads + kv_heads) continue;
-    const uint4 ob = f32_to_bf16x8(o);
-    if (h < q_heads) {
-      if (q_out) *reinterpret_cast<uint4*>(q_out + ((size_t)t * q_heads + h) * HY_HEAD_DIM + d0) = ob;
-    } else {
-      const int kh = h - q_heads;
-      if (k_out) *reinterpret_cast<uint4*>(k_out + ((size_t)t * kv_heads + kh) * HY_HEAD_DIM + d0) = ob;
-      if (slot >= 0) *reinterpret_cast<uint4*>(cache_ptr(cache, slot, 0, kh, kv_heads) + d0) = ob;
-    }
+    cur = nxt;
+    t = tn;
+    g = gn;
   }
 }
 
@@ -287,6 +323,20 @@ __global__ void __launch_bounds__(KVA_THREADS) kv_append_kernel(
   }
 }
 
+// min(units, 148 SMs x resident CTAs of the kernel), the occupancy asked once
+// per pass-group size
+template <typename K>
+int qnr_grid(K kernel, int npc, long units) {
+  static int occ[5] = {0, 0, 0, 0, 0};
+  if (occ[npc] == 0) {
+    int n = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, QNR_THREADS, 0);
+    occ[npc] = n > 0 ? n : 1;
+  }
+  const long cap = 148L * occ[npc];
+  return (int)(units < cap ? (units > 0 ? units : 1) : cap);
+}
+
 int grid_for(long warps) {
   long blocks = (warps + 7) / 8;
   if (blocks > 148L * 16) blocks = 148L * 16;
@@ -304,12 +354,24 @@ cudaError_t hy_launch_qk_norm_rope(int dtype, const void* qkv, int ld, int T, in
   if (T <= 0) return cudaSuccess;
   if (dtype == 0) {
     using B = __nv_bfloat16;
-    const long units = (long)T * ((q_heads + 2 * kv_heads + QNR_GROUPS - 1) / QNR_GROUPS);
-    const int grid = (int)(units < 148L * 8 ? units : 148L * 8);   // up to 8 CTAs per SM
-    return hy_launch(qk_norm_rope_bf16_kernel, dim3(grid), dim3(QNR_THREADS), 0, st,
-                     (const B*)qkv, (int)ld, T, q_heads, kv_heads, positions, (const B*)q_w,
-                     (const B*)k_w, rope_cos, rope_sin, max_pos, eps, (B*)q_out, (B*)k_out,
-                     (B*)cache, slot_mapping, num_blocks, err);
+    const int npass = (q_heads + 2 * kv_heads + QNR_GROUPS - 1) / QNR_GROUPS;
+    // one pass per unit while that still leaves units for fewer than 8 CTAs per
+    // SM (decode steps); otherwise up to 4 passes of a token per unit
+    const int npc = (long)T * npass <= 148L * 8 ? 1 : (npass < 4 ? npass : 4);
+    const long units = (long)T * ((npass + npc - 1) / npc);
+    // as many CTAs as are resident at once (each walks its units), at most one per unit
+#define HY_QNR_LAUNCH(N)                                                                      \
+  hy_launch(qk_norm_rope_bf16_kernel<N>, dim3(qnr_grid(qk_norm_rope_bf16_kernel<N>, N, units)), \
+            dim3(QNR_THREADS), 0, st, (const B*)qkv, (int)ld, T, q_heads, kv_heads, positions, \
+            (const B*)q_w, (const B*)k_w, rope_cos, rope_sin, max_pos, eps, (B*)q_out,         \
+            (B*)k_out, (B*)cache, slot_mapping, num_blocks, err)
+    switch (npc) {
+      case 1: return HY_QNR_LAUNCH(1);
+      case 2: return HY_QNR_LAUNCH(2);
+      case 3: return HY_QNR_LAUNCH(3);
+      default: return HY_QNR_LAUNCH(4);
+    }
+#undef HY_QNR_LAUNCH
   } else {
     const int grid = grid_for((long)T * (q_heads + 2 * kv_heads));
     qk_norm_rope_kernel<float><<<grid, 256, 0, st>>>(

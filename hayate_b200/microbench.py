@@ -18,6 +18,13 @@ timed launch would pay.
 batches).  Every op reports its algorithmic bytes; packing is latency-bound,
 so its microseconds are the figure of merit.
 
+``--stream`` times the row kernels as they run inside an engine step instead:
+back to back, replayed from a CUDA graph, each launch on its own copy of the
+inputs, with enough copies that together they are more than twice L2 (so every
+launch reads its inputs from HBM); the figure is the graph's time over its
+launches.  A single flushed launch also carries the launch and event overhead
+(~10 us), which at prefill sizes is as long as the kernel.
+
 ``python -m hayate_b200.microbench [--op attention|qk_norm_rope|kv_append|pack|argmax|
 add_rms_norm|silu_mul|all]
 [--iters N]`` prints one JSON line per op.
@@ -116,6 +123,7 @@ def attention_micro(iters: int = 20, n_decode: int = 256, prefill: bool = True,
 
 
 L2_FLUSH_BYTES = 256 << 20
+L2_BYTES = 126 << 20
 
 
 def _flusher():
@@ -143,6 +151,37 @@ def _time(launch, iters: int, flush: bool):
     return ms
 
 
+def _copies(set_bytes: int, cap: int = 16) -> int:
+    """Input copies whose total is at least twice L2."""
+    return max(2, min(cap, -(-2 * L2_BYTES // max(1, set_bytes))))
+
+
+def _time_stream(launches, iters: int):
+    """Per-launch time (ms) of ``launches`` (callables on disjoint buffers)
+    replayed back to back from one CUDA graph, ``iters`` replays after 2 warm-up
+    replays."""
+    for f in launches:
+        f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for f in launches:
+            f()
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    ms = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+        ms.append(a.elapsed_time(b) / len(launches))
+    del g
+    return ms
+
+
 def _summary(op, ms, nbytes, **extra):
     mean = statistics.mean(ms)
     out = {"op": op, "ms_mean": mean, "ms_min": min(ms), "us_mean": mean * 1e3,
@@ -167,9 +206,11 @@ def _batch_rows(n_decode: int, tokens: int):
     return prior, q
 
 
-def append_micro(iters: int = 20, n_decode: int = 256, tokens: int = 2304, fused: bool = True):
+def append_micro(iters: int = 20, n_decode: int = 256, tokens: int = 2304, fused: bool = True,
+                 stream: bool = False):
     """Fused QK-RMSNorm + RoPE + paged KV append (``fused``) or the standalone
-    KV append, over the tokens of the operator batch."""
+    KV append, over the tokens of the operator batch (``stream``: see the
+    module docstring)."""
     from hayate_b200 import kernels as K
     prior, q_lens = _batch_rows(n_decode, tokens)
     T = sum(q_lens)
@@ -191,27 +232,33 @@ def append_micro(iters: int = 20, n_decode: int = 256, tokens: int = 2304, fused
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     if fused:
         max_pos = 40960
-        qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=dev, dtype=torch.bfloat16, generator=g)
         qn = torch.ones(D, device=dev, dtype=torch.bfloat16)
         ang = torch.rand(max_pos, 64, device=dev, generator=g) * 6.28
         cos, sin = torch.cos(ang), torch.sin(ang)
-        q_out = torch.empty(T, Hq, D, device=dev, dtype=torch.bfloat16)
-
-        def launch():
-            K.qk_norm_rope(qkv, Hq, Hkv, positions, qn, qn, cos, sin, 1e-6, q_out=q_out,
-                           kv_cache_layer=cache, slot_mapping=smap, num_blocks=NB, err=err)
         # qkv row in, q out, K and V into the cache, position + slot, cos + sin rows
         nbytes = T * ((Hq + 2 * Hkv) * D * 2 + Hq * D * 2 + 2 * Hkv * D * 2 + 8 + 2 * 64 * 4)
         op = "qk_norm_rope"
-    else:
-        k = torch.randn(T, Hkv, D, device=dev, dtype=torch.bfloat16, generator=g)
-        v = torch.randn(T, Hkv, D, device=dev, dtype=torch.bfloat16, generator=g)
 
-        def launch():
-            K.kv_append(k, v, smap, cache, NB, err=err)
+        def make(c):
+            qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=dev, dtype=torch.bfloat16,
+                              generator=g)
+            q_out = torch.empty(T, Hq, D, device=dev, dtype=torch.bfloat16)
+            return lambda: K.qk_norm_rope(qkv, Hq, Hkv, positions, qn, qn, cos, sin, 1e-6,
+                                          q_out=q_out, kv_cache_layer=c, slot_mapping=smap,
+                                          num_blocks=NB, err=err)
+    else:
         nbytes = T * (2 * 2 * Hkv * D * 2 + 4)        # K and V read and written, slot
         op = "kv_append"
-    ms = _time(launch, iters, flush=True)
+
+        def make(c):
+            k = torch.randn(T, Hkv, D, device=dev, dtype=torch.bfloat16, generator=g)
+            v = torch.randn(T, Hkv, D, device=dev, dtype=torch.bfloat16, generator=g)
+            return lambda: K.kv_append(k, v, smap, c, NB, err=err)
+    if stream:
+        ms = _time_stream([make(cache if i == 0 else torch.zeros_like(cache))
+                           for i in range(_copies(nbytes))], iters)
+    else:
+        ms = _time(make(cache), iters, flush=True)
     if int(err.item()) != 0:
         raise RuntimeError(f"{op} micro: device error {int(err.item())}")
     return _summary(op, ms, nbytes, tokens=T)
@@ -280,48 +327,61 @@ def pack_micro(iters: int = 20, n_decode: int = 256, tokens: int = 2304):
     return _summary("pack", ms, nbytes, seqs=S, tokens=T, new_blocks=sum(need))
 
 
-def argmax_micro(iters: int = 20, rows: int = 260, vocab: int = 151936):
+def argmax_micro(iters: int = 20, rows: int = 260, vocab: int = 151936, stream: bool = False):
     """Greedy argmax over ``rows`` bf16 logit rows (the sampled rows of the
-    operator batch)."""
+    operator batch; ``stream``: see the module docstring)."""
     from hayate_b200 import kernels as K
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
-    logits = torch.randn(rows, vocab, device=dev, dtype=torch.bfloat16, generator=g)
-    out = torch.empty(rows, dtype=torch.int32, device=dev)
-    ms = _time(lambda: K.argmax(logits, out), iters, flush=True)
-    if not torch.equal(out.long(), logits.argmax(dim=1)):
-        raise RuntimeError("argmax micro: result differs from torch.argmax")
-    return _summary("argmax", ms, rows * vocab * 2 + rows * 4, rows=rows)
+    nbytes = rows * vocab * 2 + rows * 4
+    sets = []
+    for _ in range(_copies(nbytes) if stream else 1):
+        logits = torch.randn(rows, vocab, device=dev, dtype=torch.bfloat16, generator=g)
+        sets.append((logits, torch.empty(rows, dtype=torch.int32, device=dev)))
+    launches = [(lambda lo=lo, o=o: K.argmax(lo, o)) for lo, o in sets]
+    ms = _time_stream(launches, iters) if stream else _time(launches[0], iters, flush=True)
+    for logits, out in sets:
+        if not torch.equal(out.long(), logits.argmax(dim=1)):
+            raise RuntimeError("argmax micro: result differs from torch.argmax")
+    return _summary("argmax", ms, nbytes, rows=rows, stream=stream)
 
 
 def rowwise_micro(op: str, iters: int = 20, rows: int = 2304, hidden: int = 2560,
-                  inter: int = 9728):
+                  inter: int = 9728, stream: bool = False):
     """Residual add + RMSNorm over [rows][hidden] (``add_rms_norm``) or SiLU(gate) * up
-    over [rows][2 inter] (``silu_mul``), bf16, Qwen3-4B widths."""
+    over [rows][2 inter] (``silu_mul``), bf16, Qwen3-4B widths (``stream``: see
+    the module docstring)."""
     from hayate_b200 import kernels as K
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
     if op == "add_rms_norm":
-        x = torch.randn(rows, hidden, device=dev, dtype=torch.bfloat16, generator=g)
-        d = torch.randn(rows, hidden, device=dev, dtype=torch.bfloat16, generator=g)
-        w = torch.ones(hidden, device=dev, dtype=torch.bfloat16)
-        y = torch.empty_like(x)
-        launch = lambda: K.add_rms_norm(x, w, 1e-6, delta=d, out=y)
         nbytes = rows * hidden * 2 * 4 + hidden * 2            # x, delta in; x, y out; weights
+        w = torch.ones(hidden, device=dev, dtype=torch.bfloat16)
+
+        def make():
+            x = torch.randn(rows, hidden, device=dev, dtype=torch.bfloat16, generator=g)
+            d = torch.randn(rows, hidden, device=dev, dtype=torch.bfloat16, generator=g)
+            y = torch.empty_like(x)
+            return lambda: K.add_rms_norm(x, w, 1e-6, delta=d, out=y)
     else:
-        gu = torch.randn(rows, 2 * inter, device=dev, dtype=torch.bfloat16, generator=g)
-        y = torch.empty(rows, inter, device=dev, dtype=torch.bfloat16)
-        launch = lambda: K.silu_mul(gu, y)
         nbytes = rows * inter * 2 * 3                           # gate, up in; product out
-    ms = _time(launch, iters, flush=True)
-    return _summary(op, ms, nbytes, rows=rows)
+
+        def make():
+            gu = torch.randn(rows, 2 * inter, device=dev, dtype=torch.bfloat16, generator=g)
+            y = torch.empty(rows, inter, device=dev, dtype=torch.bfloat16)
+            return lambda: K.silu_mul(gu, y)
+    if stream:
+        ms = _time_stream([make() for _ in range(_copies(nbytes))], iters)
+    else:
+        ms = _time(make(), iters, flush=True)
+    return _summary(op, ms, nbytes, rows=rows, stream=stream)
 
 
 OPS = ("attention", "qk_norm_rope", "kv_append", "pack", "argmax", "add_rms_norm", "silu_mul")
 
 
 def run_op(op: str, iters: int, n_decode: int = 256, prefill: bool = True, tokens: int = 2304,
-           ctx_lo: int = 256, ctx_hi: int = 16384, priors=None):
+           ctx_lo: int = 256, ctx_hi: int = 16384, priors=None, stream: bool = False):
     if op == "attention":
         r = attention_micro(iters, n_decode, prefill, ctx_lo, ctx_hi, priors)
         r["op"] = op
@@ -329,13 +389,16 @@ def run_op(op: str, iters: int, n_decode: int = 256, prefill: bool = True, token
         r["prefill_tflops"] = r["prefill_flops"] / (r["ms_mean"] * 1e-3) / 1e12
         return r
     if op in ("qk_norm_rope", "kv_append"):
-        return append_micro(iters, n_decode, tokens, fused=op == "qk_norm_rope")
+        r = append_micro(iters, n_decode, tokens, fused=op == "qk_norm_rope", stream=stream)
+        r["stream"] = stream
+        return r
     if op == "pack":
         return pack_micro(iters, n_decode, tokens)
     if op == "argmax":
-        return argmax_micro(iters, rows=max(1, n_decode + max(0, tokens - n_decode) // 512))
+        return argmax_micro(iters, rows=max(1, n_decode + max(0, tokens - n_decode) // 512),
+                            stream=stream)
     if op in ("add_rms_norm", "silu_mul"):
-        return rowwise_micro(op, iters, rows=max(1, tokens))
+        return rowwise_micro(op, iters, rows=max(1, tokens), stream=stream)
     raise ValueError(f"unknown op {op!r}; one of {OPS} or 'all'")
 
 
@@ -353,12 +416,15 @@ def main():
     ap.add_argument("--priors", default=None,
                     help="attention: comma-separated prior lengths, one 512-token prefill "
                          "chunk each (default: the operator case's 0,512,1536,3584)")
+    ap.add_argument("--stream", action="store_true",
+                    help="row kernels: graph-replayed back-to-back launches over input "
+                         "copies larger than L2, instead of single flushed launches")
     a = ap.parse_args()
     priors = None if a.priors is None else [int(x) for x in a.priors.split(",") if x]
     torch.cuda.set_device(0)
     for op in (OPS if a.op == "all" else (a.op,)):
         print(json.dumps(run_op(op, a.iters, a.decode, not a.no_prefill, a.tokens, a.ctx_lo,
-                                a.ctx_hi, priors)), flush=True)
+                                a.ctx_hi, priors, a.stream)), flush=True)
 
 
 if __name__ == "__main__":

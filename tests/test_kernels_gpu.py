@@ -225,10 +225,13 @@ def test_kv_append_many_tokens(dt):
     assert np.array_equal(cache.float().cpu().numpy(), want)
 
 
-def test_qk_norm_rope_bf16_many_tokens_vs_oracle():
-    """bf16 path over more tokens than CTAs (each CTA walks several tokens),
-    against the oracle's torch ops on the CPU: at most one bf16 ulp."""
-    T, Hq, Hkv, NB = 2500, 32, 8, 200
+@pytest.mark.parametrize("Hq,Hkv", [(32, 8), (40, 8)])
+def test_qk_norm_rope_bf16_many_tokens_vs_oracle(Hq, Hkv):
+    """bf16 path over more tokens than CTAs (each CTA walks several tokens, a
+    unit covering all passes of a token: 3 full passes of 16 head rows for
+    32/8 heads, 4 passes of which the last is half empty for 40/8), against
+    the oracle's torch ops on the CPU: at most one bf16 ulp."""
+    T, NB = 2500, 200
     g = torch.Generator(device=dev).manual_seed(5)
     qkv = torch.randn(T, (Hq + 2 * Hkv) * 128, device=dev, generator=g).to(torch.bfloat16)
     wq = (1 + 0.1 * torch.randn(128, device=dev, generator=g)).to(torch.bfloat16)
