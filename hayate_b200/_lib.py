@@ -39,7 +39,7 @@ SIGNATURES = {
     "hy_attention_workspace_size": (SZ, [I32, I32, I32]),
     "hy_attention_plan": (C.c_int, [P, P, I32, I32, I32, I32, P, SZ, P, P]),
     "hy_varlen_attention": (C.c_int, [I32, P, P, I32, I32, I32, P, I32, I32, I32, P, I32, P, P,
-                                      P, I32, F32, I32, I32, P, SZ, P, P]),
+                                      P, I32, F32, I32, I32, P, SZ, I32, P, P]),
     "hy_add_rms_norm": (C.c_int, [I32, P, I64, P, I64, I32, I32, P, F32, P, I64, P]),
     "hy_add_rms_norm_splitk": (C.c_int, [I32, P, I64, P, I32, I64, I64, I32, I32, P, F32, P,
                                          I64, P]),

@@ -53,22 +53,28 @@ HY_DEVICE void cta_best(float& bv, int& bi) {
 template <typename T> struct Scan;
 
 // bf16: 16-byte vectors of 8 elements.  A batch of AM_UNROLL vectors is reduced
-// with packed bf16x2 maxima that propagate NaN; only a batch whose maximum beats
-// the thread's best (rare after the first few) is searched for the first index
-// holding it.  A thread's batches come in increasing index order, so a strictly
-// better batch maximum keeps first-index ties.
+// with packed bf16x2 maxima that propagate NaN, and the stream keeps only the
+// thread's best value and the first batch that reached it (a thread's batches
+// come in increasing index order, so a strictly better batch maximum keeps
+// first-index ties).  That one batch is read again at the end (from L1/L2) and
+// searched for the first element holding the value, so the stream itself has
+// no data-dependent branch.
 template <> struct Scan<__nv_bfloat16> {
   static constexpr int N = 8;
+  static HY_DEVICE void load_batch(const __nv_bfloat16* x, int base, int v1, uint4 (&w)[AM_UNROLL]) {
+#pragma unroll
+    for (int u = 0; u < AM_UNROLL; ++u) {
+      const int vi = base + u * AM_THREADS;
+      // -inf pairs (0xff80) for vectors past the chunk: they never win
+      w[u] = vi < v1 ? __ldg(reinterpret_cast<const uint4*>(x) + vi)
+                     : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+    }
+  }
   static HY_DEVICE void run(const __nv_bfloat16* x, int v0, int v1, float& bv, int& bi) {
+    int best_base = -1;
     for (int base = v0 + threadIdx.x; base < v1; base += AM_THREADS * AM_UNROLL) {
       uint4 w[AM_UNROLL];
-#pragma unroll
-      for (int u = 0; u < AM_UNROLL; ++u) {
-        const int vi = base + u * AM_THREADS;
-        // -inf pairs (0xff80) for vectors past the chunk: they never win
-        w[u] = vi < v1 ? __ldg(reinterpret_cast<const uint4*>(x) + vi)
-                       : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
-      }
+      load_batch(x, base, v1, w);
       __nv_bfloat162 m = *reinterpret_cast<const __nv_bfloat162*>(&w[0].x);
 #pragma unroll
       for (int u = 0; u < AM_UNROLL; ++u) {
@@ -79,22 +85,24 @@ template <> struct Scan<__nv_bfloat16> {
       const float m0 = __low2float(m), m1 = __high2float(m);
       const float bm = (isnan(m0) || m1 != m1) ? NAN : fmaxf(m0, m1);
       // the thread's first batch, or a strictly better value (NaN beats numbers)
-      const bool take = bi == 0x7fffffff || (isnan(bm) ? !isnan(bv) : bm > bv);
-      if (take) {
-        bool found = false;
+      const bool take = best_base < 0 || (isnan(bm) ? !isnan(bv) : bm > bv);
+      bv = take ? bm : bv;
+      best_base = take ? base : best_base;
+    }
+    if (best_base < 0) return;
+    uint4 w[AM_UNROLL];
+    load_batch(x, best_base, v1, w);
+    bool found = false;
 #pragma unroll
-        for (int u = 0; u < AM_UNROLL; ++u) {
-          const __nv_bfloat16* e8 = reinterpret_cast<const __nv_bfloat16*>(&w[u]);
+    for (int u = 0; u < AM_UNROLL; ++u) {
+      const __nv_bfloat16* e8 = reinterpret_cast<const __nv_bfloat16*>(&w[u]);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float f = __bfloat162float(e8[e]);
-            const bool hit = isnan(bm) ? isnan(f) : (f == bm);
-            if (!found && hit) {
-              found = true;
-              bv = f;
-              bi = (base + u * AM_THREADS) * 8 + e;
-            }
-          }
+      for (int e = 0; e < 8; ++e) {
+        const float f = __bfloat162float(e8[e]);
+        const bool hit = isnan(bv) ? isnan(f) : (f == bv);
+        if (!found && hit) {
+          found = true;
+          bi = (best_base + u * AM_THREADS) * 8 + e;
         }
       }
     }
@@ -180,10 +188,20 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(
 cudaError_t hy_launch_argmax(int dtype, const void* logits, long ld, int rows, int V,
                              int32_t* out, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  // cluster size: enough CTAs for about 8 per SM over the whole grid
-  const int want = (148 * 8) / rows;
-  int C = 1;
-  while (C * 2 <= want && C * 2 <= AM_MAX_CLUSTER) C *= 2;
+  // cluster size: as many CTAs per row as keep the whole grid resident at once
+  // (a second, partial wave would run on a few SMs alone), at most 8
+  static int occ[2] = {0, 0};
+  const int k = dtype == 0 ? 0 : 1;
+  if (occ[k] == 0) {
+    int n = 0;
+    if (dtype == 0)
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, argmax_kernel<__nv_bfloat16>, AM_THREADS, 0);
+    else
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, argmax_kernel<float>, AM_THREADS, 0);
+    occ[k] = n > 0 ? n : 1;
+  }
+  const int want = (148 * occ[k]) / rows;
+  const int C = want < 1 ? 1 : (want > AM_MAX_CLUSTER ? AM_MAX_CLUSTER : want);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(rows * C));
   cfg.blockDim = dim3(AM_THREADS);

@@ -329,11 +329,67 @@ struct MainArgs {
   const int32_t* seq_lens_k;
   float scale_log2;
   int32_t* err;
+  int early;              // HY_ATTN_EARLY: start decode K/V loads before the grid wait
 };
 
 // Tensor-map row of (block, K or V, kv head).
 HY_DEVICE int kv_row(const MainArgs& a, int blk, int kv, int g) {
   return a.layer_row_base + ((blk * 2 + kv) * a.kv_heads + g) * HY_BLOCK;
+}
+
+// Issue the K and V tiles of physical block blk (KV head g) into ring stage s
+// (one lane).
+HY_DEVICE void dec_issue(const CUtensorMap* tiles, const MainArgs& a, uint8_t* ring,
+                         uint64_t* bars, int s, int blk, int g) {
+  int rk, rv;
+  if (blk < 0 || blk >= a.num_blocks) {
+    hy_flag(a.err, HY_ERR_BOUNDS);
+    rk = rv = a.oob_row;
+  } else {
+    rk = kv_row(a, blk, 0, g);
+    rv = kv_row(a, blk, 1, g);
+  }
+  uint8_t* st = ring + s * DEC_TILE_BYTES;
+  fence_proxy_async();
+  mbar_arrive_expect_tx(&bars[s], DEC_TILE_BYTES);
+  tma_load_3d(st, tiles, 0, rk, 0, &bars[s]);            // K: both halves, one box
+  tma_load_3d(st + 4096, tiles, 0, rv, 0, &bars[s]);     // V
+}
+
+// A decode item's plan record (item, sequence fields) and its cached block ids.
+struct DecRec {
+  int4 it, info, c0, c1;
+};
+
+HY_DEVICE void dec_load_rec(const PlanView& v, int item, uint64_t keep, DecRec& r) {
+  r.it = ld_keep(&v.dec[2 * item], keep);
+  r.info = ld_keep(&v.dec[2 * item + 1], keep);
+  r.c0 = ld_keep(&v.dec_ids[2 * item], keep);
+  r.c1 = ld_keep(&v.dec_ids[2 * item + 1], keep);
+}
+
+// Before the grid wait (HY_ATTN_EARLY): load the item's record and, if its
+// block ids are cached, start the ring's first loads of blocks that hold no
+// key of the step's query token (the kernel just before wrote only that key's
+// K/V).  Returns the stages issued.
+HY_DEVICE uint32_t decode_item_early(const CUtensorMap* tiles, const MainArgs& a,
+                                     const PlanView& v, int item, uint8_t* ring, uint64_t* bars,
+                                     DecRec& r) {
+  dec_load_rec(v, item, l2_keep_policy(), r);
+  if (r.c0.x < 0) return 0u;                    // ids not cached yet (warp-uniform)
+  const int g = r.it.y, b0 = r.it.z, n = r.it.w - r.it.z;
+  const int newest = (r.info.y - 1) / HY_BLOCK;   // the block of the query token's key
+  const int ids[DEC_STAGES] = {r.c0.y, r.c0.z, r.c0.w};
+  uint32_t mask = 0u;
+#pragma unroll
+  for (int s = 0; s < DEC_STAGES; ++s)
+    if (s < n && b0 + s < newest) mask |= 1u << s;
+  if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+    for (int s = 0; s < DEC_STAGES; ++s)
+      if ((mask >> s) & 1u) dec_issue(tiles, a, ring, bars, s, ids[s], g);
+  }
+  return mask;
 }
 
 // The attention of one decode item over its block range: on return lane
@@ -344,36 +400,22 @@ struct DecodeItemInfo {
   int seq, g, tok, ns, first;
 };
 
+// have_pre: pre is the record decode_item_early loaded, which issued the
+// stages in pre_issued.
 __device__ bool decode_item_core(const CUtensorMap* tiles, const MainArgs& a, const PlanView& v,
                                  int item, uint8_t* ring, uint64_t* bars, uint32_t& phase,
-                                 float (&o)[16][4], float& m, float& l, DecodeItemInfo& di) {
+                                 float (&o)[16][4], float& m, float& l, DecodeItemInfo& di,
+                                 DecRec pre, bool have_pre, uint32_t pre_issued) {
   const int lane = threadIdx.x & 31;
   const uint64_t keep = l2_keep_policy();
-  const int4 it = ld_keep(&v.dec[2 * item], keep);        // one 32-byte record
-  const int4 info = ld_keep(&v.dec[2 * item + 1], keep);
+  DecRec rec = pre;
+  if (!have_pre) dec_load_rec(v, item, keep, rec);   // one 32-byte record + the id cache
+  const int4 it = rec.it, info = rec.info, c0 = rec.c0, c1 = rec.c1;
   const int seq = it.x, g = it.y, b0 = it.z, b1 = it.w;
   const int tok = info.x, kv_len = info.y;
   di.seq = seq; di.g = g; di.tok = tok; di.ns = info.z; di.first = info.w;
-  const int4 c0 = ld_keep(&v.dec_ids[2 * item], keep);
-  const int4 c1 = ld_keep(&v.dec_ids[2 * item + 1], keep);
   const int n = b1 - b0;
-
-  // Issue the K and V tiles of logical block b into ring stage s (lane 0 only).
-  auto issue = [&](int s, int blk) {
-    int rk, rv;
-    if (blk < 0 || blk >= a.num_blocks) {
-      hy_flag(a.err, HY_ERR_BOUNDS);
-      rk = rv = a.oob_row;
-    } else {
-      rk = kv_row(a, blk, 0, g);
-      rv = kv_row(a, blk, 1, g);
-    }
-    uint8_t* st = ring + s * DEC_TILE_BYTES;
-    fence_proxy_async();
-    mbar_arrive_expect_tx(&bars[s], DEC_TILE_BYTES);
-    tma_load_3d(st, tiles, 0, rk, 0, &bars[s]);            // K: both halves, one box
-    tma_load_3d(st + 4096, tiles, 0, rv, 0, &bars[s]);     // V
-  };
+  auto issue = [&](int s, int blk) { dec_issue(tiles, a, ring, bars, s, blk, g); };
 
   // The block-table row and the ids of the ring's first blocks and the one
   // after: cached with the item by the plan's first attention launch (block
@@ -400,7 +442,7 @@ __device__ bool decode_item_core(const CUtensorMap* tiles, const MainArgs& a, co
   if (lane == 0) {
 #pragma unroll
     for (int s = 0; s < DEC_STAGES; ++s)
-      if (s < n) issue(s, first_ids[s]);
+      if (s < n && !((pre_issued >> s) & 1u)) issue(s, first_ids[s]);
   }
   int next_id = (lane == 0 && DEC_STAGES < n) ? first_ids[DEC_STAGES] : 0;
 
@@ -509,12 +551,15 @@ __device__ bool decode_item_core(const CUtensorMap* tiles, const MainArgs& a, co
 // writes its output; otherwise the partial goes to the workspace and the last
 // of the (seq, head)'s items to finish (an atomic count) merges all of them.
 __device__ bool decode_item(const CUtensorMap* tiles, const MainArgs& a, const PlanView& v,
-                            int item, uint8_t* ring, uint64_t* bars, uint32_t& phase) {
+                            int item, uint8_t* ring, uint64_t* bars, uint32_t& phase,
+                            DecRec pre, bool have_pre, uint32_t pre_issued) {
   const int lane = threadIdx.x & 31;
   float o[16][4];
   float m, l;
   DecodeItemInfo di;
-  if (!decode_item_core(tiles, a, v, item, ring, bars, phase, o, m, l, di)) return false;
+  if (!decode_item_core(tiles, a, v, item, ring, bars, phase, o, m, l, di, pre, have_pre,
+                        pre_issued))
+    return false;
   const int seq = di.seq, g = di.g, tok = di.tok, ns = di.ns, first = di.first;
   const int r = lane >> 2, c = 2 * (lane & 3);
   if (r < HY_GROUP) {
@@ -630,7 +675,8 @@ __device__ bool decode_item(const CUtensorMap* tiles, const MainArgs& a, const P
 // atomic count.  All ATT_WARPS decode warps of the CTA call this.
 __device__ bool decode_pair_cta(const CUtensorMap* tiles, const MainArgs& a, const PlanView& v,
                                 int pair, uint8_t* payload, uint64_t (*bars)[DEC_STAGES],
-                                uint32_t& phase) {
+                                uint32_t& phase, DecRec pre, bool have_pre,
+                                uint32_t pre_issued) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq = pair / a.kv_heads, g = pair - seq * a.kv_heads;
   const int2 si = v.seqinfo[seq];               // first decode item of the sequence, items per head
@@ -643,7 +689,8 @@ __device__ bool decode_pair_cta(const CUtensorMap* tiles, const MainArgs& a, con
     float o[16][4];
     float m, l;
     DecodeItemInfo di;
-    ok = decode_item_core(tiles, a, v, first + warp, ring, bars[warp], phase, o, m, l, di);
+    ok = decode_item_core(tiles, a, v, first + warp, ring, bars[warp], phase, o, m, l, di, pre,
+                          have_pre, pre_issued);
     const int r = lane >> 2, c = 2 * (lane & 3);
     if (ok && r < HY_GROUP) {
       if (ns == 1) {                            // the only split: final output
@@ -1000,6 +1047,36 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
+  const int lane = threadIdx.x & 31;
+  const int nw = (int)gridDim.x * ATT_WARPS;
+  // HY_ATTN_EARLY: the plan, the block tables and the item id cache were
+  // written at least two launches back, so a decode-only launch reads its
+  // items and starts the K/V loads of their older blocks now, while the kernel
+  // before it (which wrote only the query tokens and their keys) still runs.
+  DecRec pre_rec = {};
+  uint32_t pre_issued = 0u;
+  bool have_pre = false;
+  if (a.early && warp < ATT_WARPS) {
+    const uint64_t keep0 = l2_keep_policy();
+    const int e_pre = ld_keep(v.header, keep0), e_dec = ld_keep(v.header + 1, keep0);
+    const int e_pairs = ld_keep(v.header + 4, keep0);
+    int item = -1;
+    if (e_pairs > 0) {
+      if ((int)blockIdx.x < e_pairs) {
+        const int seq = (int)blockIdx.x / a.kv_heads, g = (int)blockIdx.x - seq * a.kv_heads;
+        const int2 si = v.seqinfo[seq];
+        if (warp < si.y) item = si.x + g * si.y + warp;
+      }
+    } else if (e_pre == 0 && e_dec <= nw) {
+      const int it = warp * (int)gridDim.x + (int)blockIdx.x;
+      if (it < e_dec) item = it;
+    }
+    if (item >= 0) {
+      pre_issued = decode_item_early(&kv_tiles, a, v, item, payload + warp * DEC_WARP_BYTES,
+                                     sh.dec_bar[warp], pre_rec);
+      have_pre = true;
+    }
+  }
   hy_grid_wait();
   hy_grid_trigger();
   const uint64_t keep = l2_keep_policy();
@@ -1026,16 +1103,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   // assigns them statically and skips the counters' round trips; item i goes
   // to CTA i % grid, so that a small batch spreads its TMA boxes over every
   // SM (an SM's TMA unit takes a 2 KB box about every 100 cycles).
-  const int lane = threadIdx.x & 31;
-  const int nw = (int)gridDim.x * ATT_WARPS;
   if (n_pairs > 0) {                            // one (sequence, KV head) pair per CTA
     if (warp < ATT_WARPS && (int)blockIdx.x < n_pairs)
-      ok = decode_pair_cta(&kv_tiles, a, v, blockIdx.x, payload, sh.dec_bar, dec_phase);
+      ok = decode_pair_cta(&kv_tiles, a, v, blockIdx.x, payload, sh.dec_bar, dec_phase, pre_rec,
+                           have_pre, pre_issued);
   } else if (n_pre == 0 && n_dec <= nw) {
     const int item = warp * (int)gridDim.x + (int)blockIdx.x;
     if (warp < ATT_WARPS && item < n_dec && ok)
       ok = decode_item(&kv_tiles, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
-                       dec_phase);
+                       dec_phase, pre_rec, have_pre, pre_issued);
   } else {
     while (ok && warp < ATT_WARPS) {
       int item = 0;
@@ -1043,7 +1119,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
       item = __shfl_sync(0xffffffffu, item, 0);
       if (item >= n_dec) break;
       ok = decode_item(&kv_tiles, a, v, item, payload + warp * DEC_WARP_BYTES, sh.dec_bar[warp],
-                       dec_phase);
+                       dec_phase, pre_rec, false, 0u);
     }
     __syncthreads();
     if (threadIdx.x == 0) {                     // the last CTA out resets the counters
@@ -1204,7 +1280,7 @@ cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const void* cache, const voi
                                 const int32_t* seq_bt_row, const int32_t* cu_q,
                                 const int32_t* seq_lens_k, int S, float scale,
                                 const PlanDims& d, void* ws, int32_t* err, int dev,
-                                cudaStream_t st) {
+                                cudaStream_t st, int flags) {
   static bool attr_set[64] = {false};
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(attn_main_kernel,
@@ -1232,6 +1308,7 @@ cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const void* cache, const voi
   a.seq_lens_k = seq_lens_k;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.err = err;
+  a.early = (flags & HY_ATTN_EARLY) != 0;
   const PlanView v = make_view(ws, d);
   const int grid = device_sms(dev) * g_ctas_per_sm[dev < 64 && dev >= 0 ? dev : 0];
   return hy_launch(attn_main_kernel, dim3(grid), dim3(ATT_THREADS), SMEM_BYTES, st, maps.halves,

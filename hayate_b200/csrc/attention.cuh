@@ -6,6 +6,10 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#ifndef HY_ATTN_EARLY
+#define HY_ATTN_EARLY 1       /* the public header's attention flag */
+#endif
+
 // Tensor maps over the bf16 KV cache viewed as rows of 128 elements (256 B):
 //   halves: 2-D, box = 16 rows x 64 columns (one half of a block's head tile)
 //   tiles:  3-D (64 columns, rows, 2 halves 128 B apart), box = 16 rows x both
@@ -58,7 +62,7 @@ cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const void* cache, const voi
                                 const int32_t* seq_bt_row, const int32_t* cu_q,
                                 const int32_t* seq_lens_k, int S, float scale,
                                 const PlanDims& d, void* ws, int32_t* err, int dev,
-                                cudaStream_t st);
+                                cudaStream_t st, int flags = 0);
 cudaError_t hy_launch_attn_fp32(const float* q, float* out, int T, int q_heads, int kv_heads,
                                 const float* cache_layer, int num_blocks,
                                 const int32_t* block_tables, int bt_pitch,

@@ -320,8 +320,9 @@ int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tok
                         const int32_t* seq_bt_row, const int32_t* cu_seqlens_q,
                         const int32_t* seq_lens_k, int32_t num_seqs, float scale,
                         int32_t max_seqs, int32_t max_tokens, void* workspace,
-                        size_t workspace_bytes, int32_t* err, void* stream) {
+                        size_t workspace_bytes, int32_t flags, int32_t* err, void* stream) {
   if (!dtype_ok(dtype)) return fail(HY_E_INVALID, "hy_varlen_attention: dtype must be 0 or 1");
+  if ((flags & ~HY_ATTN_EARLY) != 0) return fail(HY_E_INVALID, "hy_varlen_attention: unknown flags");
   if (!q || !out || !kv_cache || !block_tables || !cu_seqlens_q || !seq_lens_k ||
       num_seqs <= 0 || num_tokens < 0 || num_layers <= 0 || num_blocks <= 0 || layer < 0 ||
       layer >= num_layers || bt_pitch <= 0)
@@ -352,7 +353,8 @@ int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tok
   return cuda_result(
       hy_launch_attn_bf16(map, kv_cache, q, out, q_heads, kv_heads, (int)(layer * layer_rows), (int)rows,
                           num_blocks, block_tables, bt_pitch, seq_bt_row, cu_seqlens_q,
-                          seq_lens_k, num_seqs, scale, d, workspace, err, dev, as_stream(stream)),
+                          seq_lens_k, num_seqs, scale, d, workspace, err, dev, as_stream(stream),
+                          flags),
       "hy_varlen_attention(bf16)");
 }
 

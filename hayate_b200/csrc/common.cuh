@@ -165,6 +165,14 @@ HY_DEVICE void fence_mbar_init() {
 }
 
 // ---------------------------------------------------------------- TMA
+// Untiled bulk copy global -> this CTA's shared memory, completion counted on
+// `bar` (both addresses 16-byte aligned, bytes a multiple of 16; no multicast).
+HY_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
 // 2-D tiled tensor load into shared memory, completion counted on `bar`.
 // No multicast: every CTA loads its own tiles.
 HY_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {

@@ -184,6 +184,127 @@ __global__ void __launch_bounds__(THREADS) add_rms_norm_kernel(
   }
 }
 
+// Prefill-sized bf16 residual add + RMSNorm, streamed: a persistent grid whose
+// warps take one row at a time (row r of warp gw = gw + k x all warps).  A
+// warp's rows arrive in its two-stage shared-memory ring by bulk copies (x and
+// delta, 2 x cols x 2 bytes), issued two rows ahead, so every warp keeps a
+// row in flight while it works on another and no registers hold the loads.
+// The sum x + delta is rounded, written to x and kept in the ring (over the x
+// row) for the second pass after the warp's sum of squares; the weights sit in
+// shared memory, loaded once per CTA.  Rounding points are those of
+// add_rms_norm_kernel, with packed f32x2 arithmetic (each lane rounded as the
+// scalar operation); only the order of the sum of squares differs.
+constexpr int RNB_WARPS = 8;
+constexpr int RNB_STAGES = 2;
+constexpr int RNB_MIN_ROWS = 256;                 // fewer rows: one CTA per row
+constexpr int RNB_MAX_SMEM = 200 * 1024;
+
+HY_DEVICE float2 bf2_to_f2(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+}
+HY_DEVICE uint32_t f2_to_bf2(float2 f) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(f.x, f.y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <bool DELTA>
+__global__ void __launch_bounds__(RNB_WARPS * 32) add_rms_norm_bulk_kernel(
+    __nv_bfloat16* __restrict__ x, long ldx, const __nv_bfloat16* __restrict__ delta, long ldd,
+    int rows, int cols, const __nv_bfloat16* __restrict__ w, float eps,
+    __nv_bfloat16* __restrict__ y, long ldy, int32_t* err) {
+  extern __shared__ __align__(128) uint8_t rnb_smem[];
+  __shared__ uint64_t bars[RNB_WARPS][RNB_STAGES];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row_bytes = cols * 2;
+  const int stage_bytes = row_bytes * (DELTA ? 2 : 1);
+  const int nvec = cols / 8;
+  uint4* ws = reinterpret_cast<uint4*>(rnb_smem);                 // the weights
+  uint8_t* ring = rnb_smem + row_bytes + (size_t)warp * RNB_STAGES * stage_bytes;
+  if (lane == 0) {
+    for (int s = 0; s < RNB_STAGES; ++s) mbar_init(&bars[warp][s], 1);
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < nvec; i += RNB_WARPS * 32)        // no earlier kernel's output
+    ws[i] = reinterpret_cast<const uint4*>(w)[i];
+  __syncthreads();
+  hy_grid_wait();
+  hy_grid_trigger();
+  const int gw = (int)blockIdx.x * RNB_WARPS + warp, GW = (int)gridDim.x * RNB_WARPS;
+  auto issue = [&](int s, int r) {                // lane 0
+    uint8_t* st = ring + s * stage_bytes;
+    mbar_arrive_expect_tx(&bars[warp][s], stage_bytes);
+    bulk_load(st, x + (size_t)r * ldx, row_bytes, &bars[warp][s]);
+    if (DELTA) bulk_load(st + row_bytes, delta + (size_t)r * ldd, row_bytes, &bars[warp][s]);
+  };
+  uint32_t pend = 0;                              // stages with a copy in flight
+  if (lane == 0)
+    for (int s = 0; s < RNB_STAGES; ++s)
+      if (gw + s * GW < rows) issue(s, gw + s * GW);
+  for (int s = 0; s < RNB_STAGES; ++s)
+    if (gw + s * GW < rows) pend |= 1u << s;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int i = 0, r = gw; r < rows; ++i, r += GW) {
+    const int s = i % RNB_STAGES;
+    if (!mbar_wait(&bars[warp][s], (phase >> s) & 1u, err)) { ok = false; break; }
+    phase ^= 1u << s;
+    pend &= ~(1u << s);
+    uint4* xs = reinterpret_cast<uint4*>(ring + s * stage_bytes);
+    const uint4* ds = reinterpret_cast<const uint4*>(ring + s * stage_bytes + row_bytes);
+    uint4* xg = reinterpret_cast<uint4*>(x + (size_t)r * ldx);
+    float2 ss2 = make_float2(0.f, 0.f);
+    for (int vi = lane; vi < nvec; vi += 32) {
+      uint4 xv = xs[vi];
+      if (DELTA) {
+        const uint4 dv = ds[vi];
+        const uint32_t* xa = &xv.x;
+        const uint32_t* da = &dv.x;
+        uint4 o;
+        uint32_t* oa = &o.x;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) oa[q] = f2_to_bf2(__fadd2_rn(bf2_to_f2(da[q]), bf2_to_f2(xa[q])));
+        xv = o;
+        xg[vi] = xv;
+        xs[vi] = xv;
+      }
+      const uint32_t* va = &xv.x;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 v = bf2_to_f2(va[q]);
+        ss2 = __fadd2_rn(ss2, __fmul2_rn(v, v));
+      }
+    }
+    float ss = __fadd_rn(ss2.x, ss2.y);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
+    const float2 rs2 = make_float2(rstd, rstd);
+    uint4* yg = reinterpret_cast<uint4*>(y + (size_t)r * ldy);
+    for (int vi = lane; vi < nvec; vi += 32) {
+      const uint4 xv = xs[vi], wv = ws[vi];
+      const uint32_t* va = &xv.x;
+      const uint32_t* wa = &wv.x;
+      uint4 o;
+      uint32_t* oa = &o.x;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        oa[q] = f2_to_bf2(__fmul2_rn(__fmul2_rn(bf2_to_f2(va[q]), rs2), bf2_to_f2(wa[q])));
+      yg[vi] = o;
+    }
+    fence_proxy_async();                          // this lane's ring writes before the next copy
+    __syncwarp();
+    const int rn = r + RNB_STAGES * GW;
+    if (rn < rows) {
+      if (lane == 0) issue(s, rn);
+      pend |= 1u << s;
+    }
+  }
+  if (!ok) {                                      // let the copies in flight land before exit
+    for (int s = 0; s < RNB_STAGES; ++s)
+      if ((pend >> s) & 1u) mbar_wait(&bars[warp][s], (phase >> s) & 1u, nullptr);
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) silu_mul_kernel(
     const T* __restrict__ gu, long ld, int rows, int inter, T* __restrict__ y, long ldy) {
@@ -237,6 +358,34 @@ static cudaError_t launch_add_rms_norm(void* x, long ldx, const void* delta, lon
 // delta (model dtype) or parts (fp32, nparts x rows, pstride apart) -- at most
 // one of them -- with row pitch ldd.  With x_rows, output row r reads residual
 // row x_rows[r] (< x_nrows) and writes the updated residual to x_out.
+// The streamed kernel for a prefill-sized bf16 add + RMSNorm (rows and row
+// pitches 16-byte aligned, which the C ABI checks).
+static cudaError_t launch_add_rms_norm_bulk(void* x, long ldx, const void* delta, long ldd,
+                                            int rows, int cols, const void* w, float eps, void* y,
+                                            long ldy, int32_t* err, cudaStream_t st) {
+  using B = __nv_bfloat16;
+  const int row_bytes = cols * 2;
+  const int smem = row_bytes + RNB_WARPS * RNB_STAGES * row_bytes * (delta ? 2 : 1);
+  static bool attr[2] = {false, false};
+  static int occ[2] = {0, 0};
+  const int k = delta ? 1 : 0;
+  auto kern = delta ? add_rms_norm_bulk_kernel<true> : add_rms_norm_bulk_kernel<false>;
+  if (!attr[k]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         RNB_MAX_SMEM + 4096);
+    if (e != cudaSuccess) return e;
+    attr[k] = true;
+  }
+  int n = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, RNB_WARPS * 32, smem);
+  occ[k] = n > 0 ? n : 1;
+  const long warps = 148L * occ[k] * RNB_WARPS;
+  const long want = (rows + 1) / 2;               // two rows per warp at least
+  const long ctas = ((want < warps ? want : warps) + RNB_WARPS - 1) / RNB_WARPS;
+  return hy_launch(kern, dim3((unsigned)ctas), dim3(RNB_WARPS * 32), smem, st, (B*)x, ldx,
+                   (const B*)delta, ldd, rows, cols, (const B*)w, eps, (B*)y, ldy, err);
+}
+
 cudaError_t hy_launch_add_rms_norm(int dtype, void* x, long ldx, const void* delta, long ldd,
                                    int rows, int cols, const void* w, float eps, void* y,
                                    long ldy, const float* parts, int nparts, long pstride,
@@ -244,6 +393,9 @@ cudaError_t hy_launch_add_rms_norm(int dtype, void* x, long ldx, const void* del
                                    void* x_out, long ldxo, int32_t* err) {
   if (rows <= 0) return cudaSuccess;
   using B = __nv_bfloat16;
+  if (dtype == 0 && !x_rows && !parts && rows >= RNB_MIN_ROWS && cols % 8 == 0 &&
+      cols * 2 + RNB_WARPS * RNB_STAGES * cols * 2 * (delta ? 2 : 1) <= RNB_MAX_SMEM)
+    return launch_add_rms_norm_bulk(x, ldx, delta, ldd, rows, cols, w, eps, y, ldy, err, st);
   if (x_rows)
     return dtype == 0 ? launch_add_rms_norm<B, true>(x, ldx, delta, ldd, rows, cols, w, eps, y,
                                                      ldy, parts, nparts, pstride, x_rows,

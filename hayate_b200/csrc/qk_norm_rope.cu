@@ -141,6 +141,14 @@ HY_DEVICE void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   }
 }
 
+HY_DEVICE float2 bf2_to_f2(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+}
+HY_DEVICE uint32_t f2_to_bf2(float2 f) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(f.x, f.y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 HY_DEVICE uint4 f32_to_bf16x8(const float (&f)[8]) {
   uint4 u;
   __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
@@ -178,7 +186,7 @@ HY_DEVICE void qnr_load(QnrUnit<NPC>& u, int t, int g, int T_tokens, int heads, 
 }
 
 template <int NPC>
-__global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
+__global__ void __launch_bounds__(QNR_THREADS, NPC >= 4 ? 2 : 3) qk_norm_rope_bf16_kernel(
     const __nv_bfloat16* __restrict__ qkv, int ld, int T_tokens, int q_heads, int kv_heads,
     const int32_t* __restrict__ positions, const __nv_bfloat16* __restrict__ q_w,
     const __nv_bfloat16* __restrict__ k_w, const float* __restrict__ rope_cos,
@@ -232,37 +240,45 @@ __global__ void __launch_bounds__(QNR_THREADS) qk_norm_rope_bf16_kernel(
       // heads or past the end) skips the norm; otherwise all its lanes run it
       // for the shuffles
       if (__all_sync(0xffffffffu, !valid || h >= q_heads + kv_heads)) continue;
-      float x[8];
-      bf16x8_to_f32(raw, x);
-      float ss = 0.f;
+      // packed f32x2 arithmetic: each lane of a pair rounded as the scalar op
+      const uint32_t* xr = &raw.x;
+      float2 ss2 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
+      for (int q = 0; q < 4; ++q) {
+        const float2 v = bf2_to_f2(xr[q]);
+        ss2 = __fadd2_rn(ss2, __fmul2_rn(v, v));
+      }
+      float ss = __fadd_rn(ss2.x, ss2.y);
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
       // mean = ss / 128 exactly (a power of two)
       const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / HY_HEAD_DIM), eps)));
-      float w[8];
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(((h < q_heads) ? q_w : k_w) + d0), w);
-      float y[8];
+      const float2 rs2 = make_float2(rstd, rstd);
+      const uint4 wraw = *reinterpret_cast<const uint4*>(((h < q_heads) ? q_w : k_w) + d0);
+      const uint32_t* wr = &wraw.x;
+      uint4 yb;                                   // y = bf16((x * rstd) * w)
+      uint32_t* yr = &yb.x;
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        y[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], rstd), w[e])));
-      const uint4 yb = f32_to_bf16x8(y);          // exact: y is already bf16-valued
+      for (int q = 0; q < 4; ++q)
+        yr[q] = f2_to_bf2(__fmul2_rn(__fmul2_rn(bf2_to_f2(xr[q]), rs2), bf2_to_f2(wr[q])));
       uint4 pb;
       pb.x = __shfl_xor_sync(0xffffffffu, yb.x, 8);
       pb.y = __shfl_xor_sync(0xffffffffu, yb.y, 8);
       pb.z = __shfl_xor_sync(0xffffffffu, yb.z, 8);
       pb.w = __shfl_xor_sync(0xffffffffu, yb.w, 8);
-      float p[8];
-      bf16x8_to_f32(pb, p);
-      float o[8];
+      const uint32_t* pr = &pb.x;
+      uint4 ob;                                   // lower: y*cos + (-y[d+64])*sin; upper: y*cos + y[d-64]*sin
+      uint32_t* orr = &ob.x;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {               // lower: y*cos + (-y[d+64])*sin; upper: y*cos + y[d-64]*sin
-        const float pe = upper ? p[e] : -p[e];
-        o[e] = __fadd_rn(__fmul_rn(y[e], cs[e]), __fmul_rn(pe, sn[e]));
+      for (int q = 0; q < 4; ++q) {
+        const float2 yv = bf2_to_f2(yr[q]);
+        float2 pe = bf2_to_f2(pr[q]);
+        if (!upper) pe = make_float2(-pe.x, -pe.y);
+        const float2 c2 = make_float2(cs[2 * q], cs[2 * q + 1]);
+        const float2 s2 = make_float2(sn[2 * q], sn[2 * q + 1]);
+        orr[q] = f2_to_bf2(__fadd2_rn(__fmul2_rn(yv, c2), __fmul2_rn(pe, s2)));
       }
       if (!valid || h >= q_heads + kv_heads) continue;
-      const uint4 ob = f32_to_bf16x8(o);
       if (h < q_heads) {
         if (q_out) *reinterpret_cast<uint4*>(q_out + ((size_t)t * q_heads + h) * HY_HEAD_DIM + d0) = ob;
       } else {

@@ -15,6 +15,7 @@ from . import _lib
 from ._lib import check
 
 DEV_BOUNDS, DEV_TIMEOUT, DEV_POOL, DEV_PLAN = 1, 2, 4, 8
+ATTN_EARLY = 1                      # hy_varlen_attention flag HY_ATTN_EARLY
 DTYPES = {torch.bfloat16: 0, torch.float32: 1}
 
 
@@ -161,8 +162,11 @@ def varlen_attention(q: torch.Tensor, out: torch.Tensor, kv_cache: torch.Tensor,
                      block_tables: torch.Tensor, cu_seqlens_q: torch.Tensor,
                      seq_lens_k: torch.Tensor, num_seqs: int, max_seqs: int, max_tokens: int,
                      workspace: Optional[torch.Tensor], seq_bt_row: Optional[torch.Tensor] = None,
-                     scale: Optional[float] = None, err: Optional[torch.Tensor] = None) -> None:
-    """kv_cache: [layers][blocks][2][kv_heads][16][128]; q/out: [tokens][q_heads][128]."""
+                     scale: Optional[float] = None, err: Optional[torch.Tensor] = None,
+                     early: bool = False) -> None:
+    """kv_cache: [layers][blocks][2][kv_heads][16][128]; q/out: [tokens][q_heads][128].
+    ``early``: HY_ATTN_EARLY (the plan, block tables and older cache entries were
+    written at least two launches back and this is not the plan's first call)."""
     T, q_heads, D = q.shape
     L, NB, two, kv_heads, bs, D2 = kv_cache.shape
     if (two, bs, D, D2) != (2, 16, 128, 128):
@@ -175,7 +179,7 @@ def varlen_attention(q: torch.Tensor, out: torch.Tensor, kv_cache: torch.Tensor,
         _dt(q), _ptr(q), _ptr(out), T, q_heads, kv_heads, _ptr(kv_cache), L, NB, layer,
         _ptr(block_tables), block_tables.shape[1], _ptr(seq_bt_row), _ptr(cu_seqlens_q),
         _ptr(seq_lens_k), num_seqs, float(scale), max_seqs, max_tokens, _ptr(workspace),
-        ws_bytes, _ptr(err), _stream()), "hy_varlen_attention")
+        ws_bytes, ATTN_EARLY if early else 0, _ptr(err), _stream()), "hy_varlen_attention")
 
 
 def add_rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float,

@@ -223,9 +223,11 @@ class Runner:
             launches += 1
             if last and n_sample == 0:
                 break                       # K/V appended; nothing samples this step
+            # from the second layer on, the plan, the block tables and the item id
+            # cache are at least two launches old: decode loads may start early
             K.varlen_attention(q, attn, self.kv_cache, l, self.block_tables, cu_q, kv_lens, S,
                                ecfg.max_num_seqs, ecfg.max_batched_tokens, self.ws,
-                               seq_bt_row=slots, err=err)
+                               seq_bt_row=slots, err=err, early=l > 0)
             launches += 1
             a2 = attn.view(T, Hq * D)
             nxt = self.final_norm if last else self.layers[l + 1].ln1

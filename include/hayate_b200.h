@@ -46,6 +46,8 @@ extern "C" {
 #define HY_DTYPE_BF16 0
 #define HY_DTYPE_FP32 1
 
+#define HY_ATTN_EARLY 1       /* hy_varlen_attention flag, see there */
+
 /* Library version (major*10000 + minor*100 + patch). */
 int hy_version(void);
 
@@ -150,6 +152,13 @@ int hy_attention_plan(const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, in
  * caches each decode item's block-table row and first block ids in the
  * workspace for the later calls: block_tables and seq_bt_row must not change
  * between a plan and the last call that uses it.
+ * flags: 0, or HY_ATTN_EARLY when the plan, the block tables and the cache
+ * (but for the keys and values of this call's query tokens) were written at
+ * least two launches before this one on the stream, and the call is not the
+ * plan's first.  A decode-only bf16 launch then reads its work items and starts
+ * loading the K/V of older blocks before it waits for the kernel just before
+ * it (programmatic dependent launch), overlapping that kernel's tail.  An
+ * engine step meets this from its second layer on.
  * Replaces: cat + F.scaled_dot_product_attention(attn_mask, enable_gqa=True),
  * hayate/model/attention.py:52-64. */
 int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tokens,
@@ -159,7 +168,7 @@ int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tok
                         const int32_t* seq_bt_row, const int32_t* cu_seqlens_q,
                         const int32_t* seq_lens_k, int32_t num_seqs, float scale,
                         int32_t max_seqs, int32_t max_tokens, void* workspace,
-                        size_t workspace_bytes, int32_t* err, void* stream);
+                        size_t workspace_bytes, int32_t flags, int32_t* err, void* stream);
 
 /* Plan + bf16 attention in one call, with no caller workspace: for callers
  * that cannot allocate device memory where they call the kernel (a plugin or

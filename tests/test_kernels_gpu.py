@@ -225,12 +225,13 @@ def test_kv_append_many_tokens(dt):
     assert np.array_equal(cache.float().cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("Hq,Hkv", [(32, 8), (40, 8)])
+@pytest.mark.parametrize("Hq,Hkv", [(32, 8), (48, 12)])
 def test_qk_norm_rope_bf16_many_tokens_vs_oracle(Hq, Hkv):
-    """bf16 path over more tokens than CTAs (each CTA walks several tokens, a
-    unit covering all passes of a token: 3 full passes of 16 head rows for
-    32/8 heads, 4 passes of which the last is half empty for 40/8), against
-    the oracle's torch ops on the CPU: at most one bf16 ulp."""
+    """bf16 path over more tokens than CTAs (each CTA walks several tokens):
+    for 32/8 heads a unit covers a token's 3 passes of 16 head rows; for 48/12
+    (72 rows) a token is two units of up to 4 passes, the second holding one
+    half-empty pass.  Against the oracle's torch ops on the CPU: at most one
+    bf16 ulp."""
     T, NB = 2500, 200
     g = torch.Generator(device=dev).manual_seed(5)
     qkv = torch.randn(T, (Hq + 2 * Hkv) * 128, device=dev, generator=g).to(torch.bfloat16)
@@ -324,6 +325,55 @@ def test_attention_bf16_vs_fp32_reference(name):
     want = reference_attention(b)
     err = (got.float() - want).abs().max().item()
     assert err <= 2e-2, f"max abs err {err}"
+
+
+EARLY_CASES = {
+    # one (sequence, KV head) pair per CTA
+    "per_cta": CASES["decode_per_cta"],
+    # 60 short contexts: 480 items, one round of warps assigned statically
+    "static": ([1] * 60, [(7 * i) % 64 + 1 for i in range(60)]),
+    # the split-K path with dynamic item pulls (the flag leaves it unchanged)
+    "split_k": CASES["decode_per_cta_over"],
+}
+
+
+@pytest.mark.parametrize("name", list(EARLY_CASES))
+def test_attention_early_start_matches_plain_launch(name):
+    """HY_ATTN_EARLY, as an engine step uses it from its second layer on: the
+    plan's first call (layer 0) caches the item ids; the launch just before the
+    flagged call appends the step's new keys and values (each sequence's last
+    position, as QK-norm+RoPE does); the flagged call must give the plain
+    call's output bit for bit, within 2e-2 of fp32 attention over the updated
+    cache."""
+    q_lens, kv_lens = EARLY_CASES[name]
+    b = random_paged_batch(q_lens, kv_lens, kv_heads=8, seed=sum(map(ord, name)), layer=1)
+    S, T, NB = b["S"], b["T"], b["cache"].shape[1]
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = torch.zeros(K.attention_workspace_size(S, T, 8), dtype=torch.uint8, device=dev)
+    K.attention_plan(b["cu"], b["kv"], S, 8, S, T, ws, err)
+    out0 = torch.empty_like(b["q"])
+    K.varlen_attention(b["q"], out0, b["cache"], 0, b["bt"], b["cu"], b["kv"], S, S, T, ws,
+                       err=err)
+    g = torch.Generator(device=dev).manual_seed(7)
+    newk = torch.randn(T, 8, 128, device=dev, generator=g).to(torch.bfloat16)
+    newv = torch.randn(T, 8, 128, device=dev, generator=g).to(torch.bfloat16)
+    last = [kv - 1 for kv in kv_lens]
+    slots = torch.tensor([int(b["bt"][i, p // 16]) * 16 + p % 16 for i, p in enumerate(last)],
+                         dtype=torch.int32, device=dev)
+    outs = []
+    for early in (False, True):
+        out = torch.full_like(b["q"], float("nan"))
+        K.kv_append(newk, newv, slots, b["cache"][1], NB, err=err)
+        K.varlen_attention(b["q"], out, b["cache"], 1, b["bt"], b["cu"], b["kv"], S, S, T, ws,
+                           err=err, early=early)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, K.describe_error(int(err.item()))
+    assert torch.equal(outs[0], outs[1])
+    for i, p in enumerate(last):
+        b["ctx_k"][i][p] = newk[i]
+        b["ctx_v"][i][p] = newv[i]
+    assert (outs[1].float() - reference_attention(b)).abs().max().item() <= 2e-2
 
 
 def test_attention_bf16_block_table_indirection_and_headroom():
@@ -467,9 +517,13 @@ def _ulp_diff_bf16(a, b):
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("cols", [2560, 256, 4096, 1000])
 @pytest.mark.parametrize("residual", [False, True])
-def test_add_rms_norm_vs_reference(dt, cols, residual):
-    x = (torch.randn(37, cols, device=dev) * 3).to(dt)
-    delta = (torch.randn(37, cols, device=dev) * 3).to(dt) if residual else None
+@pytest.mark.parametrize("rows", [37, 3000])
+def test_add_rms_norm_vs_reference(dt, cols, residual, rows):
+    """37 rows: one CTA per row; 3000 bf16 rows: the streamed kernel (warps
+    fed by bulk copies), except for 4096 columns with a residual, whose ring
+    would not fit shared memory."""
+    x = (torch.randn(rows, cols, device=dev) * 3).to(dt)
+    delta = (torch.randn(rows, cols, device=dev) * 3).to(dt) if residual else None
     w = (1 + 0.1 * torch.randn(cols, device=dev)).to(dt)
     want_x = x + delta if residual else x.clone()      # block.py:24,30 residual add
     want = R.rms_norm(want_x, w, 1e-6)                  # nn.RMSNorm semantics (F.rms_norm)
@@ -481,6 +535,25 @@ def test_add_rms_norm_vs_reference(dt, cols, residual):
         assert d.max().item() <= 1 and (d > 0).float().mean().item() < 0.02
     else:
         torch.testing.assert_close(got, want, rtol=2e-6, atol=2e-6)
+
+
+def test_add_rms_norm_streamed_strided_rows():
+    """The streamed kernel on rows of wider tensors (row pitches 2624 and 2688
+    for 2560 columns), a row count that leaves the last warps one row short."""
+    rows, cols = 1187, 2560
+    xb = (torch.randn(rows, cols + 64, device=dev) * 3).to(torch.bfloat16)
+    db = (torch.randn(rows, cols + 128, device=dev) * 3).to(torch.bfloat16)
+    x, delta = xb[:, :cols], db[:, 64:64 + cols]
+    w = (1 + 0.1 * torch.randn(cols, device=dev)).to(torch.bfloat16)
+    want_x = x + delta
+    want = R.rms_norm(want_x, w, 1e-6)
+    pad = xb[:, cols:].clone()
+    got = K.add_rms_norm(x, w, 1e-6, delta=delta)
+    torch.cuda.synchronize()
+    assert torch.equal(x, want_x)
+    assert torch.equal(xb[:, cols:], pad)               # nothing written past the rows
+    d = _ulp_diff_bf16(got, want)
+    assert d.max().item() <= 1 and (d > 0).float().mean().item() < 0.02
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
