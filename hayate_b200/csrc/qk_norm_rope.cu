@@ -293,6 +293,195 @@ __global__ void __launch_bounds__(QNR_THREADS, NPC >= 4 ? 2 : 3) qk_norm_rope_bf
   }
 }
 
+// The bf16 path for prefill-sized batches: a head row is 8 lanes x 16
+// elements (two 16-byte vectors per lane), so the per-row work that does not
+// scale with the elements (the reciprocal square root, the reduction, the
+// addressing) is spread over 4 rows per warp; the CTA's consumer warps (8 x
+// heads threads, rounded up to whole warps, at most 384: 48 head rows) cover
+// every head row of one token per iteration.  A producer warp streams the
+// CTA's tokens (one grid stride apart) into a QNR_NS-stage shared-memory ring
+// by bulk copies: each stage holds a token's whole qkv row and its cos and sin
+// table rows (the producer reads 32 tokens' positions at once), so several
+// tokens are in flight without holding registers and the consumers make no
+// dependent global load.  A thread's head row is the same for every token, so its
+// norm weights are loaded once.  The RoPE partner of element d (d +- 64) is 4
+// lanes away.  Rounding points are those of the kernel above, except that the
+// sum of squares is accumulated with fused multiply-adds (its order already
+// differs from the reference's).
+constexpr int QNR_LPR = 8;                        // lanes per head row
+constexpr int QNR_ROWS_MAX_THREADS = 384;         // consumer threads: up to 48 head rows
+constexpr int QNR_NS = 4;                         // ring stages (qkv rows of tokens)
+
+__global__ void __launch_bounds__(QNR_ROWS_MAX_THREADS + 32, 2) qk_norm_rope_rows_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int ld, int T_tokens, int q_heads, int kv_heads,
+    const int32_t* __restrict__ positions, const __nv_bfloat16* __restrict__ q_w,
+    const __nv_bfloat16* __restrict__ k_w, const float* __restrict__ rope_cos,
+    const float* __restrict__ rope_sin, int max_pos, float eps, __nv_bfloat16* __restrict__ q_out,
+    __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ cache,
+    const int32_t* __restrict__ slot_mapping, int num_blocks, int32_t* err) {
+  extern __shared__ __align__(128) uint8_t qnr_ring[];
+  __shared__ uint64_t full[QNR_NS], empty[QNR_NS];
+  const int heads = q_heads + 2 * kv_heads;
+  const int row_bytes = heads * HY_HEAD_DIM * 2;
+  const int stage_bytes = row_bytes + 2 * 64 * 4;   // qkv row, cos row, sin row
+  const int n_cons = (int)blockDim.x - 32;        // consumer threads
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grid = (int)gridDim.x;
+  const int ntok = T_tokens > (int)blockIdx.x ? (T_tokens - (int)blockIdx.x + grid - 1) / grid : 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < QNR_NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], n_cons / 32);          // one arrival per consumer warp
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if ((int)threadIdx.x >= n_cons) {               // the producer warp
+    hy_grid_wait();
+    hy_grid_trigger();
+    int i = 0;
+    bool ok = true;
+    while (ok && i < ntok) {
+      // the positions of the next 32 tokens, one per lane (a bad one flags the
+      // error and reads table row 0)
+      int pl = 0;
+      if (i + lane < ntok) {
+        pl = positions[(int)blockIdx.x + (i + lane) * grid];
+        if (pl < 0 || pl >= max_pos) { hy_flag(err, HY_ERR_BOUNDS); pl = 0; }
+      }
+      for (int k = 0; k < 32 && i < ntok; ++k, ++i) {
+        const int pos = __shfl_sync(0xffffffffu, pl, k);
+        const int s = i % QNR_NS;
+        int w_ok = 1;
+        if (lane == 0 && i >= QNR_NS) w_ok = mbar_wait(&empty[s], ((i / QNR_NS) - 1) & 1, err);
+        if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
+        if (lane == 0) {
+          const int t = (int)blockIdx.x + i * grid;
+          uint8_t* st = qnr_ring + s * stage_bytes;
+          mbar_arrive_expect_tx(&full[s], stage_bytes);
+          bulk_load(st, qkv + (size_t)t * ld, row_bytes, &full[s]);
+          bulk_load(st + row_bytes, rope_cos + (size_t)pos * 64, 256, &full[s]);
+          bulk_load(st + row_bytes + 256, rope_sin + (size_t)pos * 64, 256, &full[s]);
+        }
+      }
+    }
+    // the last copies issued land before the CTA may exit
+    if (lane == 0)
+      for (int j = i > QNR_NS ? i - QNR_NS : 0; j < i; ++j)
+        mbar_wait(&full[j % QNR_NS], (j / QNR_NS) & 1, nullptr);
+    return;
+  }
+  const int h = threadIdx.x / QNR_LPR, l = threadIdx.x % QNR_LPR;
+  const bool valid = h < heads;
+  const bool is_v = valid && h >= q_heads + kv_heads;
+  const bool is_q = h < q_heads;
+  const bool normed = valid && !is_v;
+  // a warp (4 rows) with no query or key row skips the norm and the shuffles
+  const bool warp_norm = __any_sync(0xffffffffu, normed);
+  const int d0 = l * 16;                          // this lane's 16 elements
+  const int c0 = (l & 3) * 16;                    // ... and their RoPE table columns
+  const bool upper = l >= 4;                      // elements 64..127: partner is d - 64
+  float2 wf[8];                                   // the row's norm weights, as pairs
+  {
+    const __nv_bfloat16* wsrc = (is_q ? q_w : k_w) + d0;
+    const uint4 wa = normed ? *reinterpret_cast<const uint4*>(wsrc) : make_uint4(0u, 0u, 0u, 0u);
+    const uint4 wb = normed ? *reinterpret_cast<const uint4*>(wsrc + 8) : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t* a = &wa.x;
+    const uint32_t* b = &wb.x;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) { wf[q] = bf2_to_f2(a[q]); wf[4 + q] = bf2_to_f2(b[q]); }
+  }
+  hy_grid_wait();
+  hy_grid_trigger();
+  const bool want_slot = cache != nullptr && valid && h >= q_heads;
+  const long slot_end = (long)num_blocks * HY_BLOCK;
+  int t = (int)blockIdx.x;
+  int slot_n = (ntok > 0 && want_slot) ? slot_mapping[t] : -1;   // the next token's slot
+  for (int i = 0; i < ntok; ++i, t += grid) {
+    const int s = i % QNR_NS;
+    int slot = slot_n;
+    if (i + 1 < ntok && want_slot) slot_n = slot_mapping[t + grid];
+    if (slot >= slot_end) { hy_flag(err, HY_ERR_BOUNDS); slot = -1; }
+    const bool w_ok = mbar_wait(&full[s], (i / QNR_NS) & 1, err);
+    if (__any_sync(0xffffffffu, !w_ok)) break;
+    const uint8_t* st = qnr_ring + s * stage_bytes;
+    uint4 ca = make_uint4(0u, 0u, 0u, 0u), cb = ca;
+    if (valid) {
+      const uint4* p = reinterpret_cast<const uint4*>(st + h * HY_HEAD_DIM * 2 + d0 * 2);
+      ca = p[0];
+      cb = p[1];
+    }
+    // this lane's 16 cos and sin columns stay in the stage until the RoPE
+    const float4* cp = reinterpret_cast<const float4*>(st + row_bytes) + c0 / 4;
+    const float4* sp = reinterpret_cast<const float4*>(st + row_bytes + 256) + c0 / 4;
+    if (is_v && slot >= 0) {                      // value head: cache copy only
+      uint4* dst = reinterpret_cast<uint4*>(cache_ptr(cache, slot, 1, h - q_heads - kv_heads, kv_heads) + d0);
+      dst[0] = ca;
+      dst[1] = cb;
+    }
+    if (warp_norm) {
+      uint32_t xr[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+      float2 ss2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float2 v = bf2_to_f2(xr[q]);
+        ss2 = __ffma2_rn(v, v, ss2);
+      }
+      float ss = __fadd_rn(ss2.x, ss2.y);
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      // mean = ss / 128 exactly (a power of two)
+      const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / HY_HEAD_DIM), eps)));
+      const float2 rs2 = make_float2(rstd, rstd);
+      uint32_t yr[8];                             // y = bf16((x * rstd) * w)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) yr[q] = f2_to_bf2(__fmul2_rn(__fmul2_rn(bf2_to_f2(xr[q]), rs2), wf[q]));
+      uint32_t pr[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) pr[q] = __shfl_xor_sync(0xffffffffu, yr[q], 4);
+      if (normed) {
+        uint32_t orr[8];                          // lower: y*cos + (-y[d+64])*sin; upper: y*cos + y[d-64]*sin
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float4 c4 = cp[k], s4 = sp[k];
+          const float2 cc[2] = {make_float2(c4.x, c4.y), make_float2(c4.z, c4.w)};
+          const float2 sv[2] = {upper ? make_float2(s4.x, s4.y) : make_float2(-s4.x, -s4.y),
+                                upper ? make_float2(s4.z, s4.w) : make_float2(-s4.z, -s4.w)};
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int q = 2 * k + e;
+            orr[q] = f2_to_bf2(__fadd2_rn(__fmul2_rn(bf2_to_f2(yr[q]), cc[e]),
+                                          __fmul2_rn(bf2_to_f2(pr[q]), sv[e])));
+          }
+        }
+        const uint4 oa = make_uint4(orr[0], orr[1], orr[2], orr[3]);
+        const uint4 ob = make_uint4(orr[4], orr[5], orr[6], orr[7]);
+        if (is_q) {
+          if (q_out) {
+            uint4* dst = reinterpret_cast<uint4*>(q_out + ((size_t)t * q_heads + h) * HY_HEAD_DIM + d0);
+            dst[0] = oa;
+            dst[1] = ob;
+          }
+        } else {
+          const int kh = h - q_heads;
+          if (k_out) {
+            uint4* dst = reinterpret_cast<uint4*>(k_out + ((size_t)t * kv_heads + kh) * HY_HEAD_DIM + d0);
+            dst[0] = oa;
+            dst[1] = ob;
+          }
+          if (slot >= 0) {
+            uint4* dst = reinterpret_cast<uint4*>(cache_ptr(cache, slot, 0, kh, kv_heads) + d0);
+            dst[0] = oa;
+            dst[1] = ob;
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);        // the stage is free once every warp is done with it
+  }
+}
+
 // Plain KV append: k, v are [T][kv_heads][128].  A head row is one 16-byte
 // vector per lane of a lane group (16 lanes for bf16, 32 for fp32); item
 // i = token * 2 * kv_heads + row (K rows, then V rows); KVA_UNROLL items'
@@ -370,9 +559,38 @@ cudaError_t hy_launch_qk_norm_rope(int dtype, const void* qkv, int ld, int T, in
   if (T <= 0) return cudaSuccess;
   if (dtype == 0) {
     using B = __nv_bfloat16;
-    const int npass = (q_heads + 2 * kv_heads + QNR_GROUPS - 1) / QNR_GROUPS;
-    // one pass per unit while that still leaves units for fewer than 8 CTAs per
-    // SM (decode steps); otherwise up to 4 passes of a token per unit
+    const int heads = q_heads + 2 * kv_heads;
+    const int npass = (heads + QNR_GROUPS - 1) / QNR_GROUPS;
+    // prefill-sized batches: a token per CTA iteration, 8 lanes per head row
+    // (a CTA of 8 x heads threads)
+    if ((long)T * npass > 148L * 8 && heads * QNR_LPR <= QNR_ROWS_MAX_THREADS &&
+        ld % 8 == 0 && (reinterpret_cast<uintptr_t>(qkv) & 15) == 0) {
+      // consumers (8 x heads threads in whole warps) + the producer warp
+      const int threads = (heads * QNR_LPR + 31) / 32 * 32 + 32;
+      const int smem = QNR_NS * (heads * HY_HEAD_DIM * 2 + 2 * 64 * 4);
+      static bool attr = false;
+      static int occ_rows = 0, occ_key = 0;
+      if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(qk_norm_rope_rows_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        if (e != cudaSuccess) return e;
+        attr = true;
+      }
+      if (occ_key != threads * 65536 + smem) {
+        int n = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qk_norm_rope_rows_kernel, threads, smem);
+        occ_rows = n > 0 ? n : 1;
+        occ_key = threads * 65536 + smem;
+      }
+      const long cap = 148L * occ_rows;
+      const int grid = (int)(T < cap ? T : cap);
+      return hy_launch(qk_norm_rope_rows_kernel, dim3(grid), dim3(threads), smem, st, (const B*)qkv,
+                       (int)ld, T, q_heads, kv_heads, positions, (const B*)q_w, (const B*)k_w,
+                       rope_cos, rope_sin, max_pos, eps, (B*)q_out, (B*)k_out, (B*)cache,
+                       slot_mapping, num_blocks, err);
+    }
+    // decode-sized batches: one pass of 16 head rows per unit while that still
+    // leaves units for fewer than 8 CTAs per SM; otherwise up to 4 passes
     const int npc = (long)T * npass <= 148L * 8 ? 1 : (npass < 4 ? npass : 4);
     const long units = (long)T * ((npass + npc - 1) / npc);
     // as many CTAs as are resident at once (each walks its units), at most one per unit

@@ -241,6 +241,7 @@ def test_qk_norm_rope_bf16_many_tokens_vs_oracle(Hq, Hkv):
     cos64, sin64 = cos[:, :64].contiguous().to(dev), sin[:, :64].contiguous().to(dev)
     pos = torch.randint(0, 40960, (T,), device=dev, generator=g).int()
     slots = torch.randperm(NB * 16, device=dev, generator=g)[:T].int()
+    slots[::101] = -1                             # padding tokens
     q_out = torch.empty(T, Hq, 128, dtype=torch.bfloat16, device=dev)
     cache = torch.zeros(NB, 2, Hkv, 16, 128, dtype=torch.bfloat16, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -263,12 +264,17 @@ def test_qk_norm_rope_bf16_many_tokens_vs_oracle(Hq, Hkv):
         assert (got.view(torch.int16) != want.view(torch.int16)).float().mean().item() < 0.02
     close(q_out.cpu(), wq_out)
     sl = slots.cpu().long()
-    blk, j = sl // 16, sl % 16
+    keep = sl >= 0                                # padding tokens (slot -1) write no K/V
+    blk, j = sl[keep] // 16, sl[keep] % 16
     cc = cache.cpu()
-    got_k = cc[blk, 0, :, j]                      # (T, Hkv, 128)
+    got_k = cc[blk, 0, :, j]                      # (kept tokens, Hkv, 128)
     got_v = cc[blk, 1, :, j]
-    close(got_k, wk_out)
-    assert torch.equal(got_v, vv)
+    close(got_k, wk_out[keep])
+    assert torch.equal(got_v, vv[keep])
+    written = torch.zeros(NB * 16, dtype=torch.bool)
+    written[sl[keep]] = True
+    flat = cc.permute(0, 3, 1, 2, 4).reshape(NB * 16, -1)   # slot-major view of the cache
+    assert not flat[~written].any()               # nothing else was written
 
 
 # ------------------------------------------------------------------ attention
