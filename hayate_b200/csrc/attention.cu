@@ -920,16 +920,19 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const CUtensorMap* tiles
           if (kb + i > lim || kb + i >= kv_len) s[i] = NEG_INF;
       }
       // row max and row sum as 8 independent chains (a 64-long chain of
-      // dependent max or add instructions would expose its latency)
+      // dependent max or add instructions would expose its latency); the max
+      // takes two new scores per three-input instruction
       float mxs[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mxs[k] = s[k];
+      for (int k = 0; k < 8; ++k) mxs[k] = fmax3f(s[k], s[8 + k], s[16 + k]);
 #pragma unroll
-      for (int i = 8; i < 64; i += 8)
+      for (int i = 24; i < 56; i += 16)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mxs[k] = fmaxf(mxs[k], s[i + k]);
-      float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                       fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+        for (int k = 0; k < 8; ++k) mxs[k] = fmax3f(mxs[k], s[i + k], s[i + 8 + k]);
+      float mx = fmax3f(fmax3f(mxs[0], mxs[1], mxs[2]), fmax3f(mxs[3], mxs[4], mxs[5]),
+                        fmax3f(mxs[6], mxs[7], s[56]));
+#pragma unroll
+      for (int k = 57; k < 64; k += 2) mx = fmax3f(mx, s[k], k + 1 < 64 ? s[k + 1] : s[k]);
       mx *= sl2;
       const bool grow = mx > m + RESCALE_LOG2;
       if (__any_sync(0xffffffffu, grow)) {
@@ -946,28 +949,35 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const CUtensorMap* tiles
             tmem_ld32(tO + 32 * cc, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            for (int i = 0; i < 16; ++i) {
+              const float2 r2 = __fmul2_rn(make_float2(o[2 * i], o[2 * i + 1]), make_float2(alpha, alpha));
+              o[2 * i] = r2.x;
+              o[2 * i + 1] = r2.y;
+            }
             tmem_st32(tO + 32 * cc, o);
           }
           tmem_wait_st();
         }
       }
       const float mneg = (m == NEG_INF) ? 0.f : -m;
+      const float2 sl2v = make_float2(sl2, sl2), mnegv = make_float2(mneg, mneg);
       uint32_t pk[32];
-      float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // ls[k] sums elements 8 j + 2 k (.x) and 8 j + 2 k + 1 (.y): the 8
+      // chains of scalar sums, two per packed add
+      float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                      make_float2(0.f, 0.f)};
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         // every EXP2_POLY_EVERY-th pair of weights on the FMA pipe, the rest on
         // the exp2 unit: the two units then share the tile's 64 exponentials
         const bool poly = EXP2_POLY_EVERY > 0 && (i % EXP2_POLY_EVERY) == EXP2_POLY_EVERY - 1;
-        const float x0 = fmaf(s[2 * i], sl2, mneg), x1 = fmaf(s[2 * i + 1], sl2, mneg);
-        const float p0 = poly ? exp2_poly(x0) : ex2_ftz(x0);
-        const float p1 = poly ? exp2_poly(x1) : ex2_ftz(x1);
-        ls[(2 * i) & 7] += p0;
-        ls[(2 * i + 1) & 7] += p1;
+        const float2 x = __ffma2_rn(make_float2(s[2 * i], s[2 * i + 1]), sl2v, mnegv);
+        const float2 pp = poly ? exp2_poly2(x) : make_float2(ex2_ftz(x.x), ex2_ftz(x.y));
+        const float p0 = pp.x, p1 = pp.y;
+        ls[i & 3] = __fadd2_rn(ls[i & 3], make_float2(p0, p1));
         pk[i] = pack_bf16(p0, p1);
       }
-      l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+      l += ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y));
       tmem_st32u(tS, pk);                       // P(t) over the first 32 columns of S(t)
       tmem_wait_st();
       tc_fence_before();

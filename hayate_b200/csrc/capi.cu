@@ -143,9 +143,17 @@ __global__ void wait_timeout_probe_kernel(int32_t* err, uint64_t timeout_ns, int
 }
 
 // The prefill softmax's polynomial 2^x on n inputs (one thread each).
+// Elements 2k, 2k + 1 go through the packed form the softmax uses (a last odd
+// element through the scalar one).
 __global__ void exp2_poly_probe_kernel(const float* __restrict__ x, float* __restrict__ y, int n) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) y[i] = exp2_poly(x[i]);
+  const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (i + 1 < n) {
+    const float2 r = exp2_poly2(make_float2(x[i], x[i + 1]));
+    y[i] = r.x;
+    y[i + 1] = r.y;
+  } else if (i < n) {
+    y[i] = exp2_poly(x[i]);
+  }
 }
 
 // Shared with other translation units of the library (not part of the C ABI).
@@ -452,7 +460,7 @@ int hy_selftest_wait_timeout(int32_t* err, int32_t timeout_ms, int32_t* done, vo
 int hy_selftest_exp2_poly(const float* x, float* y, int32_t n, void* stream) {
   if (!x || !y || n < 0) return fail(HY_E_INVALID, "hy_selftest_exp2_poly: bad argument");
   if (n == 0) return HY_OK;
-  exp2_poly_probe_kernel<<<(n + 255) / 256, 256, 0, as_stream(stream)>>>(x, y, n);
+  exp2_poly_probe_kernel<<<(n / 2 + 256) / 256, 256, 0, as_stream(stream)>>>(x, y, n);
   return cuda_result(cudaGetLastError(), "hy_selftest_exp2_poly");
 }
 

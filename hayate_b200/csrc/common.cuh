@@ -247,6 +247,32 @@ HY_DEVICE float exp2_poly(float x) {
   return x < -126.0f ? 0.0f : y;
 }
 
+// exp2_poly on a pair with packed f32x2 arithmetic (each lane rounded as the
+// scalar operation, so each result equals exp2_poly of its input); the
+// exponent goes in with one shift-add per lane: (round(x) << 23) is the low
+// bits of t shifted, since 1.5 * 2^23's own bits vanish in the shift.
+HY_DEVICE float2 exp2_poly2(float2 x) {
+  const float2 xc = make_float2(fmaxf(x.x, -126.0f), fmaxf(x.y, -126.0f));
+  const float2 big = make_float2(12582912.0f, 12582912.0f);
+  const float2 t = __fadd2_rn(xc, big);
+  const float2 j = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));   // round(xc)
+  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), xc);              // xc - j, exact
+  float2 p = __ffma2_rn(make_float2(0.05517166853f, 0.05517166853f), f,
+                        make_float2(0.24261112511f, 0.24261112511f));
+  p = __ffma2_rn(p, f, make_float2(0.69326096773f, 0.69326096773f));
+  p = __ffma2_rn(p, f, make_float2(0.99992805719f, 0.99992805719f));
+  const float y0 = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
+  const float y1 = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
+  return make_float2(x.x < -126.0f ? 0.0f : y0, x.y < -126.0f ? 0.0f : y1);
+}
+
+// max(a, b, c) in one instruction (sm_100's three-input max).
+HY_DEVICE float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 HY_DEVICE uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
