@@ -13,7 +13,10 @@ namespace cg = cooperative_groups;
 namespace {
 
 constexpr int AM_THREADS = 256;
-constexpr int AM_UNROLL = 4;
+#ifndef HY_AM_UNROLL
+#define HY_AM_UNROLL 2
+#endif
+constexpr int AM_UNROLL = HY_AM_UNROLL;   // 16-byte vectors per thread per batch
 constexpr int AM_MAX_CLUSTER = 8;         // portable cluster size
 
 // (v, i) beats (a, j): NaN beats every number (torch.argmax propagates NaN),
