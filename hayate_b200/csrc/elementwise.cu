@@ -366,20 +366,27 @@ static cudaError_t launch_add_rms_norm_bulk(void* x, long ldx, const void* delta
   using B = __nv_bfloat16;
   const int row_bytes = cols * 2;
   const int smem = row_bytes + RNB_WARPS * RNB_STAGES * row_bytes * (delta ? 2 : 1);
-  static bool attr[2] = {false, false};
-  static int occ[2] = {0, 0};
+  // per device: the shared-memory attribute once, the occupancy per ring size
+  static bool attr[64][2] = {};
+  static int occ[64][2] = {}, occ_smem[64][2] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
   const int k = delta ? 1 : 0;
   auto kern = delta ? add_rms_norm_bulk_kernel<true> : add_rms_norm_bulk_kernel<false>;
-  if (!attr[k]) {
+  if (!attr[dev][k]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          RNB_MAX_SMEM + 4096);
     if (e != cudaSuccess) return e;
-    attr[k] = true;
+    attr[dev][k] = true;
   }
-  int n = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, RNB_WARPS * 32, smem);
-  occ[k] = n > 0 ? n : 1;
-  const long warps = 148L * occ[k] * RNB_WARPS;
+  if (occ_smem[dev][k] != smem) {
+    int n = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, RNB_WARPS * 32, smem);
+    occ[dev][k] = n > 0 ? n : 1;
+    occ_smem[dev][k] = smem;
+  }
+  const long warps = 148L * occ[dev][k] * RNB_WARPS;
   const long want = (rows + 1) / 2;               // two rows per warp at least
   const long ctas = ((want < warps ? want : warps) + RNB_WARPS - 1) / RNB_WARPS;
   return hy_launch(kern, dim3((unsigned)ctas), dim3(RNB_WARPS * 32), smem, st, (B*)x, ldx,

@@ -568,21 +568,25 @@ cudaError_t hy_launch_qk_norm_rope(int dtype, const void* qkv, int ld, int T, in
       // consumers (8 x heads threads in whole warps) + the producer warp
       const int threads = (heads * QNR_LPR + 31) / 32 * 32 + 32;
       const int smem = QNR_NS * (heads * HY_HEAD_DIM * 2 + 2 * 64 * 4);
-      static bool attr = false;
-      static int occ_rows = 0, occ_key = 0;
-      if (!attr) {
+      // per device: the shared-memory attribute once, the occupancy per shape
+      static bool attr[64] = {};
+      static int occ_rows[64] = {}, occ_key[64] = {};
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (dev < 0 || dev >= 64) dev = 0;
+      if (!attr[dev]) {
         cudaError_t e = cudaFuncSetAttribute(qk_norm_rope_rows_kernel,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
         if (e != cudaSuccess) return e;
-        attr = true;
+        attr[dev] = true;
       }
-      if (occ_key != threads * 65536 + smem) {
+      if (occ_key[dev] != threads * 65536 + smem) {
         int n = 0;
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qk_norm_rope_rows_kernel, threads, smem);
-        occ_rows = n > 0 ? n : 1;
-        occ_key = threads * 65536 + smem;
+        occ_rows[dev] = n > 0 ? n : 1;
+        occ_key[dev] = threads * 65536 + smem;
       }
-      const long cap = 148L * occ_rows;
+      const long cap = 148L * occ_rows[dev];
       const int grid = (int)(T < cap ? T : cap);
       return hy_launch(qk_norm_rope_rows_kernel, dim3(grid), dim3(threads), smem, st, (const B*)qkv,
                        (int)ld, T, q_heads, kv_heads, positions, (const B*)q_w, (const B*)k_w,
