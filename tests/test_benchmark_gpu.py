@@ -26,3 +26,14 @@ def test_operator_microbench_small(op):
     from hayate_b200.microbench import run_op
     r = run_op(op, iters=2, n_decode=16, prefill=True, tokens=16 + 512)
     assert r["op"] == op and r["ms_mean"] > 0 and r["bytes"] > 0
+
+
+@pytest.mark.parametrize("op", ["qk_norm_rope", "kv_append", "argmax", "add_rms_norm",
+                                "silu_mul"])
+def test_row_kernel_microbench_streamed(op):
+    """The streamed timing mode: launches on input copies larger than L2,
+    replayed from one CUDA graph (prefill-sized cases, so the streamed
+    add+RMSNorm and QK-norm+RoPE kernels run)."""
+    from hayate_b200.microbench import run_op
+    r = run_op(op, iters=2, n_decode=16, prefill=True, tokens=16 + 2048, stream=True)
+    assert r["op"] == op and r["ms_mean"] > 0 and r["bytes"] > 0 and r["stream"]
