@@ -53,13 +53,14 @@ constexpr int DEC_WARP_BYTES = DEC_STAGES * DEC_TILE_BYTES;      // 24 KB
 constexpr int PRE_QROWS = 64;                                    // query tokens per prefill item
 // tcgen05 prefill: sub-tile X (0, 1) = 128 rows r: query head 4g + 2X + r / 64,
 // token t0 + r % 64; KV tiles of 64 keys (4 blocks) in rings of TC_NS slots.
-// A K slot holds the two 64-column halves outermost ([half][64 keys][64], the
-// K-major operand of S = Q K^T); a V slot holds each block's 4 KB tile as one
-// TMA box lands it ([block][half][16 keys][64], the MN-major operand of P V).
+// A K slot holds each block's 4 KB tile as one 4-D TMA box lands it
+// ([block][8-key group][half][8 keys][64]: the K-major operand of S = Q K^T,
+// its 8-key groups 2 KB apart, column half h at +1 KB h); a V slot holds each
+// block's tile as one 3-D box lands it ([block][half][16 keys][64], the MN-major
+// operand of P V).
 constexpr int TC_KEYS = 64;
 constexpr int TC_NS = 4;                                         // K and V ring slots
 constexpr int TC_KV_BYTES = TC_KEYS * HY_HEAD_DIM * 2;          // K or V of one tile: 16 KB
-constexpr int TC_HALF = TC_KEYS * 128;                           // one 64-column half: 8 KB
 constexpr int TC_Q_BYTES = 128 * HY_HEAD_DIM * 2;                // Q of one sub-tile: 32 KB
 constexpr int TC_K_OFF = 2 * TC_Q_BYTES;                         // K ring
 constexpr int TC_V_OFF = TC_K_OFF + TC_NS * TC_KV_BYTES;         // V ring
@@ -746,10 +747,10 @@ __device__ bool decode_pair_cta(const CUtensorMap* tiles, const MainArgs& a, con
 //   lane 0           b = t % 2, then O_X += P_X(t-1) V_{t-1} (A operand read from
 //                    TMEM), each followed by tcgen05.commit to the barrier its
 //                    consumer waits on;
-//   warps 9, 11      load K_t (8 TMA boxes: 4 paged blocks x two 64-column
-//                    halves) and V_t (4 boxes: one whole 4 KB block tile each) into
-//                    ring slot c % TC_NS once the MMAs of the slot's previous use
-//                    are done, each warp two of the tile's four blocks.
+//   warps 9, 11      load K_t and V_t (4 TMA boxes each: one whole 4 KB block
+//                    tile per box) into ring slot c % TC_NS once the MMAs of the
+//                    slot's previous use are done, each warp two of the tile's
+//                    four blocks.
 // With two S buffers the MMA warp issues S(t+1) while the softmax works on
 // S(t), so the softmax never waits for its scores once the pipeline is full.
 // S(t) may overwrite buffer b only after PV(t-2) has read P(t-2) from it: the
@@ -764,7 +765,7 @@ __device__ bool decode_pair_cta(const CUtensorMap* tiles, const MainArgs& a, con
 // run a full phase ahead of the role that waits on it, so a wait is always on
 // the current or the previous phase.  Returns false if a wait ran out; the
 // roles then drain their own asynchronous work before the item ends.
-__device__ bool prefill_item_tc(const CUtensorMap* map, const CUtensorMap* tiles,
+__device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* tiles,
                                 const MainArgs& a, const PlanView& v, int item, uint8_t* payload,
                                 Shared& sh, uint32_t tmem, uint32_t& ctr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -801,11 +802,10 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const CUtensorMap* tiles
 
   if (warp == TC_LOAD_WARP || warp == TC_LOAD_WARP2) {
     // Two load warps, lw = 0, 1, each for blocks 2 lw and 2 lw + 1 of every key
-    // tile: lane 0 waits for the slot and posts its byte count; lanes 0-3 then
-    // issue the K boxes (block 2 lw + lane / 2, column half lane % 2), lanes 0-1
-    // the V block boxes.  An SM's TMA unit takes more boxes per cycle from two
-    // issuing warps than from one (one warp issuing a tile's 12 boxes was the
-    // prefill pipeline's slowest role).
+    // tile: lane 0 waits for the slot and posts its byte count; lanes 0-1 then
+    // issue one 4 KB box each (block 2 lw + lane), K or V.  An SM's TMA unit
+    // takes more boxes per cycle from two issuing warps than from one (one warp
+    // issuing a tile's boxes was the prefill pipeline's slowest role).
     const int lw = warp == TC_LOAD_WARP2;
     const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
     const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
@@ -825,17 +825,17 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const CUtensorMap* tiles
         if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) { ok = false; break; }
         uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
         if (lane == 0) mbar_arrive_expect_tx(full, TC_KV_BYTES / 2);
-        const int jb = 2 * lw + (kv ? lane : (lane >> 1));
+        const int jb = 2 * lw + (lane & 1);
         const int id = __shfl_sync(0xffffffffu, ids, (4 * t + jb) & 31);
-        if (lane < (kv ? 2 : 4)) {
+        if (lane < 2) {
           int r = a.oob_row;                    // past the end: zero fill
           if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
           else if (id >= 0) r = kv_row(a, id, kv, g);
           if (kv)
             tma_load_3d(payload + TC_V_OFF + slot * TC_KV_BYTES + jb * 4096, tiles, 0, r, 0, full);
           else
-            tma_load_2d(payload + TC_K_OFF + slot * TC_KV_BYTES + (lane & 1) * TC_HALF + jb * 2048,
-                        map, 64 * (lane & 1), r, full);
+            tma_load_4d(payload + TC_K_OFF + slot * TC_KV_BYTES + jb * 4096, kgroups, 0, r, 0, 0,
+                        full);
         }
         issued[kv] = t + 1;
       }
@@ -862,12 +862,13 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const CUtensorMap* tiles
           ok = mbar_wait(&sh.tc_kfull[slot], (c / TC_NS) & 1, a.err);
           if (!ok) break;
           tc_fence_after();
-          const uint64_t dK = tc_desc_sw128(sbase + TC_K_OFF + slot * TC_KV_BYTES, 16, 1024);
+          // K slot: 8-key groups 2 KB apart (SBO), column half h at +1 KB
+          const uint64_t dK = tc_desc_sw128(sbase + TC_K_OFF + slot * TC_KV_BYTES, 16, 2048);
 #pragma unroll
           for (int kk = 0; kk < HY_HEAD_DIM / 16; ++kk)
             tc_mma_bf16(tmem + tm_s(X, c & 1),
                         dQ + (uint64_t)((((kk >> 2) * (TC_Q_BYTES / 2)) + (kk & 3) * 32) >> 4),
-                        dK + (uint64_t)((((kk >> 2) * TC_HALF) + (kk & 3) * 32) >> 4), ID_S,
+                        dK + (uint64_t)((((kk >> 2) * 1024) + (kk & 3) * 32) >> 4), ID_S,
                         kk > 0);
           tc_commit(&sh.tc_sfull[X][c & 1]);
           tc_commit(&sh.tc_kfree[slot]);
@@ -1018,14 +1019,14 @@ __device__ bool prefill_item_tc(const CUtensorMap* map, const CUtensorMap* tiles
 }
 
 __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
-    const __grid_constant__ CUtensorMap kv_map, const __grid_constant__ CUtensorMap kv_tiles,
+    const __grid_constant__ CUtensorMap kv_kgroups, const __grid_constant__ CUtensorMap kv_tiles,
     MainArgs a, PlanView v) {
   __shared__ Shared sh;
   extern __shared__ uint8_t dyn_smem[];
   uint8_t* payload = payload_base(dyn_smem);
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
-    prefetch_tmap(&kv_map);
+    prefetch_tmap(&kv_kgroups);
     prefetch_tmap(&kv_tiles);
     for (int w = 0; w < ATT_WARPS; ++w)
       for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&sh.dec_bar[w][s], 1);
@@ -1104,7 +1105,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
       const int k = sh.pre_item;
       __syncthreads();                          // read before thread 0 writes the next one
       if (k >= n_pre) break;
-      ok = prefill_item_tc(&kv_map, &kv_tiles, a, v, k, payload, sh, tmem, tile_ctr);
+      ok = prefill_item_tc(&kv_kgroups, &kv_tiles, a, v, k, payload, sh, tmem, tile_ctr);
     }
   }
   // decode items (warps 0..ATT_WARPS-1): each warp takes the next one from this
@@ -1321,7 +1322,7 @@ cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const void* cache, const voi
   a.early = (flags & HY_ATTN_EARLY) != 0;
   const PlanView v = make_view(ws, d);
   const int grid = device_sms(dev) * g_ctas_per_sm[dev < 64 && dev >= 0 ? dev : 0];
-  return hy_launch(attn_main_kernel, dim3(grid), dim3(ATT_THREADS), SMEM_BYTES, st, maps.halves,
+  return hy_launch(attn_main_kernel, dim3(grid), dim3(ATT_THREADS), SMEM_BYTES, st, maps.kgroups,
                    maps.tiles, a, v);
 }
 

@@ -11,12 +11,15 @@
 #endif
 
 // Tensor maps over the bf16 KV cache viewed as rows of 128 elements (256 B):
-//   halves: 2-D, box = 16 rows x 64 columns (one half of a block's head tile)
-//   tiles:  3-D (64 columns, rows, 2 halves 128 B apart), box = 16 rows x both
-//           halves: one (block, K or V, head) tile, landing in shared memory as
-//           the two half boxes would (half h at +2 KB h, 128-byte swizzle)
+//   kgroups: 4-D (64 columns, rows, 2 halves 128 B apart, 2 eight-row groups
+//            2 KB apart), box = 64 x 8 x 2 x 2: one (block, K, head) tile landing
+//            as four 1 KB swizzle atoms, [key group][half][8 rows][64] (128-byte
+//            swizzle), so that a key tile's 8-row groups sit a uniform 2 KB apart
+//   tiles:   3-D (64 columns, rows, 2 halves 128 B apart), box = 16 rows x both
+//            halves: one (block, K or V, head) tile landing as [half][16 rows][64]
+//            (half h at +2 KB h, 128-byte swizzle)
 struct KvMaps {
-  CUtensorMap halves;
+  CUtensorMap kgroups;
   CUtensorMap tiles;
 };
 

@@ -96,12 +96,15 @@ int kv_map_for(int dev, const void* base, long rows, KvMaps* out) {
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
     return fail(HY_E_INVALID, "kv_cache must be 16-byte aligned");
   KvMaps m;
-  cuuint64_t dims2[2] = {HY_HEAD_DIM, (cuuint64_t)rows};
-  cuuint64_t strides2[1] = {HY_HEAD_DIM * 2};
-  cuuint32_t box2[2] = {64, HY_BLOCK};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(&m.halves, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
-                        dims2, strides2, box2, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  // element (x, y, z, w) at x + 128 y + 64 z + 1024 w: column x of half z of
+  // row y + 8 w; a box at row y = a block's first row covers its 16 rows, and
+  // a y past the end (the zero-fill row) leaves the whole box zero
+  cuuint64_t dims4[4] = {64, (cuuint64_t)rows, 2, 2};
+  cuuint64_t strides4[3] = {HY_HEAD_DIM * 2, 128, 8 * HY_HEAD_DIM * 2};
+  cuuint32_t box4[4] = {64, 8, 2, 2};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(&m.kgroups, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base),
+                        dims4, strides4, box4, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r == CUDA_SUCCESS) {

@@ -194,6 +194,16 @@ HY_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, int32_t x, int32_t
       : "memory");
 }
 
+HY_DEVICE void tma_load_4d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                           int32_t w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];"
+      :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z),
+         "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+
 HY_DEVICE void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
