@@ -3,8 +3,10 @@
 ``python -m hayate_b200.build [--force] [--verbose]`` compiles every
 ``csrc/*.cu`` to an object under ``_build/`` (in parallel) and links the shared
 library next to this file.  Objects are rebuilt when their source or any header
-is newer.  ``-Xptxas -v`` output (registers, spills, shared memory) is kept in
-``_build/ptxas.log``.  ``HY_NVCC_DEFINES`` (e.g. ``-DHY_EXP2_POLY_EVERY=2``)
+is newer.  ``-Xptxas -v`` output (registers, spills, shared memory) of each
+source's latest compile is kept in ``_build/<source>.ptxas.log``, and
+``_build/ptxas.log`` is rewritten on every build as their concatenation, so it
+always describes the objects the library was linked from.  ``HY_NVCC_DEFINES`` (e.g. ``-DHY_EXP2_POLY_EVERY=2``)
 adds preprocessor definitions to every compile, for building a tuning variant
 of a kernel constant; rebuild with ``--force`` after changing it.
 """
@@ -70,13 +72,19 @@ def build(force: bool = False, verbose: bool = False) -> str:
     hdrs = _headers()
     todo = [s for s in srcs
             if force or _stale(os.path.join(BUILD, os.path.basename(s)[:-3] + ".o"), [s, *hdrs])]
-    logs = []
     if todo:
         with cf.ThreadPoolExecutor(max_workers=min(8, len(todo))) as ex:
             for obj, log in ex.map(lambda s: _compile(s, verbose), todo):
-                logs.append(f"== {os.path.basename(obj)}\n{log}")
-        with open(os.path.join(BUILD, "ptxas.log"), "a") as f:
-            f.write("\n".join(logs))
+                with open(obj[:-2] + ".ptxas.log", "w") as f:
+                    f.write(log)
+    logs = []
+    for src in srcs:
+        per = os.path.join(BUILD, os.path.basename(src)[:-3] + ".ptxas.log")
+        if os.path.exists(per):
+            with open(per) as f:
+                logs.append(f"== {os.path.basename(src)[:-3]}.o\n{f.read()}")
+    with open(os.path.join(BUILD, "ptxas.log"), "w") as f:
+        f.write("\n".join(logs))
     objs = [os.path.join(BUILD, os.path.basename(s)[:-3] + ".o") for s in srcs]
     if force or todo or _stale(LIB, objs):
         cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcudart_static"]
