@@ -119,10 +119,10 @@ struct Shared {
   uint64_t dec_bar[ATT_WARPS][DEC_STAGES];
   // tcgen05 prefill.  Ring barriers complete once per use of their slot, the
   // per-sub-tile ones once per key tile.
-  uint64_t tc_kfull[TC_NS];  // K tile landed (TMA transaction bytes)
-  uint64_t tc_vfull[TC_NS];  // V tile landed
-  uint64_t tc_kfree[TC_NS];  // both S MMAs that read the K slot are done (2 commits)
-  uint64_t tc_vfree[TC_NS];  // both PV MMAs that read the V slot are done (2 commits)
+  uint64_t tc_full[TC_NS];   // K and V tiles landed (TMA transaction bytes)
+  uint64_t tc_free[TC_NS];   // both PV MMAs of the slot's tile are done (2 commits): with
+                             // them the S MMAs that read its K (issued earlier by the
+                             // same threads) are done too
   uint64_t tc_sfull[2][2];   // S_X[b] = Q_X K^T complete (once per use of buffer b)
   uint64_t tc_pfull[2][2];   // P_X[b] written over S_X[b] by the 4 softmax warps of X
   uint64_t tc_odone[2];      // O_X += P_X V complete (once per key tile)
@@ -802,55 +802,50 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
 
   if (warp == TC_LOAD_WARP || warp == TC_LOAD_WARP2) {
     // Two load warps, lw = 0, 1, each for blocks 2 lw and 2 lw + 1 of every key
-    // tile: lane 0 waits for the slot and posts its byte count; lanes 0-1 then
-    // issue one 4 KB box each (block 2 lw + lane), K or V.  An SM's TMA unit
-    // takes more boxes per cycle from two issuing warps than from one (one warp
-    // issuing a tile's boxes was the prefill pipeline's slowest role).
+    // tile: lane 0 waits for the slot and posts the warp's byte count; lanes 0-3
+    // then issue one 4 KB box each (K of blocks 2 lw, 2 lw + 1, then their V).
+    // One wait and one arm per tile: a load warp's wait, arm and first box are
+    // serial round trips of ~150-270 cycles each, so the tile's supply rate is
+    // set by how many of them a warp makes per tile.
     const int lw = warp == TC_LOAD_WARP2;
     const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
     const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
     int ids = -1;                               // lane i: block 32 (t / 8) + i of the sequence
-    int issued[2] = {0, 0};                     // tiles whose K / V loads were issued
+    int issued = 0;                             // tiles whose loads were issued
     for (int t = 0; t < ntiles && ok; ++t) {
       if ((t & 7) == 0) {
         const int b = 4 * t + lane;
         ids = (b < nblk && b < a.bt_pitch) ? bt[b] : -1;
       }
       const uint32_t c = c0 + t, slot = c % TC_NS, use = c / TC_NS;
-#pragma unroll 1
-      for (int kv = 0; kv < 2; ++kv) {
-        bool w_ok = true;
-        if (lane == 0)
-          w_ok = mbar_wait(kv ? &sh.tc_vfree[slot] : &sh.tc_kfree[slot], (use & 1) ^ 1, a.err);
-        if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) { ok = false; break; }
-        uint64_t* full = kv ? &sh.tc_vfull[slot] : &sh.tc_kfull[slot];
-        if (lane == 0) mbar_arrive_expect_tx(full, TC_KV_BYTES / 2);
-        const int jb = 2 * lw + (lane & 1);
-        const int id = __shfl_sync(0xffffffffu, ids, (4 * t + jb) & 31);
-        if (lane < 2) {
-          int r = a.oob_row;                    // past the end: zero fill
-          if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
-          else if (id >= 0) r = kv_row(a, id, kv, g);
-          if (kv)
-            tma_load_3d(payload + TC_V_OFF + slot * TC_KV_BYTES + jb * 4096, tiles, 0, r, 0, full);
-          else
-            tma_load_4d(payload + TC_K_OFF + slot * TC_KV_BYTES + jb * 4096, kgroups, 0, r, 0, 0,
-                        full);
-        }
-        issued[kv] = t + 1;
+      bool w_ok = true;
+      if (lane == 0) w_ok = mbar_wait(&sh.tc_free[slot], (use & 1) ^ 1, a.err);
+      if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) { ok = false; break; }
+      uint64_t* full = &sh.tc_full[slot];
+      if (lane == 0) mbar_arrive_expect_tx(full, TC_KV_BYTES);
+      const int kv = (lane >> 1) & 1, jb = 2 * lw + (lane & 1);
+      const int id = __shfl_sync(0xffffffffu, ids, (4 * t + jb) & 31);
+      if (lane < 4) {
+        int r = a.oob_row;                      // past the end: zero fill
+        if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
+        else if (id >= 0) r = kv_row(a, id, kv, g);
+        if (kv)
+          tma_load_3d(payload + TC_V_OFF + slot * TC_KV_BYTES + jb * 4096, tiles, 0, r, 0, full);
+        else
+          tma_load_4d(payload + TC_K_OFF + slot * TC_KV_BYTES + jb * 4096, kgroups, 0, r, 0, 0,
+                      full);
       }
+      issued = t + 1;
     }
     if (!ok && lane == 0) {                     // loads still in flight must land first
-      for (int kv = 0; kv < 2; ++kv)
-        for (int t = max(0, issued[kv] - TC_NS); t < issued[kv]; ++t) {
-          const uint32_t c = c0 + t;
-          mbar_wait(kv ? &sh.tc_vfull[c % TC_NS] : &sh.tc_kfull[c % TC_NS], (c / TC_NS) & 1,
-                    nullptr);
-        }
+      for (int t = max(0, issued - TC_NS); t < issued; ++t) {
+        const uint32_t c = c0 + t;
+        mbar_wait(&sh.tc_full[c % TC_NS], (c / TC_NS) & 1, nullptr);
+      }
     }
   } else if (warp == TC_MMA_WARP || warp == TC_MMA_WARP1) {
     // one MMA warp per sub-tile X: its lane 0 issues S_X(t), then O_X += P_X(t-1)
-    // V_{t-1}; both warps commit to the K and V slots' free barriers (count 2)
+    // V_{t-1}; both warps commit to the slot's free barrier after P V (count 2)
     const int X = warp == TC_MMA_WARP ? 0 : 1;
     if (lane == 0) {
       constexpr uint32_t ID_S = tc_idesc_bf16(128, TC_KEYS, false);
@@ -859,7 +854,7 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
       for (int t = 0; t <= ntiles && ok; ++t) {
         if (t < ntiles) {                       // S_X(t) = Q_X K_t^T into buffer c % 2
           const uint32_t c = c0 + t, slot = c % TC_NS;
-          ok = mbar_wait(&sh.tc_kfull[slot], (c / TC_NS) & 1, a.err);
+          ok = mbar_wait(&sh.tc_full[slot], (c / TC_NS) & 1, a.err);   // K and V landed
           if (!ok) break;
           tc_fence_after();
           // K slot: 8-key groups 2 KB apart (SBO), column half h at +1 KB
@@ -871,12 +866,11 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
                         dK + (uint64_t)((((kk >> 2) * 1024) + (kk & 3) * 32) >> 4), ID_S,
                         kk > 0);
           tc_commit(&sh.tc_sfull[X][c & 1]);
-          tc_commit(&sh.tc_kfree[slot]);
         }
         if (t > 0) {                            // O_X += P_X(t-1) V_{t-1}
           const uint32_t c = c0 + t - 1, slot = c % TC_NS;
-          ok = mbar_wait(&sh.tc_vfull[slot], (c / TC_NS) & 1, a.err) &&
-               mbar_wait(&sh.tc_pfull[X][c & 1], (c >> 1) & 1, a.err);
+          // V_{t-1} landed with K_{t-1}, waited for before S(t-1)
+          ok = mbar_wait(&sh.tc_pfull[X][c & 1], (c >> 1) & 1, a.err);
           if (!ok) break;
           tc_fence_after();
           // V slot: block kk's tile at kk x 4 KB, its column halves 2 KB apart (LBO),
@@ -887,7 +881,7 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
             tc_mma_bf16_ta(tmem + TM_O + 128 * X, tmem + tm_s(X, c & 1) + 8 * kk,
                            dV + (uint64_t)((kk * 4096) >> 4), ID_O, (t > 1 || kk > 0));
           tc_commit(&sh.tc_odone[X]);
-          tc_commit(&sh.tc_vfree[slot]);
+          tc_commit(&sh.tc_free[slot]);
         }
       }
       if (!ok) {                                // let every issued MMA finish
@@ -1031,10 +1025,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     for (int w = 0; w < ATT_WARPS; ++w)
       for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&sh.dec_bar[w][s], 1);
     for (int s = 0; s < TC_NS; ++s) {
-      mbar_init(&sh.tc_kfull[s], 2);            // one arrival per load warp
-      mbar_init(&sh.tc_vfull[s], 2);
-      mbar_init(&sh.tc_kfree[s], 2);            // one commit per MMA warp
-      mbar_init(&sh.tc_vfree[s], 2);
+      mbar_init(&sh.tc_full[s], 2);             // one arrival per load warp
+      mbar_init(&sh.tc_free[s], 2);             // one commit per MMA warp
     }
     for (int x = 0; x < 2; ++x) {
       for (int b = 0; b < 2; ++b) {
