@@ -100,6 +100,47 @@ constexpr int MERGE_ML_BYTES = MERGE_CHUNK * HY_GROUP * 8;
 static_assert(MERGE_O_BYTES + MERGE_ML_BYTES + MERGE_CHUNK * HY_GROUP * 4 <= DEC_WARP_BYTES,
               "merge staging must fit a decode warp's ring");
 constexpr float NEG_INF = -INFINITY;
+// Split prefill items: a step with fewer prefill items (64 query tokens x one
+// KV head) than SMs cuts the long ones into pieces over equal key-tile ranges,
+// at least PRE_SPLIT_MIN tiles each, so that the pieces fill the idle SMs;
+// each piece leaves its unnormalised O, running max and sum in the workspace
+// and the last piece to finish merges them.  Without this such a step waits
+// for its longest items (one 512-token chunk after 3584 cached tokens: 64
+// items of 57-64 key tiles, 84 SMs idle: 80.0 us uncut, 57.6 us cut).  A
+// step with at least as many items as SMs, or with decode work for the idle
+// SMs, is not cut: a piece costs a second Q load, a 128 KB partial and its
+// share of the merge (~25k cycles per cut item, measured), more than the
+// balance gains there (4 chunks of 512: 80.6 us uncut, 93.0 us cut to the
+// tiles per SM; one chunk beside 256 decode sequences: 704 us uncut, 732 us
+// cut).
+#ifndef HY_PRE_SPLIT_MIN
+#define HY_PRE_SPLIT_MIN 16
+#endif
+constexpr int PRE_SPLIT_MIN = HY_PRE_SPLIT_MIN;                  // key tiles
+constexpr int PRE_MAX_PIECES = 31;
+constexpr int PRE_PART_F4 = 32 * 256;                            // float4 of O per piece
+
+// key tiles of the prefill item at query offset t0 of a sequence of q query
+// tokens and kv keys
+HY_DEVICE int pre_item_tiles(int kv, int q, int t0) {
+  return (kv - q + t0 + min(PRE_QROWS, q - t0) + TC_KEYS - 1) / TC_KEYS;
+}
+HY_DEVICE int pre_pieces(int nt, int cap) {
+  return nt > cap ? min(PRE_MAX_PIECES, (nt + cap - 1) / cap) : 1;
+}
+// An item's w field: 0 for a whole item, else (pieces << 26) | (piece << 20) |
+// the first partial slot of the item (its pieces use consecutive slots).
+HY_DEVICE int pre_piece_code(int ns, int sp, int slot) { return (ns << 26) | (sp << 20) | slot; }
+HY_DEVICE int pre_code_pieces(int w) { return (w >> 26) & 31; }
+HY_DEVICE int pre_code_piece(int w) { return (w >> 20) & 63; }
+HY_DEVICE int pre_code_slot(int w) { return w & 0xFFFFF; }
+// key tiles [lo, hi) that the item (w) of nt key tiles covers
+HY_DEVICE void pre_piece_range(int w, int nt, int& lo, int& hi) {
+  if (w == 0) { lo = 0; hi = nt; return; }
+  const int ns = pre_code_pieces(w), sp = pre_code_piece(w);
+  lo = sp * nt / ns;
+  hi = (sp + 1) * nt / ns;
+}
 #ifndef HY_EXP2_POLY_EVERY
 #define HY_EXP2_POLY_EVERY 0
 #endif
@@ -129,6 +170,7 @@ struct Shared {
   uint64_t tc_drain[2];      // error path: all MMAs an issuing warp issued are complete
   uint32_t tmem_base;        // TMEM columns from tcgen05.alloc
   int pre_item;              // prefill item handed to this CTA
+  int pre_last;              // this CTA's piece of a split prefill item finished last
 };
 
 HY_DEVICE uint8_t* payload_base(uint8_t* dyn) {
@@ -177,21 +219,28 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
   hy_grid_wait();
   hy_grid_trigger();
   __shared__ int ws[32];
-  __shared__ int s_total, s_cpre, s_cdec, s_bad, s_maxblk, s_anypre;
+  __shared__ int s_total, s_cpre, s_cdec, s_cpart, s_bad, s_maxblk, s_anypre, s_ptiles, s_pitems;
   if (threadIdx.x == 0) {
-    s_total = 0; s_cpre = 0; s_cdec = 0; s_bad = 0; s_maxblk = 0; s_anypre = 0;
+    s_total = 0; s_cpre = 0; s_cdec = 0; s_cpart = 0; s_bad = 0; s_maxblk = 0; s_anypre = 0;
+    s_ptiles = 0; s_pitems = 0;
   }
   __syncthreads();
-  // Pass 1: KV blocks over all decode sequences, the longest, any prefill.
-  int part = 0, mxb = 0, pre = 0;
+  // Pass 1: KV blocks over all decode sequences, the longest, any prefill, and
+  // the prefill items and their key tiles (per KV head).
+  int part = 0, mxb = 0, pre = 0, ptiles = 0, pitems = 0;
   for (int i = threadIdx.x; i < S; i += PLAN_THREADS) {
-    const int q = cu_q[i + 1] - cu_q[i];
+    const int q = cu_q[i + 1] - cu_q[i], kv = seq_lens_k[i];
     if (q == 1) {
-      const int nb = (seq_lens_k[i] + HY_BLOCK - 1) / HY_BLOCK;
+      const int nb = (kv + HY_BLOCK - 1) / HY_BLOCK;
       part += nb;
       mxb = max(mxb, nb);
     } else if (q > 1) {
       pre = 1;
+      if (kv >= q)
+        for (int t0 = 0; t0 < q; t0 += PRE_QROWS) {
+          ptiles += pre_item_tiles(kv, q, t0);
+          ++pitems;
+        }
     }
   }
 #pragma unroll
@@ -199,13 +248,33 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
     part += __shfl_xor_sync(0xffffffffu, part, o);
     mxb = max(mxb, __shfl_xor_sync(0xffffffffu, mxb, o));
     pre |= __shfl_xor_sync(0xffffffffu, pre, o);
+    ptiles += __shfl_xor_sync(0xffffffffu, ptiles, o);
+    pitems += __shfl_xor_sync(0xffffffffu, pitems, o);
   }
   if ((threadIdx.x & 31) == 0) {                // 32 shared atomics, not 1024
     atomicAdd(&s_total, part);
     atomicMax(&s_maxblk, mxb);
     atomicOr(&s_anypre, pre);
+    atomicAdd(&s_ptiles, ptiles);
+    atomicAdd(&s_pitems, pitems);
   }
   __syncthreads();
+  // Prefill pieces, only when the n items are fewer than the SMs and the
+  // step's decode work would not fill the idle SMs anyway (a decode block of
+  // one KV head, 8 KB of K/V at an SM's share of HBM bandwidth, takes about a
+  // fifth of a key tile's ~1 us on the tensor cores; the decode work must be
+  // at most a quarter of the prefill tiles).  An item of nt key tiles is cut
+  // into ceil(nt / cap) pieces, cap >= tiles / (SMs - n), so the pieces, at
+  // most tiles / cap + n, are at most the SMs: the workspace's slots.
+  const int n_sm = warp_slots / ATT_WARPS;
+  const long tiles_all = (long)s_ptiles * kv_heads;
+  const long n_items = (long)s_pitems * kv_heads;
+  const long dec_tiles = (long)s_total * kv_heads / 5;
+  const int cap = v.max_pre_part >= n_sm && n_items > 0 && n_items < n_sm &&
+                          4 * dec_tiles <= tiles_all
+                      ? (int)max((long)PRE_SPLIT_MIN,
+                                 (tiles_all + (n_sm - n_items) - 1) / (n_sm - n_items))
+                      : 0x7fffffff;
   const long target = (long)ITEMS_PER_WARP * warp_slots;
   const long want = ((long)kv_heads * s_total + target - 1) / target;
   const int split = (int)max((long)MIN_SPLIT, want);
@@ -216,10 +285,11 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
   // Pass 2: item counts, offsets, items.
   for (int base = 0; base < S; base += PLAN_THREADS) {
     const int i = base + threadIdx.x;
-    int npre = 0, ndec = 0, ns = 0, ntile = 0, nblk = 0, row = 0, kv = 0;
+    int npre = 0, ndec = 0, ns = 0, ntile = 0, nblk = 0, row = 0, kv = 0, q = 0;
+    int npart = 0, ph = 0, psl = 0;             // pieces and partial slots per KV head
     if (i < S) {
       row = cu_q[i];
-      const int q = cu_q[i + 1] - row;
+      q = cu_q[i + 1] - row;
       kv = seq_lens_k[i];
       if (q < 0 || kv < q) atomicOr(&s_bad, HY_ERR_BOUNDS);
       else if (q == 1) {
@@ -228,21 +298,30 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
         ndec = kv_heads * ns;
       } else if (q > 1) {
         ntile = (q + PRE_QROWS - 1) / PRE_QROWS;
-        npre = kv_heads * ntile;
+        for (int t = 0; t < ntile; ++t) {
+          const int n = pre_pieces(pre_item_tiles(kv, q, t * PRE_QROWS), cap);
+          ph += n;
+          if (n > 1) psl += n;
+        }
+        npre = kv_heads * ph;
+        npart = kv_heads * psl;
       }
     }
-    int tpre, tdec;
+    int tpre, tdec, tpart;
     const int opre = plan_scan(npre, ws, tpre);
     const int odec = plan_scan(ndec, ws, tdec);
-    const int cpre = s_cpre, cdec = s_cdec;
+    const int opart = plan_scan(npart, ws, tpart);
+    const int cpre = s_cpre, cdec = s_cdec, cpart = s_cpart;
     if (i < S && i < v.max_seqs)
       for (int g = 0; g < kv_heads; ++g) v.counters[i * kv_heads + g] = 0;
     bool wr = false;
-    int p0 = 0, d0 = 0;
+    int p0 = 0, d0 = 0, s0 = 0;
     if (i < S) {
       p0 = cpre + opre;
       d0 = cdec + odec;
-      if (p0 + npre > v.max_pre || d0 + ndec > v.max_dec || i >= v.max_seqs) {
+      s0 = cpart + opart;
+      if (p0 + npre > v.max_pre || d0 + ndec > v.max_dec || i >= v.max_seqs ||
+          s0 + npart > v.max_pre_part) {
         atomicOr(&s_bad, HY_ERR_PLAN);
       } else {
         v.seqinfo[i] = make_int2(d0, ns);
@@ -260,7 +339,9 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
       const int jp0 = __shfl_sync(0xffffffffu, p0, j), jd0 = __shfl_sync(0xffffffffu, d0, j);
       const int jns = __shfl_sync(0xffffffffu, ns, j), jnb = __shfl_sync(0xffffffffu, nblk, j);
       const int jrow = __shfl_sync(0xffffffffu, row, j), jkv = __shfl_sync(0xffffffffu, kv, j);
-      const int jnt = __shfl_sync(0xffffffffu, ntile, j);
+      const int jnt = __shfl_sync(0xffffffffu, ntile, j), jq = __shfl_sync(0xffffffffu, q, j);
+      const int jph = __shfl_sync(0xffffffffu, ph, j), jpsl = __shfl_sync(0xffffffffu, psl, j);
+      const int js0 = __shfl_sync(0xffffffffu, s0, j);
       for (int k = lane; k < kv_heads * jns; k += 32) {   // splits differ by at most one block
         const int g = k / jns, sp = k - g * jns;
         const int lo = mul_div(sp, jnb, jns), hi = mul_div(sp + 1, jnb, jns);
@@ -268,13 +349,24 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
         v.dec[2 * (jd0 + k) + 1] = make_int4(jrow, jkv, jns, jd0 + g * jns);
         v.dec_ids[2 * (jd0 + k)] = make_int4(-1, 0, 0, 0);
       }
+      // (KV head g, query tile t): its pieces follow those of head g's earlier
+      // query tiles; a cut item's pieces take consecutive partial slots
       for (int k = lane; k < kv_heads * jnt; k += 32) {
         const int g = k / jnt, t = k - g * jnt;
-        v.pre[jp0 + k] = make_int4(ji, g, t * PRE_QROWS, 0);
+        int pos = jp0 + g * jph, slot = js0 + g * jpsl;
+        for (int u = 0; u < t; ++u) {
+          const int n = pre_pieces(pre_item_tiles(jkv, jq, u * PRE_QROWS), cap);
+          pos += n;
+          if (n > 1) slot += n;
+        }
+        const int n = pre_pieces(pre_item_tiles(jkv, jq, t * PRE_QROWS), cap);
+        for (int sp = 0; sp < n; ++sp)
+          v.pre[pos + sp] = make_int4(ji, g, t * PRE_QROWS, n > 1 ? pre_piece_code(n, sp, slot) : 0);
+        if (n > 1) v.pre_ctr[slot] = 0;
       }
     }
     __syncthreads();
-    if (threadIdx.x == 0) { s_cpre += tpre; s_cdec += tdec; }
+    if (threadIdx.x == 0) { s_cpre += tpre; s_cdec += tdec; s_cpart += tpart; }
     __syncthreads();
   }
   if (threadIdx.x < 64 * GRAB_INTS) v.grab[threadIdx.x] = 0;
@@ -286,8 +378,9 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_kernel(
   __shared__ int bins[PLAN_THREADS];
   auto cost_bin = [&](int4 it) {                // bin 0 = most key tiles
     const int q = cu_q[it.x + 1] - cu_q[it.x], kv = seq_lens_k[it.x];
-    const int tiles = (kv - q + it.z + min(PRE_QROWS, q - it.z) + TC_KEYS - 1) / TC_KEYS;
-    return PLAN_THREADS - 1 - min(max(tiles, 0), PLAN_THREADS - 1);
+    int lo, hi;
+    pre_piece_range(it.w, pre_item_tiles(kv, q, it.z), lo, hi);
+    return PLAN_THREADS - 1 - min(max(hi - lo, 0), PLAN_THREADS - 1);
   };
   bins[threadIdx.x] = 0;
   __syncthreads();
@@ -735,6 +828,91 @@ __device__ bool decode_pair_cta(const CUtensorMap* tiles, const MainArgs& a, con
   return true;
 }
 
+// The end of one piece of a split prefill item, run by all ATT_WARPS * 32
+// softmax threads (thread rr holds row rr of the item's 256 rows): the row's
+// unnormalised O (TMEM column base tO) and (m, l) go to the piece's partial
+// slot; the piece that finishes last (counted at the item's first slot)
+// merges every piece's partials into the output row op (nullptr: a padding row)
+// and resets the count.  Piece s weighs 2^(m_s - M), M the largest m_s.
+// Returns whether every thread's waits succeeded.
+__device__ bool prefill_piece_finish(const PlanView& v, int w, int rr, uint32_t tO, float m,
+                                     float l, bool ok, __nv_bfloat16* op, Shared& sh) {
+  const int ns = pre_code_pieces(w), sp = pre_code_piece(w), slot = pre_code_slot(w);
+  const bool all_ok = !named_sync_or(MERGE_BAR, ATT_WARPS * 32, !ok);
+  if (all_ok) {
+    float4* po = v.pre_part_o + (size_t)(slot + sp) * PRE_PART_F4 + rr;
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {
+      float o[32];
+      tmem_ld32(tO + 32 * cc, o);
+      tmem_wait_ld();
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        __stcg(po + (cc * 8 + k) * 256,
+               make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]));
+    }
+    __stcg(v.pre_part_ml + (size_t)(slot + sp) * 256 + rr, make_float2(m, l));
+    __threadfence();                            // this row's partial, before the count
+  }
+  named_sync(MERGE_BAR, ATT_WARPS * 32);
+  if (threadIdx.x == 0) sh.pre_last = all_ok && atomicAdd(&v.pre_ctr[slot], 1) == ns - 1;
+  named_sync(MERGE_BAR, ATT_WARPS * 32);
+  if (!sh.pre_last) return all_ok;
+  __threadfence();                              // the other pieces' partials, after the count
+  const float2* ml = v.pre_part_ml + (size_t)slot * 256 + rr;
+  float M = NEG_INF;
+#pragma unroll 4
+  for (int s = 0; s < ns; ++s) M = fmaxf(M, __ldcg(ml + s * 256).x);
+  float L = 0.f;
+#pragma unroll 4
+  for (int s = 0; s < ns; ++s) {
+    const float2 e = __ldcg(ml + s * 256);
+    L += e.y * (M == NEG_INF ? 0.f : ex2_ftz(e.x - M));
+  }
+  const float inv = 1.f / L;
+#pragma unroll 1
+  for (int cc = 0; cc < 4; ++cc) {
+    float acc[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) acc[k] = 0.f;
+    // two pieces per round: their 16 loads are in flight together
+#pragma unroll 1
+    for (int s = 0; s < ns; s += 2) {
+      const int s1 = min(s + 1, ns - 1);
+      const float w0 = M == NEG_INF ? 0.f : ex2_ftz(__ldcg(ml + s * 256).x - M);
+      const float w1 = (s1 == s || M == NEG_INF) ? 0.f : ex2_ftz(__ldcg(ml + s1 * 256).x - M);
+      const float4* p0 = v.pre_part_o + (size_t)(slot + s) * PRE_PART_F4 + cc * 8 * 256 + rr;
+      const float4* p1 = v.pre_part_o + (size_t)(slot + s1) * PRE_PART_F4 + cc * 8 * 256 + rr;
+      float4 f0[8], f1[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        f0[k] = __ldcg(p0 + k * 256);
+        f1[k] = __ldcg(p1 + k * 256);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        acc[4 * k] += w0 * f0[k].x + w1 * f1[k].x;
+        acc[4 * k + 1] += w0 * f0[k].y + w1 * f1[k].y;
+        acc[4 * k + 2] += w0 * f0[k].z + w1 * f1[k].z;
+        acc[4 * k + 3] += w0 * f0[k].w + w1 * f1[k].w;
+      }
+    }
+    if (op) {
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint4 pk4;
+        pk4.x = pack_bf16(acc[8 * q4 + 0] * inv, acc[8 * q4 + 1] * inv);
+        pk4.y = pack_bf16(acc[8 * q4 + 2] * inv, acc[8 * q4 + 3] * inv);
+        pk4.z = pack_bf16(acc[8 * q4 + 4] * inv, acc[8 * q4 + 5] * inv);
+        pk4.w = pack_bf16(acc[8 * q4 + 6] * inv, acc[8 * q4 + 7] * inv);
+        *reinterpret_cast<uint4*>(op + 32 * cc + 8 * q4) = pk4;
+      }
+    }
+  }
+  if (threadIdx.x == 0) v.pre_ctr[slot] = 0;   // for the next launch on this plan
+  return all_ok;
+}
+
 // ------------------------------------------------------------------ prefill item
 // tcgen05, warp-specialised.  Item = (seq, kv head g, 64-token tile t0): two
 // M=128 sub-tiles X of the same tokens (query heads 4g+2X, 4g+2X+1), which see
@@ -777,7 +955,9 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
   const int prefix = kv_len - q_len;
   const int nrows = min(PRE_QROWS, q_len - t0);
   const int kv_end = prefix + t0 + nrows;
-  const int ntiles = (kv_end + TC_KEYS - 1) / TC_KEYS;
+  int tlo, thi;                                 // key tiles of this item (or piece)
+  pre_piece_range(it.w, (kv_end + TC_KEYS - 1) / TC_KEYS, tlo, thi);
+  const int ntiles = thi - tlo;
   const int nblk = (kv_end + HY_BLOCK - 1) / HY_BLOCK;
   const uint32_t sbase = smem_u32(payload);
   const uint32_t c0 = ctr;
@@ -810,11 +990,12 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
     const int lw = warp == TC_LOAD_WARP2;
     const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
     const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
-    int ids = -1;                               // lane i: block 32 (t / 8) + i of the sequence
+    int ids = -1;                               // lane i: block 32 (kt / 8) + i of the sequence
     int issued = 0;                             // tiles whose loads were issued
     for (int t = 0; t < ntiles && ok; ++t) {
-      if ((t & 7) == 0) {
-        const int b = 4 * t + lane;
+      const int kt = tlo + t;                   // key tile of the sequence
+      if (t == 0 || (kt & 7) == 0) {
+        const int b = 4 * (kt & ~7) + lane;
         ids = (b < nblk && b < a.bt_pitch) ? bt[b] : -1;
       }
       const uint32_t c = c0 + t, slot = c % TC_NS, use = c / TC_NS;
@@ -824,7 +1005,7 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
       uint64_t* full = &sh.tc_full[slot];
       if (lane == 0) mbar_arrive_expect_tx(full, TC_KV_BYTES);
       const int kv = (lane >> 1) & 1, jb = 2 * lw + (lane & 1);
-      const int id = __shfl_sync(0xffffffffu, ids, (4 * t + jb) & 31);
+      const int id = __shfl_sync(0xffffffffu, ids, (4 * kt + jb) & 31);
       if (lane < 4) {
         int r = a.oob_row;                      // past the end: zero fill
         if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
@@ -908,7 +1089,7 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
       tmem_ld32(tS, *reinterpret_cast<float(*)[32]>(&s[0]));
       tmem_ld32(tS + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
       tmem_wait_ld();
-      const int kb = t * TC_KEYS;
+      const int kb = (tlo + t) * TC_KEYS;
       if (kb + TC_KEYS - 1 > prefix + t0) {     // the tile reaches the diagonal or the end
 #pragma unroll
         for (int i = 0; i < 64; ++i)
@@ -979,15 +1160,19 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.tc_pfull[X][c & 1]);
     }
-    if (ok) {                                   // epilogue: O_X / l -> out
+    if (ok) {                                   // epilogue: O_X complete
       const uint32_t c = c0 + ntiles - 1;
       ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_odone[X], c & 1, a.err));
       tc_fence_after();
-      // tcgen05.ld is warp-collective: every lane loads, only real rows store
-      const bool store = ok && j < nrows;
+    }
+    // tcgen05.ld is warp-collective: every lane loads, only real rows store
+    const bool store = ok && j < nrows;
+    __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + 2 * X +
+                                 (r >> 6)) * HY_HEAD_DIM;
+    if (it.w != 0) {                            // a piece: every softmax thread takes part
+      ok = prefill_piece_finish(v, it.w, X * 128 + r, tO, m, l, ok, store ? op : nullptr, sh);
+    } else if (ok) {                            // O_X / l -> out
       const float inv = 1.f / l;
-      __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + 2 * X +
-                                   (r >> 6)) * HY_HEAD_DIM;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
         float o[32];
@@ -1215,10 +1400,13 @@ int device_sms(int dev) {
 // ------------------------------------------------------------------ host side
 int hy_attn_warp_slots(int dev) { return device_sms(dev) * ATT_WARPS; }
 
-PlanDims hy_attn_plan_dims(int max_seqs, int max_tokens, int kv_heads, int dev) {
+PlanDims hy_attn_plan_dims(int max_seqs, int max_tokens, int kv_heads, int dev,
+                           bool split_prefill) {
   PlanDims d;
   d.max_seqs = max_seqs;
-  d.max_pre = kv_heads * (max_tokens / PRE_QROWS + max_seqs);
+  // a step's split pieces are at most the SMs (see plan_kernel)
+  d.max_pre_part = split_prefill ? device_sms(dev) : 0;
+  d.max_pre = kv_heads * (max_tokens / PRE_QROWS + max_seqs) + d.max_pre_part;
   d.max_dec = kv_heads * max_seqs + ITEMS_PER_WARP * hy_attn_warp_slots(dev);
   d.kv_heads = kv_heads;
   return d;
@@ -1237,6 +1425,9 @@ size_t hy_attn_workspace_bytes(const PlanDims& d) {
   off = align256(off + (size_t)d.max_dec * HY_GROUP * sizeof(float2));
   off = align256(off + (size_t)d.max_seqs * d.kv_heads * sizeof(int));
   off = align256(off + 64 * GRAB_INTS * sizeof(int));
+  off = align256(off + (size_t)d.max_pre_part * PRE_PART_F4 * sizeof(float4));
+  off = align256(off + (size_t)d.max_pre_part * 256 * sizeof(float2));
+  off = align256(off + (size_t)d.max_pre_part * sizeof(int));
   return off;
 }
 
@@ -1263,9 +1454,16 @@ static PlanView make_view(void* ws, const PlanDims& d) {
   v.counters = reinterpret_cast<int*>(p + off);
   off = align256(off + (size_t)d.max_seqs * d.kv_heads * sizeof(int));
   v.grab = reinterpret_cast<int*>(p + off);
+  off = align256(off + 64 * GRAB_INTS * sizeof(int));
+  v.pre_part_o = reinterpret_cast<float4*>(p + off);
+  off = align256(off + (size_t)d.max_pre_part * PRE_PART_F4 * sizeof(float4));
+  v.pre_part_ml = reinterpret_cast<float2*>(p + off);
+  off = align256(off + (size_t)d.max_pre_part * 256 * sizeof(float2));
+  v.pre_ctr = reinterpret_cast<int*>(p + off);
   v.max_pre = d.max_pre;
   v.max_dec = d.max_dec;
   v.max_seqs = d.max_seqs;
+  v.max_pre_part = d.max_pre_part;
   return v;
 }
 

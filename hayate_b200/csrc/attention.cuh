@@ -25,10 +25,12 @@ struct KvMaps {
 
 // Capacities of one attention workspace.
 struct PlanDims {
-  int max_pre;     // prefill items (kv_head x 16-token tile)
-  int max_dec;     // decode items (kv_head x block range)
+  int max_pre;       // prefill items (kv_head x 64-token tile, or a key range of one)
+  int max_dec;       // decode items (kv_head x block range)
   int max_seqs;
   int kv_heads;
+  int max_pre_part;  // partial-result slots of prefill items split over key ranges
+                     // (0: the plan splits none)
 };
 
 // Device view of a workspace (see attention.cu for the layout).
@@ -48,11 +50,20 @@ struct PlanView {
   float2* part_ml;    // [max_dec][4]  (running max in log2 units, sum)
   int* counters;      // [max_seqs][kv_heads] finished split items (zeroed by the plan)
   int* grab;          // [64][4] per layer: next decode item, CTAs done, next prefill item
-  int max_pre, max_dec, max_seqs;
+  float4* pre_part_o; // [max_pre_part][32][256]: per piece of a split prefill item, its
+                      // unnormalised O as float4 c of row r at [c][r] (rows in the
+                      // item's order: sub-tile X row r at 128 X + r)
+  float2* pre_part_ml;// [max_pre_part][256] (running max in log2 units, sum) per row
+  int* pre_ctr;       // [max_pre_part] finished pieces, at a split item's first slot
+                      // (zeroed by the plan and by the merging piece)
+  int max_pre, max_dec, max_seqs, max_pre_part;
 };
 
 int hy_attn_warp_slots(int dev);
-PlanDims hy_attn_plan_dims(int max_seqs, int max_tokens, int kv_heads, int dev);
+// split_prefill false: a plan on these dimensions splits no prefill item over
+// key ranges, and the workspace holds no partial results for them
+PlanDims hy_attn_plan_dims(int max_seqs, int max_tokens, int kv_heads, int dev,
+                           bool split_prefill = true);
 size_t hy_attn_workspace_bytes(const PlanDims& d);
 
 cudaError_t hy_launch_attn_plan(const int32_t* cu_q, const int32_t* seq_lens_k, int S,

@@ -97,7 +97,8 @@ extern "C" int hy_varlen_attention_noalloc(
   }
   int dev = 0;
   cudaGetDevice(&dev);
-  const PlanDims d = hy_attn_plan_dims(num_seqs, num_tokens, kv_heads, dev);
+  // no prefill splits: their partial results would not fit the fixed scratch
+  const PlanDims d = hy_attn_plan_dims(num_seqs, num_tokens, kv_heads, dev, false);
   const size_t need = hy_attn_workspace_bytes(d);
   if (need > HY_NOALLOC_SCRATCH_BYTES) {
     char buf[256];
