@@ -147,8 +147,8 @@ HY_DEVICE void pre_piece_range(int w, int nt, int& lo, int& hi) {
 // prefill softmax: 1 in EXP2_POLY_EVERY pairs of weights by exp2_poly (0: none).
 // Off: with the row max and sum as independent chains the exp2 unit is not
 // the limit, and the polynomial's extra instructions cost issue slots (4
-// prefill chunks of 512 / 16 chunks: 94.8 / 339.5 us with none, 98.1 / 352.3
-// with 1 in 8, 103.7 / 371.5 with 1 in 4, 112.3 / 403.7 with 1 in 2).
+// prefill chunks of 512 / 16 chunks, one box: 83.3 / 300.7 us with none,
+// 82.9 / 299.3 with 1 in 8, 85.0 / 307.2 with 1 in 4, 93.0 / 334.1 with 1 in 2).
 constexpr int EXP2_POLY_EVERY = HY_EXP2_POLY_EVERY;
 // Lazy rescaling: the running max is only raised when a new score exceeds it
 // by more than 2^RESCALE_LOG2; until then probabilities may exceed 1 by up to
@@ -168,6 +168,7 @@ struct Shared {
   uint64_t tc_pfull[2][2];   // P_X[b] written over S_X[b] by the 4 softmax warps of X
   uint64_t tc_odone[2];      // O_X += P_X V complete (once per key tile)
   uint64_t tc_drain[2];      // error path: all MMAs an issuing warp issued are complete
+  uint64_t tc_qfull;         // the item's Q landed (TMA transaction bytes, once per item)
   uint32_t tmem_base;        // TMEM columns from tcgen05.alloc
   int pre_item;              // prefill item handed to this CTA
   int pre_last;              // this CTA's piece of a split prefill item finished last
@@ -944,8 +945,9 @@ __device__ bool prefill_piece_finish(const PlanView& v, int w, int rr, uint32_t 
 // the current or the previous phase.  Returns false if a wait ran out; the
 // roles then drain their own asynchronous work before the item ends.
 __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* tiles,
-                                const MainArgs& a, const PlanView& v, int item, uint8_t* payload,
-                                Shared& sh, uint32_t tmem, uint32_t& ctr) {
+                                const CUtensorMap* qmap, const MainArgs& a, const PlanView& v,
+                                int item, uint8_t* payload, Shared& sh, uint32_t tmem,
+                                uint32_t& ctr, uint32_t qpar, int* next_ctr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int4 it = v.pre_sorted[item];
   const int seq = it.x, g = it.y, t0 = it.z;
@@ -963,22 +965,7 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
   const uint32_t c0 = ctr;
   ctr += ntiles;
   bool ok = true;
-
-  if (warp < ATT_WARPS) {                       // Q rows -> smem (128B-swizzled, K-major)
-    const int X = warp >> 2, r = (warp & 3) * 32 + lane;
-    const int h = 2 * X + (r >> 6), j = r & 63;
-    const bool valid = j < nrows;
-    const uint4* qp = reinterpret_cast<const uint4*>(
-        a.q + ((size_t)(row0 + t0 + (valid ? j : 0)) * a.q_heads + g * HY_GROUP + h) * HY_HEAD_DIM);
-    uint8_t* qrow = payload + X * TC_Q_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const uint4 val = valid ? qp[c] : make_uint4(0u, 0u, 0u, 0u);
-      *reinterpret_cast<uint4*>(qrow + (c >> 3) * (TC_Q_BYTES / 2) + (((c & 7) ^ (r & 7)) << 4)) = val;
-    }
-    fence_proxy_async();                        // generic smem writes -> async proxy
-  }
-  __syncthreads();
+  int next = 0x7fffffff;                        // thread 0: the CTA's next item
 
   if (warp == TC_LOAD_WARP || warp == TC_LOAD_WARP2) {
     // Two load warps, lw = 0, 1, each for blocks 2 lw and 2 lw + 1 of every key
@@ -988,6 +975,18 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
     // serial round trips of ~150-270 cycles each, so the tile's supply rate is
     // set by how many of them a warp makes per tile.
     const int lw = warp == TC_LOAD_WARP2;
+    // Q first: one 32 KB box per sub-tile X (64 columns x 64 tokens x query heads
+    // 4g + 2X, 4g + 2X + 1 x both column halves), landing as the K-major
+    // operand [half][128 rows][64] with row = 64 (head - 4g - 2X) + token; the
+    // Q region is free, the previous item's MMAs having completed before it
+    // ended.  Rows past the chunk read later tokens (or zeros past the last
+    // token): their scores are computed but never stored.
+    if (lw == 0 && lane == 0) {
+      mbar_arrive_expect_tx(&sh.tc_qfull, 2 * TC_Q_BYTES);
+      for (int X = 0; X < 2; ++X)
+        tma_load_4d(payload + X * TC_Q_BYTES, qmap, 0, row0 + t0, g * HY_GROUP + 2 * X, 0,
+                    &sh.tc_qfull);
+    }
     const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
     const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
     int ids = -1;                               // lane i: block 32 (kt / 8) + i of the sequence
@@ -1024,6 +1023,8 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
         mbar_wait(&sh.tc_full[c % TC_NS], (c / TC_NS) & 1, nullptr);
       }
     }
+    // Q has landed before the item ends (the next item's Q reuses the region)
+    if (lw == 0 && lane == 0) mbar_wait(&sh.tc_qfull, qpar, nullptr);
   } else if (warp == TC_MMA_WARP || warp == TC_MMA_WARP1) {
     // one MMA warp per sub-tile X: its lane 0 issues S_X(t), then O_X += P_X(t-1)
     // V_{t-1}; both warps commit to the slot's free barrier after P V (count 2)
@@ -1032,6 +1033,8 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
       constexpr uint32_t ID_S = tc_idesc_bf16(128, TC_KEYS, false);
       constexpr uint32_t ID_O = tc_idesc_bf16(128, HY_HEAD_DIM, true);
       const uint64_t dQ = tc_desc_sw128(sbase + X * TC_Q_BYTES, 16, 1024);
+      ok = mbar_wait(&sh.tc_qfull, qpar, a.err);                // Q_X landed
+      tc_fence_after();
       for (int t = 0; t <= ntiles && ok; ++t) {
         if (t < ntiles) {                       // S_X(t) = Q_X K_t^T into buffer c % 2
           const uint32_t c = c0 + t, slot = c % TC_NS;
@@ -1081,6 +1084,11 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
     for (int t = 0; t < ntiles && ok; ++t) {
       const uint32_t c = c0 + t;
       const uint32_t tS = tmem + lane_base + tm_s(X, c & 1);
+      // the next item is taken when this one's last key tile starts: its
+      // latency hides behind the tile, and a CTA holds no item it cannot start
+      // soon (CTAs start microseconds apart; taking it at the item's start
+      // left late CTAs without items: one or two per CTA ran 15-25 % slower)
+      if (t == ntiles - 1 && threadIdx.x == 0) next = atomicAdd(next_ctr, 1);
       // waits are made warp-uniform: tcgen05.ld/st below are warp-collective
       ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_sfull[X][c & 1], (c >> 1) & 1, a.err));
       if (!ok) break;
@@ -1192,6 +1200,7 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
       }
     }
   }
+  if (threadIdx.x == 0) sh.pre_item = next;
   tc_fence_before();
   if (__syncthreads_or(!ok)) ok = false;
   return ok;
@@ -1199,7 +1208,7 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
 
 __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     const __grid_constant__ CUtensorMap kv_kgroups, const __grid_constant__ CUtensorMap kv_tiles,
-    MainArgs a, PlanView v) {
+    const __grid_constant__ CUtensorMap q_map, MainArgs a, PlanView v) {
   __shared__ Shared sh;
   extern __shared__ uint8_t dyn_smem[];
   uint8_t* payload = payload_base(dyn_smem);
@@ -1207,6 +1216,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   if (threadIdx.x == 0) {
     prefetch_tmap(&kv_kgroups);
     prefetch_tmap(&kv_tiles);
+    prefetch_tmap(&q_map);
     for (int w = 0; w < ATT_WARPS; ++w)
       for (int s = 0; s < DEC_STAGES; ++s) mbar_init(&sh.dec_bar[w][s], 1);
     for (int s = 0; s < TC_NS; ++s) {
@@ -1222,6 +1232,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
     }
     mbar_init(&sh.tc_drain[0], 1);
     mbar_init(&sh.tc_drain[1], 1);
+    mbar_init(&sh.tc_qfull, 1);
     fence_mbar_init();
   }
   // set-up that reads nothing an earlier kernel wrote runs before the wait: the
@@ -1274,15 +1285,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   uint32_t dec_phase = 0, tile_ctr = 0;
   bool ok = true;
   int* grab = v.grab + GRAB_INTS * (a.layer & 63);
-  // prefill items: CTA-wide, in the plan's order (most key tiles first)
+  // prefill items: CTA-wide, in the plan's order (most key tiles first); thread
+  // 0 takes the next item from the counter during the current one's last tile
   if (use_tmem) {
-    while (ok) {
-      if (threadIdx.x == 0) sh.pre_item = atomicAdd(&grab[2], 1);
-      __syncthreads();
+    if (threadIdx.x == 0) sh.pre_item = atomicAdd(&grab[2], 1);
+    __syncthreads();
+    for (uint32_t n = 0; ok; ++n) {
       const int k = sh.pre_item;
       __syncthreads();                          // read before thread 0 writes the next one
       if (k >= n_pre) break;
-      ok = prefill_item_tc(&kv_kgroups, &kv_tiles, a, v, k, payload, sh, tmem, tile_ctr);
+      ok = prefill_item_tc(&kv_kgroups, &kv_tiles, &q_map, a, v, k, payload, sh, tmem, tile_ctr,
+                           n & 1, &grab[2]);
     }
   }
   // decode items (warps 0..ATT_WARPS-1): each warp takes the next one from this
@@ -1474,8 +1487,8 @@ cudaError_t hy_launch_attn_plan(const int32_t* cu_q, const int32_t* seq_lens_k, 
                    kv_heads, hy_attn_warp_slots(dev), make_view(ws, d), err);
 }
 
-cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const void* cache, const void* q, void* out,
-                                int q_heads,
+cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const CUtensorMap& qmap, const void* cache,
+                                const void* q, void* out, int q_heads,
                                 int kv_heads, int layer_row_base, int oob_row, int num_blocks,
                                 const int32_t* block_tables, int bt_pitch,
                                 const int32_t* seq_bt_row, const int32_t* cu_q,
@@ -1513,7 +1526,7 @@ cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const void* cache, const voi
   const PlanView v = make_view(ws, d);
   const int grid = device_sms(dev) * g_ctas_per_sm[dev < 64 && dev >= 0 ? dev : 0];
   return hy_launch(attn_main_kernel, dim3(grid), dim3(ATT_THREADS), SMEM_BYTES, st, maps.kgroups,
-                   maps.tiles, a, v);
+                   maps.tiles, qmap, a, v);
 }
 
 cudaError_t hy_launch_attn_fp32(const float* q, float* out, int T, int q_heads, int kv_heads,

@@ -69,8 +69,12 @@ size_t hy_attn_workspace_bytes(const PlanDims& d);
 cudaError_t hy_launch_attn_plan(const int32_t* cu_q, const int32_t* seq_lens_k, int S,
                                 int kv_heads, const PlanDims& d, void* ws, int32_t* err,
                                 int dev, cudaStream_t st);
-cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const void* cache, const void* q, void* out,
-                                int q_heads,
+// The query rows' tensor map (hy_attention_q_map in capi.cu): 4-D (64 columns,
+// tokens at q_heads x 256 B, heads at 256 B, 2 halves at 128 B), box 64 x 64 x
+// 2 x 2 (one prefill sub-tile's Q, 32 KB, 128-byte swizzle).
+int hy_attention_q_map(const void* q, int num_tokens, int q_heads, CUtensorMap* out);
+cudaError_t hy_launch_attn_bf16(const KvMaps& maps, const CUtensorMap& qmap, const void* cache,
+                                const void* q, void* out, int q_heads,
                                 int kv_heads, int layer_row_base, int oob_row, int num_blocks,
                                 const int32_t* block_tables, int bt_pitch,
                                 const int32_t* seq_bt_row, const int32_t* cu_q,

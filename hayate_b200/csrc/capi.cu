@@ -164,6 +164,30 @@ int hy_attention_kv_map(int dev, const void* base, long rows, KvMaps* out) {
   return kv_map_for(dev, base, rows, out);
 }
 
+// The query rows of one call as a tensor map (encoded per call: the token count
+// changes every step, and encoding is host arithmetic).  Element (x, t, h, z) is
+// column 64 z + x of head h of token t; tokens past num_tokens read zeros.
+int hy_attention_q_map(const void* q, int num_tokens, int q_heads, CUtensorMap* out) {
+  int rc = get_encoder();
+  if (rc) return rc;
+  if ((reinterpret_cast<uintptr_t>(q) & 15) != 0)
+    return fail(HY_E_INVALID, "hy_varlen_attention: q must be 16-byte aligned");
+  cuuint64_t dims[4] = {64, (cuuint64_t)num_tokens, (cuuint64_t)q_heads, 2};
+  cuuint64_t strides[3] = {(cuuint64_t)q_heads * HY_HEAD_DIM * 2, HY_HEAD_DIM * 2, 128};
+  cuuint32_t box[4] = {64, 64, 2, 2};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(q), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[64];
+    snprintf(buf, sizeof(buf), "%d", (int)r);
+    return fail(HY_E_CUDA, "cuTensorMapEncodeTiled failed on q (CUresult %s)", buf);
+  }
+  return HY_OK;
+}
+
 void hy_set_error(const char* msg) { snprintf(g_last_error, sizeof(g_last_error), "%s", msg); }
 
 bool hy_pdl_enabled() {
@@ -361,8 +385,11 @@ int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tok
   KvMaps map;
   int rc = kv_map_for(dev, kv_cache, rows, &map);
   if (rc) return rc;
+  CUtensorMap qmap;
+  rc = hy_attention_q_map(q, num_tokens, q_heads, &qmap);
+  if (rc) return rc;
   return cuda_result(
-      hy_launch_attn_bf16(map, kv_cache, q, out, q_heads, kv_heads, (int)(layer * layer_rows), (int)rows,
+      hy_launch_attn_bf16(map, qmap, kv_cache, q, out, q_heads, kv_heads, (int)(layer * layer_rows), (int)rows,
                           num_blocks, block_tables, bt_pitch, seq_bt_row, cu_seqlens_q,
                           seq_lens_k, num_seqs, scale, d, workspace, err, dev, as_stream(stream),
                           flags),

@@ -113,11 +113,14 @@ extern "C" int hy_varlen_attention_noalloc(
   KvMaps map;
   int rc = hy_attention_kv_map(dev, kv_cache, rows, &map);
   if (rc) return rc;
+  CUtensorMap qmap;
+  rc = hy_attention_q_map(q, num_tokens, q_heads, &qmap);
+  if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = hy_launch_attn_plan(cu_seqlens_q, seq_lens_k, num_seqs, kv_heads, d, ws, err,
                                       dev, st);
   if (e == cudaSuccess)
-    e = hy_launch_attn_bf16(map, kv_cache, q, out, q_heads, kv_heads, (int)(layer * layer_rows), (int)rows,
+    e = hy_launch_attn_bf16(map, qmap, kv_cache, q, out, q_heads, kv_heads, (int)(layer * layer_rows), (int)rows,
                             num_blocks, block_tables, bt_pitch, seq_bt_row, cu_seqlens_q,
                             seq_lens_k, num_seqs, scale, d, ws, err, dev, st);
   if (e != cudaSuccess) {

@@ -146,8 +146,11 @@ int hy_attention_plan(const int32_t* cu_seqlens_q, const int32_t* seq_lens_k, in
 
 /* Causal varlen GQA attention over the paged cache of one layer, chunked
  * prefill and decode in one launch.  seq_bt_row (nullable) maps sequence i to
- * its block-table row.  bf16 runs the TMA + tensor-core kernel; fp32 a scalar
- * kernel for parity runs.  max_seqs/max_tokens must equal those given to
+ * its block-table row.  bf16 runs the TMA + tensor-core kernel (q and the cache
+ * 16-byte aligned: both are read by TMA); fp32 a scalar kernel for parity runs.
+ * The plan of a prefill-only step with fewer prefill items (64 query tokens x
+ * KV head) than SMs cuts long items into key-range pieces; the workspace holds
+ * their partial results.  max_seqs/max_tokens must equal those given to
  * hy_attention_plan for the same workspace.  The first bf16 call after a plan
  * caches each decode item's block-table row and first block ids in the
  * workspace for the later calls: block_tables and seq_bt_row must not change
