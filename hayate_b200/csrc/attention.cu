@@ -926,10 +926,14 @@ __device__ bool prefill_piece_finish(const PlanView& v, int w, int rr, uint32_t 
 //   lane 0           b = t % 2, then O_X += P_X(t-1) V_{t-1} (A operand read from
 //                    TMEM), each followed by tcgen05.commit to the barrier its
 //                    consumer waits on;
-//   warps 9, 11      load K_t and V_t (4 TMA boxes each: one whole 4 KB block
-//                    tile per box) into ring slot c % TC_NS once the MMAs of the
-//                    slot's previous use are done, each warp two of the tile's
-//                    four blocks.
+//   warps 9, 11      warp 9 first loads the item's Q (one 32 KB TMA box per
+//                    sub-tile, waited for by the MMA warps on tc_qfull, once
+//                    per item); both load K_t and V_t (4 TMA boxes each: one
+//                    whole 4 KB block tile per box) into ring slot c % TC_NS
+//                    once the MMAs of the slot's previous use are done, each
+//                    warp two of the tile's four blocks.
+// The item may cover a key-tile range [tlo, thi) only (a piece of a cut item:
+// see prefill_piece_finish); the key tiles below are those of the range.
 // With two S buffers the MMA warp issues S(t+1) while the softmax works on
 // S(t), so the softmax never waits for its scores once the pipeline is full.
 // S(t) may overwrite buffer b only after PV(t-2) has read P(t-2) from it: the
