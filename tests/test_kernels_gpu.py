@@ -410,6 +410,91 @@ def test_attention_split_prefill_pieces(name, items):
     assert (outs[0].float() - reference_attention(b)).abs().max().item() <= 2e-2
 
 
+def _plan_items(ws, S, T, kv_heads):
+    """The plan's prefill items in run order, read from the workspace: header
+    word 0 is their count; the sorted items follow the by-sequence ones
+    (256-byte aligned int4 arrays of max_pre entries, max_pre = kv_heads x
+    (T / 64 + S) + one piece slot per SM)."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    max_pre = kv_heads * (T // 64 + S) + sms
+    a256 = lambda x: (x + 255) // 256 * 256
+    off = 256 + a256(max_pre * 16)
+    n = int(ws[:4].view(torch.int32).item())
+    items = ws[off:off + 16 * n].view(torch.int32).view(n, 4).cpu().tolist()
+    return items, sms
+
+
+@pytest.mark.parametrize("name", ["prefill_long_prior", "prefill_longer_prior",
+                                  "prefill_ragged_prior", "prefill_many"])
+def test_attention_plan_pieces_partition_each_item(name):
+    """Every 64-token query tile x KV head appears as one whole item or as
+    pieces that agree on their count and partial slot, number 0..n-1 once each,
+    and cover its key tiles [0, nt) exactly; at most one piece per SM; items in
+    run order have non-increasing key tiles.  (prefill_many: 376 items, more
+    than the SMs, so none is cut.)"""
+    q_lens, kv_lens = CASES[name]
+    S, T = len(q_lens), sum(q_lens)
+    cu = i32(np.concatenate([[0], np.cumsum(q_lens)]).tolist())
+    kv = i32(kv_lens)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = torch.zeros(K.attention_workspace_size(S, T, 8), dtype=torch.uint8, device=dev)
+    K.attention_plan(cu, kv, S, 8, S, T, ws, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    items, sms = _plan_items(ws, S, T, 8)
+    groups, tiles_seen, pieces = {}, [], 0
+    for seq, g, t0, w in items:
+        q, k = q_lens[seq], kv_lens[seq]
+        nt = (k - q + t0 + min(64, q - t0) + 63) // 64
+        if w == 0:
+            lo, hi, key = 0, nt, None
+        else:
+            ns, sp, slot = (w >> 26) & 31, (w >> 20) & 63, w & 0xFFFFF
+            lo, hi = sp * nt // ns, (sp + 1) * nt // ns
+            key = (ns, slot)
+            pieces += 1
+        groups.setdefault((seq, g, t0), []).append((lo, hi, key))
+        tiles_seen.append(hi - lo)
+    want = {(s, g, t0) for s, q in enumerate(q_lens) if q > 1 for g in range(8)
+            for t0 in range(0, q, 64)}
+    assert set(groups) == want
+    for parts in groups.values():
+        assert len({p[2] for p in parts}) == 1                    # one count and slot
+        if parts[0][2] is not None:
+            assert len(parts) == parts[0][2][0]
+        cover = sorted((lo, hi) for lo, hi, _ in parts)
+        assert cover[0][0] == 0 and all(a[1] == b[0] for a, b in zip(cover, cover[1:]))
+        assert all(hi > lo for lo, hi in cover)
+    assert pieces <= sms
+    assert tiles_seen == sorted(tiles_seen, reverse=True)
+    if name == "prefill_many":
+        assert pieces == 0
+    else:
+        assert pieces > 0
+
+
+def test_attention_rejects_unaligned_queries():
+    """The bf16 path reads q by TMA: a q that does not start on 16 bytes is
+    refused on the host (no launch), and the next aligned call is exact."""
+    from hayate_b200._lib import HayateError
+    b = random_paged_batch([40, 1], [300, 77], kv_heads=8, seed=9)
+    S, T = b["S"], b["T"]
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = torch.zeros(K.attention_workspace_size(S, T, 8), dtype=torch.uint8, device=dev)
+    K.attention_plan(b["cu"], b["kv"], S, 8, S, T, ws, err)
+    shifted = torch.empty(T * 32 * 128 + 1, dtype=torch.bfloat16, device=dev)[1:].view(T, 32, 128)
+    shifted.copy_(b["q"])
+    out = torch.full_like(b["q"], float("nan"))
+    with pytest.raises(HayateError, match="16-byte aligned"):
+        K.varlen_attention(shifted, out, b["cache"], b["layer"], b["bt"], b["cu"], b["kv"], S, S,
+                           T, ws, err=err)
+    K.varlen_attention(b["q"], out, b["cache"], b["layer"], b["bt"], b["cu"], b["kv"], S, S, T, ws,
+                       err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert (out.float() - reference_attention(b)).abs().max().item() <= 2e-2
+
+
 def test_attention_bf16_block_table_indirection_and_headroom():
     q_lens, kv_lens = [1, 40, 1, 1], [77, 300, 16, 5]
     b = random_paged_batch(q_lens, kv_lens, kv_heads=2, seed=5)
