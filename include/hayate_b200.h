@@ -182,9 +182,10 @@ int hy_varlen_attention(int32_t dtype, const void* q, void* out, int32_t num_tok
  * until the process exits; batches above 256 sequences, 8192 query tokens or
  * 8 KV heads are rejected (HY_E_INVALID).  The first call on a device looks up
  * the array's address there; make that first call before any stream capture.
- * All calls share the array, so calls that overlap on the GPU race.  No
- * counterpart in the reference: it adds an allocation-free way into
- * hy_varlen_attention's kernels. */
+ * All calls share the array, so calls that overlap on the GPU race.  Its plan
+ * cuts no prefill item into key-range pieces (their partial results would not
+ * fit the array).  No counterpart in the reference: it adds an allocation-free
+ * way into hy_varlen_attention's kernels. */
 int hy_varlen_attention_noalloc(const void* q, void* out, int32_t num_tokens, int32_t q_heads,
                                 int32_t kv_heads, const void* kv_cache, int32_t num_layers,
                                 int32_t num_blocks, int32_t layer, const int32_t* block_tables,
