@@ -90,6 +90,8 @@ constexpr int ITEMS_PER_WARP = HY_ITEMS_PER_WARP;                // decode items
 #endif
 constexpr int GROUP_MAX_BLOCKS = HY_GROUP_MAX_BLOCKS;
 constexpr int MERGE_BAR = 1;                                     // named barrier of the decode warps
+constexpr int PRE_LOAD_BAR = 2;                                  // named barrier of the two prefill
+                                                                 // load warps
 constexpr int GRAB_INTS = 4;                                     // per layer: decode item, CTAs
                                                                  // done, prefill item, spare
 // a split-K merge stages the partials of MERGE_CHUNK splits at a time (2 KB of O
@@ -172,6 +174,8 @@ struct Shared {
   uint32_t tmem_base;        // TMEM columns from tcgen05.alloc
   int pre_item;              // prefill item handed to this CTA
   int pre_last;              // this CTA's piece of a split prefill item finished last
+  int pre_prefetch;          // the next item's key tiles its Q and loads were issued
+                             // for by the current item's load warps (-1: none)
 };
 
 HY_DEVICE uint8_t* payload_base(uint8_t* dyn) {
@@ -915,6 +919,70 @@ __device__ bool prefill_piece_finish(const PlanView& v, int w, int rr, uint32_t 
 }
 
 // ------------------------------------------------------------------ prefill item
+// Geometry of the prefill item (or piece) at run-order index `item`.
+struct PreItem {
+  int seq, g, t0, row0, nrows, prefix, kv_len, tlo, thi, nblk, w;
+};
+HY_DEVICE PreItem pre_item_geom(const MainArgs& a, const PlanView& v, int item) {
+  const int4 it = v.pre_sorted[item];
+  PreItem p;
+  p.seq = it.x;
+  p.g = it.y;
+  p.t0 = it.z;
+  p.w = it.w;
+  p.row0 = a.cu_q[p.seq];
+  const int q_len = a.cu_q[p.seq + 1] - p.row0;
+  p.kv_len = a.seq_lens_k[p.seq];
+  p.prefix = p.kv_len - q_len;
+  p.nrows = min(PRE_QROWS, q_len - p.t0);
+  const int kv_end = p.prefix + p.t0 + p.nrows;
+  pre_piece_range(p.w, (kv_end + TC_KEYS - 1) / TC_KEYS, p.tlo, p.thi);
+  p.nblk = (kv_end + HY_BLOCK - 1) / HY_BLOCK;
+  return p;
+}
+HY_DEVICE const int32_t* pre_block_table(const MainArgs& a, int seq) {
+  const int row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
+  return a.block_tables + (size_t)row * a.bt_pitch;
+}
+// Q of item p: one 32 KB box per sub-tile X (64 columns x 64 tokens x query
+// heads 4g + 2X, 4g + 2X + 1 x both column halves), landing as the K-major
+// operand [half][128 rows][64] with row = 64 (head - 4g - 2X) + token, counted
+// on tc_qfull.  Rows past the chunk read later tokens (or zeros past the last
+// token): their scores are computed but never stored.  One thread.
+HY_DEVICE void pre_issue_q(const CUtensorMap* qmap, const PreItem& p, uint8_t* payload,
+                           Shared& sh) {
+  mbar_arrive_expect_tx(&sh.tc_qfull, 2 * TC_Q_BYTES);
+  for (int X = 0; X < 2; ++X)
+    tma_load_4d(payload + X * TC_Q_BYTES, qmap, 0, p.row0 + p.t0, p.g * HY_GROUP + 2 * X, 0,
+                &sh.tc_qfull);
+}
+// One load warp's (lw) share of key tile kt of item p, ring counter c: lane 0
+// waits for the slot and posts the warp's byte count; lanes 0-3 issue one 4 KB
+// box each (K of blocks 2 lw, 2 lw + 1, then their V; `id` is the lane's block
+// id).  Returns false (warp-uniform) if the wait ran out.
+HY_DEVICE bool pre_issue_tile(const CUtensorMap* kgroups, const CUtensorMap* tiles,
+                              const MainArgs& a, int g, int lw, int lane, uint32_t c, int id,
+                              uint8_t* payload, Shared& sh) {
+  const uint32_t slot = c % TC_NS, use = c / TC_NS;
+  bool w_ok = true;
+  if (lane == 0) w_ok = mbar_wait(&sh.tc_free[slot], (use & 1) ^ 1, a.err);
+  if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) return false;
+  uint64_t* full = &sh.tc_full[slot];
+  if (lane == 0) mbar_arrive_expect_tx(full, TC_KV_BYTES);
+  if (lane < 4) {
+    const int kv = (lane >> 1) & 1, jb = 2 * lw + (lane & 1);
+    int r = a.oob_row;                          // past the end: zero fill
+    if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
+    else if (id >= 0) r = kv_row(a, id, kv, g);
+    if (kv)
+      tma_load_3d(payload + TC_V_OFF + slot * TC_KV_BYTES + jb * 4096, tiles, 0, r, 0, full);
+    else
+      tma_load_4d(payload + TC_K_OFF + slot * TC_KV_BYTES + jb * 4096, kgroups, 0, r, 0, 0,
+                  full);
+  }
+  return true;
+}
+
 // tcgen05, warp-specialised.  Item = (seq, kv head g, 64-token tile t0): two
 // M=128 sub-tiles X of the same tokens (query heads 4g+2X, 4g+2X+1), which see
 // the same keys and masks, so each 64-key K/V tile is loaded once for both.
@@ -934,6 +1002,11 @@ __device__ bool prefill_piece_finish(const PlanView& v, int w, int rr, uint32_t 
 //                    warp two of the tile's four blocks.
 // The item may cover a key-tile range [tlo, thi) only (a piece of a cut item:
 // see prefill_piece_finish); the key tiles below are those of the range.
+// Once their own loads are issued, the load warps take the CTA's next item
+// from the counter and issue its Q (after the S MMAs of this item's last tile)
+// and its first TC_NS key tiles (as this item's P V MMAs free the slots), so
+// that the next item's first MMA needs no load latency after this item's
+// epilogue; the next call skips what was issued (pf).
 // With two S buffers the MMA warp issues S(t+1) while the softmax works on
 // S(t), so the softmax never waits for its scores once the pipeline is full.
 // S(t) may overwrite buffer b only after PV(t-2) has read P(t-2) from it: the
@@ -946,78 +1019,47 @@ __device__ bool prefill_piece_finish(const PlanView& v, int w, int rr, uint32_t 
 // completes exactly once per tile (odone), per use of its buffer (sfull, pfull:
 // every second tile) or per use of its slot (ring barriers), and no role can
 // run a full phase ahead of the role that waits on it, so a wait is always on
-// the current or the previous phase.  Returns false if a wait ran out; the
+// the current or the previous phase (the load warps, which can get ahead of
+// the S MMAs of a short item, wait for its S phases in order).  Returns false if a wait ran out; the
 // roles then drain their own asynchronous work before the item ends.
 __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* tiles,
                                 const CUtensorMap* qmap, const MainArgs& a, const PlanView& v,
                                 int item, uint8_t* payload, Shared& sh, uint32_t tmem,
-                                uint32_t& ctr, uint32_t qpar, int* next_ctr) {
+                                uint32_t& ctr, uint32_t qpar, int pf, int* next_ctr,
+                                int n_pre) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int4 it = v.pre_sorted[item];
-  const int seq = it.x, g = it.y, t0 = it.z;
-  const int row0 = a.cu_q[seq];
-  const int q_len = a.cu_q[seq + 1] - row0;
-  const int kv_len = a.seq_lens_k[seq];
-  const int prefix = kv_len - q_len;
-  const int nrows = min(PRE_QROWS, q_len - t0);
-  const int kv_end = prefix + t0 + nrows;
-  int tlo, thi;                                 // key tiles of this item (or piece)
-  pre_piece_range(it.w, (kv_end + TC_KEYS - 1) / TC_KEYS, tlo, thi);
-  const int ntiles = thi - tlo;
-  const int nblk = (kv_end + HY_BLOCK - 1) / HY_BLOCK;
+  const PreItem P = pre_item_geom(a, v, item);
+  const int seq = P.seq, g = P.g, t0 = P.t0, row0 = P.row0, nrows = P.nrows;
+  const int kv_len = P.kv_len, prefix = P.prefix, tlo = P.tlo;
+  const int ntiles = P.thi - P.tlo;             // key tiles of this item (or piece)
   const uint32_t sbase = smem_u32(payload);
   const uint32_t c0 = ctr;
   ctr += ntiles;
   bool ok = true;
-  int next = 0x7fffffff;                        // thread 0: the CTA's next item
 
   if (warp == TC_LOAD_WARP || warp == TC_LOAD_WARP2) {
     // Two load warps, lw = 0, 1, each for blocks 2 lw and 2 lw + 1 of every key
-    // tile: lane 0 waits for the slot and posts the warp's byte count; lanes 0-3
-    // then issue one 4 KB box each (K of blocks 2 lw, 2 lw + 1, then their V).
-    // One wait and one arm per tile: a load warp's wait, arm and first box are
-    // serial round trips of ~150-270 cycles each, so the tile's supply rate is
-    // set by how many of them a warp makes per tile.
+    // tile, one wait and one arm per tile (a load warp's wait, arm and first
+    // box are serial round trips of ~150-270 cycles each, so the tile's supply
+    // rate is set by how many of them a warp makes per tile).  pf >= 0: the
+    // previous item's load warps already issued this item's Q and its first pf
+    // key tiles; -1: Q first.
     const int lw = warp == TC_LOAD_WARP2;
-    // Q first: one 32 KB box per sub-tile X (64 columns x 64 tokens x query heads
-    // 4g + 2X, 4g + 2X + 1 x both column halves), landing as the K-major
-    // operand [half][128 rows][64] with row = 64 (head - 4g - 2X) + token; the
-    // Q region is free, the previous item's MMAs having completed before it
-    // ended.  Rows past the chunk read later tokens (or zeros past the last
-    // token): their scores are computed but never stored.
-    if (lw == 0 && lane == 0) {
-      mbar_arrive_expect_tx(&sh.tc_qfull, 2 * TC_Q_BYTES);
-      for (int X = 0; X < 2; ++X)
-        tma_load_4d(payload + X * TC_Q_BYTES, qmap, 0, row0 + t0, g * HY_GROUP + 2 * X, 0,
-                    &sh.tc_qfull);
-    }
-    const int bt_row = a.seq_bt_row ? a.seq_bt_row[seq] : seq;
-    const int32_t* bt = a.block_tables + (size_t)bt_row * a.bt_pitch;
+    if (pf < 0 && lw == 0 && lane == 0) pre_issue_q(qmap, P, payload, sh);
+    const int first = max(pf, 0);
+    const int32_t* bt = pre_block_table(a, seq);
     int ids = -1;                               // lane i: block 32 (kt / 8) + i of the sequence
-    int issued = 0;                             // tiles whose loads were issued
-    for (int t = 0; t < ntiles && ok; ++t) {
+    int issued = first;                         // tiles whose loads were issued
+    for (int t = first; t < ntiles && ok; ++t) {
       const int kt = tlo + t;                   // key tile of the sequence
-      if (t == 0 || (kt & 7) == 0) {
+      if (t == first || (kt & 7) == 0) {
         const int b = 4 * (kt & ~7) + lane;
-        ids = (b < nblk && b < a.bt_pitch) ? bt[b] : -1;
+        ids = (b < P.nblk && b < a.bt_pitch) ? bt[b] : -1;
       }
-      const uint32_t c = c0 + t, slot = c % TC_NS, use = c / TC_NS;
-      bool w_ok = true;
-      if (lane == 0) w_ok = mbar_wait(&sh.tc_free[slot], (use & 1) ^ 1, a.err);
-      if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) { ok = false; break; }
-      uint64_t* full = &sh.tc_full[slot];
-      if (lane == 0) mbar_arrive_expect_tx(full, TC_KV_BYTES);
-      const int kv = (lane >> 1) & 1, jb = 2 * lw + (lane & 1);
-      const int id = __shfl_sync(0xffffffffu, ids, (4 * kt + jb) & 31);
-      if (lane < 4) {
-        int r = a.oob_row;                      // past the end: zero fill
-        if (id >= a.num_blocks) hy_flag(a.err, HY_ERR_BOUNDS);
-        else if (id >= 0) r = kv_row(a, id, kv, g);
-        if (kv)
-          tma_load_3d(payload + TC_V_OFF + slot * TC_KV_BYTES + jb * 4096, tiles, 0, r, 0, full);
-        else
-          tma_load_4d(payload + TC_K_OFF + slot * TC_KV_BYTES + jb * 4096, kgroups, 0, r, 0, 0,
-                      full);
+      const int id = __shfl_sync(0xffffffffu, ids, (4 * kt + 2 * lw + (lane & 1)) & 31);
+      if (!pre_issue_tile(kgroups, tiles, a, g, lw, lane, c0 + t, id, payload, sh)) {
+        ok = false;
+        break;
       }
       issued = t + 1;
     }
@@ -1029,6 +1071,66 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
     }
     // Q has landed before the item ends (the next item's Q reuses the region)
     if (lw == 0 && lane == 0) mbar_wait(&sh.tc_qfull, qpar, nullptr);
+    // The CTA's next item, taken now (this item's loads are all issued, a few
+    // tiles before its end): its Q, once both sub-tiles' S of this item's last
+    // tile completed, and its first key tiles, as this item's P V MMAs free
+    // the ring slots, load while this item's last tiles and epilogue run.
+    // Both load warps always reach the two barriers below.
+    // Load warp 0 decides for both: it takes the item and waits for the S MMAs.
+    named_sync(PRE_LOAD_BAR, 64);
+    if (lw == 0 && lane == 0) {
+      int nx = ok ? atomicAdd(next_ctr, 1) : 0x7fffffff;
+      bool go = nx < n_pre;
+      if (go) {
+        // S of this item's last tile cl, after S of tile cl - 2 (the same S
+        // buffer): waiting in order keeps each parity wait on the barrier's
+        // current or previous phase (a short item whose tiles were all loaded
+        // ahead gets here before its first S, two phases behind; phases before
+        // cl - 2 completed before the load of tile cl was issued, or belong to
+        // the previous item)
+        const uint32_t cl = c0 + ntiles - 1;
+        for (uint32_t c = ntiles >= 3 ? cl - 2 : cl; go && c <= cl; c += 2)
+          go = mbar_wait(&sh.tc_sfull[0][c & 1], (c >> 1) & 1, a.err) &&
+               mbar_wait(&sh.tc_sfull[1][c & 1], (c >> 1) & 1, a.err);
+        if (!go) {                              // the CTA stops after this item
+          ok = false;
+          nx = 0x7fffffff;
+        }
+      }
+      sh.pre_item = nx;
+      sh.pre_prefetch = go ? 0 : -1;
+    }
+    named_sync(PRE_LOAD_BAR, 64);
+    if (sh.pre_prefetch == 0) {
+      const PreItem N = pre_item_geom(a, v, sh.pre_item);
+      if (lw == 0 && lane == 0) pre_issue_q(qmap, N, payload, sh);
+      const int32_t* nbt = pre_block_table(a, N.seq);
+      const int want = min(TC_NS, N.thi - N.tlo);
+      int pfn = 0;
+      bool p_ok = true;
+      for (; pfn < want; ++pfn) {
+        const int b = 4 * (N.tlo + pfn) + 2 * lw + (lane & 1);
+        const int id = (lane < 4 && b < N.nblk && b < a.bt_pitch) ? nbt[b] : -1;
+        if (!pre_issue_tile(kgroups, tiles, a, N.g, lw, lane, c0 + ntiles + pfn, id, payload,
+                            sh)) {
+          p_ok = false;
+          break;
+        }
+      }
+      // both warps issued `want` tiles unless a wait ran out in either: then the
+      // CTA stops after this item, and each warp's look-ahead loads land first
+      const bool any_fail = named_sync_or(PRE_LOAD_BAR, 64, !p_ok);
+      if (any_fail) {
+        ok = false;
+        if (lane == 0)
+          for (int t = 0; t < pfn; ++t) {
+            const uint32_t c = c0 + ntiles + t;
+            mbar_wait(&sh.tc_full[c % TC_NS], (c / TC_NS) & 1, nullptr);
+          }
+        if (lw == 0 && lane == 0) mbar_wait(&sh.tc_qfull, qpar ^ 1u, nullptr);
+      }
+      if (lw == 0 && lane == 0) sh.pre_prefetch = any_fail ? -1 : want;
+    }
   } else if (warp == TC_MMA_WARP || warp == TC_MMA_WARP1) {
     // one MMA warp per sub-tile X: its lane 0 issues S_X(t), then O_X += P_X(t-1)
     // V_{t-1}; both warps commit to the slot's free barrier after P V (count 2)
@@ -1088,11 +1190,6 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
     for (int t = 0; t < ntiles && ok; ++t) {
       const uint32_t c = c0 + t;
       const uint32_t tS = tmem + lane_base + tm_s(X, c & 1);
-      // the next item is taken when this one's last key tile starts: its
-      // latency hides behind the tile, and a CTA holds no item it cannot start
-      // soon (CTAs start microseconds apart; taking it at the item's start
-      // left late CTAs without items: one or two per CTA ran 15-25 % slower)
-      if (t == ntiles - 1 && threadIdx.x == 0) next = atomicAdd(next_ctr, 1);
       // waits are made warp-uniform: tcgen05.ld/st below are warp-collective
       ok = __all_sync(0xffffffffu, mbar_wait(&sh.tc_sfull[X][c & 1], (c >> 1) & 1, a.err));
       if (!ok) break;
@@ -1181,8 +1278,8 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
     const bool store = ok && j < nrows;
     __nv_bfloat16* op = a.out + ((size_t)(row0 + t0 + j) * a.q_heads + g * HY_GROUP + 2 * X +
                                  (r >> 6)) * HY_HEAD_DIM;
-    if (it.w != 0) {                            // a piece: every softmax thread takes part
-      ok = prefill_piece_finish(v, it.w, X * 128 + r, tO, m, l, ok, store ? op : nullptr, sh);
+    if (P.w != 0) {                             // a piece: every softmax thread takes part
+      ok = prefill_piece_finish(v, P.w, X * 128 + r, tO, m, l, ok, store ? op : nullptr, sh);
     } else if (ok) {                            // O_X / l -> out
       const float inv = 1.f / l;
 #pragma unroll 1
@@ -1204,7 +1301,6 @@ __device__ bool prefill_item_tc(const CUtensorMap* kgroups, const CUtensorMap* t
       }
     }
   }
-  if (threadIdx.x == 0) sh.pre_item = next;
   tc_fence_before();
   if (__syncthreads_or(!ok)) ok = false;
   return ok;
@@ -1289,17 +1385,32 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_main_kernel(
   uint32_t dec_phase = 0, tile_ctr = 0;
   bool ok = true;
   int* grab = v.grab + GRAB_INTS * (a.layer & 63);
-  // prefill items: CTA-wide, in the plan's order (most key tiles first); thread
-  // 0 takes the next item from the counter during the current one's last tile
+  // prefill items: CTA-wide, in the plan's order (most key tiles first); the
+  // load warps take each next item from the counter once the current item's
+  // loads are issued, and start its loads
   if (use_tmem) {
-    if (threadIdx.x == 0) sh.pre_item = atomicAdd(&grab[2], 1);
+    if (threadIdx.x == 0) {
+      sh.pre_item = atomicAdd(&grab[2], 1);
+      sh.pre_prefetch = -1;
+    }
     __syncthreads();
-    for (uint32_t n = 0; ok; ++n) {
-      const int k = sh.pre_item;
-      __syncthreads();                          // read before thread 0 writes the next one
+    uint32_t n = 0;
+    for (; ok; ++n) {
+      const int k = sh.pre_item, pf = sh.pre_prefetch;
+      __syncthreads();                          // read before the load warps write the next
       if (k >= n_pre) break;
       ok = prefill_item_tc(&kv_kgroups, &kv_tiles, &q_map, a, v, k, payload, sh, tmem, tile_ctr,
-                           n & 1, &grab[2]);
+                           n & 1, pf, &grab[2], n_pre);
+    }
+    // a CTA stopped by a wait that ran out: loads issued ahead for an item it
+    // will not run land before the shared memory is reused
+    if (!ok && (warp == TC_LOAD_WARP || warp == TC_LOAD_WARP2) && lane == 0) {
+      const int pf = sh.pre_prefetch;
+      for (int t = 0; t < pf; ++t) {
+        const uint32_t c = tile_ctr + t;
+        mbar_wait(&sh.tc_full[c % TC_NS], (c / TC_NS) & 1, nullptr);
+      }
+      if (pf >= 0 && warp == TC_LOAD_WARP) mbar_wait(&sh.tc_qfull, n & 1, nullptr);
     }
   }
   // decode items (warps 0..ATT_WARPS-1): each warp takes the next one from this
