@@ -47,6 +47,8 @@ SIGNATURES = {
                                          F32, P, I64, P, I64, P, P]),
     "hy_silu_mul": (C.c_int, [I32, P, I64, I32, I32, P, I64, P]),
     "hy_argmax": (C.c_int, [I32, P, I64, I32, I32, P, P]),
+    "hy_lm_head_argmax_workspace_size": (I64, []),
+    "hy_lm_head_argmax": (C.c_int, [P, I64, I32, P, I64, I32, I32, P, P, P, P]),
     "hy_selftest_wait_timeout": (C.c_int, [P, I32, P, P]),
     "hy_selftest_exp2_poly": (C.c_int, [P, P, I32, P]),
     "hy_varlen_attention_noalloc": (C.c_int, [P, P, I32, I32, I32, P, I32, I32, I32, P, I32, P,

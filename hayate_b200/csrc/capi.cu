@@ -188,6 +188,30 @@ int hy_attention_q_map(const void* q, int num_tokens, int q_heads, CUtensorMap* 
   return HY_OK;
 }
 
+// A row-major bf16 matrix (rows x cols, row pitch row_bytes) as a 2-D tensor
+// map whose box is 64 columns (one 128-byte swizzle row) x box_rows rows, with
+// 128-byte swizzle in shared memory; rows past the end read zeros.
+int hy_encode_rows_map(const void* base, long cols, long rows, long row_bytes, int box_rows,
+                       CUtensorMap* out) {
+  int rc = get_encoder();
+  if (rc) return rc;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[64];
+    snprintf(buf, sizeof(buf), "%d", (int)r);
+    return fail(HY_E_CUDA, "cuTensorMapEncodeTiled failed on a row-major matrix (CUresult %s)",
+                buf);
+  }
+  return HY_OK;
+}
+
 void hy_set_error(const char* msg) { snprintf(g_last_error, sizeof(g_last_error), "%s", msg); }
 
 bool hy_pdl_enabled() {

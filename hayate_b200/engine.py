@@ -160,7 +160,7 @@ class Engine:
         # A subclass that overrides ``sample`` (the reference's hook for the
         # next-token choice, engine.py:69-71) gets the step's last-token logits
         # and its choice is committed on the device; the built-in greedy choice
-        # runs the fused argmax kernel.  Decode steps are only captured in CUDA
+        # runs the argmax on the device (in bf16, inside the LM-head kernel).  Decode steps are only captured in CUDA
         # graphs for the built-in choice.
         self._sampler = None if type(self).sample is Engine.sample else self.sample
         self.use_graphs = bool(compile or self.ecfg.cuda_graphs) and self._sampler is None

@@ -270,3 +270,27 @@ def argmax(logits: torch.Tensor, out: torch.Tensor) -> None:
     _i32(out, "out")
     check(_lib.load().hy_argmax(_dt(logits), _ptr(logits), logits.stride(0), rows, V, _ptr(out),
                                 _stream()), "hy_argmax")
+
+
+def lm_head_argmax_workspace_size() -> int:
+    return int(_lib.load().hy_lm_head_argmax_workspace_size())
+
+
+def lm_head_argmax(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, workspace: torch.Tensor,
+                   err: Optional[torch.Tensor] = None) -> None:
+    """out[r] = argmax_v bf16(x[r] . w[v]): the LM head and greedy sampling in
+    one kernel (bf16; ``workspace`` zeroed once, left zeroed by every call)."""
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("lm_head_argmax is bf16 only")
+    rows, hidden = x.shape
+    vocab, hidden_w = w.shape
+    if hidden_w != hidden or x.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError("x (rows, hidden) and w (vocab, hidden) need contiguous rows of one width")
+    if out.numel() < rows:
+        raise ValueError("out holds fewer entries than x has rows")
+    _i32(out, "out")
+    if workspace.numel() * workspace.element_size() < lm_head_argmax_workspace_size():
+        raise ValueError("workspace smaller than hy_lm_head_argmax_workspace_size()")
+    check(_lib.load().hy_lm_head_argmax(_ptr(x), x.stride(0), rows, _ptr(w), w.stride(0), vocab,
+                                        hidden, _ptr(out), _ptr(workspace), _ptr(err), _stream()),
+          "hy_lm_head_argmax")

@@ -10,7 +10,9 @@ qk_norm_rope / kv_append / pack / argmax / add_rms_norm / silu_mul: the same
 batch (2304 query tokens: 256 decode rows + 4 x 512 prefill rows) through the
 fused QK-norm+RoPE+append kernel, the standalone KV append, the packing kernel,
 the greedy argmax over the 256+4 sampled rows (vocab 151936), and the residual
-add + RMSNorm (hidden 2560) and SiLU(gate)*up (9728) on its rows.  These inputs fit in L2, so each timed
+add + RMSNorm (hidden 2560) and SiLU(gate)*up (9728) on its rows.  lm_head: the
+LM head and greedy choice over the 256 decode rows (hidden 2560, vocab 151936),
+the fused kernel against cuBLAS + argmax.  These inputs fit in L2, so each timed
 launch is preceded by an L2 flush outside the timed window: a read of 256 MiB,
 which evicts the op's data without leaving dirty lines whose write-back the
 timed launch would pay.
@@ -26,7 +28,7 @@ launches.  A single flushed launch also carries the launch and event overhead
 (~10 us), which at prefill sizes is as long as the kernel.
 
 ``python -m hayate_b200.microbench [--op attention|qk_norm_rope|kv_append|pack|argmax|
-add_rms_norm|silu_mul|all]
+lm_head|add_rms_norm|silu_mul|all]
 [--iters N]`` prints one JSON line per op.
 """
 from __future__ import annotations
@@ -346,6 +348,32 @@ def argmax_micro(iters: int = 20, rows: int = 260, vocab: int = 151936, stream: 
     return _summary("argmax", ms, nbytes, rows=rows, stream=stream)
 
 
+def lm_head_micro(iters: int = 20, rows: int = 256, vocab: int = 151936, hidden: int = 2560):
+    """The LM head and the greedy choice over ``rows`` sampled rows at Qwen3-4B
+    sizes: ``hy_lm_head_argmax`` (one kernel, logits never written) against the
+    cuBLAS GEMM + ``hy_argmax`` pair it replaces.  The weights (778 MB) exceed
+    L2, so launches need no flush between them.  ``bytes`` is the fused
+    kernel's algorithmic traffic: W and x read once, the tokens written."""
+    import torch.nn.functional as F
+    from hayate_b200 import kernels as K
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn(vocab, hidden, device=dev, dtype=torch.bfloat16, generator=g) * 0.02
+    x = torch.randn(rows, hidden, device=dev, dtype=torch.bfloat16, generator=g)
+    ws = torch.zeros(K.lm_head_argmax_workspace_size(), dtype=torch.uint8, device=dev)
+    out_f = torch.empty(rows, dtype=torch.int32, device=dev)
+    out_u = torch.empty(rows, dtype=torch.int32, device=dev)
+    ms_f = _time(lambda: K.lm_head_argmax(x, w, out_f, ws), iters, flush=False)
+    ms_u = _time(lambda: K.argmax(F.linear(x, w), out_u), iters, flush=False)
+    mism = int((out_f != out_u).sum().item())
+    nbytes = vocab * hidden * 2 + rows * hidden * 2 + rows * 4
+    r = _summary("lm_head", ms_f, nbytes, rows=rows, vocab=vocab, hidden=hidden)
+    r["tflops"] = 2.0 * rows * vocab * hidden / (r["ms_mean"] * 1e-3) / 1e12
+    r["unfused_ms_mean"] = statistics.mean(ms_u)
+    r["token_mismatches_vs_unfused"] = mism
+    return r
+
+
 def rowwise_micro(op: str, iters: int = 20, rows: int = 2304, hidden: int = 2560,
                   inter: int = 9728, stream: bool = False):
     """Residual add + RMSNorm over [rows][hidden] (``add_rms_norm``) or SiLU(gate) * up
@@ -377,7 +405,8 @@ def rowwise_micro(op: str, iters: int = 20, rows: int = 2304, hidden: int = 2560
     return _summary(op, ms, nbytes, rows=rows, stream=stream)
 
 
-OPS = ("attention", "qk_norm_rope", "kv_append", "pack", "argmax", "add_rms_norm", "silu_mul")
+OPS = ("attention", "qk_norm_rope", "kv_append", "pack", "argmax", "lm_head", "add_rms_norm",
+       "silu_mul")
 
 
 def run_op(op: str, iters: int, n_decode: int = 256, prefill: bool = True, tokens: int = 2304,
@@ -397,6 +426,8 @@ def run_op(op: str, iters: int, n_decode: int = 256, prefill: bool = True, token
     if op == "argmax":
         return argmax_micro(iters, rows=max(1, n_decode + max(0, tokens - n_decode) // 512),
                             stream=stream)
+    if op == "lm_head":
+        return lm_head_micro(iters, rows=max(1, n_decode))
     if op in ("add_rms_norm", "silu_mul"):
         return rowwise_micro(op, iters, rows=max(1, tokens), stream=stream)
     raise ValueError(f"unknown op {op!r}; one of {OPS} or 'all'")

@@ -5,16 +5,18 @@ One ``Runner.launch_step`` is the device half of a continuous-batching step:
   pack (on-GPU batch build + block allocation) -> attention plan ->
   embed -> RMSNorm -> 36 x [QKV GEMM, QK-norm+RoPE+KV append, varlen attention,
   O GEMM, residual add + RMSNorm, gate/up GEMM, SiLU*up, down GEMM, residual add +
-  next RMSNorm] -> LM-head GEMM on the sampled rows only -> argmax -> commit.
+  next RMSNorm] -> LM head + argmax on the sampled rows only -> commit.
 
 It replaces ``Qwen3Model.forward`` (hayate/model/qwen.py:46-124) with its block
 and attention modules (block.py:21-31, attention.py:26-66, linear.py:11-14) and
 the engine's gather/scatter around it (engine.py:80-163).  The projections, the
 MLP and the LM head stay on cuBLAS through torch; the residual adds fused with
 the RMSNorms, and SiLU*up, are this library's row kernels with the reference's
-rounding points.  The
-LM head runs on the last row of each sampled sequence only, where the
-reference computes logits for every position (qwen.py:122-123).
+rounding points.  The LM head runs on the last row of each sampled sequence
+only, where the reference computes logits for every position (qwen.py:122-123);
+in bf16 greedy steps it is this library's tcgen05 kernel with the argmax in its
+epilogue (``hy_lm_head_argmax``: the logits never reach HBM), otherwise a
+cuBLAS GEMM whose logits go to ``hy_argmax`` or the caller's sampler.
 
 Nothing here synchronises: the step is a fixed sequence of launches over
 static buffers, so a decode step can be captured in a CUDA graph.
@@ -45,6 +47,8 @@ class LayerWeights:
 
 
 _SPLITK_ON = os.environ.get("HY_SPLITK", "1") != "0"
+# HY_LM_FUSED=0: bf16 greedy steps take the cuBLAS LM head + hy_argmax instead
+_LM_FUSED_ON = os.environ.get("HY_LM_FUSED", "1") != "0"
 
 
 def linear_splitk(x: torch.Tensor, w: torch.Tensor, s: int) -> torch.Tensor:
@@ -134,9 +138,13 @@ class Runner:
         self.q_buf = torch.empty(T, cfg.num_heads, cfg.head_dim, dtype=dtype, device=dev)
         self.attn_buf = torch.empty_like(self.q_buf)
         self.ws = None
+        self.lm_ws = None                                # fused LM head + argmax (bf16)
         if dtype == torch.bfloat16:
             nbytes = K.attention_workspace_size(S, T, cfg.num_kv_heads)
             self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+            if _LM_FUSED_ON:
+                self.lm_ws = torch.zeros(K.lm_head_argmax_workspace_size(), dtype=torch.uint8,
+                                         device=dev)
         self.kernel_launches = 0
 
     # ------------------------------------------------------------------ memory
@@ -163,18 +171,30 @@ class Runner:
         """Enqueue one step for the schedule already in ``self.sched[:4*S]``:
         pack, the model, the LM head on the sampled rows, the next tokens
         (greedy argmax kernel, or ``sampler(logits) -> (n, 1) or (n,)`` token
-        ids on the device) committed to the requests' token rows."""
-        logits = self.forward_logits(S, T, n_sample)
-        if logits is None:
-            return
+        ids on the device) committed to the requests' token rows.  bf16
+        greedy steps run the LM head and the argmax as one kernel."""
         toks = self.next_tokens[:n_sample]
-        if sampler is None:
-            K.argmax(logits, toks)
+        if sampler is None and self.lm_ws is not None:
+            h = self.forward_hidden(S, T, n_sample)
+            if h is None:
+                return
+            K.lm_head_argmax(h, self.embed, toks, self.lm_ws, self.error_word)
         else:
-            toks.copy_(sampler(logits).reshape(-1))
+            logits = self.forward_logits(S, T, n_sample)
+            if logits is None:
+                return
+            if sampler is None:
+                K.argmax(logits, toks)
+            else:
+                toks.copy_(sampler(logits).reshape(-1))
         K.commit_tokens(toks, n_sample, self.sample_seq, self.sched[:4 * S], S, self.req_tokens,
                         self.error_word)
-        self.kernel_launches += 2 if sampler is None else 1
+        if sampler is not None:
+            self.kernel_launches += 1
+        elif self.lm_ws is not None:                # one LM-head launch per 256 rows
+            self.kernel_launches += 1 + (n_sample + 255) // 256
+        else:
+            self.kernel_launches += 2
 
     def forward_logits(self, S: int, T: int, n_sample: int) -> Optional[torch.Tensor]:
         """The model half of a step: pack the schedule in ``self.sched[:4*S]``
@@ -190,6 +210,13 @@ class Runner:
         gathered by ``hy_gather_add_rms_norm``, and the final norm follows on
         those rows (the reference norms and projects every position,
         qwen.py:122-123)."""
+        h = self.forward_hidden(S, T, n_sample)
+        return None if h is None else F.linear(h, self.embed)
+
+    def forward_hidden(self, S: int, T: int, n_sample: int) -> Optional[torch.Tensor]:
+        """``forward_logits`` up to the LM head: the final RMSNorm's output
+        ``(n_sample, hidden)`` for the sampled rows (schedule order), or None
+        when no sequence samples."""
         cfg, ecfg = self.cfg, self.ecfg
         err = self.error_word
         Hq, Hkv, D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
@@ -266,7 +293,7 @@ class Runner:
         if n_sample == 0:
             return None
         # decode steps sample every row, in order: h holds exactly those rows
-        return F.linear(h, self.embed)
+        return h
 
     def commit_next_tokens(self, tokens: torch.Tensor, S: int, n_sample: int) -> None:
         """Append ``tokens`` (int32, one per sampled sequence, schedule order) to
@@ -304,6 +331,7 @@ class Runner:
     def launches_per_step(self, n_sample: bool = True) -> int:
         """Kernels of this library one decode step (every row sampled) launches:
         pack, plan, the first RMSNorm, per layer QK-norm+RoPE, attention, two
-        add+RMSNorm and SiLU*up, then argmax and commit."""
+        add+RMSNorm and SiLU*up, then the argmax (fused with the LM head in
+        bf16) and commit."""
         per_layer = 5
         return 2 + (self.ws is not None) + per_layer * len(self.layers) + (2 if n_sample else 0)

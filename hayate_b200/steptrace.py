@@ -35,6 +35,7 @@ LABELS = (
     ("indexSelect", "embedding / row gather"),
     ("plan_kernel", "attention plan"),
     ("pack_kernel", "pack"),
+    ("lm_head_argmax", "LM head + argmax (fused)"),
     ("argmax", "argmax"),
     ("commit", "commit"),
     ("Memcpy", "memcpy"),

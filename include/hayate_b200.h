@@ -250,6 +250,28 @@ int hy_silu_mul(int32_t dtype, const void* gu, int64_t ld, int32_t rows, int32_t
 int hy_argmax(int32_t dtype, const void* logits, int64_t ld, int32_t rows, int32_t vocab,
               int32_t* out, void* stream);
 
+/* Greedy sampling fused into the LM head (bf16 only): out[r] = argmax over
+ * v < vocab of bf16(sum_k x[r][k] * w[v][k]), the last-token logits of the
+ * sampled rows computed on the tensor cores and reduced in the same kernel, so
+ * the rows x vocab logits are never written.  x: rows x hidden (row pitch ldx
+ * elements; the final RMSNorm's output), w: the tied embedding, vocab x hidden
+ * (pitch ldw); hidden a multiple of 64; x, w 16-byte aligned with pitches a
+ * multiple of 8 elements.  Each logit is rounded to bf16 before the comparison,
+ * which follows torch.argmax (first index on ties, NaN above every number,
+ * -0 == +0); a logit whose fp32 sum lies within rounding distance of a bf16
+ * boundary can round the other way than a library GEMM with another summation
+ * order.  Any number of rows (launches of up to 256).  workspace:
+ * hy_lm_head_argmax_workspace_size() bytes, 16-byte aligned, zeroed once by
+ * the caller before its first use; every call leaves it zeroed again, so calls
+ * on one stream may share it and calls that may overlap on the GPU may not.
+ * Waits that run out set HY_DEV_TIMEOUT in *err (may be null).
+ * Replaces: out_head and Engine.sample, hayate/model/qwen.py:122-123 (logits
+ * of every position) and hayate/engine/engine.py:69-71 (torch.argmax). */
+int64_t hy_lm_head_argmax_workspace_size(void);
+int hy_lm_head_argmax(const void* x, int64_t ldx, int32_t rows, const void* w, int64_t ldw,
+                      int32_t vocab, int32_t hidden, int32_t* out, void* workspace,
+                      int32_t* err, void* stream);
+
 /* ------------------------------------------------------------- diagnostics */
 
 /* Failure-detection self-test (no reference counterpart: the reference has no
