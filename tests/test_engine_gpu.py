@@ -194,6 +194,26 @@ def test_graphs_captured_ahead_give_the_same_tokens():
     assert eng.check_device_errors() == 0
 
 
+def test_decode_graphs_of_more_than_128_rows_give_the_eager_tokens():
+    """150 sequences decoding at once: the bucket-160 decode graph samples 160
+    rows, so its LM head + argmax runs on CTA pairs (clusters of two) inside the
+    graph; its tokens must equal those of the same engine without graphs."""
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(1, TINY.vocab_size, (8,), generator=g).tolist() for _ in range(150)]
+    toks = []
+    for graphs in (True, False):
+        eng = tiny_engine(torch.bfloat16, graphs, max_seqs=160)
+        # 256 tokens a step: all 150 prompts are in by the 7th step, before the
+        # first request's 16 tokens are done, so later steps decode 150 rows
+        reqs = eng.generate_text(prompts, max_tokens=16)
+        assert all(r.is_completed and len(r.tokens) == 16 for r in reqs)
+        assert eng.check_device_errors() == 0
+        if graphs:
+            assert 160 in eng._graphs
+        toks.append([r.tokens for r in reqs])
+    assert toks[0] == toks[1]
+
+
 _PDL_SCRIPT = """
 import json, sys, torch
 sys.path.insert(0, {tests!r})
