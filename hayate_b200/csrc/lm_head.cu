@@ -398,6 +398,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) lm_head_argmax_kernel(
   }
 }
 
+std::mutex g_setup_mu;                      // guards the per-device set-up below
 int g_sms[64] = {0};
 int g_pairs[64] = {0};                      // co-resident CTA pairs (clusters of two)
 bool g_attr[64] = {false};
@@ -469,6 +470,7 @@ cudaError_t launch(bool pair, int grid, cudaStream_t st, const CUtensorMap& xmap
 // Per device, once: shared-memory attributes, SM count, co-resident pairs (the
 // tiles are dealt to owners in advance, so every pair must be resident at once).
 cudaError_t setup(int dev) {
+  std::lock_guard<std::mutex> lk(g_setup_mu);
   if (g_attr[dev]) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(lm_head_argmax_kernel<false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, LM_SMEM);
