@@ -55,3 +55,22 @@ def test_splitk_slices_for_decode_sized_bf16_steps_only():
     assert Runner.splitk_parts(bf16, 129, 4096) == 1
     assert Runner.splitk_parts(fp32, 16, 4096) == 1
     assert Runner.splitk_parts(bf16, 16, 4100) == 1
+
+
+def test_replica_shares_partition_the_request_set_with_balanced_work():
+    """The bench's per-rank workload: the ranks' shares of the world x 256
+    replica set (prompts U[512,4096], 256 tokens) are disjoint, cover it
+    exactly, and carry near-equal work (prompt + output tokens) under the
+    least-outstanding-work rule; at world 1 the share is the whole set."""
+    from hayate_b200.workloads import replica_share, replicas
+    one = replica_share(1, 0)
+    assert len(one) == 256
+    assert all(512 <= len(w.prompt) <= 4096 and w.max_tokens == 256 for w in one)
+    world = 4
+    full = replicas(n=256 * world)
+    shares = [replica_share(world, r) for r in range(world)]
+    key = lambda w: tuple(w.prompt[:8]) + (len(w.prompt),)   # noqa: E731
+    got = sorted(key(w) for s in shares for w in s)
+    assert got == sorted(key(w) for w in full)
+    work = [sum(len(w.prompt) + w.max_tokens for w in s) for s in shares]
+    assert max(work) - min(work) <= 4096 + 256            # within one request's work
